@@ -1,0 +1,142 @@
+/*
+ * b200_hstu.h -- C ABI of the B200 (sm_100a) HSTU jagged attention library.
+ *
+ * The library implements one operator, forward and backward: the HSTU jagged
+ * causal pointwise (SiLU, not softmax) attention that the reference exposes as
+ *
+ *   hammer::triton_ragged_attention_fwd(int N, float alpha, Tensor q, Tensor k,
+ *       Tensor v, Tensor seq_offsets, str invalid_attn_mask_type,
+ *       Tensor? num_targets, Tensor? attn_scale, int max_attn_len,
+ *       int contextual_seq_len, int full_attn_size, int num_softmax_heads=0)
+ *       -> (Tensor, Tensor)
+ *
+ * (reference: recir/ops/kjt_split_per_feature.cpp:602-693, schema :780-783),
+ * and whose backward argument list the reference fixes in
+ * recir/ops/helion/jagged_hstu_attention.py:875-887.
+ *
+ * Conventions
+ *  - Every pointer in B200HstuParams is a DEVICE pointer owned by the caller.
+ *    The entry points below never allocate or free device memory, never
+ *    synchronise, and launch only on the stream they are given.
+ *  - q, k: [T, H, Dqk]; v, o, d_o: [T, H, Dv]; gradients have the shape of the
+ *    tensor they belong to.  Heads are dense inside a token row; the distance
+ *    between token rows is given per tensor in ELEMENTS (>= H*D), the innermost
+ *    dimension is contiguous.
+ *  - Rows at or past seq_offsets[B] of every output are written as zeros.
+ *  - Return value: 0 on success, a negative B200_HSTU_E* code otherwise.
+ *    Argument errors are detected on the host before anything is launched.
+ *  - Thread safety: the entry points keep no mutable global state besides
+ *    one-time function-attribute set-up; they may be called concurrently from
+ *    several host threads on different streams.
+ */
+#ifndef B200_HSTU_H_
+#define B200_HSTU_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_HSTU_ABI_VERSION 1
+
+/* B200HstuParams.dtype */
+#define B200_HSTU_F32 0
+#define B200_HSTU_BF16 1
+#define B200_HSTU_F16 2
+
+/* B200HstuParams.flags */
+#define B200_HSTU_FLAG_CAUSAL 0x1u          /* invalid_attn_mask_type == "lower_triangular" */
+#define B200_HSTU_FLAG_OFFSETS_I64 0x2u     /* seq_offsets is int64 (else int32) */
+#define B200_HSTU_FLAG_TARGETS_I64 0x4u     /* num_targets is int64 (else int32) */
+#define B200_HSTU_FLAG_SCALE_PER_TOKEN 0x8u /* attn_scale has T values (else 1) */
+#define B200_HSTU_FLAG_FORCE_SIMT 0x10u     /* use the plain CUDA-core kernels (cross-check path) */
+
+/* error codes */
+#define B200_HSTU_OK 0
+#define B200_HSTU_EINVAL (-1)      /* null/ill-formed argument */
+#define B200_HSTU_EUNSUPPORTED (-2) /* dtype / head dim outside what the kernels cover */
+#define B200_HSTU_EALIGN (-3)      /* pointer or stride alignment */
+#define B200_HSTU_EWORKSPACE (-4)  /* workspace missing or too small */
+#define B200_HSTU_ELAUNCH (-5)     /* CUDA launch / driver error */
+#define B200_HSTU_EVERSION (-6)    /* struct_size does not match this library */
+
+typedef struct B200HstuParams {
+  uint32_t struct_size; /* sizeof(B200HstuParams) as compiled by the caller */
+  uint32_t flags;
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;         /* forward output (forward only) */
+  const void* d_o; /* upstream gradient (backward only) */
+  void* dq;        /* backward outputs */
+  void* dk;
+  void* dv;
+  const void* seq_offsets; /* [B+1], monotone, last value <= T */
+  const void* num_targets; /* [B] or NULL */
+  const float* attn_scale; /* NULL => 1/max_seq_len; else 1 or T fp32 values */
+  void* workspace;         /* >= b200_hstu_workspace_bytes(), 256-byte aligned */
+  uint64_t workspace_bytes;
+  int32_t* status; /* optional int32[4]: device-side diagnostics, see b200_hstu_strerror */
+  int64_t T;       /* token rows in q/k/v */
+  int64_t q_row_stride, k_row_stride, v_row_stride, o_row_stride;
+  int64_t do_row_stride, dq_row_stride, dk_row_stride, dv_row_stride;
+  int32_t B, H, Dqk, Dv;
+  int32_t dtype;
+  int32_t max_seq_len; /* N: only used for the default 1/N scale */
+  int32_t max_attn_len;
+  int32_t contextual_seq_len;
+  int32_t full_attn_size;
+  float alpha;
+} B200HstuParams;
+
+/* Forward: o = ((silu(alpha q k^T) * scale) .* keep) v.
+ * Replaces raggedAttention, recir/ops/kjt_split_per_feature.cpp:602-693. */
+int b200_hstu_fwd(const B200HstuParams* params, void* cuda_stream);
+
+/* Backward: dq, dk, dv from d_o (two passes: a dK/dV-major pass and a dQ pass, no atomics
+ * on the gradients).  Replaces autograd through raggedAttention / the backward op of
+ * recir/ops/helion/jagged_hstu_attention.py:875-920. */
+int b200_hstu_bwd(const B200HstuParams* params, void* cuda_stream);
+
+/* Scratch bytes the call needs in params->workspace.  pass: 0 = forward, 1 = backward.
+ * Depends only on B, H, T, Dqk, Dv, dtype and flags. */
+size_t b200_hstu_workspace_bytes(const B200HstuParams* params, int pass);
+
+/* 1 if the tensor-core (tcgen05/TMA) kernels will serve this problem, 0 if the CUDA-core
+ * kernels will, negative error code if the arguments are invalid.  pass as above. */
+int b200_hstu_uses_tensor_cores(const B200HstuParams* params, int pass);
+
+/* Number of kernels one call of the given pass launches (for launch accounting). */
+int b200_hstu_launch_count(const B200HstuParams* params, int pass);
+
+const char* b200_hstu_strerror(int code);
+int b200_hstu_version(void);
+/* sizeof(B200HstuParams) as this library was compiled (for foreign-language bindings). */
+size_t b200_hstu_params_size(void);
+
+/* ---- host-only diagnostics (no GPU needed) ---------------------------------------------
+ * They evaluate, on the host, the very same inline functions the kernels compile for the
+ * device, so a CPU test can check the mask rule and the tile-skipping logic against the
+ * reference rule (recir/ops/kjt_split_per_feature.cpp:639-674).
+ * A sequence is described by len, has_targets/num_targets; the mask by causal,
+ * max_attn_len, contextual_seq_len and full_attn_size. */
+typedef struct B200HstuMaskQuery {
+  int32_t len, has_targets, num_targets;
+  int32_t causal, max_attn_len, contextual_seq_len, full_attn_size;
+} B200HstuMaskQuery;
+
+/* keep(m, n): 1 if query m attends to key n (0 <= m, n < len). */
+int b200_hstu_debug_keep(const B200HstuMaskQuery* mq, int m, int n);
+/* Class of the 128x128 tile at (m0, n0): 0 = skipped, 1 = partial, 2 = fully kept. */
+int b200_hstu_debug_classify_tile(const B200HstuMaskQuery* mq, int m0, int n0);
+/* Key blocks visited for the query block starting at m0: out = {lo, hi, extra_block0}. */
+void b200_hstu_debug_key_blocks(const B200HstuMaskQuery* mq, int m0, int32_t out[3]);
+/* Query blocks visited for the key block starting at n0: out = {lo, hi, 0}. */
+void b200_hstu_debug_query_blocks(const B200HstuMaskQuery* mq, int n0, int32_t out[3]);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B200_HSTU_H_ */

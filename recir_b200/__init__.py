@@ -1,0 +1,9 @@
+"""B200-native HSTU jagged attention (forward and backward) behind the reference's operator surface.
+
+Importing this package registers the ``recir::b200_*`` operators; the kernels live in
+``libb200_hstu.so`` (C ABI in ``include/b200_hstu.h``), built by ``python -m recir_b200.build``.
+"""
+from .ops import hstu_attention, hstu_attention_backward, validate_inputs  # noqa: F401
+from . import sharding, workload  # noqa: F401
+
+__all__ = ["hstu_attention", "hstu_attention_backward", "validate_inputs", "sharding", "workload"]

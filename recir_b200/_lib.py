@@ -1,0 +1,108 @@
+"""ctypes binding of the C ABI in ``include/b200_hstu.h`` (the only route to the kernels).
+
+There is no fallback: if the shared library is missing, loading raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libb200_hstu.so")
+
+F32, BF16, F16 = 0, 1, 2
+FLAG_CAUSAL = 0x1
+FLAG_OFFSETS_I64 = 0x2
+FLAG_TARGETS_I64 = 0x4
+FLAG_SCALE_PER_TOKEN = 0x8
+FLAG_FORCE_SIMT = 0x10
+
+EXPORTS = (
+    "b200_hstu_fwd", "b200_hstu_bwd", "b200_hstu_workspace_bytes", "b200_hstu_uses_tensor_cores",
+    "b200_hstu_launch_count", "b200_hstu_strerror", "b200_hstu_version", "b200_hstu_params_size",
+    "b200_hstu_debug_keep", "b200_hstu_debug_classify_tile", "b200_hstu_debug_key_blocks",
+    "b200_hstu_debug_query_blocks",
+)
+
+
+class B200HstuMaskQuery(ctypes.Structure):
+    """Mirror of ``struct B200HstuMaskQuery`` (host-only diagnostics)."""
+
+    _fields_ = [(n, ctypes.c_int32) for n in (
+        "len", "has_targets", "num_targets", "causal", "max_attn_len", "contextual_seq_len",
+        "full_attn_size")]
+
+
+class B200HstuParams(ctypes.Structure):
+    """Mirror of ``struct B200HstuParams``; field order and types must match the header."""
+
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("flags", ctypes.c_uint32),
+        ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
+        ("o", ctypes.c_void_p), ("d_o", ctypes.c_void_p),
+        ("dq", ctypes.c_void_p), ("dk", ctypes.c_void_p), ("dv", ctypes.c_void_p),
+        ("seq_offsets", ctypes.c_void_p), ("num_targets", ctypes.c_void_p),
+        ("attn_scale", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
+        ("status", ctypes.c_void_p),
+        ("T", ctypes.c_int64),
+        ("q_row_stride", ctypes.c_int64), ("k_row_stride", ctypes.c_int64),
+        ("v_row_stride", ctypes.c_int64), ("o_row_stride", ctypes.c_int64),
+        ("do_row_stride", ctypes.c_int64), ("dq_row_stride", ctypes.c_int64),
+        ("dk_row_stride", ctypes.c_int64), ("dv_row_stride", ctypes.c_int64),
+        ("B", ctypes.c_int32), ("H", ctypes.c_int32), ("Dqk", ctypes.c_int32), ("Dv", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("max_seq_len", ctypes.c_int32), ("max_attn_len", ctypes.c_int32),
+        ("contextual_seq_len", ctypes.c_int32), ("full_attn_size", ctypes.c_int32),
+        ("alpha", ctypes.c_float),
+    ]
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load ``libb200_hstu.so`` (built by ``python -m recir_b200.build``); raises if absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: the CUDA library has not been built "
+            "(run `python -m recir_b200.build`); there is no fallback implementation")
+    lib = ctypes.CDLL(LIB_PATH)
+    P = ctypes.POINTER(B200HstuParams)
+    lib.b200_hstu_fwd.argtypes = [P, ctypes.c_void_p]
+    lib.b200_hstu_fwd.restype = ctypes.c_int
+    lib.b200_hstu_bwd.argtypes = [P, ctypes.c_void_p]
+    lib.b200_hstu_bwd.restype = ctypes.c_int
+    lib.b200_hstu_workspace_bytes.argtypes = [P, ctypes.c_int]
+    lib.b200_hstu_workspace_bytes.restype = ctypes.c_size_t
+    lib.b200_hstu_uses_tensor_cores.argtypes = [P, ctypes.c_int]
+    lib.b200_hstu_uses_tensor_cores.restype = ctypes.c_int
+    lib.b200_hstu_launch_count.argtypes = [P, ctypes.c_int]
+    lib.b200_hstu_launch_count.restype = ctypes.c_int
+    lib.b200_hstu_strerror.argtypes = [ctypes.c_int]
+    lib.b200_hstu_strerror.restype = ctypes.c_char_p
+    lib.b200_hstu_version.argtypes = []
+    lib.b200_hstu_version.restype = ctypes.c_int
+    lib.b200_hstu_params_size.argtypes = []
+    lib.b200_hstu_params_size.restype = ctypes.c_size_t
+    MQ = ctypes.POINTER(B200HstuMaskQuery)
+    lib.b200_hstu_debug_keep.argtypes = [MQ, ctypes.c_int, ctypes.c_int]
+    lib.b200_hstu_debug_keep.restype = ctypes.c_int
+    lib.b200_hstu_debug_classify_tile.argtypes = [MQ, ctypes.c_int, ctypes.c_int]
+    lib.b200_hstu_debug_classify_tile.restype = ctypes.c_int
+    lib.b200_hstu_debug_key_blocks.argtypes = [MQ, ctypes.c_int, ctypes.POINTER(ctypes.c_int32 * 3)]
+    lib.b200_hstu_debug_key_blocks.restype = None
+    lib.b200_hstu_debug_query_blocks.argtypes = [MQ, ctypes.c_int, ctypes.POINTER(ctypes.c_int32 * 3)]
+    lib.b200_hstu_debug_query_blocks.restype = None
+    if lib.b200_hstu_params_size() != ctypes.sizeof(B200HstuParams):
+        raise RuntimeError("B200HstuParams layout mismatch between Python binding and library")
+    _lib = lib
+    return lib
+
+
+def strerror(code: int) -> str:
+    return load().b200_hstu_strerror(code).decode()

@@ -1,0 +1,119 @@
+// Shared pieces of the tensor-core kernels: the work list built on the device, tile
+// classification against the keep mask, and tensor-map helpers.
+#pragma once
+#include <cuda.h>
+
+#include "hstu_common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace hstu {
+namespace tc {
+
+constexpr int BLK = 128;  // rows per query block and per key block
+constexpr int HEAD_DIM = 128;
+
+// ---- workspace layout (ints) ------------------------------------------------
+// [0]            number of work items
+// [1]            number of non-empty sequences
+// [2 .. 15]      reserved
+// [16 .. )       sorted[B]   : sequence ids, longest first
+//                hist[nbins] : sequences per block count, then reused as fill counters
+//                cnt[nbins]  : cnt[j] = sequences with more than j blocks
+//                start[nbins]: first work item of block index j
+//                items[2 * max_items] : (seq | head << 16, block index) per work item
+struct WorkspaceLayout {
+  long long nbins, max_items;
+  long long off_sorted, off_hist, off_cnt, off_start, off_items, total_ints;
+};
+
+HSTU_HD WorkspaceLayout workspace_layout(long long T, int B, int H) {
+  WorkspaceLayout w;
+  w.nbins = (T + BLK - 1) / BLK + 2;
+  w.max_items = (long long)H * (T / BLK + B);
+  w.off_sorted = 16;
+  w.off_hist = w.off_sorted + B;
+  w.off_cnt = w.off_hist + w.nbins;
+  w.off_start = w.off_cnt + w.nbins;
+  w.off_items = (w.off_start + w.nbins + 1) & ~1LL;  // int2 alignment
+  w.total_ints = w.off_items + 2 * w.max_items;
+  return w;
+}
+
+enum TileClass { TILE_SKIP = 0, TILE_PARTIAL = 1, TILE_FULL = 2 };
+
+// Classifies the 128x128 tile with query rows [m0, m0+128) and key rows [n0, n0+128) of one
+// sequence under a causal ("lower_triangular") mask:
+//   SKIP    no pair of the tile is kept (safe to never compute),
+//   FULL    every pair is kept and every row/column lies inside the sequence,
+//   PARTIAL anything else (the exact predicate is evaluated per element).
+HSTU_HD int classify_tile(int m0, int n0, const SeqInfo& s, const MaskOpts& o) {
+  const int L = s.len;
+  if (m0 >= L || n0 >= L) return TILE_SKIP;
+  const int m1 = m0 + BLK - 1, n1 = n0 + BLK - 1;
+  const int m1e = m1 < L ? m1 : L - 1, n1e = n1 < L ? n1 : L - 1;
+  if (o.ctx && s.has_targets && s.hist == 0) return TILE_PARTIAL;  // whole square kept
+  if (n0 > m1e) return TILE_SKIP;                                  // strictly above the diagonal
+  const int hist = s.has_targets ? s.hist : L;
+  const bool diag = (n0 <= m1e) && (m0 <= n1e);
+  if (hist < 0) return diag ? TILE_PARTIAL : TILE_SKIP;  // every id equal: diagonal only
+  const int idm0 = m0 < hist ? m0 : hist, idm1 = m1e < hist ? m1e : hist;
+  const int idn0 = n0 < hist ? n0 : hist, idn1 = n1e < hist ? n1e : hist;
+  const int maxd = idm1 - idn0, mind = idm0 - idn1;
+  bool any = diag;
+  any = any || (maxd > 0 && (o.window <= 0 || mind <= o.window));
+  any = any || (o.ctx && n0 == 0);
+  if (o.window > 0 && o.full > 0) {
+    const int gm = idm1 < s.boundary ? 0 : idm1;
+    const int gn = idn0 < s.boundary ? 0 : idn0;
+    any = any || (gm - gn > 0);
+  }
+  if (!any) return TILE_SKIP;
+  if (m1 >= L || n1 >= L) return TILE_PARTIAL;
+  if (mind > 0 && (o.window <= 0 || maxd <= o.window)) return TILE_FULL;
+  return TILE_PARTIAL;
+}
+
+// Key blocks a query block [m0, m0+128) can touch: optionally block 0, then lo..hi.
+struct BlockRange {
+  int lo, hi, extra0;
+  HSTU_HD int count() const { return hi - lo + 1 + extra0; }
+  HSTU_HD int at(int idx) const { return extra0 ? (idx == 0 ? 0 : lo + idx - 1) : lo + idx; }
+};
+
+HSTU_HD BlockRange key_blocks_for_query_block(int m0, const SeqInfo& s, const MaskOpts& o) {
+  BlockRange r;
+  const int L = s.len;
+  const bool whole = o.ctx && s.has_targets && s.hist == 0;
+  const int m1e = (m0 + BLK - 1 < L ? m0 + BLK - 1 : L - 1);
+  r.hi = (whole ? L - 1 : m1e) / BLK;
+  r.lo = 0;
+  r.extra0 = 0;
+  if (o.window > 0 && o.full <= 0 && !whole) {
+    const int hist = s.has_targets ? s.hist : L;
+    if (hist >= 0) {
+      const int idm0 = m0 < hist ? m0 : hist;
+      int nlo = idm0 - o.window;
+      if (nlo < 0) nlo = 0;
+      r.lo = nlo / BLK;
+      if (r.lo > r.hi) r.lo = r.hi;
+      r.extra0 = (o.ctx && r.lo > 0) ? 1 : 0;
+    }
+  }
+  return r;
+}
+
+// Query blocks a key block [n0, n0+128) can be touched by: lo..hi (hi = last block).
+// With a sliding window the far rows are dropped unless a full-attention tail, the
+// contextual column or the target rows need them; classification skips the rest.
+HSTU_HD BlockRange query_blocks_for_key_block(int n0, const SeqInfo& s, const MaskOpts& o) {
+  BlockRange r;
+  const int L = s.len;
+  const bool whole = o.ctx && s.has_targets && s.hist == 0;
+  r.lo = whole ? 0 : n0 / BLK;
+  r.hi = (L - 1) / BLK;
+  r.extra0 = 0;
+  return r;
+}
+
+}  // namespace tc
+}  // namespace hstu

@@ -1,0 +1,140 @@
+"""Drop-in boundary without a GPU: operator schemas, fake kernels under make_fx, the
+positional swap the reference performs (recir/lowering/op_swap.py:78-97), input validation
+messages (recir/ops/pallas/tests/test_jagged_hstu_attention.py:679-711) and the absence of
+any CPU implementation."""
+import operator
+
+import pytest
+import torch
+from torch.fx.experimental.proxy_tensor import make_fx
+from torch._subclasses.fake_tensor import FakeTensorMode
+
+import recir_b200
+from recir_b200 import ops
+
+
+def _fake_inputs(mode, T=12, H=2, D=8, dtype=torch.float32):
+    with mode:
+        q = torch.empty(T, H, D, dtype=dtype, device="cpu")
+        k = torch.empty(T, H, D, dtype=dtype, device="cpu")
+        v = torch.empty(T, H, D, dtype=dtype, device="cpu")
+        off = torch.empty(3, dtype=torch.int64, device="cpu")
+        nt = torch.empty(2, dtype=torch.int64, device="cpu")
+    return q, k, v, off, nt
+
+
+def test_schema_is_positionally_compatible_with_reference_op():
+    # hammer::triton_ragged_attention_fwd, recir/ops/kjt_split_per_feature.cpp:780-783
+    want = ("N alpha q k v seq_offsets invalid_attn_mask_type num_targets attn_scale max_attn_len "
+            "contextual_seq_len full_attn_size num_softmax_heads").split()
+    schema = torch.ops.recir.b200_ragged_attention_fwd.default._schema
+    assert [a.name for a in schema.arguments] == want
+    assert len(schema.returns) == 2
+    bwd = torch.ops.recir.b200_ragged_attention_bwd.default._schema
+    # recir/ops/helion/jagged_hstu_attention.py:875-887
+    assert [a.name for a in bwd.arguments][:11] == (
+        "dout q k v seq_offsets num_targets attn_scale N alpha max_attn_len full_attn_size").split()
+
+
+def test_fake_kernels_trace_forward_and_backward_as_opaque_nodes():
+    mode = FakeTensorMode(allow_non_fake_inputs=True)
+    q, k, v, off, nt = _fake_inputs(mode)
+
+    def step(q, k, v):
+        q = q.detach().requires_grad_(True)
+        k = k.detach().requires_grad_(True)
+        v = v.detach().requires_grad_(True)
+        o = torch.ops.recir.b200_hstu_attention_fwd(q, k, v, off, 8, 0.5, True, nt, 0, 0, None, 0)
+        dq, dk, dv = torch.autograd.grad(o.sum(), (q, k, v))
+        return o, dq, dk, dv
+
+    with mode:
+        gm = make_fx(step, tracing_mode="fake")(q, k, v)
+    targets = [n.target for n in gm.graph.nodes if n.op == "call_function"]
+    assert torch.ops.recir.b200_hstu_attention_fwd.default in targets
+    assert torch.ops.recir.b200_hstu_attention_bwd.default in targets
+    bwd_node = next(n for n in gm.graph.nodes if n.target == torch.ops.recir.b200_hstu_attention_bwd.default)
+    assert sum(1 for u in bwd_node.users if u.target is operator.getitem) == 3
+    assert bwd_node.meta["val"][0].shape == q.shape
+
+
+def test_meta_kernel_visible_to_the_lowering_predicate():
+    # recir/lowering/lowering_utils.py:19-27 keeps an op inside a compiled segment only if a
+    # Meta kernel can be computed for it
+    for name in ("b200_hstu_attention_fwd", "b200_hstu_attention_bwd", "b200_ragged_attention_fwd",
+                 "b200_ragged_attention_bwd"):
+        op = getattr(torch.ops.recir, name).default
+        assert torch._C._dispatch_has_computed_kernel_for_dispatch_key(op.name(), "Meta")
+
+
+@torch.library.custom_op("recir_b200_test::source_ragged_attention", mutates_args=())
+def _source_op(N: int, alpha: float, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+               seq_offsets: torch.Tensor, invalid_attn_mask_type: str, num_targets: torch.Tensor | None,
+               attn_scale: torch.Tensor | None, max_attn_len: int, contextual_seq_len: int,
+               full_attn_size: int, num_softmax_heads: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    raise RuntimeError("source op is a stand-in and must be swapped out")
+
+
+@_source_op.register_fake
+def _(N, alpha, q, k, v, seq_offsets, invalid_attn_mask_type, num_targets, attn_scale, max_attn_len,
+      contextual_seq_len, full_attn_size, num_softmax_heads=0):
+    return torch.empty_like(v), q.new_empty((1,), dtype=torch.float32)
+
+
+def _swap(gm, mapping):
+    """What recir/lowering/op_swap.py:78-97 does: retarget matching call_function nodes."""
+    n = 0
+    for node in gm.graph.nodes:
+        if node.op == "call_function" and node.target in mapping:
+            node.target = mapping[node.target]
+            n += 1
+    gm.recompile()
+    return n
+
+
+def test_positional_swap_of_the_attention_node():
+    mode = FakeTensorMode(allow_non_fake_inputs=True)
+    q, k, v, off, nt = _fake_inputs(mode)
+
+    def fwd(q, k, v):
+        out, _aux = torch.ops.recir_b200_test.source_ragged_attention(
+            8, 0.5, q, k, v, off, "lower_triangular", nt, None, 0, 0, 0, 0)
+        return out * 2
+
+    with mode:
+        gm = make_fx(fwd, tracing_mode="fake")(q, k, v)
+    src = torch.ops.recir_b200_test.source_ragged_attention.default
+    assert _swap(gm, {src: torch.ops.recir.b200_ragged_attention_fwd.default}) == 1
+    tg = [n.target for n in gm.graph.nodes if n.op == "call_function"]
+    assert torch.ops.recir.b200_ragged_attention_fwd.default in tg and src not in tg
+    with mode:  # the swapped graph still runs under fake tensors (Meta kernel present)
+        out = gm(q, k, v)
+    assert out.shape == v.shape
+
+
+def test_validation_messages():
+    q = torch.zeros(5, 2, 4)
+    off = torch.tensor([0, 3, 5])
+    with pytest.raises(ValueError, match=r"shape \[B\]"):
+        recir_b200.validate_inputs(q, q, q, off, torch.zeros(3, dtype=torch.int64), 4)
+    with pytest.raises(ValueError, match="packed shape"):
+        recir_b200.validate_inputs(q, q, q, off, None, 4, dout=torch.zeros(2, 2, 4, 6))
+    with pytest.raises(ValueError, match=r"shape \[T, H, D\]"):
+        recir_b200.validate_inputs(q[0], q, q, off, None, 4)
+    with pytest.raises(ValueError, match="share packed-token and head"):
+        recir_b200.validate_inputs(q, q[:, :1], q, off, None, 4)
+    with pytest.raises(ValueError, match="feature dimension"):
+        recir_b200.validate_inputs(q, q[:, :, :2], q, off, None, 4)
+    with pytest.raises(ValueError, match=r"shape \[B \+ 1\]"):
+        recir_b200.validate_inputs(q, q, q, off[:1], None, 4)
+    with pytest.raises(ValueError, match="max_seq_len must be positive"):
+        recir_b200.validate_inputs(q, q, q, off, None, 0)
+    with pytest.raises(ValueError, match="same dtype"):
+        recir_b200.validate_inputs(q, q, q, off, None, 4, dout=q.double())
+
+
+def test_no_cpu_implementation():
+    q = torch.zeros(5, 2, 4)
+    off = torch.tensor([0, 3, 5])
+    with pytest.raises((NotImplementedError, RuntimeError)):
+        recir_b200.hstu_attention(q, q, q, off, 4)

@@ -1,0 +1,114 @@
+"""CPU-side checks of the C ABI: the library loads without a GPU, exports every symbol the
+header declares, and its mask / tile-skipping logic (the same inline functions the kernels
+use) agrees with the oracle's restatement of the reference mask rule."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from oracle import hstu_oracle
+from recir_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _header_functions():
+    text = open(os.path.join(ROOT, "include", "b200_hstu.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(b200_hstu_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = _header_functions()
+    assert len(names) >= 12
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/b200_hstu.h but not exported"
+    assert set(names) == set(_lib.EXPORTS)
+
+
+def test_version_size_and_strerror():
+    lib = _lib.load()
+    assert lib.b200_hstu_version() == 1
+    assert lib.b200_hstu_params_size() == ctypes.sizeof(_lib.B200HstuParams)
+    assert _lib.strerror(0) == "ok"
+    for code in range(-6, 0):
+        assert "unknown" not in _lib.strerror(code)
+    assert "unknown" in _lib.strerror(-99)
+
+
+def test_argument_errors_detected_on_host():
+    lib = _lib.load()
+    p = _lib.B200HstuParams()
+    assert lib.b200_hstu_fwd(ctypes.byref(p), None) == -6  # struct_size 0
+    p.struct_size = ctypes.sizeof(p)
+    p.dtype = 7
+    assert lib.b200_hstu_fwd(ctypes.byref(p), None) == -2
+    p.dtype = _lib.BF16
+    p.H, p.Dqk, p.Dv, p.T, p.B, p.max_seq_len = 2, 128, 128, 16, 1, 16
+    assert lib.b200_hstu_fwd(ctypes.byref(p), None) == -1  # null seq_offsets
+    assert lib.b200_hstu_workspace_bytes(ctypes.byref(p), 0) == 0
+
+
+def _mq(L, t, causal, w, ctx, f):
+    q = _lib.B200HstuMaskQuery()
+    q.len, q.has_targets, q.num_targets = L, int(t is not None), 0 if t is None else t
+    q.causal, q.max_attn_len, q.contextual_seq_len, q.full_attn_size = int(causal), w, ctx, f
+    return q
+
+
+@pytest.mark.parametrize("seed", range(30))
+def test_device_keep_rule_matches_oracle_mask(seed):
+    lib = _lib.load()
+    rng = np.random.default_rng(seed)
+    L = int(rng.integers(1, 40))
+    t = [None, int(rng.integers(0, L + 3))][seed % 2]
+    causal = seed % 5 != 4
+    w = int(rng.choice([0, 1, 4, 11]))
+    ctx = int(rng.integers(0, 2)) * 2
+    f = int(rng.choice([0, 3, 50])) if w > 0 else 0
+    ref = hstu_oracle.keep_mask(L, t, causal, w, ctx, f)
+    q = _mq(L, t, causal, w, ctx, f)
+    got = np.array([[lib.b200_hstu_debug_keep(ctypes.byref(q), m, n) for n in range(L)] for m in range(L)], bool)
+    assert (got == ref).all()
+
+
+@pytest.mark.parametrize("seed", range(60))
+def test_tile_classes_and_block_ranges_are_sound(seed):
+    """SKIP tiles hold no kept pair, FULL tiles only kept in-range pairs, and the block
+    ranges the kernels iterate contain every tile that is not SKIP."""
+    lib = _lib.load()
+    rng = np.random.default_rng(1000 + seed)
+    L = int(rng.integers(1, 700))
+    t = [None, int(rng.integers(0, min(L + 3, 300)))][seed % 2]
+    if seed % 11 == 0:
+        t = L  # all targets
+    w = int(rng.choice([0, 0, 5, 100, 130, 300]))
+    ctx = int(rng.integers(0, 2))
+    f = int(rng.choice([0, 0, 7, 200])) if w > 0 else 0
+    keep = hstu_oracle.keep_mask(L, t, True, w, ctx, f)
+    q = _mq(L, t, True, w, ctx, f)
+    nblk = (L + 127) // 128
+    out = (ctypes.c_int32 * 3)()
+    for qb in range(nblk):
+        lib.b200_hstu_debug_key_blocks(ctypes.byref(q), qb * 128, ctypes.byref(out))
+        visited = set(range(out[0], out[1] + 1)) | ({0} if out[2] else set())
+        for kb in range(nblk + 1):
+            cls = lib.b200_hstu_debug_classify_tile(ctypes.byref(q), qb * 128, kb * 128)
+            sub = keep[qb * 128:(qb + 1) * 128, kb * 128:(kb + 1) * 128]
+            if cls == 0:
+                assert not sub.any(), (qb, kb)
+            else:
+                assert kb in visited, (qb, kb, list(out))
+            if cls == 2:
+                assert sub.shape == (128, 128) and sub.all(), (qb, kb)
+            if kb not in visited:
+                assert not sub.any(), (qb, kb, list(out))
+    for kb in range(nblk):
+        lib.b200_hstu_debug_query_blocks(ctypes.byref(q), kb * 128, ctypes.byref(out))
+        visited = set(range(out[0], out[1] + 1))
+        for qb in range(nblk):
+            if qb not in visited:
+                assert not keep[qb * 128:(qb + 1) * 128, kb * 128:(kb + 1) * 128].any()
