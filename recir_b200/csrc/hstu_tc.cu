@@ -20,6 +20,7 @@
 
 #include "hstu_launch.h"
 #include "hstu_tc_common.cuh"
+#include "hstu_tc_host.h"
 
 namespace hstu {
 namespace tc {
@@ -148,8 +149,6 @@ __global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, W
 
 constexpr int NUM_K_STAGES = 3;
 constexpr int NUM_V_STAGES = 3;
-constexpr int TILE_BYTES = BLK * HEAD_DIM * 2;  // 32 KB: one 128x128 16-bit tile (two 64-column boxes)
-constexpr int HALF_TILE_BYTES = TILE_BYTES / 2;
 constexpr int FWD_THREADS = 384;
 constexpr int TMEM_COLS = 512;
 constexpr int TMEM_S0 = 0, TMEM_S1 = 128, TMEM_O0 = 256, TMEM_O1 = 384;
@@ -171,29 +170,6 @@ struct FwdShared {
 struct TensorMaps {
   CUtensorMap q, k, v;
 };
-
-// error codes written to status[1] by a wait that gave up
-enum { WAIT_PRODUCER = 101, WAIT_MMA = 102, WAIT_EPILOGUE = 103 };
-
-template <bool IS_BF16>
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  return IS_BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
-}
-
-// Clears row `row` of a 128x128 16-bit tile (two 64-column boxes, 128 bytes per box row) if it
-// lies at or past `first_bad`, and makes the write visible to the async proxy (TMA / MMA).
-// The swizzle only permutes 16-byte chunks inside a 128-byte row, so whole rows can be cleared
-// without knowing it.
-__device__ __forceinline__ void zero_tile_rows(unsigned char* tile, int first_bad, int row) {
-  if (row >= first_bad) {
-    uint4* r0 = reinterpret_cast<uint4*>(tile + row * 128);
-    uint4* r1 = reinterpret_cast<uint4*>(tile + HALF_TILE_BYTES + row * 128);
-    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) { r0[i] = z; r1[i] = z; }
-  }
-  fence_proxy_async();
-}
 
 template <bool IS_BF16>
 __global__ void __launch_bounds__(FWD_THREADS, 1)
@@ -470,11 +446,13 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, const int* __
 // Host side
 // ------------------------------------------------------------------------------------
 
+}  // namespace
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-EncodeTiledFn encode_fn() {
+static EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -515,7 +493,7 @@ int sm_count() {
 }
 
 template <typename T>
-cudaError_t launch_prep(const KernelArgs& a, int* ws, const WorkspaceLayout& w, bool backward, cudaStream_t st) {
+static cudaError_t launch_prep_t(const KernelArgs& a, int* ws, const WorkspaceLayout& w, bool backward, cudaStream_t st) {
   build_block_index<<<1, 1024, 0, st>>>(a, ws, w);
   const int blocks = sm_count() * 2;
   if (!backward)
@@ -528,12 +506,15 @@ cudaError_t launch_prep(const KernelArgs& a, int* ws, const WorkspaceLayout& w, 
   return cudaGetLastError();
 }
 
-}  // namespace
+cudaError_t launch_prep(const KernelArgs& a, bool bf16, int* ws, const WorkspaceLayout& w, bool backward,
+                        cudaStream_t st) {
+  return bf16 ? launch_prep_t<__nv_bfloat16>(a, ws, w, backward, st) : launch_prep_t<__half>(a, ws, w, backward, st);
+}
+
 }  // namespace tc
 
 bool tc_supported(const B200HstuParams& p, const KernelArgs& a, int pass) {
   if (p.flags & B200_HSTU_FLAG_FORCE_SIMT) return false;
-  if (pass != 0) return false;  // backward: CUDA-core kernels for now
   if (p.dtype != B200_HSTU_BF16 && p.dtype != B200_HSTU_F16) return false;
   if (a.Dqk != tc::HEAD_DIM || a.Dv != tc::HEAD_DIM) return false;
   if (!a.mask.causal) return false;
@@ -545,6 +526,8 @@ bool tc_supported(const B200HstuParams& p, const KernelArgs& a, int pass) {
   };
   if (!ok16(a.q, a.q_rs) || !ok16(a.k, a.k_rs) || !ok16(a.v, a.v_rs)) return false;
   if (pass == 0 && !ok16(a.o, a.o_rs)) return false;
+  if (pass == 1 && (!ok16(a.d_o, a.do_rs) || !ok16(a.dq, a.dq_rs) || !ok16(a.dk, a.dk_rs) || !ok16(a.dv, a.dv_rs)))
+    return false;
   return true;
 }
 
@@ -569,7 +552,7 @@ cudaError_t tc_forward(const KernelArgs& a, int dtype, void* workspace, cudaStre
   if (!make_map(&maps.q, a.q, a.T, width, a.q_rs, bf16) || !make_map(&maps.k, a.k, a.T, width, a.k_rs, bf16) ||
       !make_map(&maps.v, a.v, a.T, width, a.v_rs, bf16))
     return cudaErrorInvalidValue;
-  cudaError_t e = bf16 ? launch_prep<__nv_bfloat16>(a, ws, w, false, st) : launch_prep<__half>(a, ws, w, false, st);
+  cudaError_t e = launch_prep(a, bf16, ws, w, false, st);
   if (e != cudaSuccess) return e;
   const size_t smem = sizeof(FwdShared) + 1024;
   auto kern = bf16 ? hstu_fwd_tc<true> : hstu_fwd_tc<false>;
@@ -581,6 +564,5 @@ cudaError_t tc_forward(const KernelArgs& a, int dtype, void* workspace, cudaStre
   return cudaGetLastError();
 }
 
-cudaError_t tc_backward(const KernelArgs&, int, void*, cudaStream_t) { return cudaErrorNotSupported; }
 
 }  // namespace hstu

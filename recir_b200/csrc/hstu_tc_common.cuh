@@ -115,5 +115,44 @@ HSTU_HD BlockRange query_blocks_for_key_block(int n0, const SeqInfo& s, const Ma
   return r;
 }
 
+constexpr int TILE_BYTES = BLK * HEAD_DIM * 2;  // 32 KB: one 128x128 16-bit tile (two 64-column boxes)
+constexpr int HALF_TILE_BYTES = TILE_BYTES / 2;
+constexpr int SUBTILE_BYTES = 64 * 128;  // 64 rows of one box: rows [64, 128) of a tile start here
+
+// codes written to status[1] by a wait that gave up
+enum { WAIT_PRODUCER = 101, WAIT_MMA = 102, WAIT_EPILOGUE = 103 };
+
+#if defined(__CUDACC__)
+template <bool IS_BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  return IS_BF16 ? sm100::pack_bf16x2(lo, hi) : sm100::pack_f16x2(lo, hi);
+}
+
+// Clears row `row` of a 128x128 16-bit tile (two 64-column boxes, 128 bytes per box row) if it
+// lies at or past `first_bad`, and makes the write visible to the async proxy (TMA / MMA).
+// The swizzle only permutes 16-byte chunks inside a 128-byte row, so whole rows can be cleared
+// without knowing it.
+__device__ __forceinline__ void zero_tile_rows(unsigned char* tile, int first_bad, int row) {
+  if (row >= first_bad) {
+    uint4* r0 = reinterpret_cast<uint4*>(tile + row * 128);
+    uint4* r1 = reinterpret_cast<uint4*>(tile + HALF_TILE_BYTES + row * 128);
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { r0[i] = z; r1[i] = z; }
+  }
+  sm100::fence_proxy_async();
+}
+// Same for one 64-column half (`half` = 0 or 1) of the row.
+__device__ __forceinline__ void zero_tile_half_row(unsigned char* tile, int first_bad, int row, int half) {
+  if (row >= first_bad) {
+    uint4* r = reinterpret_cast<uint4*>(tile + half * HALF_TILE_BYTES + row * 128);
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r[i] = z;
+  }
+  sm100::fence_proxy_async();
+}
+#endif
+
 }  // namespace tc
 }  // namespace hstu

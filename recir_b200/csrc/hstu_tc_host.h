@@ -1,0 +1,20 @@
+// Host-side helpers shared by the tensor-core translation units.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "hstu_tc_common.cuh"
+
+namespace hstu {
+namespace tc {
+
+// Tensor map over a [rows, width] 16-bit matrix with the given row stride (elements):
+// box = 64 columns x 128 rows, 128-byte swizzle, zero fill outside the matrix.
+bool make_map(CUtensorMap* m, const void* base, long long rows, long long width, long long row_stride, bool bf16);
+int sm_count();
+// Builds the work list in the workspace and zeroes the output rows no sequence owns.
+cudaError_t launch_prep(const KernelArgs& a, bool bf16, int* ws, const WorkspaceLayout& w, bool backward,
+                        cudaStream_t st);
+
+}  // namespace tc
+}  // namespace hstu
