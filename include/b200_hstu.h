@@ -61,6 +61,7 @@ extern "C" {
 #define B200_HSTU_EWORKSPACE (-4)  /* workspace missing or too small */
 #define B200_HSTU_ELAUNCH (-5)     /* CUDA launch / driver error */
 #define B200_HSTU_EVERSION (-6)    /* struct_size does not match this library */
+#define B200_HSTU_ESCRATCH (-7)    /* problem needs more scratch than the built-in array holds */
 
 typedef struct B200HstuParams {
   uint32_t struct_size; /* sizeof(B200HstuParams) as compiled by the caller */
@@ -110,6 +111,30 @@ int b200_hstu_uses_tensor_cores(const B200HstuParams* params, int pass);
 
 /* Number of kernels one call of the given pass launches (for launch accounting). */
 int b200_hstu_launch_count(const B200HstuParams* params, int pass);
+
+/* Forward for callers that cannot provide scratch memory.  (No counterpart in the reference;
+ * added for this library's own callers.)
+ *
+ * b200_hstu_fwd needs a small work list in params->workspace, which normally comes from the
+ * caller's allocator.  Some callers have no allocator to ask at the point of the call: a
+ * host thread that must not block on cudaMalloc's implicit device synchronisation, a plugin
+ * loaded into a runtime that owns all device memory and hands out none, or a replay loop
+ * whose memory plan is frozen.  This entry point computes exactly what b200_hstu_fwd
+ * computes but keeps the work list in an array built into the library
+ * (B200_HSTU_STATIC_SCRATCH_BYTES of device memory, reserved on every GPU that loads the
+ * library, until the process exits).  params->workspace and workspace_bytes are ignored.
+ *
+ *  - It never calls cudaMalloc/cudaFree or any allocating routine.
+ *  - Problems whose work list does not fit (b200_hstu_workspace_bytes(params, 0) greater than
+ *    B200_HSTU_STATIC_SCRATCH_BYTES) are rejected with B200_HSTU_ESCRATCH before anything
+ *    is launched.
+ *  - The first call on each device looks up the array's device address; make that first
+ *    call before starting any stream capture on that device.
+ *  - All calls on one device share the one array (it keeps the previous call's contents;
+ *    every call rebuilds what it reads).  Two calls that overlap on the GPU, e.g. on two
+ *    streams, race on it: serialise them. */
+#define B200_HSTU_STATIC_SCRATCH_BYTES (4u << 20)
+int b200_hstu_fwd_static_scratch(const B200HstuParams* params, void* cuda_stream);
 
 const char* b200_hstu_strerror(int code);
 int b200_hstu_version(void);

@@ -21,8 +21,9 @@ EXPORTS = (
     "b200_hstu_fwd", "b200_hstu_bwd", "b200_hstu_workspace_bytes", "b200_hstu_uses_tensor_cores",
     "b200_hstu_launch_count", "b200_hstu_strerror", "b200_hstu_version", "b200_hstu_params_size",
     "b200_hstu_debug_keep", "b200_hstu_debug_classify_tile", "b200_hstu_debug_key_blocks",
-    "b200_hstu_debug_query_blocks",
+    "b200_hstu_debug_query_blocks", "b200_hstu_fwd_static_scratch",
 )
+STATIC_SCRATCH_BYTES = 4 << 20
 
 
 class B200HstuMaskQuery(ctypes.Structure):
@@ -75,6 +76,8 @@ def load() -> ctypes.CDLL:
     P = ctypes.POINTER(B200HstuParams)
     lib.b200_hstu_fwd.argtypes = [P, ctypes.c_void_p]
     lib.b200_hstu_fwd.restype = ctypes.c_int
+    lib.b200_hstu_fwd_static_scratch.argtypes = [P, ctypes.c_void_p]
+    lib.b200_hstu_fwd_static_scratch.restype = ctypes.c_int
     lib.b200_hstu_bwd.argtypes = [P, ctypes.c_void_p]
     lib.b200_hstu_bwd.restype = ctypes.c_int
     lib.b200_hstu_workspace_bytes.argtypes = [P, ctypes.c_int]

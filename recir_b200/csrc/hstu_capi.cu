@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "hstu_common.cuh"
 #include "hstu_launch.h"
 #include "hstu_tc_common.cuh"
@@ -86,6 +88,7 @@ const char* b200_hstu_strerror(int code) {
     case B200_HSTU_EWORKSPACE: return "workspace missing, misaligned or smaller than b200_hstu_workspace_bytes()";
     case B200_HSTU_ELAUNCH: return "CUDA launch or driver call failed";
     case B200_HSTU_EVERSION: return "struct_size does not match this library's B200HstuParams";
+    case B200_HSTU_ESCRATCH: return "work list larger than the built-in scratch array (B200_HSTU_STATIC_SCRATCH_BYTES)";
     default: return "unknown b200_hstu error code";
   }
 }
@@ -172,6 +175,54 @@ void b200_hstu_debug_query_blocks(const B200HstuMaskQuery* mq, int n0, int32_t o
 }
 
 int b200_hstu_fwd(const B200HstuParams* p, void* stream) { return run(p, 0, stream); }
+
+}  // extern "C"
+
+// ---- forward with built-in scratch -------------------------------------------------------
+// The work list of the tensor-core forward lives in this array instead of caller memory.
+// In host code the name below is only a handle for the runtime: the device address has to be
+// looked up per device with cudaGetSymbolAddress and that pointer is what the kernels get.
+static __device__ __align__(256) unsigned char g_static_scratch[B200_HSTU_STATIC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of g_static_scratch on the current device (looked up once per device).
+int static_scratch_address(void** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return B200_HSTU_ELAUNCH;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_static_scratch) != cudaSuccess || ptr == nullptr) return B200_HSTU_ELAUNCH;
+    g_scratch_ptr[dev] = ptr;
+  }
+  *out = g_scratch_ptr[dev];
+  return B200_HSTU_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int b200_hstu_fwd_static_scratch(const B200HstuParams* p, void* stream) {
+  KernelArgs a;
+  const int rc = validate(p, 0, &a);
+  if (rc != B200_HSTU_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (hstu::tc_supported(*p, a, 0)) {
+    if (hstu::tc_workspace_bytes(a, 0) > B200_HSTU_STATIC_SCRATCH_BYTES) return B200_HSTU_ESCRATCH;
+    void* scratch = nullptr;
+    const int src = static_scratch_address(&scratch);
+    if (src != B200_HSTU_OK) return src;
+    e = hstu::tc_forward(a, p->dtype, scratch, st);
+  } else {
+    e = hstu::simt_forward(a, p->dtype, p->max_seq_len, st);  // needs no scratch at all
+  }
+  return e == cudaSuccess ? B200_HSTU_OK : B200_HSTU_ELAUNCH;
+}
 int b200_hstu_bwd(const B200HstuParams* p, void* stream) { return run(p, 1, stream); }
 
 }  // extern "C"
