@@ -154,8 +154,14 @@ typedef struct B200HstuMaskQuery {
 
 /* keep(m, n): 1 if query m attends to key n (0 <= m, n < len). */
 int b200_hstu_debug_keep(const B200HstuMaskQuery* mq, int m, int n);
-/* Class of the 128x128 tile at (m0, n0): 0 = skipped, 1 = partial, 2 = fully kept. */
-int b200_hstu_debug_classify_tile(const B200HstuMaskQuery* mq, int m0, int n0);
+/* Class of the 128x128 tile at (m0, n0): 0 = skipped, 1 = partial, 2 = fully kept.
+ * rows_dont_care != 0: query rows past the sequence end may be treated as kept. */
+int b200_hstu_debug_classify_tile(const B200HstuMaskQuery* mq, int m0, int n0, int rows_dont_care);
+/* Interval form of the rule the tensor-core kernels evaluate per element:
+ * row:  keep(m, n) <=> out[0] <= n < out[1] || n == out[2] || n == out[3]
+ * col:  keep(m, n) <=> m == out[3] || out[0] <= m < out[1] || out[2] <= m < len */
+void b200_hstu_debug_row_mask(const B200HstuMaskQuery* mq, int m, int32_t out[4]);
+void b200_hstu_debug_col_mask(const B200HstuMaskQuery* mq, int n, int32_t out[4]);
 /* Key blocks visited for the query block starting at m0: out = {lo, hi, extra_block0}. */
 void b200_hstu_debug_key_blocks(const B200HstuMaskQuery* mq, int m0, int32_t out[3]);
 /* Query blocks visited for the key block starting at n0: out = {lo, hi, 0}. */

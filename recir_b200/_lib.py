@@ -21,7 +21,8 @@ EXPORTS = (
     "b200_hstu_fwd", "b200_hstu_bwd", "b200_hstu_workspace_bytes", "b200_hstu_uses_tensor_cores",
     "b200_hstu_launch_count", "b200_hstu_strerror", "b200_hstu_version", "b200_hstu_params_size",
     "b200_hstu_debug_keep", "b200_hstu_debug_classify_tile", "b200_hstu_debug_key_blocks",
-    "b200_hstu_debug_query_blocks", "b200_hstu_fwd_static_scratch",
+    "b200_hstu_debug_query_blocks", "b200_hstu_fwd_static_scratch", "b200_hstu_debug_row_mask",
+    "b200_hstu_debug_col_mask",
 )
 STATIC_SCRATCH_BYTES = 4 << 20
 
@@ -95,7 +96,10 @@ def load() -> ctypes.CDLL:
     MQ = ctypes.POINTER(B200HstuMaskQuery)
     lib.b200_hstu_debug_keep.argtypes = [MQ, ctypes.c_int, ctypes.c_int]
     lib.b200_hstu_debug_keep.restype = ctypes.c_int
-    lib.b200_hstu_debug_classify_tile.argtypes = [MQ, ctypes.c_int, ctypes.c_int]
+    lib.b200_hstu_debug_classify_tile.argtypes = [MQ, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    for fn in (lib.b200_hstu_debug_row_mask, lib.b200_hstu_debug_col_mask):
+        fn.argtypes = [MQ, ctypes.c_int, ctypes.POINTER(ctypes.c_int32 * 4)]
+        fn.restype = None
     lib.b200_hstu_debug_classify_tile.restype = ctypes.c_int
     lib.b200_hstu_debug_key_blocks.argtypes = [MQ, ctypes.c_int, ctypes.POINTER(ctypes.c_int32 * 3)]
     lib.b200_hstu_debug_key_blocks.restype = None

@@ -154,10 +154,24 @@ int b200_hstu_debug_keep(const B200HstuMaskQuery* mq, int m, int n) {
   return hstu::keep(m, n, s, o) ? 1 : 0;
 }
 
-int b200_hstu_debug_classify_tile(const B200HstuMaskQuery* mq, int m0, int n0) {
+int b200_hstu_debug_classify_tile(const B200HstuMaskQuery* mq, int m0, int n0, int rows_dont_care) {
   hstu::SeqInfo s; hstu::MaskOpts o;
   mask_query(mq, &s, &o);
-  return hstu::tc::classify_tile(m0, n0, s, o);
+  return hstu::tc::classify_tile(m0, n0, s, o, rows_dont_care != 0);
+}
+
+void b200_hstu_debug_row_mask(const B200HstuMaskQuery* mq, int m, int32_t out[4]) {
+  hstu::SeqInfo s; hstu::MaskOpts o;
+  mask_query(mq, &s, &o);
+  const hstu::tc::RowMask r = hstu::tc::row_mask(m, s, o);
+  out[0] = r.lo; out[1] = r.hi; out[2] = r.diag; out[3] = r.extra;
+}
+
+void b200_hstu_debug_col_mask(const B200HstuMaskQuery* mq, int n, int32_t out[4]) {
+  hstu::SeqInfo s; hstu::MaskOpts o;
+  mask_query(mq, &s, &o);
+  const hstu::tc::ColMask c = hstu::tc::col_mask(n, s, o);
+  out[0] = c.a_lo; out[1] = c.a_hi; out[2] = c.b_lo; out[3] = c.diag;
 }
 
 void b200_hstu_debug_key_blocks(const B200HstuMaskQuery* mq, int m0, int32_t out[3]) {

@@ -122,6 +122,28 @@ __device__ __forceinline__ SeqInfo load_seq(const KernelArgs& a, int b) {
   return r;
 }
 
+// Same without the diagnostics: no branch depends on the loaded values, so the loads can stay
+// in flight while other work proceeds (used to fetch the next work item early).
+__device__ __forceinline__ SeqInfo load_seq_quiet(const KernelArgs& a, int b) {
+  long long s = load_index(a.seq_offsets, a.offsets_i64, b);
+  long long e = load_index(a.seq_offsets, a.offsets_i64, b + 1);
+  s = s < 0 ? 0 : (s > a.T ? a.T : s);
+  e = e < s ? s : (e > a.T ? a.T : e);
+  e = (e - s > 0x3fffffffLL) ? s + 0x3fffffffLL : e;
+  SeqInfo r;
+  r.start = s;
+  r.len = static_cast<int>(e - s);
+  long long t = 0;
+  r.has_targets = a.num_targets != nullptr;
+  if (r.has_targets) {
+    t = load_index(a.num_targets, a.targets_i64, b);
+    t = t < -0x3fffffffLL ? -0x3fffffffLL : (t > 0x3fffffffLL ? 0x3fffffffLL : t);
+  }
+  r.hist = r.has_targets ? static_cast<int>(r.len - t) : r.len;
+  r.boundary = static_cast<int>(r.len - t) - a.mask.full;
+  return r;
+}
+
 __device__ __forceinline__ float row_scale(const KernelArgs& a, long long token) {
   if (a.scale_mode == 0) return a.inv_n;
   if (a.scale_mode == 1) return __ldg(a.attn_scale);

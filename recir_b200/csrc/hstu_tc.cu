@@ -16,6 +16,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <stdlib.h>
+
 #include <mutex>
 
 #include "hstu_launch.h"
@@ -147,22 +149,25 @@ __global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, W
 // Forward kernel
 // ------------------------------------------------------------------------------------
 
-constexpr int NUM_K_STAGES = 3;
+constexpr int NUM_K_STAGES = 2;
 constexpr int NUM_V_STAGES = 3;
 constexpr int FWD_THREADS = 384;
 constexpr int TMEM_COLS = 512;
 constexpr int TMEM_S0 = 0, TMEM_S1 = 128, TMEM_O0 = 256, TMEM_O1 = 384;
+constexpr int META_RING = 16;
 
 struct FwdShared {
   // tiles first: every tile base must be 1024-byte aligned for the 128-byte swizzle
   unsigned char q[TILE_BYTES];
   unsigned char k[NUM_K_STAGES][TILE_BYTES];
   unsigned char v[NUM_V_STAGES][TILE_BYTES];
+  unsigned char o_stage[TILE_BYTES];  // O tile on its way to global memory (row-major, chunk-swizzled)
   unsigned long long q_full, q_empty;
   unsigned long long k_full[NUM_K_STAGES], k_empty[NUM_K_STAGES];
   unsigned long long v_full[NUM_V_STAGES], v_empty[NUM_V_STAGES];
   unsigned long long s_full[2], p_ready[2];
   unsigned long long o_full[2], o_empty[2];
+  int meta[META_RING];  // per key tile, written by the producer: bit 0 = last tile of its item
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -171,9 +176,31 @@ struct TensorMaps {
   CUtensorMap q, k, v;
 };
 
-template <bool IS_BF16>
+// Optional cycle accounting (PROF): per-role wait/busy cycles, summed over CTAs into 14 ints.
+enum { PF_MMA_TOTAL = 0, PF_MMA_KFULL, PF_MMA_PREADY, PF_MMA_VFULL, PF_MMA_ITEM, PF_EPI_TOTAL, PF_EPI_SFULL,
+       PF_EPI_OFULL, PF_EPI_PARTIAL, PF_EPI_FULL, PF_N_PARTIAL, PF_N_FULL, PF_PROD_WAIT, PF_PROD_TOTAL };
+
+template <bool PROF>
+struct Stopwatch {
+  long long t;
+  __device__ __forceinline__ void start() { if (PROF) t = clock64(); }
+  __device__ __forceinline__ void stop(long long& acc) { if (PROF) acc += clock64() - t; }
+};
+
+// One 32-column chunk of scores -> 16 packed 16-bit pairs of P; `bits` = kept columns of the chunk.
+template <bool IS_BF16, bool MASKED>
+__device__ __forceinline__ void silu_chunk(const uint32_t (&sv)[32], uint32_t (&pk)[16], float c1, uint32_t bits) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    uint32_t p2 = silu_pair<IS_BF16>(sv[2 * i], sv[2 * i + 1], c1);
+    if (MASKED) p2 &= pair_mask(bits, 2 * i);
+    pk[i] = p2;
+  }
+}
+
+template <bool IS_BF16, bool PROF>
 __global__ void __launch_bounds__(FWD_THREADS, 1)
-hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, const int* __restrict__ ws, long long off_items) {
+hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restrict__ ws, long long off_items) {
   extern __shared__ unsigned char smem_raw[];
   // dynamic shared memory is only guaranteed 16-byte aligned: round up to 1024
   FwdShared& sh = *reinterpret_cast<FwdShared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -182,6 +209,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, const int* __
   if (static_cast<int>(blockIdx.x) >= total_items) return;  // uniform per CTA
   const int2* items = reinterpret_cast<const int2*>(ws + off_items);
   volatile int* abort_flag = &sh.abort_flag;
+  int* prof = ws + 2;
 
   if (threadIdx.x == 0) {
     sh.abort_flag = 0;
@@ -191,7 +219,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, const int* __
     for (int i = 0; i < NUM_V_STAGES; ++i) { mbar_init(smem_u32(&sh.v_full[i]), 1); mbar_init(smem_u32(&sh.v_empty[i]), 1); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(&sh.s_full[i]), 1);
-      mbar_init(smem_u32(&sh.p_ready[i]), 128);
+      mbar_init(smem_u32(&sh.p_ready[i]), 256);
       mbar_init(smem_u32(&sh.o_full[i]), 1);
       mbar_init(smem_u32(&sh.o_empty[i]), 256);
     }
@@ -207,123 +235,183 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, const int* __
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
 
+  // warps 0-3 (producer, MMA issuer, two idle) give registers to the eight epilogue warps
+  if (warp < 4) setmaxnreg_dec<120>(); else setmaxnreg_inc<184>();
+
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      prefetch_tensormap(&maps.q);
-      prefetch_tensormap(&maps.k);
-      prefetch_tensormap(&maps.v);
-      uint32_t g = 0, it = 0;
+    // ------------------------------------------------------------------ TMA producer / tile scheduler
+    // Whole warp on one control path; one elected lane issues the copies.
+    {
+      if (lane == 0) {
+        prefetch_tensormap(&maps.q);
+        prefetch_tensormap(&maps.k);
+        prefetch_tensormap(&maps.v);
+      }
+      long long pf_wait = 0, pf_total = 0;
+      Stopwatch<PROF> sw_total, sw;
+      sw_total.start();
+      uint32_t g = 0, it = 0, ks = 0, kph = 0, vs = 0, vph = 0;
       bool ok = true;
+      auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
+        sw.start();
+        const bool r = __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_PRODUCER));
+        sw.stop(pf_wait);
+        return r;
+      };
       for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
         const int2 w = items[item];
-        if (w.x < 0) continue;
         const int b = w.x & 0xffff, head = w.x >> 16, qblk = w.y;
         const SeqInfo s = load_seq(a, b);
         const int m0 = qblk * BLK;
         const int row0 = static_cast<int>(s.start) + m0;
         const int col0 = head * HEAD_DIM;
         // Q: wait until the previous item's score MMAs have drained the buffer
-        ok = mbar_wait(smem_u32(&sh.q_empty), (it & 1) ^ 1, abort_flag, a.status, WAIT_PRODUCER);
+        ok = wait_all(&sh.q_empty, (it & 1) ^ 1);
         if (!ok) break;
-        mbar_arrive_expect_tx(smem_u32(&sh.q_full), TILE_BYTES);
-        tma_load_2d(smem_u32(sh.q), &maps.q, smem_u32(&sh.q_full), col0, row0);
-        tma_load_2d(smem_u32(sh.q) + HALF_TILE_BYTES, &maps.q, smem_u32(&sh.q_full), col0 + 64, row0);
+        if (elect_one()) {
+          mbar_arrive_expect_tx(smem_u32(&sh.q_full), TILE_BYTES);
+          tma_load_2d(smem_u32(sh.q), &maps.q, smem_u32(&sh.q_full), col0, row0);
+          tma_load_2d(smem_u32(sh.q) + HALF_TILE_BYTES, &maps.q, smem_u32(&sh.q_full), col0 + 64, row0);
+        }
+        __syncwarp();
         const BlockRange kr = key_blocks_for_query_block(m0, s, a.mask);
-        for (int idx = 0; idx < kr.count() && ok; ++idx) {
-          const int nb = kr.at(idx);
-          if (classify_tile(m0, nb * BLK, s, a.mask) == TILE_SKIP) continue;
-          const int krow = static_cast<int>(s.start) + nb * BLK;
-          const uint32_t ks = g % NUM_K_STAGES, kph = (g / NUM_K_STAGES) & 1;
-          ok = mbar_wait(smem_u32(&sh.k_empty[ks]), kph ^ 1, abort_flag, a.status, WAIT_PRODUCER);
-          if (!ok) break;
-          mbar_arrive_expect_tx(smem_u32(&sh.k_full[ks]), TILE_BYTES);
-          tma_load_2d(smem_u32(sh.k[ks]), &maps.k, smem_u32(&sh.k_full[ks]), col0, krow);
-          tma_load_2d(smem_u32(sh.k[ks]) + HALF_TILE_BYTES, &maps.k, smem_u32(&sh.k_full[ks]), col0 + 64, krow);
-          const uint32_t vs = g % NUM_V_STAGES, vph = (g / NUM_V_STAGES) & 1;
-          ok = mbar_wait(smem_u32(&sh.v_empty[vs]), vph ^ 1, abort_flag, a.status, WAIT_PRODUCER);
-          if (!ok) break;
-          mbar_arrive_expect_tx(smem_u32(&sh.v_full[vs]), TILE_BYTES);
-          tma_load_2d(smem_u32(sh.v[vs]), &maps.v, smem_u32(&sh.v_full[vs]), col0, krow);
-          tma_load_2d(smem_u32(sh.v[vs]) + HALF_TILE_BYTES, &maps.v, smem_u32(&sh.v_full[vs]), col0 + 64, krow);
-          ++g;
+        const int cnt = kr.count();
+        // 32 candidate key blocks are classified at a time, one per lane; the last candidate of an
+        // item (the diagonal block, or the last block of the sequence) is never skipped
+        for (int base = 0; base < cnt && ok; base += 32) {
+          int my_cls = TILE_SKIP;
+          if (base + lane < cnt) my_cls = classify_tile(m0, kr.at(base + lane) * BLK, s, a.mask, true);
+          uint32_t todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+          while (todo != 0u && ok) {
+            const int bit = __ffs(todo) - 1;
+            todo &= todo - 1;
+            const int idx = base + bit;
+            const int krow = static_cast<int>(s.start) + kr.at(idx) * BLK;
+            ok = wait_all(&sh.k_empty[ks], kph ^ 1);
+            if (!ok) break;
+            if (elect_one()) {
+              sh.meta[g & (META_RING - 1)] = (idx == cnt - 1) ? 1 : 0;
+              mbar_arrive_expect_tx(smem_u32(&sh.k_full[ks]), TILE_BYTES);
+              tma_load_2d(smem_u32(sh.k[ks]), &maps.k, smem_u32(&sh.k_full[ks]), col0, krow);
+              tma_load_2d(smem_u32(sh.k[ks]) + HALF_TILE_BYTES, &maps.k, smem_u32(&sh.k_full[ks]), col0 + 64, krow);
+            }
+            __syncwarp();
+            ok = wait_all(&sh.v_empty[vs], vph ^ 1);
+            if (!ok) break;
+            if (elect_one()) {
+              mbar_arrive_expect_tx(smem_u32(&sh.v_full[vs]), TILE_BYTES);
+              tma_load_2d(smem_u32(sh.v[vs]), &maps.v, smem_u32(&sh.v_full[vs]), col0, krow);
+              tma_load_2d(smem_u32(sh.v[vs]) + HALF_TILE_BYTES, &maps.v, smem_u32(&sh.v_full[vs]), col0 + 64, krow);
+            }
+            __syncwarp();
+            ++g;
+            if (++ks == NUM_K_STAGES) { ks = 0; kph ^= 1; }
+            if (++vs == NUM_V_STAGES) { vs = 0; vph ^= 1; }
+          }
         }
         ++it;
       }
+      sw_total.stop(pf_total);
+      if (PROF && lane == 0) { atomicAdd(prof + PF_PROD_WAIT, (int)(pf_wait >> 6)); atomicAdd(prof + PF_PROD_TOTAL, (int)(pf_total >> 6)); }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp walks the loop (uniform control flow, uniform descriptor arithmetic);
+    // one elected lane issues the tcgen05 instructions.
+    {
       constexpr uint32_t IDESC_S = idesc_f16(IS_BF16 ? 1 : 0, BLK, BLK, 0, 0);       // Q (K-major) x K (K-major)
       constexpr uint32_t IDESC_O = idesc_f16(IS_BF16 ? 1 : 0, BLK, HEAD_DIM, 0, 1);  // P (TMEM) x V (N-major)
-      uint32_t g = 0, it = 0;
+      constexpr uint32_t HI = desc_hi_sw128(1024);
+      const uint32_t q_lo = desc_lo_sw128(smem_u32(sh.q), 16);
+      const uint32_t k_lo0 = desc_lo_sw128(smem_u32(sh.k[0]), 16);
+      const uint32_t v_lo0 = desc_lo_sw128(smem_u32(sh.v[0]), HALF_TILE_BYTES);
+      long long pf[5] = {0, 0, 0, 0, 0};
+      Stopwatch<PROF> sw_total, sw;
+      sw_total.start();
+      uint32_t g = 0, it = 0, ks = 0, kph = 0, vs_cur = 0, vph_cur = 0;
       bool ok = true;
+      auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
+        return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_MMA));
+      };
       for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-        const int2 w = items[item];
-        if (w.x < 0) continue;
-        const int b = w.x & 0xffff, qblk = w.y;
-        const SeqInfo s = load_seq(a, b);
-        const int m0 = qblk * BLK;
         const uint32_t ob = it & 1;
         const uint32_t o_tmem = tmem + (ob ? TMEM_O1 : TMEM_O0);
-        ok = mbar_wait(smem_u32(&sh.q_full), it & 1, abort_flag, a.status, WAIT_MMA);
+        sw.start();
+        ok = wait_all(&sh.q_full, it & 1);
+        if (ok) ok = wait_all(&sh.o_empty[ob], ((it >> 1) & 1) ^ 1);
+        sw.stop(pf[PF_MMA_ITEM]);
         if (!ok) break;
-        ok = mbar_wait(smem_u32(&sh.o_empty[ob]), ((it >> 1) & 1) ^ 1, abort_flag, a.status, WAIT_MMA);
-        if (!ok) break;
-        tc_fence_after();
-        const BlockRange kr = key_blocks_for_query_block(m0, s, a.mask);
         bool have_prev = false;
-        uint32_t prev_g = 0, n_pv = 0;
-        // issues O += P V for the key block whose scores were issued as tile `pg`
-        auto issue_pv = [&](uint32_t pg) -> bool {
+        uint32_t prev_g = 0, prev_vs = 0, prev_vph = 0, n_pv = 0;
+        // issues O += P V for the key tile whose scores were issued as tile `pg`
+        auto issue_pv = [&](uint32_t pg, uint32_t vs, uint32_t vph) -> bool {
           const uint32_t sb = pg & 1, ph = (pg >> 1) & 1;
-          if (!mbar_wait(smem_u32(&sh.p_ready[sb]), ph, abort_flag, a.status, WAIT_MMA)) return false;
-          const uint32_t vs = pg % NUM_V_STAGES, vph = (pg / NUM_V_STAGES) & 1;
-          if (!mbar_wait(smem_u32(&sh.v_full[vs]), vph, abort_flag, a.status, WAIT_MMA)) return false;
+          sw.start();
+          bool good = wait_all(&sh.p_ready[sb], ph);
+          sw.stop(pf[PF_MMA_PREADY]);
+          if (!good) return false;
+          sw.start();
+          good = wait_all(&sh.v_full[vs], vph);
+          sw.stop(pf[PF_MMA_VFULL]);
+          if (!good) return false;
           tc_fence_after();
           const uint32_t p_tmem = tmem + (sb ? TMEM_S1 : TMEM_S0);
-          const uint32_t vbase = smem_u32(sh.v[vs]);
+          const uint32_t v_lo = v_lo0 + vs * (TILE_BYTES >> 4);
+          if (elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < BLK / 16; ++kk) {
-            // A: 16 key columns of P = 8 TMEM columns; B: 16 key rows of V (N-major, two 64-wide halves)
-            const uint64_t bd = smem_desc_sw128(vbase + kk * 2048, HALF_TILE_BYTES, 1024);
-            mma_ts(o_tmem, p_tmem + kk * 8, bd, IDESC_O, (n_pv > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < BLK / 16; ++kk) {
+              // A: 16 key columns of P = 8 TMEM columns (keys 0..63 at columns 0..31, keys 64..127 at
+              // columns 64..95: each epilogue group stores P over its own score columns);
+              // B: 16 key rows of V (N-major, two 64-wide halves)
+              mma_ts(o_tmem, p_tmem + (kk >> 2) * 64 + (kk & 3) * 8, desc_join(v_lo + kk * (2048 >> 4), HI), IDESC_O,
+                     (n_pv > 0 || kk > 0) ? 1u : 0u);
+            }
+            tc_commit(smem_u32(&sh.v_empty[vs]));
           }
-          tc_commit(smem_u32(&sh.v_empty[vs]));
+          __syncwarp();
           ++n_pv;
           return true;
         };
-        for (int idx = 0; idx < kr.count() && ok; ++idx) {
-          const int nb = kr.at(idx);
-          if (classify_tile(m0, nb * BLK, s, a.mask) == TILE_SKIP) continue;
-          const uint32_t ks = g % NUM_K_STAGES, kph = (g / NUM_K_STAGES) & 1;
-          ok = mbar_wait(smem_u32(&sh.k_full[ks]), kph, abort_flag, a.status, WAIT_MMA);
+        bool last = false;
+        while (!last && ok) {
+          sw.start();
+          ok = wait_all(&sh.k_full[ks], kph);
+          sw.stop(pf[PF_MMA_KFULL]);
           if (!ok) break;
+          last = sh.meta[g & (META_RING - 1)] & 1;
           tc_fence_after();
           const uint32_t s_tmem = tmem + ((g & 1) ? TMEM_S1 : TMEM_S0);
-          const uint32_t qbase = smem_u32(sh.q), kbase = smem_u32(sh.k[ks]);
+          const uint32_t k_lo = k_lo0 + ks * (TILE_BYTES >> 4);
+          if (elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < HEAD_DIM / 16; ++kk) {
-            // 16 feature columns = 32 bytes inside a 64-column (128-byte) box; boxes are 16 KB apart
-            const uint32_t off = (kk >> 2) * HALF_TILE_BYTES + (kk & 3) * 32;
-            const uint64_t ad = smem_desc_sw128(qbase + off, 16, 1024);
-            const uint64_t bd = smem_desc_sw128(kbase + off, 16, 1024);
-            mma_ss(s_tmem, ad, bd, IDESC_S, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < HEAD_DIM / 16; ++kk) {
+              // 16 feature columns = 32 bytes inside a 64-column (128-byte) box; boxes are 16 KB apart
+              const uint32_t off = ((kk >> 2) * HALF_TILE_BYTES + (kk & 3) * 32) >> 4;
+              mma_ss(s_tmem, desc_join(q_lo + off, HI), desc_join(k_lo + off, HI), IDESC_S, kk > 0 ? 1u : 0u);
+            }
+            tc_commit(smem_u32(&sh.k_empty[ks]));
+            tc_commit(smem_u32(&sh.s_full[g & 1]));
           }
-          tc_commit(smem_u32(&sh.k_empty[ks]));
-          tc_commit(smem_u32(&sh.s_full[g & 1]));
-          if (have_prev) ok = issue_pv(prev_g);
-          prev_g = g;
+          __syncwarp();
+          if (have_prev) ok = issue_pv(prev_g, prev_vs, prev_vph);
+          prev_g = g; prev_vs = vs_cur; prev_vph = vph_cur;
           have_prev = true;
           ++g;
+          if (++ks == NUM_K_STAGES) { ks = 0; kph ^= 1; }
+          if (++vs_cur == NUM_V_STAGES) { vs_cur = 0; vph_cur ^= 1; }
         }
         if (!ok) break;
-        tc_commit(smem_u32(&sh.q_empty));  // every score MMA of this item has been issued
-        if (have_prev) ok = issue_pv(prev_g);
+        if (elect_one()) tc_commit(smem_u32(&sh.q_empty));  // every score MMA of this item has been issued
+        __syncwarp();
+        if (have_prev) ok = issue_pv(prev_g, prev_vs, prev_vph);
         if (!ok) break;
-        tc_commit(smem_u32(&sh.o_full[ob]));
+        if (elect_one()) tc_commit(smem_u32(&sh.o_full[ob]));
+        __syncwarp();
         ++it;
       }
+      sw_total.stop(pf[PF_MMA_TOTAL]);
+      if (PROF && lane == 0)
+        for (int i = 0; i < 5; ++i) atomicAdd(prof + i, (int)(pf[i] >> 6));
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue groups
@@ -331,80 +419,43 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, const int* __
     const int row = ((warp & 3) << 5) | lane;       // TMEM lane = query row inside the block
     const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) << 5) << 16;
     const float c1 = 0.5f * a.alpha;
+    const bool prof_thread = PROF && (threadIdx.x == 128 || threadIdx.x == 256);
+    long long pf_total = 0, pf_sfull = 0, pf_ofull = 0, pf_part = 0, pf_fullt = 0, pf_fence = 0, pf_drain = 0;
+    int n_part = 0, n_fullt = 0;
+    Stopwatch<PROF> sw_total, sw;
+    sw_total.start();
     uint32_t g = 0, it = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-      const int2 w = items[item];
-      if (w.x < 0) continue;
-      const int b = w.x & 0xffff, head = w.x >> 16, qblk = w.y;
-      const SeqInfo s = load_seq(a, b);
-      const int m0 = qblk * BLK;
-      const int m = m0 + row;
-      const BlockRange kr = key_blocks_for_query_block(m0, s, a.mask);
-      for (int idx = 0; idx < kr.count() && ok; ++idx) {
-        const int nb = kr.at(idx);
-        const int cls = classify_tile(m0, nb * BLK, s, a.mask);
-        if (cls == TILE_SKIP) continue;
-        if ((g & 1) == static_cast<uint32_t>(wg)) {
-          const uint32_t sb = g & 1, ph = (g >> 1) & 1;
-          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[sb]), ph, abort_flag, a.status, WAIT_EPILOGUE));
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t s_addr = tmem + lane_addr + (sb ? TMEM_S1 : TMEM_S0);
-          const int n0 = nb * BLK;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t sv[32];
-            tmem_ld32(s_addr + c * 32, sv);
-            tmem_wait_ld();
-            uint32_t pk[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float u0 = c1 * __uint_as_float(sv[2 * i]);
-              const float u1 = c1 * __uint_as_float(sv[2 * i + 1]);
-              float p0 = fmaf(u0, tanh_approx(u0), u0);
-              float p1 = fmaf(u1, tanh_approx(u1), u1);
-              if (cls == TILE_PARTIAL) {
-                const int n = n0 + c * 32 + 2 * i;
-                if (!(m < s.len && n < s.len && keep(m, n, s, a.mask))) p0 = 0.f;
-                if (!(m < s.len && n + 1 < s.len && keep(m, n + 1, s, a.mask))) p1 = 0.f;
-              }
-              pk[i] = pack2<IS_BF16>(p0, p1);
-            }
-            tmem_st16(s_addr + c * 16, pk);
-          }
-          if (n0 + BLK > s.len) {
-            // Key rows past the end of the sequence belong to someone else (or to nobody) and may
-            // hold anything, NaN included; their P columns are exact zeros, but 0 * NaN is NaN,
-            // so the V rows themselves are cleared before the MMA reads the tile.
-            const uint32_t vs = g % NUM_V_STAGES, vph = (g / NUM_V_STAGES) & 1;
-            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.v_full[vs]), vph, abort_flag, a.status, WAIT_EPILOGUE));
-            if (!ok) break;
-            zero_tile_rows(sh.v[vs], s.len - n0, row);
-          }
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(smem_u32(&sh.p_ready[sb]));
-        }
-        ++g;
-      }
-      if (!ok) break;
+    // O of a finished item leaves TMEM: group wg converts columns [64 wg, 64 wg + 64) of its row.
+    // It runs one key tile into the next item, so that the tensor cores already have new work
+    // while the epilogue warps drain the previous accumulator.
+    long long d_start = 0;
+    int d_len = 0, d_m0 = 0, d_head = 0;
+    uint32_t d_it = 0;
+    bool drain_pending = false;
+    auto drain_o = [&]() -> bool {
       // ---- O leaves TMEM: group wg converts columns [64*wg, 64*wg+64) of its row
-      const uint32_t ob = it & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.o_full[ob]), (it >> 1) & 1, abort_flag, a.status, WAIT_EPILOGUE));
-      if (!ok) break;
+      const uint32_t ob = d_it & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.o_full[ob]), (d_it >> 1) & 1, abort_flag, a.status, WAIT_EPILOGUE));
+      if (!ok) return false;
       tc_fence_after();
       const uint32_t o_addr = tmem + lane_addr + (ob ? TMEM_O1 : TMEM_O0) + wg * 64;
       uint32_t ov0[32], ov1[32];
       tmem_ld32(o_addr, ov0);
       tmem_ld32(o_addr + 32, ov1);
-      tmem_wait_ld();
+      tmem_wait_ld(ov0);
+      tmem_wait_ld(ov1);
       tc_fence_before();
       mbar_arrive(smem_u32(&sh.o_empty[ob]));
-      if (m < s.len) {
-        const float sc = row_scale(a, s.start + m);
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<unsigned short*>(a.o) +
-                                              (s.start + m) * a.o_rs + head * HEAD_DIM + wg * 64);
+      {
+        // Rows are handed to global memory through shared memory so that a warp writes whole
+        // 128-byte row segments (4 rows per instruction) instead of 32 scattered 16-byte pieces.
+        // Each group stages and writes its own 64 columns; chunk index XOR (row & 7) keeps both
+        // the row-wise writes and the segment-wise reads free of avoidable bank conflicts.
+        const float sc = d_m0 + row < d_len ? row_scale(a, d_start + d_m0 + row) : 0.f;
+        const int tid_wg = row;  // 0..127 inside the group
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");  // previous item's reads are done
+        unsigned char* my_row = sh.o_stage + row * 256;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           uint4 x;
@@ -412,7 +463,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, const int* __
           x.y = pack2<IS_BF16>(__uint_as_float(ov0[8 * j + 2]) * sc, __uint_as_float(ov0[8 * j + 3]) * sc);
           x.z = pack2<IS_BF16>(__uint_as_float(ov0[8 * j + 4]) * sc, __uint_as_float(ov0[8 * j + 5]) * sc);
           x.w = pack2<IS_BF16>(__uint_as_float(ov0[8 * j + 6]) * sc, __uint_as_float(ov0[8 * j + 7]) * sc);
-          dst[j] = x;
+          *reinterpret_cast<uint4*>(my_row + (((wg * 8 + j) ^ (row & 7)) << 4)) = x;
         }
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -421,10 +472,113 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, const int* __
           x.y = pack2<IS_BF16>(__uint_as_float(ov1[8 * j + 2]) * sc, __uint_as_float(ov1[8 * j + 3]) * sc);
           x.z = pack2<IS_BF16>(__uint_as_float(ov1[8 * j + 4]) * sc, __uint_as_float(ov1[8 * j + 5]) * sc);
           x.w = pack2<IS_BF16>(__uint_as_float(ov1[8 * j + 6]) * sc, __uint_as_float(ov1[8 * j + 7]) * sc);
-          dst[4 + j] = x;
+          *reinterpret_cast<uint4*>(my_row + (((wg * 8 + 4 + j) ^ (row & 7)) << 4)) = x;
+        }
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");  // the group's half tile is staged
+        const int chunk = tid_wg & 7;
+        unsigned short* obase = reinterpret_cast<unsigned short*>(a.o) + (d_start + d_m0) * a.o_rs + d_head * HEAD_DIM +
+                                wg * 64 + chunk * 8;
+        const int rows_valid = d_len - d_m0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = i * 16 + (tid_wg >> 3);
+          if (r < rows_valid) {
+            const uint4 x = *reinterpret_cast<const uint4*>(sh.o_stage + r * 256 + (((wg * 8 + chunk) ^ (r & 7)) << 4));
+            *reinterpret_cast<uint4*>(obase + static_cast<long long>(r) * a.o_rs) = x;
+          }
         }
       }
+      drain_pending = false;
+      return true;
+    };
+    int2 w_next = items[blockIdx.x];
+    SeqInfo s_next = load_seq(a, w_next.x & 0xffff);
+    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
+      const int2 w = w_next;
+      const SeqInfo s = s_next;
+      if (item + static_cast<int>(gridDim.x) < total_items) {
+        // fetch the next item's description now; it is needed only after this item's tiles
+        w_next = items[item + gridDim.x];
+        s_next = load_seq_quiet(a, w_next.x & 0xffff);
+      }
+      const int head = w.x >> 16, qblk = w.y;
+      const int m0 = qblk * BLK;
+      const int m = m0 + row;
+      const RowMask rm = row_mask(m, s, a.mask);
+      const BlockRange kr = key_blocks_for_query_block(m0, s, a.mask);
+      const int cnt = kr.count();
+      // 32 candidate key blocks are classified at a time, one per lane
+      for (int base = 0; base < cnt && ok; base += 32) {
+        int my_cls = TILE_SKIP;
+        if (base + lane < cnt) my_cls = classify_tile(m0, kr.at(base + lane) * BLK, s, a.mask, true);
+        uint32_t todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+        const uint32_t full_bits = __ballot_sync(0xffffffffu, my_cls == TILE_FULL);
+        while (todo != 0u && ok) {
+          const int bit = __ffs(todo) - 1;
+          todo &= todo - 1;
+          const int n0 = kr.at(base + bit) * BLK;
+          const int cls = ((full_bits >> bit) & 1u) ? TILE_FULL : TILE_PARTIAL;
+          // both groups work on every key tile: group wg owns score columns [64 wg, 64 wg + 64)
+          const uint32_t sb = g & 1, ph = (g >> 1) & 1;
+          sw.start();
+          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[sb]), ph, abort_flag, a.status, WAIT_EPILOGUE));
+          sw.stop(pf_sfull);
+          if (!ok) break;
+          sw.start();
+          tc_fence_after();
+          sw.stop(pf_fence);
+          sw.start();
+          const uint32_t s_addr = tmem + lane_addr + (sb ? TMEM_S1 : TMEM_S0) + wg * 64;
+          const uint32_t p_addr = s_addr;  // P (32 columns) goes over the group's own score columns
+          uint32_t sa[32], sb2[32], pk[16];
+          tmem_ld32(s_addr, sa);
+          tmem_ld32(s_addr + 32, sb2);
+          if (cls == TILE_FULL) {
+            tmem_wait_ld(sa);
+            tmem_wait_ld(sb2);
+            silu_chunk<IS_BF16, false>(sa, pk, c1, 0u);
+            tmem_st16(p_addr, pk);
+            silu_chunk<IS_BF16, false>(sb2, pk, c1, 0u);
+            tmem_st16(p_addr + 16, pk);
+          } else {
+            const unsigned long long bits = row_mask_bits64(rm, n0 + wg * 64);
+            tmem_wait_ld(sa);
+            tmem_wait_ld(sb2);
+            silu_chunk<IS_BF16, true>(sa, pk, c1, static_cast<uint32_t>(bits));
+            tmem_st16(p_addr, pk);
+            silu_chunk<IS_BF16, true>(sb2, pk, c1, static_cast<uint32_t>(bits >> 32));
+            tmem_st16(p_addr + 16, pk);
+          }
+          if (n0 + BLK > s.len) {
+            // Key rows past the end of the sequence belong to someone else (or to nobody) and may
+            // hold anything, NaN included; their P columns are exact zeros, but 0 * NaN is NaN,
+            // so the V rows themselves are cleared before the MMA reads the tile.
+            const uint32_t vs = g % NUM_V_STAGES, vph = (g / NUM_V_STAGES) & 1;
+            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.v_full[vs]), vph, abort_flag, a.status, WAIT_EPILOGUE));
+            if (!ok) break;
+            zero_tile_half_row(sh.v[vs], s.len - n0, row, wg);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(smem_u32(&sh.p_ready[sb]));
+          if (cls == TILE_FULL) { sw.stop(pf_fullt); ++n_fullt; } else { sw.stop(pf_part); ++n_part; }
+          ++g;
+          if (drain_pending) { sw.start(); ok = drain_o(); sw.stop(pf_drain); }
+        }
+      }
+      if (!ok) break;
+      // hand the accumulator over: it is drained after the first key tile of the next item
+      d_start = s.start; d_len = s.len; d_m0 = m0; d_head = head; d_it = it;
+      drain_pending = true;
       ++it;
+    }
+    if (ok && drain_pending) ok = drain_o();
+    sw_total.stop(pf_total);
+    if (prof_thread) {
+      atomicAdd(prof + PF_EPI_TOTAL, (int)(pf_total >> 6)); atomicAdd(prof + PF_EPI_SFULL, (int)(pf_sfull >> 6));
+      atomicAdd(prof + PF_EPI_OFULL, (int)(pf_ofull >> 6)); atomicAdd(prof + PF_EPI_PARTIAL, (int)(pf_part >> 6));
+      atomicAdd(prof + PF_EPI_FULL, (int)(pf_fullt >> 6)); atomicAdd(prof + PF_N_PARTIAL, (int)(pf_fence >> 6));
+      atomicAdd(prof + PF_N_FULL, (int)(pf_drain >> 6));
     }
   }
 
@@ -555,7 +709,9 @@ cudaError_t tc_forward(const KernelArgs& a, int dtype, void* workspace, cudaStre
   cudaError_t e = launch_prep(a, bf16, ws, w, false, st);
   if (e != cudaSuccess) return e;
   const size_t smem = sizeof(FwdShared) + 1024;
-  auto kern = bf16 ? hstu_fwd_tc<true> : hstu_fwd_tc<false>;
+  static const bool profile = getenv("B200_HSTU_PROFILE") != nullptr;  // cycle accounting into workspace ints 2..15
+  auto kern = profile ? (bf16 ? hstu_fwd_tc<true, true> : hstu_fwd_tc<false, true>)
+                      : (bf16 ? hstu_fwd_tc<true, false> : hstu_fwd_tc<false, false>);
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   long long grid = w.max_items < sm_count() ? w.max_items : sm_count();

@@ -46,7 +46,11 @@ enum TileClass { TILE_SKIP = 0, TILE_PARTIAL = 1, TILE_FULL = 2 };
 //   SKIP    no pair of the tile is kept (safe to never compute),
 //   FULL    every pair is kept and every row/column lies inside the sequence,
 //   PARTIAL anything else (the exact predicate is evaluated per element).
-HSTU_HD int classify_tile(int m0, int n0, const SeqInfo& s, const MaskOpts& o) {
+//
+// rows_dont_care: the caller never uses query rows at or past the sequence end (query-major
+// passes: such rows are not stored and cannot influence other rows), so a tile may be FULL
+// even if it hangs over the end of the sequence in the row direction.
+HSTU_HD int classify_tile(int m0, int n0, const SeqInfo& s, const MaskOpts& o, bool rows_dont_care = false) {
   const int L = s.len;
   if (m0 >= L || n0 >= L) return TILE_SKIP;
   const int m1 = m0 + BLK - 1, n1 = n0 + BLK - 1;
@@ -68,7 +72,7 @@ HSTU_HD int classify_tile(int m0, int n0, const SeqInfo& s, const MaskOpts& o) {
     any = any || (gm - gn > 0);
   }
   if (!any) return TILE_SKIP;
-  if (m1 >= L || n1 >= L) return TILE_PARTIAL;
+  if ((m1 >= L && !rows_dont_care) || n1 >= L) return TILE_PARTIAL;
   if (mind > 0 && (o.window <= 0 || maxd <= o.window)) return TILE_FULL;
   return TILE_PARTIAL;
 }
@@ -115,6 +119,60 @@ HSTU_HD BlockRange query_blocks_for_key_block(int n0, const SeqInfo& s, const Ma
   return r;
 }
 
+// Exact per-row form of the causal keep rule: for a fixed query m,
+//   keep(m, n)  <=>  lo <= n < hi  ||  n == diag  ||  n == extra      (diag / extra = -1: unused)
+// Rows at or past the sequence end keep nothing.
+struct RowMask {
+  int lo, hi, diag, extra;
+};
+
+HSTU_HD RowMask row_mask(int m, const SeqInfo& s, const MaskOpts& o) {
+  RowMask r;
+  r.lo = 0; r.hi = 0; r.diag = -1; r.extra = -1;
+  const int L = s.len;
+  if (m >= L || m < 0) return r;
+  r.diag = m;
+  if (o.ctx && s.has_targets && s.hist == 0) { r.hi = L; return r; }  // every id is 0: whole square
+  const int hist = s.has_targets ? s.hist : L;
+  if (hist <= 0) return r;  // all ids equal: diagonal only
+  const int idm = m < hist ? m : hist;
+  r.hi = idm;  // keys n < min(m, hist) have a smaller id
+  if (o.window > 0) {
+    r.lo = idm - o.window > 0 ? idm - o.window : 0;
+    if (o.full > 0 && idm >= s.boundary && idm > 0) r.lo = 0;  // full-attention tail row
+  }
+  if (o.ctx) r.extra = 0;  // key 0 carries id 0 (hist > 0 here)
+  return r;
+}
+
+// Exact per-column form: for a fixed key n,
+//   keep(m, n)  <=>  m == diag  ||  a_lo <= m < a_hi  ||  b_lo <= m < len
+struct ColMask {
+  int a_lo, a_hi, b_lo, diag;
+};
+
+HSTU_HD ColMask col_mask(int n, const SeqInfo& s, const MaskOpts& o) {
+  ColMask c;
+  const int L = s.len;
+  c.a_lo = 0; c.a_hi = 0; c.b_lo = L; c.diag = -1;
+  if (n >= L || n < 0) return c;
+  c.diag = n;
+  if (o.ctx && s.has_targets && s.hist == 0) { c.a_hi = L; return c; }
+  const int hist = s.has_targets ? s.hist : L;
+  if (hist <= 0 || n >= hist) return c;  // target column (or all ids equal): diagonal only
+  if (o.ctx && n == 0) { c.a_hi = L; return c; }  // id 0: visible to every query
+  c.a_lo = n + 1;
+  if (o.window <= 0) { c.a_hi = L; return c; }
+  c.a_hi = n + o.window + 1 < hist ? n + o.window + 1 : hist;  // history rows inside the window
+  if (hist - n <= o.window) c.a_hi = L;                        // target rows carry id hist
+  if (o.full > 0) {
+    int bl = s.boundary > n + 1 ? s.boundary : n + 1;
+    if (bl < 1) bl = 1;
+    c.b_lo = bl < L ? bl : L;
+  }
+  return c;
+}
+
 constexpr int TILE_BYTES = BLK * HEAD_DIM * 2;  // 32 KB: one 128x128 16-bit tile (two 64-column boxes)
 constexpr int HALF_TILE_BYTES = TILE_BYTES / 2;
 constexpr int SUBTILE_BYTES = 64 * 128;  // 64 rows of one box: rows [64, 128) of a tile start here
@@ -126,6 +184,28 @@ enum { WAIT_PRODUCER = 101, WAIT_MMA = 102, WAIT_EPILOGUE = 103 };
 template <bool IS_BF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return IS_BF16 ? sm100::pack_bf16x2(lo, hi) : sm100::pack_f16x2(lo, hi);
+}
+
+// Bitmap of the kept columns among the 64 columns [cbase, cbase + 64) for a row mask.
+__device__ __forceinline__ unsigned long long row_mask_bits64(const RowMask& rm, int cbase) {
+  int lo = rm.lo - cbase, hi = rm.hi - cbase;
+  lo = lo < 0 ? 0 : (lo > 64 ? 64 : lo);
+  hi = hi < 0 ? 0 : (hi > 64 ? 64 : hi);
+  const unsigned long long below_hi = hi >= 64 ? ~0ull : ((1ull << hi) - 1ull);
+  const unsigned long long below_lo = lo >= 64 ? ~0ull : ((1ull << lo) - 1ull);
+  unsigned long long bits = hi > lo ? (below_hi & ~below_lo) : 0ull;
+  const int d = rm.diag - cbase, e = rm.extra - cbase;
+  if (rm.diag >= 0 && d >= 0 && d < 64) bits |= 1ull << d;
+  if (rm.extra >= 0 && e >= 0 && e < 64) bits |= 1ull << e;
+  return bits;
+}
+
+// x sigma(x) for two scores with packed 16-bit math: u = (alpha/2) s in fp32, then
+// t = tanh(u) (one MUFU operation for the pair) and p = u t + u in 16-bit FMA.
+template <bool IS_BF16>
+__device__ __forceinline__ uint32_t silu_pair(uint32_t s0, uint32_t s1, float c1) {
+  const uint32_t u2 = pack2<IS_BF16>(c1 * __uint_as_float(s0), c1 * __uint_as_float(s1));
+  return sm100::fma2<IS_BF16>(u2, sm100::tanh2<IS_BF16>(u2), u2);
 }
 
 // Clears row `row` of a 128x128 16-bit tile (two 64-column boxes, 128 bytes per box row) if it

@@ -11,6 +11,19 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// One lane of a converged warp: true in exactly one lane.  Keeping the whole warp on the same
+// control path and predicating only the issuing instructions lets the compiler keep descriptor
+// arithmetic in the uniform datapath.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 rx;\n\t.reg .pred px;\n\t"
+      "elect.sync rx|px, 0xFFFFFFFF;\n\t"
+      "selp.u32 %0, 1, 0, px;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // ------------------------------------------------------------------ mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
@@ -65,6 +78,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
       }
     }
   }
+}
+
+// Register reallocation between warpgroups (all four warps of a warpgroup must execute it).
+template <int N> __device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N> __device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ------------------------------------------------------------------ TMA
@@ -137,6 +158,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr)
       : "memory");
 }
+// wait::ld that also names the destination registers, so the compiler cannot schedule
+// arithmetic on them ahead of the wait
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+        "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+        "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+        "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+}
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -159,6 +192,20 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr, uint32_t
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;    // stride byte offset, bits [32,46)
   d |= static_cast<uint64_t>(1) << 46;                             // descriptor version (Blackwell)
   d |= static_cast<uint64_t>(2) << 61;                             // layout type: SWIZZLE_128B
+  return d;
+}
+
+// The same descriptor split into its two 32-bit words, so that a k-step only adds to the low
+// word: low = start address (16-byte units) | lbo << 16; high = sbo | version | swizzle mode.
+__device__ __forceinline__ uint32_t desc_lo_sw128(uint32_t smem_addr, uint32_t lbo_bytes) {
+  return ((smem_addr & 0x3FFFFu) >> 4) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
+}
+__host__ __device__ constexpr uint32_t desc_hi_sw128(uint32_t sbo_bytes) {
+  return ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
+}
+__device__ __forceinline__ uint64_t desc_join(uint32_t lo, uint32_t hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
   return d;
 }
 
@@ -188,6 +235,45 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+// Packed 16-bit math: two elements per instruction (and per MUFU operation for tanh).
+template <bool BF16> __device__ __forceinline__ uint32_t tanh2(uint32_t x) {
+  uint32_t y;
+  if (BF16) asm("tanh.approx.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
+  else asm("tanh.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+template <bool BF16> __device__ __forceinline__ uint32_t fma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t y;
+  if (BF16) asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(y) : "r"(a), "r"(b), "r"(c));
+  else asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(y) : "r"(a), "r"(b), "r"(c));
+  return y;
+}
+template <bool BF16> __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+  uint32_t y;
+  if (BF16) asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(y) : "r"(a), "r"(b));
+  else asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(y) : "r"(a), "r"(b));
+  return y;
+}
+template <bool BF16> __device__ __forceinline__ uint32_t add2(uint32_t a, uint32_t b) {
+  uint32_t y;
+  if (BF16) asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(y) : "r"(a), "r"(b));
+  else asm("add.rn.f16x2 %0, %1, %2;" : "=r"(y) : "r"(a), "r"(b));
+  return y;
+}
+template <bool BF16> __device__ __forceinline__ uint32_t neg2(uint32_t a) { return a ^ 0x80008000u; }
+// 1.0 in both halves
+template <bool BF16> __device__ __forceinline__ constexpr uint32_t one2() { return BF16 ? 0x3F803F80u : 0x3C003C00u; }
+
+// Per-pair AND mask from bits (2i, 2i+1) of a column bitmap: 0xFFFF in each kept half.
+__device__ __forceinline__ uint32_t pair_mask(uint32_t bits, int pos) {
+  int lo, hi;
+  uint32_t m;
+  asm("bfe.s32 %0, %1, %2, 1;" : "=r"(lo) : "r"(bits), "r"(pos));
+  asm("bfe.s32 %0, %1, %2, 1;" : "=r"(hi) : "r"(bits), "r"(pos + 1));
+  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(m) : "r"(lo), "r"(hi));
+  return m;
 }
 
 }  // namespace sm100

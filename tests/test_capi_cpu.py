@@ -95,9 +95,15 @@ def test_tile_classes_and_block_ranges_are_sound(seed):
     for qb in range(nblk):
         lib.b200_hstu_debug_key_blocks(ctypes.byref(q), qb * 128, ctypes.byref(out))
         visited = set(range(out[0], out[1] + 1)) | ({0} if out[2] else set())
+        # the kernels rely on the last candidate block of a query block never being skipped
+        assert lib.b200_hstu_debug_classify_tile(ctypes.byref(q), qb * 128, out[1] * 128, 1) != 0
         for kb in range(nblk + 1):
-            cls = lib.b200_hstu_debug_classify_tile(ctypes.byref(q), qb * 128, kb * 128)
+            cls = lib.b200_hstu_debug_classify_tile(ctypes.byref(q), qb * 128, kb * 128, 0)
             sub = keep[qb * 128:(qb + 1) * 128, kb * 128:(kb + 1) * 128]
+            cls_q = lib.b200_hstu_debug_classify_tile(ctypes.byref(q), qb * 128, kb * 128, 1)
+            assert (cls_q == 0) == (cls == 0)
+            if cls_q == 2:  # query rows past the end may be anything; keys must all be in range
+                assert sub.shape[1] == 128 and sub.all(), (qb, kb)
             if cls == 0:
                 assert not sub.any(), (qb, kb)
             else:
@@ -112,3 +118,32 @@ def test_tile_classes_and_block_ranges_are_sound(seed):
         for qb in range(nblk):
             if qb not in visited:
                 assert not keep[qb * 128:(qb + 1) * 128, kb * 128:(kb + 1) * 128].any()
+
+
+@pytest.mark.parametrize("seed", range(60))
+def test_row_and_column_interval_masks_equal_the_keep_rule(seed):
+    lib = _lib.load()
+    rng = np.random.default_rng(5000 + seed)
+    L = int(rng.integers(1, 90))
+    t = [None, int(rng.integers(0, L + 3))][seed % 2]
+    if seed % 13 == 0:
+        t = L
+    w = int(rng.choice([0, 0, 1, 5, 20, 200]))
+    ctx = int(rng.integers(0, 2))
+    f = int(rng.choice([0, 0, 3, 30, 500])) if w > 0 else 0
+    keep = hstu_oracle.keep_mask(L, t, True, w, ctx, f)
+    q = _mq(L, t, True, w, ctx, f)
+    out = (ctypes.c_int32 * 4)()
+    ids = np.arange(L)
+    for m in range(L + 2):
+        lib.b200_hstu_debug_row_mask(ctypes.byref(q), m, ctypes.byref(out))
+        lo, hi, diag, extra = list(out)
+        got = ((ids >= lo) & (ids < hi)) | (ids == diag) | (ids == extra)
+        want = keep[m] if m < L else np.zeros(L, bool)
+        assert (got == want).all(), (m, list(out))
+    for n in range(L + 2):
+        lib.b200_hstu_debug_col_mask(ctypes.byref(q), n, ctypes.byref(out))
+        a_lo, a_hi, b_lo, diag = list(out)
+        got = (ids == diag) | ((ids >= a_lo) & (ids < a_hi)) | (ids >= b_lo)
+        want = keep[:, n] if n < L else np.zeros(L, bool)
+        assert (got == want).all(), (n, list(out))
