@@ -9,9 +9,14 @@
 //   dK/dV pass (rows = keys)  : dV += P^T dO, dK += dS^T Q   with S^T = K Q^T, dP^T = V dO^T
 // Score tiles are processed as 64-column halves of a 128-row shared-memory tile so that two
 // halves can be in flight (one in the tensor cores, one in the epilogue warps) inside the
-// 512 TMEM columns.  silu'(x) = sigma (1 + x (1 - sigma)); with t = tanh(x / 2) this is
-// 0.5 (1 + t)(1 + (x/2)(1 - t)); the 0.5, alpha and a scalar attn_scale are applied once per
-// output row when the accumulator leaves TMEM.
+// 512 TMEM columns; epilogue group w owns half w of every tile.
+// With u = (alpha/2) s and t = tanh(u):  x sigma(x) = u t + u  and
+// silu'(x) = 0.5 (1 + t)(1 + u (1 - t)); the 0.5, alpha and a scalar attn_scale are applied
+// once per output row when the accumulator leaves TMEM.
+//
+// Warp roles (384 threads): warp 0 = TMA producer and tile scheduler, warp 1 = MMA issuer
+// (both walk their loops warp-uniformly, one elected lane issues), warps 4-11 = two epilogue
+// groups.  Registers are moved from warps 0-3 to the epilogue warps (setmaxnreg).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -27,22 +32,89 @@ using namespace sm100;
 
 constexpr int BWD_THREADS = 384;
 constexpr int TMEM_COLS = 512;
+constexpr int META_RING = 16;
 
 struct MapsBwd {
   CUtensorMap q, k, v, d_o;
 };
 
-// 16 feature columns (one MMA k-step) inside a K-major tile: 32 bytes inside a 64-column box,
-// boxes 16 KB apart.
-__device__ __forceinline__ uint32_t kstep_offset(int kk) { return (kk >> 2) * HALF_TILE_BYTES + (kk & 3) * 32; }
+// low-word offset (16-byte units) of k-step kk inside a K-major tile: 32 bytes inside a
+// 64-column box, boxes 16 KB apart
+__device__ __forceinline__ constexpr uint32_t kstep_lo(int kk) { return (kk >> 2) * (HALF_TILE_BYTES >> 4) + (kk & 3) * 2; }
 
-// u = alpha/2 * s, t = tanh(u):  p = x sigma(x) = u t + u,  2 silu'(x) = (1 + t)(1 + u (1 - t))
-__device__ __forceinline__ void silu_terms(float s, float c1, float& p, float& dsilu2) {
-  const float u = c1 * s;
-  const float t = tanh_approx(u);
-  p = fmaf(u, t, u);
-  dsilu2 = (1.f + t) * (fmaf(-u, t, u) + 1.f);
+// P and dS for two scores with packed 16-bit math (one MUFU operation for the pair).
+//   u = (alpha/2) s, t = tanh(u);  p = u t + u;  2 silu'(x) = (1 + t)(1 + u (1 - t));  ds = dp * 2 silu'
+template <bool IS_BF16, bool WANT_P>
+__device__ __forceinline__ void bwd_pair(uint32_t s0, uint32_t s1, uint32_t dp0, uint32_t dp1, float c1, uint32_t& p2,
+                                         uint32_t& ds2) {
+  const uint32_t u2 = pack2<IS_BF16>(c1 * __uint_as_float(s0), c1 * __uint_as_float(s1));
+  const uint32_t t2 = tanh2<IS_BF16>(u2);
+  if (WANT_P) p2 = fma2<IS_BF16>(u2, t2, u2);
+  const uint32_t w1 = add2<IS_BF16>(t2, one2<IS_BF16>());
+  const uint32_t w2 = add2<IS_BF16>(fma2<IS_BF16>(neg2<IS_BF16>(u2), t2, u2), one2<IS_BF16>());
+  const uint32_t d2 = pack2<IS_BF16>(__uint_as_float(dp0), __uint_as_float(dp1));
+  ds2 = mul2<IS_BF16>(d2, mul2<IS_BF16>(w1, w2));
 }
+
+// Bitmap of the kept rows among the 64 query rows [mbase, mbase + 64) for a column mask.
+__device__ __forceinline__ unsigned long long col_mask_bits64(const ColMask& cm, int len, int mbase) {
+  auto range = [&](int lo, int hi) -> unsigned long long {
+    lo -= mbase; hi -= mbase;
+    lo = lo < 0 ? 0 : (lo > 64 ? 64 : lo);
+    hi = hi < 0 ? 0 : (hi > 64 ? 64 : hi);
+    if (hi <= lo) return 0ull;
+    const unsigned long long below_hi = hi >= 64 ? ~0ull : ((1ull << hi) - 1ull);
+    const unsigned long long below_lo = (1ull << lo) - 1ull;  // lo < 64 here
+    return below_hi & ~below_lo;
+  };
+  unsigned long long bits = range(cm.a_lo, cm.a_hi) | range(cm.b_lo, len);
+  const int d = cm.diag - mbase;
+  if (cm.diag >= 0 && d >= 0 && d < 64) bits |= 1ull << d;
+  return bits;
+}
+
+// Writes this thread's 64 accumulator columns (two 32-column register blocks, scaled) as one
+// 128-byte row of a staging half tile; chunk index XOR (row & 7) spreads the banks.
+template <bool IS_BF16>
+__device__ __forceinline__ void stage_row64(unsigned char* half_tile, int row, const uint32_t (&v0)[32],
+                                            const uint32_t (&v1)[32], float sc) {
+  unsigned char* my_row = half_tile + row * 128;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 x;
+    x.x = pack2<IS_BF16>(__uint_as_float(v0[8 * j + 0]) * sc, __uint_as_float(v0[8 * j + 1]) * sc);
+    x.y = pack2<IS_BF16>(__uint_as_float(v0[8 * j + 2]) * sc, __uint_as_float(v0[8 * j + 3]) * sc);
+    x.z = pack2<IS_BF16>(__uint_as_float(v0[8 * j + 4]) * sc, __uint_as_float(v0[8 * j + 5]) * sc);
+    x.w = pack2<IS_BF16>(__uint_as_float(v0[8 * j + 6]) * sc, __uint_as_float(v0[8 * j + 7]) * sc);
+    *reinterpret_cast<uint4*>(my_row + ((j ^ (row & 7)) << 4)) = x;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 x;
+    x.x = pack2<IS_BF16>(__uint_as_float(v1[8 * j + 0]) * sc, __uint_as_float(v1[8 * j + 1]) * sc);
+    x.y = pack2<IS_BF16>(__uint_as_float(v1[8 * j + 2]) * sc, __uint_as_float(v1[8 * j + 3]) * sc);
+    x.z = pack2<IS_BF16>(__uint_as_float(v1[8 * j + 4]) * sc, __uint_as_float(v1[8 * j + 5]) * sc);
+    x.w = pack2<IS_BF16>(__uint_as_float(v1[8 * j + 6]) * sc, __uint_as_float(v1[8 * j + 7]) * sc);
+    *reinterpret_cast<uint4*>(my_row + (((4 + j) ^ (row & 7)) << 4)) = x;
+  }
+}
+
+// Copies a staged half tile (128 rows x 64 columns) to global memory: 8 lanes write one
+// 128-byte row segment, a warp writes 4 rows per instruction.  dst points at (row 0, column 0).
+__device__ __forceinline__ void store_staged64(const unsigned char* half_tile, unsigned short* dst, long long row_stride,
+                                               int rows_valid, int tid_wg) {
+  const int chunk = tid_wg & 7;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 16 + (tid_wg >> 3);
+    if (r < rows_valid) {
+      const uint4 x = *reinterpret_cast<const uint4*>(half_tile + r * 128 + ((chunk ^ (r & 7)) << 4));
+      *reinterpret_cast<uint4*>(dst + static_cast<long long>(r) * row_stride + chunk * 8) = x;
+    }
+  }
+}
+
+__device__ __forceinline__ void group_barrier(int wg) { asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory"); }
 
 // ------------------------------------------------------------------------------------
 // dQ pass
@@ -53,9 +125,11 @@ constexpr int DQ_QA = 0, DQ_DOA = 64, DQ_S0 = 128, DQ_DP0 = 256, DQ_ACC = 384;  
 struct DqShared {
   unsigned char k[DQ_STAGES][TILE_BYTES];
   unsigned char v[DQ_STAGES][TILE_BYTES];
+  unsigned char stage[TILE_BYTES];
   unsigned long long k_full[DQ_STAGES], k_empty[DQ_STAGES];
   unsigned long long v_full[DQ_STAGES], v_empty[DQ_STAGES];
   unsigned long long a_ready, s_full[2], ds_ready[2], acc_full, acc_empty;
+  int meta[META_RING];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -92,127 +166,148 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
+  if (warp < 4) setmaxnreg_dec<120>(); else setmaxnreg_inc<184>();
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      prefetch_tensormap(&maps.k);
-      prefetch_tensormap(&maps.v);
-      uint32_t gt = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-        const int2 w = items[item];
-        if (w.x < 0) continue;
-        const int b = w.x & 0xffff, head = w.x >> 16, qblk = w.y;
-        const SeqInfo s = load_seq(a, b);
-        const int m0 = qblk * BLK, col0 = head * HEAD_DIM;
-        const BlockRange kr = key_blocks_for_query_block(m0, s, a.mask);
-        for (int idx = 0; idx < kr.count() && ok; ++idx) {
-          const int nb = kr.at(idx);
-          if (classify_tile(m0, nb * BLK, s, a.mask) == TILE_SKIP) continue;
-          const int krow = static_cast<int>(s.start) + nb * BLK;
-          const uint32_t st = gt % DQ_STAGES, ph = (gt / DQ_STAGES) & 1;
-          ok = mbar_wait(smem_u32(&sh.k_empty[st]), ph ^ 1, abort_flag, a.status, WAIT_PRODUCER);
+    // ------------------------------------------------------------------ TMA producer / tile scheduler
+    if (lane == 0) { prefetch_tensormap(&maps.k); prefetch_tensormap(&maps.v); }
+    uint32_t gt = 0, st = 0, ph = 0;
+    bool ok = true;
+    auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_PRODUCER));
+    };
+    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
+      const int2 w = items[item];
+      const int b = w.x & 0xffff, head = w.x >> 16, qblk = w.y;
+      const SeqInfo s = load_seq(a, b);
+      const int m0 = qblk * BLK, col0 = head * HEAD_DIM;
+      const BlockRange kr = key_blocks_for_query_block(m0, s, a.mask);
+      const int cnt = kr.count();
+      // the last candidate (diagonal block, or last block of the sequence) is never skipped
+      for (int base = 0; base < cnt && ok; base += 32) {
+        int my_cls = TILE_SKIP;
+        if (base + lane < cnt) my_cls = classify_tile(m0, kr.at(base + lane) * BLK, s, a.mask, true);
+        uint32_t todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+        while (todo != 0u && ok) {
+          const int bit = __ffs(todo) - 1;
+          todo &= todo - 1;
+          const int idx = base + bit;
+          const int krow = static_cast<int>(s.start) + kr.at(idx) * BLK;
+          ok = wait_all(&sh.k_empty[st], ph ^ 1);
           if (!ok) break;
-          mbar_arrive_expect_tx(smem_u32(&sh.k_full[st]), TILE_BYTES);
-          tma_load_2d(smem_u32(sh.k[st]), &maps.k, smem_u32(&sh.k_full[st]), col0, krow);
-          tma_load_2d(smem_u32(sh.k[st]) + HALF_TILE_BYTES, &maps.k, smem_u32(&sh.k_full[st]), col0 + 64, krow);
-          ok = mbar_wait(smem_u32(&sh.v_empty[st]), ph ^ 1, abort_flag, a.status, WAIT_PRODUCER);
+          if (elect_one()) {
+            sh.meta[gt & (META_RING - 1)] = (idx == cnt - 1) ? 1 : 0;
+            mbar_arrive_expect_tx(smem_u32(&sh.k_full[st]), TILE_BYTES);
+            tma_load_2d(smem_u32(sh.k[st]), &maps.k, smem_u32(&sh.k_full[st]), col0, krow);
+            tma_load_2d(smem_u32(sh.k[st]) + HALF_TILE_BYTES, &maps.k, smem_u32(&sh.k_full[st]), col0 + 64, krow);
+          }
+          __syncwarp();
+          ok = wait_all(&sh.v_empty[st], ph ^ 1);
           if (!ok) break;
-          mbar_arrive_expect_tx(smem_u32(&sh.v_full[st]), TILE_BYTES);
-          tma_load_2d(smem_u32(sh.v[st]), &maps.v, smem_u32(&sh.v_full[st]), col0, krow);
-          tma_load_2d(smem_u32(sh.v[st]) + HALF_TILE_BYTES, &maps.v, smem_u32(&sh.v_full[st]), col0 + 64, krow);
+          if (elect_one()) {
+            mbar_arrive_expect_tx(smem_u32(&sh.v_full[st]), TILE_BYTES);
+            tma_load_2d(smem_u32(sh.v[st]), &maps.v, smem_u32(&sh.v_full[st]), col0, krow);
+            tma_load_2d(smem_u32(sh.v[st]) + HALF_TILE_BYTES, &maps.v, smem_u32(&sh.v_full[st]), col0 + 64, krow);
+          }
+          __syncwarp();
           ++gt;
+          if (++st == DQ_STAGES) { st = 0; ph ^= 1; }
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t IDESC_S = idesc_f16(IS_BF16 ? 1 : 0, BLK, 64, 0, 0);          // A (TMEM) x K/V half (K-major)
-      constexpr uint32_t IDESC_ACC = idesc_f16(IS_BF16 ? 1 : 0, BLK, HEAD_DIM, 0, 1);  // dS (TMEM) x K half (N-major)
-      uint32_t gt = 0, it = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-        const int2 w = items[item];
-        if (w.x < 0) continue;
-        const int b = w.x & 0xffff, qblk = w.y;
-        const SeqInfo s = load_seq(a, b);
-        const int m0 = qblk * BLK;
-        ok = mbar_wait(smem_u32(&sh.a_ready), it & 1, abort_flag, a.status, WAIT_MMA);
-        if (!ok) break;
+    constexpr uint32_t IDESC_S = idesc_f16(IS_BF16 ? 1 : 0, BLK, 64, 0, 0);          // A (TMEM) x K/V half (K-major)
+    constexpr uint32_t IDESC_ACC = idesc_f16(IS_BF16 ? 1 : 0, BLK, HEAD_DIM, 0, 1);  // dS (TMEM) x K half (N-major)
+    constexpr uint32_t HI = desc_hi_sw128(1024);
+    const uint32_t k_lo0 = desc_lo_sw128(smem_u32(sh.k[0]), 16);
+    const uint32_t v_lo0 = desc_lo_sw128(smem_u32(sh.v[0]), 16);
+    const uint32_t kn_lo0 = desc_lo_sw128(smem_u32(sh.k[0]), HALF_TILE_BYTES);  // K as N-major operand
+    uint32_t gt = 0, it = 0, st = 0, ph = 0;
+    bool ok = true;
+    auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_MMA));
+    };
+    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
+      ok = wait_all(&sh.a_ready, it & 1);
+      if (!ok) break;
+      tc_fence_after();
+      bool have_prev = false;
+      uint32_t prev_gt = 0, prev_sub = 0, prev_st = 0, n_acc = 0;
+      auto issue_acc = [&](uint32_t pgt, uint32_t psub, uint32_t pst) -> bool {
+        if (!wait_all(&sh.ds_ready[psub], pgt & 1)) return false;
+        if (n_acc == 0 && !wait_all(&sh.acc_empty, (it & 1) ^ 1)) return false;
         tc_fence_after();
-        bool have_prev = false;
-        uint32_t prev_gt = 0, prev_sub = 0, n_acc = 0;
-        auto issue_acc = [&](uint32_t pgt, uint32_t psub) -> bool {
-          if (!mbar_wait(smem_u32(&sh.ds_ready[psub]), pgt & 1, abort_flag, a.status, WAIT_MMA)) return false;
-          if (n_acc == 0 && !mbar_wait(smem_u32(&sh.acc_empty), (it & 1) ^ 1, abort_flag, a.status, WAIT_MMA))
-            return false;
-          tc_fence_after();
-          const uint32_t st = pgt % DQ_STAGES;
-          const uint32_t kbase = smem_u32(sh.k[st]) + psub * SUBTILE_BYTES;
-          const uint32_t ds_tmem = tmem + DQ_DP0 + psub * 64;
+        const uint32_t kn_lo = kn_lo0 + pst * (TILE_BYTES >> 4) + psub * (SUBTILE_BYTES >> 4);
+        const uint32_t ds_tmem = tmem + DQ_DP0 + psub * 64;
+        if (elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t bd = smem_desc_sw128(kbase + kk * 2048, HALF_TILE_BYTES, 1024);
-            mma_ts(tmem + DQ_ACC, ds_tmem + kk * 8, bd, IDESC_ACC, (n_acc > 0 || kk > 0) ? 1u : 0u);
-          }
-          if (psub == 1) tc_commit(smem_u32(&sh.k_empty[st]));
-          ++n_acc;
-          return true;
-        };
-        const BlockRange kr = key_blocks_for_query_block(m0, s, a.mask);
-        for (int idx = 0; idx < kr.count() && ok; ++idx) {
-          const int nb = kr.at(idx);
-          if (classify_tile(m0, nb * BLK, s, a.mask) == TILE_SKIP) continue;
-          const uint32_t st = gt % DQ_STAGES, ph = (gt / DQ_STAGES) & 1;
-          ok = mbar_wait(smem_u32(&sh.k_full[st]), ph, abort_flag, a.status, WAIT_MMA);
-          if (!ok) break;
-          ok = mbar_wait(smem_u32(&sh.v_full[st]), ph, abort_flag, a.status, WAIT_MMA);
-          if (!ok) break;
-          tc_fence_after();
-          for (uint32_t sub = 0; sub < 2 && ok; ++sub) {
-            const uint32_t kbase = smem_u32(sh.k[st]) + sub * SUBTILE_BYTES;
-            const uint32_t vbase = smem_u32(sh.v[st]) + sub * SUBTILE_BYTES;
-#pragma unroll
-            for (int kk = 0; kk < HEAD_DIM / 16; ++kk)
-              mma_ts(tmem + DQ_S0 + sub * 64, tmem + DQ_QA + kk * 8,
-                     smem_desc_sw128(kbase + kstep_offset(kk), 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
-#pragma unroll
-            for (int kk = 0; kk < HEAD_DIM / 16; ++kk)
-              mma_ts(tmem + DQ_DP0 + sub * 64, tmem + DQ_DOA + kk * 8,
-                     smem_desc_sw128(vbase + kstep_offset(kk), 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
-            tc_commit(smem_u32(&sh.s_full[sub]));
-            if (have_prev) ok = issue_acc(prev_gt, prev_sub);
-            prev_gt = gt; prev_sub = sub; have_prev = true;
-          }
-          if (!ok) break;
-          tc_commit(smem_u32(&sh.v_empty[st]));
-          ++gt;
+          for (int kk = 0; kk < 4; ++kk)
+            mma_ts(tmem + DQ_ACC, ds_tmem + kk * 8, desc_join(kn_lo + kk * (2048 >> 4), HI), IDESC_ACC,
+                   (n_acc > 0 || kk > 0) ? 1u : 0u);
+          if (psub == 1) tc_commit(smem_u32(&sh.k_empty[pst]));
         }
+        __syncwarp();
+        ++n_acc;
+        return true;
+      };
+      bool last = false;
+      while (!last && ok) {
+        ok = wait_all(&sh.k_full[st], ph);
+        if (ok) ok = wait_all(&sh.v_full[st], ph);
         if (!ok) break;
-        if (have_prev) ok = issue_acc(prev_gt, prev_sub);
-        if (!ok) break;
-        tc_commit(smem_u32(&sh.acc_full));
-        ++it;
+        last = sh.meta[gt & (META_RING - 1)] & 1;
+        tc_fence_after();
+        for (uint32_t sub = 0; sub < 2 && ok; ++sub) {
+          const uint32_t k_lo = k_lo0 + st * (TILE_BYTES >> 4) + sub * (SUBTILE_BYTES >> 4);
+          const uint32_t v_lo = v_lo0 + st * (TILE_BYTES >> 4) + sub * (SUBTILE_BYTES >> 4);
+          if (elect_one()) {
+#pragma unroll
+            for (int kk = 0; kk < HEAD_DIM / 16; ++kk)
+              mma_ts(tmem + DQ_S0 + sub * 64, tmem + DQ_QA + kk * 8, desc_join(k_lo + kstep_lo(kk), HI), IDESC_S,
+                     kk > 0 ? 1u : 0u);
+#pragma unroll
+            for (int kk = 0; kk < HEAD_DIM / 16; ++kk)
+              mma_ts(tmem + DQ_DP0 + sub * 64, tmem + DQ_DOA + kk * 8, desc_join(v_lo + kstep_lo(kk), HI), IDESC_S,
+                     kk > 0 ? 1u : 0u);
+            tc_commit(smem_u32(&sh.s_full[sub]));
+            if (sub == 1) tc_commit(smem_u32(&sh.v_empty[st]));
+          }
+          __syncwarp();
+          if (have_prev) ok = issue_acc(prev_gt, prev_sub, prev_st);
+          prev_gt = gt; prev_sub = sub; prev_st = st; have_prev = true;
+        }
+        ++gt;
+        if (++st == DQ_STAGES) { st = 0; ph ^= 1; }
       }
+      if (!ok) break;
+      if (have_prev) ok = issue_acc(prev_gt, prev_sub, prev_st);
+      if (!ok) break;
+      if (elect_one()) tc_commit(smem_u32(&sh.acc_full));
+      __syncwarp();
+      ++it;
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue groups
     const int wg = (warp - 4) >> 2;
-    const int tid_wg = (threadIdx.x - 128) & 127;
-    const int row = ((warp & 3) << 5) | lane;
+    const int row = ((warp & 3) << 5) | lane;  // query row inside the block = thread index in the group
     const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) << 5) << 16;
     const float c1 = 0.5f * a.alpha;
+    unsigned char* stage = sh.stage + wg * HALF_TILE_BYTES;
     uint32_t gt = 0, it = 0;
     bool ok = true;
+    int2 w_next = items[blockIdx.x];
+    SeqInfo s_next = load_seq_quiet(a, w_next.x & 0xffff);
     for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-      const int2 w = items[item];
-      if (w.x < 0) continue;
-      const int b = w.x & 0xffff, head = w.x >> 16, qblk = w.y;
-      const SeqInfo s = load_seq(a, b);
+      const int2 w = w_next;
+      const SeqInfo s = s_next;
+      if (item + static_cast<int>(gridDim.x) < total_items) {
+        w_next = items[item + gridDim.x];
+        s_next = load_seq_quiet(a, w_next.x & 0xffff);
+      }
+      const int head = w.x >> 16, qblk = w.y;
       const int m0 = qblk * BLK, m = m0 + row;
-      // ---- A operands straight from global memory into TMEM: group 0 loads Q, group 1 loads dO.
+      // ---- A operands straight from global memory into TMEM: group 0 loads Q, group 1 loads dO
       // (the previous item's MMAs are complete: both groups waited for its accumulator)
       {
         const unsigned short* src = wg == 0
@@ -234,82 +329,70 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
         tc_fence_before();
         mbar_arrive(smem_u32(&sh.a_ready));
       }
+      const RowMask rm = row_mask(m, s, a.mask);
       const BlockRange kr = key_blocks_for_query_block(m0, s, a.mask);
-      for (int idx = 0; idx < kr.count() && ok; ++idx) {
-        const int nb = kr.at(idx);
-        const int cls = classify_tile(m0, nb * BLK, s, a.mask);
-        if (cls == TILE_SKIP) continue;
-        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[wg]), gt & 1, abort_flag, a.status, WAIT_EPILOGUE));
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t s_addr = tmem + lane_addr + DQ_S0 + wg * 64;
-        const uint32_t dp_addr = tmem + lane_addr + DQ_DP0 + wg * 64;
-        const int nbase = nb * BLK + wg * 64;
+      const int cnt = kr.count();
+      for (int base = 0; base < cnt && ok; base += 32) {
+        int my_cls = TILE_SKIP;
+        if (base + lane < cnt) my_cls = classify_tile(m0, kr.at(base + lane) * BLK, s, a.mask, true);
+        uint32_t todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+        const uint32_t full_bits = __ballot_sync(0xffffffffu, my_cls == TILE_FULL);
+        while (todo != 0u && ok) {
+          const int bit = __ffs(todo) - 1;
+          todo &= todo - 1;
+          const int n0 = kr.at(base + bit) * BLK;
+          const bool full = (full_bits >> bit) & 1u;
+          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[wg]), gt & 1, abort_flag, a.status, WAIT_EPILOGUE));
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t s_addr = tmem + lane_addr + DQ_S0 + wg * 64;
+          const uint32_t dp_addr = tmem + lane_addr + DQ_DP0 + wg * 64;
+          const unsigned long long bits = full ? ~0ull : row_mask_bits64(rm, n0 + wg * 64);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t sv[32], dpv[32], pk[16];
-          tmem_ld32(s_addr + half * 32, sv);
-          tmem_ld32(dp_addr + half * 32, dpv);
-          tmem_wait_ld();
+          for (int half = 0; half < 2; ++half) {
+            uint32_t sv[32], dpv[32], pk[16];
+            tmem_ld32(s_addr + half * 32, sv);
+            tmem_ld32(dp_addr + half * 32, dpv);
+            tmem_wait_ld(sv);
+            tmem_wait_ld(dpv);
+            const uint32_t hb = static_cast<uint32_t>(bits >> (32 * half));
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float p0, g0, p1, g1;
-            silu_terms(__uint_as_float(sv[2 * i]), c1, p0, g0);
-            silu_terms(__uint_as_float(sv[2 * i + 1]), c1, p1, g1);
-            float d0 = __uint_as_float(dpv[2 * i]) * g0;
-            float d1 = __uint_as_float(dpv[2 * i + 1]) * g1;
-            if (cls == TILE_PARTIAL) {
-              const int n = nbase + half * 32 + 2 * i;
-              if (!(m < s.len && n < s.len && keep(m, n, s, a.mask))) d0 = 0.f;
-              if (!(m < s.len && n + 1 < s.len && keep(m, n + 1, s, a.mask))) d1 = 0.f;
+            for (int i = 0; i < 16; ++i) {
+              uint32_t p2 = 0u, d2;
+              bwd_pair<IS_BF16, false>(sv[2 * i], sv[2 * i + 1], dpv[2 * i], dpv[2 * i + 1], c1, p2, d2);
+              if (!full) d2 &= pair_mask(hb, 2 * i);
+              pk[i] = d2;
             }
-            pk[i] = pack2<IS_BF16>(d0, d1);
+            tmem_st16(dp_addr + half * 16, pk);
           }
-          tmem_st16(dp_addr + half * 16, pk);
+          if (n0 + BLK > s.len) {
+            // key rows past the sequence end feed the dQ MMA as B rows: clear them (0 * NaN = NaN)
+            zero_tile_half_row(sh.k[gt % DQ_STAGES], s.len - n0, wg * 64 + (row & 63), row >> 6);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(smem_u32(&sh.ds_ready[wg]));
+          ++gt;
         }
-        if (nb * BLK + BLK > s.len) {
-          // key rows past the sequence end feed the dQ MMA as B rows: clear them (0 * NaN = NaN)
-          zero_tile_half_row(sh.k[gt % DQ_STAGES], s.len - nb * BLK, wg * 64 + (tid_wg & 63), tid_wg >> 6);
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(smem_u32(&sh.ds_ready[wg]));
-        ++gt;
       }
       if (!ok) break;
-      // ---- dQ leaves TMEM: group wg converts columns [64*wg, 64*wg+64) of its row
+      // ---- dQ leaves TMEM: group wg converts columns [64 wg, 64 wg + 64) of its row
       ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.acc_full), it & 1, abort_flag, a.status, WAIT_EPILOGUE));
       if (!ok) break;
       tc_fence_after();
       uint32_t ov0[32], ov1[32];
       tmem_ld32(tmem + lane_addr + DQ_ACC + wg * 64, ov0);
       tmem_ld32(tmem + lane_addr + DQ_ACC + wg * 64 + 32, ov1);
-      tmem_wait_ld();
+      tmem_wait_ld(ov0);
+      tmem_wait_ld(ov1);
       tc_fence_before();
       mbar_arrive(smem_u32(&sh.acc_empty));
-      if (m < s.len) {
-        const float sc = 0.5f * a.alpha * row_scale(a, s.start + m);
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<unsigned short*>(a.dq) + (s.start + m) * a.dq_rs +
-                                              head * HEAD_DIM + wg * 64);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 x;
-          x.x = pack2<IS_BF16>(__uint_as_float(ov0[8 * j + 0]) * sc, __uint_as_float(ov0[8 * j + 1]) * sc);
-          x.y = pack2<IS_BF16>(__uint_as_float(ov0[8 * j + 2]) * sc, __uint_as_float(ov0[8 * j + 3]) * sc);
-          x.z = pack2<IS_BF16>(__uint_as_float(ov0[8 * j + 4]) * sc, __uint_as_float(ov0[8 * j + 5]) * sc);
-          x.w = pack2<IS_BF16>(__uint_as_float(ov0[8 * j + 6]) * sc, __uint_as_float(ov0[8 * j + 7]) * sc);
-          dst[j] = x;
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 x;
-          x.x = pack2<IS_BF16>(__uint_as_float(ov1[8 * j + 0]) * sc, __uint_as_float(ov1[8 * j + 1]) * sc);
-          x.y = pack2<IS_BF16>(__uint_as_float(ov1[8 * j + 2]) * sc, __uint_as_float(ov1[8 * j + 3]) * sc);
-          x.z = pack2<IS_BF16>(__uint_as_float(ov1[8 * j + 4]) * sc, __uint_as_float(ov1[8 * j + 5]) * sc);
-          x.w = pack2<IS_BF16>(__uint_as_float(ov1[8 * j + 6]) * sc, __uint_as_float(ov1[8 * j + 7]) * sc);
-          dst[4 + j] = x;
-        }
-      }
+      const float sc = m < s.len ? 0.5f * a.alpha * row_scale(a, s.start + m) : 0.f;
+      group_barrier(wg);  // previous item's staged rows have been copied out
+      stage_row64<IS_BF16>(stage, row, ov0, ov1, sc);
+      group_barrier(wg);
+      store_staged64(stage, reinterpret_cast<unsigned short*>(a.dq) + (s.start + m0) * a.dq_rs + head * HEAD_DIM + wg * 64,
+                     a.dq_rs, s.len - m0, row);
       ++it;
     }
   }
@@ -337,9 +420,11 @@ struct DkvShared {
   unsigned char v[TILE_BYTES];
   unsigned char q[KV_STAGES][TILE_BYTES];
   unsigned char d_o[KV_STAGES][TILE_BYTES];
+  unsigned char stage[TILE_BYTES];
   unsigned long long kv_full, kv_empty;
   unsigned long long qd_full[KV_STAGES], qd_empty[KV_STAGES];
   unsigned long long s_full[2], p_ready[2], acc_full, acc_empty;
+  int meta[META_RING];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -374,225 +459,263 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* _
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
+  if (warp < 4) setmaxnreg_dec<136>(); else setmaxnreg_inc<176>();
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------------ TMA producer / tile scheduler
     if (lane == 0) {
-      prefetch_tensormap(&maps.q);
-      prefetch_tensormap(&maps.k);
-      prefetch_tensormap(&maps.v);
-      prefetch_tensormap(&maps.d_o);
-      uint32_t gt = 0, it = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-        const int2 w = items[item];
-        if (w.x < 0) continue;
-        const int b = w.x & 0xffff, head = w.x >> 16;
-        const SeqInfo s = load_seq(a, b);
-        const int kvblk = (s.len + BLK - 1) / BLK - 1 - w.y;
-        const int n0 = kvblk * BLK, col0 = head * HEAD_DIM;
-        const int krow = static_cast<int>(s.start) + n0;
-        ok = mbar_wait(smem_u32(&sh.kv_empty), (it & 1) ^ 1, abort_flag, a.status, WAIT_PRODUCER);
-        if (!ok) break;
+      prefetch_tensormap(&maps.q); prefetch_tensormap(&maps.k);
+      prefetch_tensormap(&maps.v); prefetch_tensormap(&maps.d_o);
+    }
+    uint32_t gt = 0, it = 0, st = 0, ph = 0;
+    bool ok = true;
+    auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_PRODUCER));
+    };
+    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
+      const int2 w = items[item];
+      const int b = w.x & 0xffff, head = w.x >> 16;
+      const SeqInfo s = load_seq(a, b);
+      const int kvblk = (s.len + BLK - 1) / BLK - 1 - w.y;
+      const int n0 = kvblk * BLK, col0 = head * HEAD_DIM;
+      const int krow = static_cast<int>(s.start) + n0;
+      ok = wait_all(&sh.kv_empty, (it & 1) ^ 1);
+      if (!ok) break;
+      if (elect_one()) {
         mbar_arrive_expect_tx(smem_u32(&sh.kv_full), 2 * TILE_BYTES);
         tma_load_2d(smem_u32(sh.k), &maps.k, smem_u32(&sh.kv_full), col0, krow);
         tma_load_2d(smem_u32(sh.k) + HALF_TILE_BYTES, &maps.k, smem_u32(&sh.kv_full), col0 + 64, krow);
         tma_load_2d(smem_u32(sh.v), &maps.v, smem_u32(&sh.kv_full), col0, krow);
         tma_load_2d(smem_u32(sh.v) + HALF_TILE_BYTES, &maps.v, smem_u32(&sh.kv_full), col0 + 64, krow);
-        const BlockRange qr = query_blocks_for_key_block(n0, s, a.mask);
-        for (int idx = 0; idx < qr.count() && ok; ++idx) {
-          const int qb = qr.at(idx);
-          if (classify_tile(qb * BLK, n0, s, a.mask) == TILE_SKIP) continue;
-          const int qrow = static_cast<int>(s.start) + qb * BLK;
-          const uint32_t st = gt % KV_STAGES, ph = (gt / KV_STAGES) & 1;
-          ok = mbar_wait(smem_u32(&sh.qd_empty[st]), ph ^ 1, abort_flag, a.status, WAIT_PRODUCER);
-          if (!ok) break;
-          mbar_arrive_expect_tx(smem_u32(&sh.qd_full[st]), 2 * TILE_BYTES);
-          tma_load_2d(smem_u32(sh.q[st]), &maps.q, smem_u32(&sh.qd_full[st]), col0, qrow);
-          tma_load_2d(smem_u32(sh.q[st]) + HALF_TILE_BYTES, &maps.q, smem_u32(&sh.qd_full[st]), col0 + 64, qrow);
-          tma_load_2d(smem_u32(sh.d_o[st]), &maps.d_o, smem_u32(&sh.qd_full[st]), col0, qrow);
-          tma_load_2d(smem_u32(sh.d_o[st]) + HALF_TILE_BYTES, &maps.d_o, smem_u32(&sh.qd_full[st]), col0 + 64, qrow);
-          ++gt;
-        }
-        ++it;
       }
+      __syncwarp();
+      const BlockRange qr = query_blocks_for_key_block(n0, s, a.mask);
+      const int cnt = qr.count();
+      // first pass: how many query blocks are kept (to flag the last one for the MMA warp)
+      int n_tiles = 0;
+      for (int base = 0; base < cnt; base += 32) {
+        int my_cls = TILE_SKIP;
+        if (base + lane < cnt) my_cls = classify_tile(qr.at(base + lane) * BLK, n0, s, a.mask);
+        n_tiles += __popc(__ballot_sync(0xffffffffu, my_cls != TILE_SKIP));
+      }
+      int emitted = 0;
+      for (int base = 0; base < cnt && ok; base += 32) {
+        int my_cls = TILE_SKIP;
+        if (base + lane < cnt) my_cls = classify_tile(qr.at(base + lane) * BLK, n0, s, a.mask);
+        uint32_t todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+        while (todo != 0u && ok) {
+          const int bit = __ffs(todo) - 1;
+          todo &= todo - 1;
+          const int qrow = static_cast<int>(s.start) + qr.at(base + bit) * BLK;
+          ok = wait_all(&sh.qd_empty[st], ph ^ 1);
+          if (!ok) break;
+          ++emitted;
+          if (elect_one()) {
+            sh.meta[gt & (META_RING - 1)] = (emitted == n_tiles) ? 1 : 0;
+            mbar_arrive_expect_tx(smem_u32(&sh.qd_full[st]), 2 * TILE_BYTES);
+            tma_load_2d(smem_u32(sh.q[st]), &maps.q, smem_u32(&sh.qd_full[st]), col0, qrow);
+            tma_load_2d(smem_u32(sh.q[st]) + HALF_TILE_BYTES, &maps.q, smem_u32(&sh.qd_full[st]), col0 + 64, qrow);
+            tma_load_2d(smem_u32(sh.d_o[st]), &maps.d_o, smem_u32(&sh.qd_full[st]), col0, qrow);
+            tma_load_2d(smem_u32(sh.d_o[st]) + HALF_TILE_BYTES, &maps.d_o, smem_u32(&sh.qd_full[st]), col0 + 64, qrow);
+          }
+          __syncwarp();
+          ++gt;
+          if (++st == KV_STAGES) { st = 0; ph ^= 1; }
+        }
+      }
+      ++it;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t IDESC_S = idesc_f16(IS_BF16 ? 1 : 0, BLK, 64, 0, 0);          // K/V (K-major) x Q/dO half (K-major)
-      constexpr uint32_t IDESC_ACC = idesc_f16(IS_BF16 ? 1 : 0, BLK, HEAD_DIM, 0, 1);  // P^T/dS^T (TMEM) x dO/Q half (N-major)
-      uint32_t gt = 0, it = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-        const int2 w = items[item];
-        if (w.x < 0) continue;
-        const int b = w.x & 0xffff;
-        const SeqInfo s = load_seq(a, b);
-        const int kvblk = (s.len + BLK - 1) / BLK - 1 - w.y;
-        const int n0 = kvblk * BLK;
-        ok = mbar_wait(smem_u32(&sh.kv_full), it & 1, abort_flag, a.status, WAIT_MMA);
-        if (!ok) break;
+    constexpr uint32_t IDESC_S = idesc_f16(IS_BF16 ? 1 : 0, BLK, 64, 0, 0);          // K/V (K-major) x Q/dO half (K-major)
+    constexpr uint32_t IDESC_ACC = idesc_f16(IS_BF16 ? 1 : 0, BLK, HEAD_DIM, 0, 1);  // P^T/dS^T (TMEM) x dO/Q half (N-major)
+    constexpr uint32_t HI = desc_hi_sw128(1024);
+    const uint32_t k_lo = desc_lo_sw128(smem_u32(sh.k), 16);
+    const uint32_t v_lo = desc_lo_sw128(smem_u32(sh.v), 16);
+    const uint32_t q_lo0 = desc_lo_sw128(smem_u32(sh.q[0]), 16);
+    const uint32_t do_lo0 = desc_lo_sw128(smem_u32(sh.d_o[0]), 16);
+    const uint32_t qn_lo0 = desc_lo_sw128(smem_u32(sh.q[0]), HALF_TILE_BYTES);     // Q as N-major operand
+    const uint32_t don_lo0 = desc_lo_sw128(smem_u32(sh.d_o[0]), HALF_TILE_BYTES);  // dO as N-major operand
+    uint32_t gt = 0, it = 0, st = 0, ph = 0;
+    bool ok = true;
+    auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_MMA));
+    };
+    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
+      ok = wait_all(&sh.kv_full, it & 1);
+      if (!ok) break;
+      tc_fence_after();
+      bool have_prev = false;
+      uint32_t prev_gt = 0, prev_sub = 0, prev_st = 0, n_acc = 0;
+      auto issue_acc = [&](uint32_t pgt, uint32_t psub, uint32_t pst) -> bool {
+        if (!wait_all(&sh.p_ready[psub], pgt & 1)) return false;
+        if (n_acc == 0 && !wait_all(&sh.acc_empty, (it & 1) ^ 1)) return false;
         tc_fence_after();
-        bool have_prev = false;
-        uint32_t prev_gt = 0, prev_sub = 0, n_acc = 0;
-        auto issue_acc = [&](uint32_t pgt, uint32_t psub) -> bool {
-          if (!mbar_wait(smem_u32(&sh.p_ready[psub]), pgt & 1, abort_flag, a.status, WAIT_MMA)) return false;
-          if (n_acc == 0 && !mbar_wait(smem_u32(&sh.acc_empty), (it & 1) ^ 1, abort_flag, a.status, WAIT_MMA))
-            return false;
-          tc_fence_after();
-          const uint32_t st = pgt % KV_STAGES;
-          const uint32_t dobase = smem_u32(sh.d_o[st]) + psub * SUBTILE_BYTES;
-          const uint32_t qbase = smem_u32(sh.q[st]) + psub * SUBTILE_BYTES;
-          const uint32_t acc = (n_acc > 0) ? 1u : 0u;
+        const uint32_t don_lo = don_lo0 + pst * (TILE_BYTES >> 4) + psub * (SUBTILE_BYTES >> 4);
+        const uint32_t qn_lo = qn_lo0 + pst * (TILE_BYTES >> 4) + psub * (SUBTILE_BYTES >> 4);
+        const uint32_t acc = (n_acc > 0) ? 1u : 0u;
+        if (elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_ts(tmem + KV_DV, tmem + KV_ST0 + psub * 64 + kk * 8,
-                   smem_desc_sw128(dobase + kk * 2048, HALF_TILE_BYTES, 1024), IDESC_ACC, (acc || kk > 0) ? 1u : 0u);
+            mma_ts(tmem + KV_DV, tmem + KV_ST0 + psub * 64 + kk * 8, desc_join(don_lo + kk * (2048 >> 4), HI), IDESC_ACC,
+                   (acc || kk > 0) ? 1u : 0u);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_ts(tmem + KV_DK, tmem + KV_DPT0 + psub * 64 + kk * 8,
-                   smem_desc_sw128(qbase + kk * 2048, HALF_TILE_BYTES, 1024), IDESC_ACC, (acc || kk > 0) ? 1u : 0u);
-          if (psub == 1) tc_commit(smem_u32(&sh.qd_empty[st]));
-          ++n_acc;
-          return true;
-        };
-        const BlockRange qr = query_blocks_for_key_block(n0, s, a.mask);
-        const uint32_t kb = smem_u32(sh.k), vb = smem_u32(sh.v);
-        for (int idx = 0; idx < qr.count() && ok; ++idx) {
-          const int qb = qr.at(idx);
-          if (classify_tile(qb * BLK, n0, s, a.mask) == TILE_SKIP) continue;
-          const uint32_t st = gt % KV_STAGES, ph = (gt / KV_STAGES) & 1;
-          ok = mbar_wait(smem_u32(&sh.qd_full[st]), ph, abort_flag, a.status, WAIT_MMA);
-          if (!ok) break;
-          tc_fence_after();
-          for (uint32_t sub = 0; sub < 2 && ok; ++sub) {
-            const uint32_t qbase = smem_u32(sh.q[st]) + sub * SUBTILE_BYTES;
-            const uint32_t dobase = smem_u32(sh.d_o[st]) + sub * SUBTILE_BYTES;
-#pragma unroll
-            for (int kk = 0; kk < HEAD_DIM / 16; ++kk)
-              mma_ss(tmem + KV_ST0 + sub * 64, smem_desc_sw128(kb + kstep_offset(kk), 16, 1024),
-                     smem_desc_sw128(qbase + kstep_offset(kk), 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
-#pragma unroll
-            for (int kk = 0; kk < HEAD_DIM / 16; ++kk)
-              mma_ss(tmem + KV_DPT0 + sub * 64, smem_desc_sw128(vb + kstep_offset(kk), 16, 1024),
-                     smem_desc_sw128(dobase + kstep_offset(kk), 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
-            tc_commit(smem_u32(&sh.s_full[sub]));
-            if (have_prev) ok = issue_acc(prev_gt, prev_sub);
-            prev_gt = gt; prev_sub = sub; have_prev = true;
-          }
-          if (!ok) break;
-          ++gt;
+            mma_ts(tmem + KV_DK, tmem + KV_DPT0 + psub * 64 + kk * 8, desc_join(qn_lo + kk * (2048 >> 4), HI), IDESC_ACC,
+                   (acc || kk > 0) ? 1u : 0u);
+          if (psub == 1) tc_commit(smem_u32(&sh.qd_empty[pst]));
         }
+        __syncwarp();
+        ++n_acc;
+        return true;
+      };
+      bool last = false;
+      while (!last && ok) {
+        ok = wait_all(&sh.qd_full[st], ph);
         if (!ok) break;
-        tc_commit(smem_u32(&sh.kv_empty));  // every score MMA of this item has been issued
-        if (have_prev) ok = issue_acc(prev_gt, prev_sub);
-        if (!ok) break;
-        tc_commit(smem_u32(&sh.acc_full));
-        ++it;
+        last = sh.meta[gt & (META_RING - 1)] & 1;
+        tc_fence_after();
+        for (uint32_t sub = 0; sub < 2 && ok; ++sub) {
+          const uint32_t q_lo = q_lo0 + st * (TILE_BYTES >> 4) + sub * (SUBTILE_BYTES >> 4);
+          const uint32_t do_lo = do_lo0 + st * (TILE_BYTES >> 4) + sub * (SUBTILE_BYTES >> 4);
+          if (elect_one()) {
+#pragma unroll
+            for (int kk = 0; kk < HEAD_DIM / 16; ++kk)
+              mma_ss(tmem + KV_ST0 + sub * 64, desc_join(k_lo + kstep_lo(kk), HI), desc_join(q_lo + kstep_lo(kk), HI),
+                     IDESC_S, kk > 0 ? 1u : 0u);
+#pragma unroll
+            for (int kk = 0; kk < HEAD_DIM / 16; ++kk)
+              mma_ss(tmem + KV_DPT0 + sub * 64, desc_join(v_lo + kstep_lo(kk), HI), desc_join(do_lo + kstep_lo(kk), HI),
+                     IDESC_S, kk > 0 ? 1u : 0u);
+            tc_commit(smem_u32(&sh.s_full[sub]));
+          }
+          __syncwarp();
+          if (have_prev) ok = issue_acc(prev_gt, prev_sub, prev_st);
+          prev_gt = gt; prev_sub = sub; prev_st = st; have_prev = true;
+        }
+        ++gt;
+        if (++st == KV_STAGES) { st = 0; ph ^= 1; }
       }
+      if (!ok) break;
+      if (elect_one()) tc_commit(smem_u32(&sh.kv_empty));  // every score MMA of this item has been issued
+      __syncwarp();
+      if (have_prev) ok = issue_acc(prev_gt, prev_sub, prev_st);
+      if (!ok) break;
+      if (elect_one()) tc_commit(smem_u32(&sh.acc_full));
+      __syncwarp();
+      ++it;
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue groups
     const int wg = (warp - 4) >> 2;
-    const int tid_wg = (threadIdx.x - 128) & 127;
-    const int row = ((warp & 3) << 5) | lane;  // key row inside the block
+    const int row = ((warp & 3) << 5) | lane;  // key row inside the block = thread index in the group
     const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) << 5) << 16;
     const float c1 = 0.5f * a.alpha;
     const bool per_token = a.scale_mode == 2;
+    unsigned char* stage = sh.stage + wg * HALF_TILE_BYTES;
     uint32_t gt = 0, it = 0;
     bool ok = true;
+    int2 w_next = items[blockIdx.x];
+    SeqInfo s_next = load_seq_quiet(a, w_next.x & 0xffff);
     for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-      const int2 w = items[item];
-      if (w.x < 0) continue;
-      const int b = w.x & 0xffff, head = w.x >> 16;
-      const SeqInfo s = load_seq(a, b);
+      const int2 w = w_next;
+      const SeqInfo s = s_next;
+      if (item + static_cast<int>(gridDim.x) < total_items) {
+        w_next = items[item + gridDim.x];
+        s_next = load_seq_quiet(a, w_next.x & 0xffff);
+      }
+      const int head = w.x >> 16;
       const int kvblk = (s.len + BLK - 1) / BLK - 1 - w.y;
       const int n0 = kvblk * BLK, n = n0 + row;
+      const ColMask cm = col_mask(n, s, a.mask);
       const BlockRange qr = query_blocks_for_key_block(n0, s, a.mask);
-      for (int idx = 0; idx < qr.count() && ok; ++idx) {
-        const int qb = qr.at(idx);
-        const int cls = classify_tile(qb * BLK, n0, s, a.mask);
-        if (cls == TILE_SKIP) continue;
-        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[wg]), gt & 1, abort_flag, a.status, WAIT_EPILOGUE));
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t st_addr = tmem + lane_addr + KV_ST0 + wg * 64;
-        const uint32_t dp_addr = tmem + lane_addr + KV_DPT0 + wg * 64;
-        const int mbase = qb * BLK + wg * 64;
+      const int cnt = qr.count();
+      for (int base = 0; base < cnt && ok; base += 32) {
+        int my_cls = TILE_SKIP;
+        if (base + lane < cnt) my_cls = classify_tile(qr.at(base + lane) * BLK, n0, s, a.mask);
+        uint32_t todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+        const uint32_t full_bits = __ballot_sync(0xffffffffu, my_cls == TILE_FULL);
+        while (todo != 0u && ok) {
+          const int bit = __ffs(todo) - 1;
+          todo &= todo - 1;
+          const int q0 = qr.at(base + bit) * BLK;
+          const bool full = (full_bits >> bit) & 1u;
+          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[wg]), gt & 1, abort_flag, a.status, WAIT_EPILOGUE));
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t st_addr = tmem + lane_addr + KV_ST0 + wg * 64;
+          const uint32_t dp_addr = tmem + lane_addr + KV_DPT0 + wg * 64;
+          const int mbase = q0 + wg * 64;
+          const unsigned long long bits = full ? ~0ull : col_mask_bits64(cm, s.len, mbase);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t sv[32], dpv[32], pp[16], pd[16];
-          tmem_ld32(st_addr + half * 32, sv);
-          tmem_ld32(dp_addr + half * 32, dpv);
-          tmem_wait_ld();
+          for (int half = 0; half < 2; ++half) {
+            uint32_t sv[32], dpv[32], pp[16], pd[16];
+            tmem_ld32(st_addr + half * 32, sv);
+            tmem_ld32(dp_addr + half * 32, dpv);
+            tmem_wait_ld(sv);
+            tmem_wait_ld(dpv);
+            const uint32_t hb = static_cast<uint32_t>(bits >> (32 * half));
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float p0, g0, p1, g1;
-            silu_terms(__uint_as_float(sv[2 * i]), c1, p0, g0);
-            silu_terms(__uint_as_float(sv[2 * i + 1]), c1, p1, g1);
-            float d0 = __uint_as_float(dpv[2 * i]) * g0;
-            float d1 = __uint_as_float(dpv[2 * i + 1]) * g1;
-            const int mm = mbase + half * 32 + 2 * i;
-            if (per_token) {  // one scale per query token = per column here
-              const float s0 = mm < s.len ? __ldg(a.attn_scale + s.start + mm) : 0.f;
-              const float s1 = mm + 1 < s.len ? __ldg(a.attn_scale + s.start + mm + 1) : 0.f;
-              p0 *= s0; d0 *= s0; p1 *= s1; d1 *= s1;
+            for (int i = 0; i < 16; ++i) {
+              uint32_t p2, d2;
+              bwd_pair<IS_BF16, true>(sv[2 * i], sv[2 * i + 1], dpv[2 * i], dpv[2 * i + 1], c1, p2, d2);
+              if (per_token) {  // one scale per query token = per column here
+                const int mm = mbase + half * 32 + 2 * i;
+                const float s0 = mm < s.len ? __ldg(a.attn_scale + s.start + mm) : 0.f;
+                const float s1 = mm + 1 < s.len ? __ldg(a.attn_scale + s.start + mm + 1) : 0.f;
+                const uint32_t sc2 = pack2<IS_BF16>(s0, s1);
+                p2 = mul2<IS_BF16>(p2, sc2);
+                d2 = mul2<IS_BF16>(d2, sc2);
+              }
+              if (!full) {
+                const uint32_t pm = pair_mask(hb, 2 * i);
+                p2 &= pm;
+                d2 &= pm;
+              }
+              pp[i] = p2;
+              pd[i] = d2;
             }
-            if (cls == TILE_PARTIAL) {
-              const bool k0 = n < s.len && mm < s.len && keep(mm, n, s, a.mask);
-              const bool k1 = n < s.len && mm + 1 < s.len && keep(mm + 1, n, s, a.mask);
-              if (!k0) { p0 = 0.f; d0 = 0.f; }
-              if (!k1) { p1 = 0.f; d1 = 0.f; }
-            }
-            pp[i] = pack2<IS_BF16>(p0, p1);
-            pd[i] = pack2<IS_BF16>(d0, d1);
+            tmem_st16(st_addr + half * 16, pp);
+            tmem_st16(dp_addr + half * 16, pd);
           }
-          tmem_st16(st_addr + half * 16, pp);
-          tmem_st16(dp_addr + half * 16, pd);
+          if (q0 + BLK > s.len) {
+            // query rows past the sequence end are B rows of the dV / dK MMAs: clear them
+            const int r = wg * 64 + (row & 63);
+            zero_tile_half_row(sh.q[gt % KV_STAGES], s.len - q0, r, row >> 6);
+            zero_tile_half_row(sh.d_o[gt % KV_STAGES], s.len - q0, r, row >> 6);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(smem_u32(&sh.p_ready[wg]));
+          ++gt;
         }
-        if (qb * BLK + BLK > s.len) {
-          // query rows past the sequence end are B rows of the dV / dK MMAs: clear them
-          const int r = wg * 64 + (tid_wg & 63);
-          zero_tile_half_row(sh.q[gt % KV_STAGES], s.len - qb * BLK, r, tid_wg >> 6);
-          zero_tile_half_row(sh.d_o[gt % KV_STAGES], s.len - qb * BLK, r, tid_wg >> 6);
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(smem_u32(&sh.p_ready[wg]));
-        ++gt;
       }
       if (!ok) break;
-      // ---- accumulators leave TMEM: group 0 writes dK, group 1 writes dV (128 columns each)
+      // ---- accumulators leave TMEM: group 0 writes dK, group 1 writes dV, 64 columns at a time
       ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.acc_full), it & 1, abort_flag, a.status, WAIT_EPILOGUE));
       if (!ok) break;
       tc_fence_after();
       const float scal = per_token ? 1.f : row_scale(a, 0);
-      const float sc = wg == 0 ? 0.5f * a.alpha * scal : scal;
-      unsigned short* outp = wg == 0 ? reinterpret_cast<unsigned short*>(a.dk) + (s.start + n) * a.dk_rs
-                                     : reinterpret_cast<unsigned short*>(a.dv) + (s.start + n) * a.dv_rs;
-      uint4* dst = reinterpret_cast<uint4*>(outp + head * HEAD_DIM);
+      const float sc = n < s.len ? (wg == 0 ? 0.5f * a.alpha * scal : scal) : 0.f;
+      const long long out_rs = wg == 0 ? a.dk_rs : a.dv_rs;
+      unsigned short* out0 = (wg == 0 ? reinterpret_cast<unsigned short*>(a.dk) : reinterpret_cast<unsigned short*>(a.dv)) +
+                             (s.start + n0) * out_rs + head * HEAD_DIM;
       const uint32_t acc_addr = tmem + lane_addr + (wg == 0 ? KV_DK : KV_DV);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t ov[32];
-        tmem_ld32(acc_addr + c * 32, ov);
-        tmem_wait_ld();
-        if (c == 3) {
+      for (int round = 0; round < 2; ++round) {
+        uint32_t ov0[32], ov1[32];
+        tmem_ld32(acc_addr + round * 64, ov0);
+        tmem_ld32(acc_addr + round * 64 + 32, ov1);
+        tmem_wait_ld(ov0);
+        tmem_wait_ld(ov1);
+        if (round == 1) {
           tc_fence_before();
           mbar_arrive(smem_u32(&sh.acc_empty));
         }
-        if (n < s.len) {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            uint4 x;
-            x.x = pack2<IS_BF16>(__uint_as_float(ov[8 * j + 0]) * sc, __uint_as_float(ov[8 * j + 1]) * sc);
-            x.y = pack2<IS_BF16>(__uint_as_float(ov[8 * j + 2]) * sc, __uint_as_float(ov[8 * j + 3]) * sc);
-            x.z = pack2<IS_BF16>(__uint_as_float(ov[8 * j + 4]) * sc, __uint_as_float(ov[8 * j + 5]) * sc);
-            x.w = pack2<IS_BF16>(__uint_as_float(ov[8 * j + 6]) * sc, __uint_as_float(ov[8 * j + 7]) * sc);
-            dst[c * 4 + j] = x;
-          }
-        }
+        group_barrier(wg);  // the previous copy out of the staging buffer has finished
+        stage_row64<IS_BF16>(stage, row, ov0, ov1, sc);
+        group_barrier(wg);
+        store_staged64(stage, out0 + round * 64, out_rs, s.len - n0, row);
       }
       ++it;
     }
