@@ -65,7 +65,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -189,7 +189,7 @@ def cpu_baseline(batch, budget_s: float = 20.0):
         run()
         reps += 1
         dt = time.perf_counter() - t0
-        if dt > budget_s / 2 or reps >= 5:
+        if dt > budget_s / 2 or reps >= 40:
             break
     return {"value": flops * reps / dt / 1e12, "unit": UNIT, "cores": cores, "kind": "reference",
             "sample": f"{len(sel)} of {len(batch.lengths)} sequences (every 4th by sorted length), bf16, "
@@ -285,7 +285,6 @@ def main():
         torch.cuda.synchronize()
         fwd_ms.append(fe[0].elapsed_time(fe[1]))
         bwd_ms.append(fe[1].elapsed_time(fe[2]))
-    clocks = sampler.stop()
     value = flops_step * args.steps / (ms_total * 1e-3) / 1e12
 
     # ------------------------------------------------------------ end to end (host buffers)
@@ -312,6 +311,7 @@ def main():
     e1.record()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    clocks = sampler.stop()  # sampled over the resident, per-pass and end-to-end timed regions
     e2e_value = flops_step * args.steps / (e2e_ms * 1e-3) / 1e12
     bytes_local = sum(host[k].numel() * host[k].element_size() for k in host)
     if world > 1:

@@ -102,9 +102,12 @@ __global__ void __launch_bounds__(1024) build_block_index(KernelArgs a, int* ws,
 }
 
 // One thread per work item: find its block index by bisection over start[], then decode.
+// The list is sorted by descending cost; CTA c of a grid of `stride` CTAs walks entries c,
+// c + stride, ...  Every other round of `stride` entries is stored mirrored, so that no CTA
+// always receives the most expensive item of its round (serpentine deal).
 // Also zeroes the output rows no sequence owns (rows at or past the last offset).
 template <typename T>
-__global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, WorkspaceLayout w, T* z0,
+__global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, WorkspaceLayout w, int stride, T* z0,
                                                         long long rs0, int w0, T* z1, long long rs1, int w1,
                                                         T* z2, long long rs2, int w2) {
   const int* sorted = ws + w.off_sorted;
@@ -114,8 +117,11 @@ __global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, W
   const int total = ws[0];
   const long long gtid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   const long long gsz = (long long)gridDim.x * blockDim.x;
-  for (long long p = gtid; p < total; p += gsz) {
-    // start[] is non-increasing in j; find the largest... smallest j with start[j] <= p
+  for (long long slot = gtid; slot < total; slot += gsz) {
+    const long long round = slot / stride, c = slot - round * stride;
+    const long long round_size = (total - round * stride < stride) ? (total - round * stride) : stride;
+    const long long p = round * stride + ((round & 1) ? (round_size - 1 - c) : c);  // rank in the sorted order
+    // start[] is non-increasing in j; find the smallest j with start[j] <= p
     long long lo = 0, hi = w.nbins - 1;
     while (lo < hi) {
       const long long mid = (lo + hi) >> 1;
@@ -127,7 +133,7 @@ __global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, W
     int2 it;
     it.x = (i < cnt[j]) ? (sorted[i] | (head << 16)) : -1;
     it.y = j;
-    items[p] = it;
+    items[slot] = it;
   }
   // tail rows
   long long first = load_index(a.seq_offsets, a.offsets_i64, a.B);
@@ -634,6 +640,12 @@ bool make_map(CUtensorMap* m, const void* base, long long rows, long long width,
   return r == CUDA_SUCCESS;
 }
 
+// Grid of the persistent kernels: one CTA per SM, fewer if there cannot be that many items.
+int main_grid(const WorkspaceLayout& w) {
+  long long grid = w.max_items < sm_count() ? w.max_items : sm_count();
+  return grid < 1 ? 1 : static_cast<int>(grid);
+}
+
 int sm_count() {
   static int n = 0;
   static std::once_flag once;
@@ -650,11 +662,12 @@ template <typename T>
 static cudaError_t launch_prep_t(const KernelArgs& a, int* ws, const WorkspaceLayout& w, bool backward, cudaStream_t st) {
   build_block_index<<<1, 1024, 0, st>>>(a, ws, w);
   const int blocks = sm_count() * 2;
+  const int stride = main_grid(w);
   if (!backward)
-    build_work_items<T><<<blocks, 256, 0, st>>>(a, ws, w, reinterpret_cast<T*>(a.o), a.o_rs, a.H * a.Dv,
+    build_work_items<T><<<blocks, 256, 0, st>>>(a, ws, w, stride, reinterpret_cast<T*>(a.o), a.o_rs, a.H * a.Dv,
                                                 (T*)nullptr, 0, 0, (T*)nullptr, 0, 0);
   else
-    build_work_items<T><<<blocks, 256, 0, st>>>(a, ws, w, reinterpret_cast<T*>(a.dq), a.dq_rs, a.H * a.Dqk,
+    build_work_items<T><<<blocks, 256, 0, st>>>(a, ws, w, stride, reinterpret_cast<T*>(a.dq), a.dq_rs, a.H * a.Dqk,
                                                 reinterpret_cast<T*>(a.dk), a.dk_rs, a.H * a.Dqk,
                                                 reinterpret_cast<T*>(a.dv), a.dv_rs, a.H * a.Dv);
   return cudaGetLastError();
@@ -714,9 +727,7 @@ cudaError_t tc_forward(const KernelArgs& a, int dtype, void* workspace, cudaStre
                       : (bf16 ? hstu_fwd_tc<true, false> : hstu_fwd_tc<false, false>);
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  long long grid = w.max_items < sm_count() ? w.max_items : sm_count();
-  if (grid < 1) grid = 1;
-  kern<<<static_cast<unsigned>(grid), FWD_THREADS, smem, st>>>(maps, a, ws, w.off_items);
+  kern<<<static_cast<unsigned>(main_grid(w)), FWD_THREADS, smem, st>>>(maps, a, ws, w.off_items);
   return cudaGetLastError();
 }
 

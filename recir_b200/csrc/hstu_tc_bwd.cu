@@ -19,6 +19,7 @@
 // groups.  Registers are moved from warps 0-3 to the epilogue warps (setmaxnreg).
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <stdlib.h>
 
 #include "hstu_launch.h"
 #include "hstu_tc_common.cuh"
@@ -33,6 +34,16 @@ using namespace sm100;
 constexpr int BWD_THREADS = 384;
 constexpr int TMEM_COLS = 512;
 constexpr int META_RING = 16;
+
+// Optional cycle accounting (PROF): per-role wait/busy cycles, summed over CTAs into workspace ints 2..15.
+enum { PB_MMA_TOTAL = 0, PB_MMA_WAIT_LOAD, PB_MMA_WAIT_P, PB_MMA_WAIT_ACC, PB_MMA_WAIT_ITEM, PB_EPI_TOTAL,
+       PB_EPI_WAIT_S, PB_EPI_WAIT_ACC, PB_EPI_TILE, PB_EPI_DRAIN, PB_EPI_LD, PB_EPI_ST, PB_PROD_WAIT, PB_PROD_TOTAL };
+template <bool PROF>
+struct Stopwatch {
+  long long t;
+  __device__ __forceinline__ void start() { if (PROF) t = clock64(); }
+  __device__ __forceinline__ void stop(long long& acc) { if (PROF) acc += clock64() - t; }
+};
 
 struct MapsBwd {
   CUtensorMap q, k, v, d_o;
@@ -54,6 +65,37 @@ __device__ __forceinline__ void bwd_pair(uint32_t s0, uint32_t s1, uint32_t dp0,
   const uint32_t w2 = add2<IS_BF16>(fma2<IS_BF16>(neg2<IS_BF16>(u2), t2, u2), one2<IS_BF16>());
   const uint32_t d2 = pack2<IS_BF16>(__uint_as_float(dp0), __uint_as_float(dp1));
   ds2 = mul2<IS_BF16>(d2, mul2<IS_BF16>(w1, w2));
+}
+
+// 32 score columns -> 16 packed pairs of dS (and P).  Branch-free inside: the mask and the
+// per-token scale are compile-time variants, so the 16 pairs interleave freely.
+template <bool IS_BF16, bool WANT_P, bool MASKED>
+__device__ __forceinline__ void bwd_chunk(const uint32_t (&sv)[32], const uint32_t (&dpv)[32], uint32_t (&pp)[16],
+                                          uint32_t (&pd)[16], float c1, uint32_t bits) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    uint32_t p2 = 0u, d2;
+    bwd_pair<IS_BF16, WANT_P>(sv[2 * i], sv[2 * i + 1], dpv[2 * i], dpv[2 * i + 1], c1, p2, d2);
+    if (MASKED) {
+      const uint32_t pm = pair_mask(bits, 2 * i);
+      if (WANT_P) p2 &= pm;
+      d2 &= pm;
+    }
+    if (WANT_P) pp[i] = p2;
+    pd[i] = d2;
+  }
+}
+
+// Multiplies 16 packed pairs by one fp32 scale per column (scales of columns col0 .. col0 + 31).
+template <bool IS_BF16>
+__device__ __forceinline__ void scale_chunk(uint32_t (&x)[16], const float* scales, long long first, int col0, int len) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int c = col0 + 2 * i;
+    const float s0 = c < len ? __ldg(scales + first + c) : 0.f;
+    const float s1 = c + 1 < len ? __ldg(scales + first + c + 1) : 0.f;
+    x[i] = mul2<IS_BF16>(x[i], pack2<IS_BF16>(s0, s1));
+  }
 }
 
 // Bitmap of the kept rows among the 64 query rows [mbase, mbase + 64) for a column mask.
@@ -152,7 +194,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
       mbar_init(smem_u32(&sh.v_full[i]), 1); mbar_init(smem_u32(&sh.v_empty[i]), 1);
     }
     mbar_init(smem_u32(&sh.a_ready), 256);
-    for (int i = 0; i < 2; ++i) { mbar_init(smem_u32(&sh.s_full[i]), 1); mbar_init(smem_u32(&sh.ds_ready[i]), 128); }
+    for (int i = 0; i < 2; ++i) { mbar_init(smem_u32(&sh.s_full[i]), 1); mbar_init(smem_u32(&sh.ds_ready[i]), 256); }
     mbar_init(smem_u32(&sh.acc_full), 1);
     mbar_init(smem_u32(&sh.acc_empty), 256);
     fence_barrier_init();
@@ -243,7 +285,8 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
         if (elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_ts(tmem + DQ_ACC, ds_tmem + kk * 8, desc_join(kn_lo + kk * (2048 >> 4), HI), IDESC_ACC,
+            // dS of keys 0..31 of the half tile sits at columns 0..15, keys 32..63 at columns 32..47
+            mma_ts(tmem + DQ_ACC, ds_tmem + (kk >> 1) * 32 + (kk & 1) * 8, desc_join(kn_lo + kk * (2048 >> 4), HI), IDESC_ACC,
                    (n_acc > 0 || kk > 0) ? 1u : 0u);
           if (psub == 1) tc_commit(smem_u32(&sh.k_empty[pst]));
         }
@@ -342,36 +385,33 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
           todo &= todo - 1;
           const int n0 = kr.at(base + bit) * BLK;
           const bool full = (full_bits >> bit) & 1u;
-          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[wg]), gt & 1, abort_flag, a.status, WAIT_EPILOGUE));
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t s_addr = tmem + lane_addr + DQ_S0 + wg * 64;
-          const uint32_t dp_addr = tmem + lane_addr + DQ_DP0 + wg * 64;
-          const unsigned long long bits = full ? ~0ull : row_mask_bits64(rm, n0 + wg * 64);
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t sv[32], dpv[32], pk[16];
-            tmem_ld32(s_addr + half * 32, sv);
-            tmem_ld32(dp_addr + half * 32, dpv);
+          // both groups work on every 64-column half tile: group wg owns its columns [32 wg, 32 wg + 32)
+          for (int sub = 0; sub < 2 && ok; ++sub) {
+            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[sub]), gt & 1, abort_flag, a.status, WAIT_EPILOGUE));
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t s_addr = tmem + lane_addr + DQ_S0 + sub * 64 + wg * 32;
+            const uint32_t dp_addr = tmem + lane_addr + DQ_DP0 + sub * 64 + wg * 32;
+            uint32_t sv[32], dpv[32], pk[16], unused[16];
+            tmem_ld32(s_addr, sv);
+            tmem_ld32(dp_addr, dpv);
             tmem_wait_ld(sv);
             tmem_wait_ld(dpv);
-            const uint32_t hb = static_cast<uint32_t>(bits >> (32 * half));
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              uint32_t p2 = 0u, d2;
-              bwd_pair<IS_BF16, false>(sv[2 * i], sv[2 * i + 1], dpv[2 * i], dpv[2 * i + 1], c1, p2, d2);
-              if (!full) d2 &= pair_mask(hb, 2 * i);
-              pk[i] = d2;
+            if (full) {
+              bwd_chunk<IS_BF16, false, false>(sv, dpv, unused, pk, c1, 0u);
+            } else {
+              const uint32_t hb = static_cast<uint32_t>(row_mask_bits64(rm, n0 + sub * 64) >> (32 * wg));
+              bwd_chunk<IS_BF16, false, true>(sv, dpv, unused, pk, c1, hb);
             }
-            tmem_st16(dp_addr + half * 16, pk);
+            tmem_st16(dp_addr, pk);  // dS (16 columns) over the group's own dP columns
+            if (n0 + BLK > s.len && wg == 0) {
+              // key rows past the sequence end feed the dQ MMA as B rows: clear them (0 * NaN = NaN)
+              zero_tile_half_row(sh.k[gt % DQ_STAGES], s.len - n0, sub * 64 + (row & 63), row >> 6);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(smem_u32(&sh.ds_ready[sub]));
           }
-          if (n0 + BLK > s.len) {
-            // key rows past the sequence end feed the dQ MMA as B rows: clear them (0 * NaN = NaN)
-            zero_tile_half_row(sh.k[gt % DQ_STAGES], s.len - n0, wg * 64 + (row & 63), row >> 6);
-          }
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(smem_u32(&sh.ds_ready[wg]));
           ++gt;
         }
       }
@@ -429,9 +469,9 @@ struct DkvShared {
   int abort_flag;
 };
 
-template <bool IS_BF16>
+template <bool IS_BF16, bool PROF>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
-hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __restrict__ ws, long long off_items) {
+hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restrict__ ws, long long off_items) {
   extern __shared__ unsigned char smem_raw[];
   DkvShared& sh = *reinterpret_cast<DkvShared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -439,13 +479,14 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* _
   if (static_cast<int>(blockIdx.x) >= total_items) return;
   const int2* items = reinterpret_cast<const int2*>(ws + off_items);
   volatile int* abort_flag = &sh.abort_flag;
+  int* prof = ws + 2;
 
   if (threadIdx.x == 0) {
     sh.abort_flag = 0;
     mbar_init(smem_u32(&sh.kv_full), 1);
     mbar_init(smem_u32(&sh.kv_empty), 1);
     for (int i = 0; i < KV_STAGES; ++i) { mbar_init(smem_u32(&sh.qd_full[i]), 1); mbar_init(smem_u32(&sh.qd_empty[i]), 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(smem_u32(&sh.s_full[i]), 1); mbar_init(smem_u32(&sh.p_ready[i]), 128); }
+    for (int i = 0; i < 2; ++i) { mbar_init(smem_u32(&sh.s_full[i]), 1); mbar_init(smem_u32(&sh.p_ready[i]), 256); }
     mbar_init(smem_u32(&sh.acc_full), 1);
     mbar_init(smem_u32(&sh.acc_empty), 256);
     fence_barrier_init();
@@ -538,18 +579,29 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* _
     const uint32_t don_lo0 = desc_lo_sw128(smem_u32(sh.d_o[0]), HALF_TILE_BYTES);  // dO as N-major operand
     uint32_t gt = 0, it = 0, st = 0, ph = 0;
     bool ok = true;
+    long long pf[5] = {0, 0, 0, 0, 0};
+    Stopwatch<PROF> sw_total, sw;
+    sw_total.start();
     auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_MMA));
     };
     for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
+      sw.start();
       ok = wait_all(&sh.kv_full, it & 1);
+      sw.stop(pf[PB_MMA_WAIT_ITEM]);
       if (!ok) break;
       tc_fence_after();
       bool have_prev = false;
       uint32_t prev_gt = 0, prev_sub = 0, prev_st = 0, n_acc = 0;
       auto issue_acc = [&](uint32_t pgt, uint32_t psub, uint32_t pst) -> bool {
-        if (!wait_all(&sh.p_ready[psub], pgt & 1)) return false;
-        if (n_acc == 0 && !wait_all(&sh.acc_empty, (it & 1) ^ 1)) return false;
+        sw.start();
+        const bool g1 = wait_all(&sh.p_ready[psub], pgt & 1);
+        sw.stop(pf[PB_MMA_WAIT_P]);
+        if (!g1) return false;
+        sw.start();
+        const bool g2 = n_acc != 0 || wait_all(&sh.acc_empty, (it & 1) ^ 1);
+        sw.stop(pf[PB_MMA_WAIT_ACC]);
+        if (!g2) return false;
         tc_fence_after();
         const uint32_t don_lo = don_lo0 + pst * (TILE_BYTES >> 4) + psub * (SUBTILE_BYTES >> 4);
         const uint32_t qn_lo = qn_lo0 + pst * (TILE_BYTES >> 4) + psub * (SUBTILE_BYTES >> 4);
@@ -557,11 +609,11 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* _
         if (elect_one()) {
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_ts(tmem + KV_DV, tmem + KV_ST0 + psub * 64 + kk * 8, desc_join(don_lo + kk * (2048 >> 4), HI), IDESC_ACC,
+            mma_ts(tmem + KV_DV, tmem + KV_ST0 + psub * 64 + (kk >> 1) * 32 + (kk & 1) * 8, desc_join(don_lo + kk * (2048 >> 4), HI), IDESC_ACC,
                    (acc || kk > 0) ? 1u : 0u);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_ts(tmem + KV_DK, tmem + KV_DPT0 + psub * 64 + kk * 8, desc_join(qn_lo + kk * (2048 >> 4), HI), IDESC_ACC,
+            mma_ts(tmem + KV_DK, tmem + KV_DPT0 + psub * 64 + (kk >> 1) * 32 + (kk & 1) * 8, desc_join(qn_lo + kk * (2048 >> 4), HI), IDESC_ACC,
                    (acc || kk > 0) ? 1u : 0u);
           if (psub == 1) tc_commit(smem_u32(&sh.qd_empty[pst]));
         }
@@ -571,7 +623,9 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* _
       };
       bool last = false;
       while (!last && ok) {
+        sw.start();
         ok = wait_all(&sh.qd_full[st], ph);
+        sw.stop(pf[PB_MMA_WAIT_LOAD]);
         if (!ok) break;
         last = sh.meta[gt & (META_RING - 1)] & 1;
         tc_fence_after();
@@ -605,6 +659,9 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* _
       __syncwarp();
       ++it;
     }
+    sw_total.stop(pf[PB_MMA_TOTAL]);
+    if (PROF && lane == 0)
+      for (int i = 0; i < 5; ++i) atomicAdd(prof + i, (int)(pf[i] >> 6));
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue groups
     const int wg = (warp - 4) >> 2;
@@ -615,6 +672,9 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* _
     unsigned char* stage = sh.stage + wg * HALF_TILE_BYTES;
     uint32_t gt = 0, it = 0;
     bool ok = true;
+    long long pe_total = 0, pe_ws = 0, pe_wacc = 0, pe_tile = 0, pe_drain = 0, pe_ld = 0, pe_st = 0;
+    Stopwatch<PROF> sw_total, sw, sw2;
+    sw_total.start();
     int2 w_next = items[blockIdx.x];
     SeqInfo s_next = load_seq_quiet(a, w_next.x & 0xffff);
     for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
@@ -640,84 +700,98 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* _
           todo &= todo - 1;
           const int q0 = qr.at(base + bit) * BLK;
           const bool full = (full_bits >> bit) & 1u;
-          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[wg]), gt & 1, abort_flag, a.status, WAIT_EPILOGUE));
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t st_addr = tmem + lane_addr + KV_ST0 + wg * 64;
-          const uint32_t dp_addr = tmem + lane_addr + KV_DPT0 + wg * 64;
-          const int mbase = q0 + wg * 64;
-          const unsigned long long bits = full ? ~0ull : col_mask_bits64(cm, s.len, mbase);
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
+          // both groups work on every 64-column half tile: group wg owns its columns [32 wg, 32 wg + 32)
+          for (int sub = 0; sub < 2 && ok; ++sub) {
+            sw.start();
+            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[sub]), gt & 1, abort_flag, a.status, WAIT_EPILOGUE));
+            sw.stop(pe_ws);
+            if (!ok) break;
+            tc_fence_after();
+            sw.start();
+            const uint32_t st_addr = tmem + lane_addr + KV_ST0 + sub * 64 + wg * 32;
+            const uint32_t dp_addr = tmem + lane_addr + KV_DPT0 + sub * 64 + wg * 32;
+            const int mbase = q0 + sub * 64;
             uint32_t sv[32], dpv[32], pp[16], pd[16];
-            tmem_ld32(st_addr + half * 32, sv);
-            tmem_ld32(dp_addr + half * 32, dpv);
+            sw2.start();
+            tmem_ld32(st_addr, sv);
+            tmem_ld32(dp_addr, dpv);
             tmem_wait_ld(sv);
             tmem_wait_ld(dpv);
-            const uint32_t hb = static_cast<uint32_t>(bits >> (32 * half));
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              uint32_t p2, d2;
-              bwd_pair<IS_BF16, true>(sv[2 * i], sv[2 * i + 1], dpv[2 * i], dpv[2 * i + 1], c1, p2, d2);
-              if (per_token) {  // one scale per query token = per column here
-                const int mm = mbase + half * 32 + 2 * i;
-                const float s0 = mm < s.len ? __ldg(a.attn_scale + s.start + mm) : 0.f;
-                const float s1 = mm + 1 < s.len ? __ldg(a.attn_scale + s.start + mm + 1) : 0.f;
-                const uint32_t sc2 = pack2<IS_BF16>(s0, s1);
-                p2 = mul2<IS_BF16>(p2, sc2);
-                d2 = mul2<IS_BF16>(d2, sc2);
-              }
-              if (!full) {
-                const uint32_t pm = pair_mask(hb, 2 * i);
-                p2 &= pm;
-                d2 &= pm;
-              }
-              pp[i] = p2;
-              pd[i] = d2;
+            sw2.stop(pe_ld);
+            if (full) {
+              bwd_chunk<IS_BF16, true, false>(sv, dpv, pp, pd, c1, 0u);
+            } else {
+              const uint32_t hb = static_cast<uint32_t>(col_mask_bits64(cm, s.len, mbase) >> (32 * wg));
+              bwd_chunk<IS_BF16, true, true>(sv, dpv, pp, pd, c1, hb);
             }
-            tmem_st16(st_addr + half * 16, pp);
-            tmem_st16(dp_addr + half * 16, pd);
+            if (per_token) {  // one scale per query token = per column here (masked entries stay zero)
+              scale_chunk<IS_BF16>(pp, a.attn_scale, s.start, mbase + wg * 32, s.len);
+              scale_chunk<IS_BF16>(pd, a.attn_scale, s.start, mbase + wg * 32, s.len);
+            }
+            tmem_st16(st_addr, pp);  // P^T and dS^T (16 columns each) over the group's own score columns
+            tmem_st16(dp_addr, pd);
+            if (q0 + BLK > s.len && wg == 0) {
+              // query rows past the sequence end are B rows of the dV / dK MMAs: clear them
+              const int r = sub * 64 + (row & 63);
+              zero_tile_half_row(sh.q[gt % KV_STAGES], s.len - q0, r, row >> 6);
+              zero_tile_half_row(sh.d_o[gt % KV_STAGES], s.len - q0, r, row >> 6);
+            }
+            sw2.start();
+            tmem_wait_st();
+            sw2.stop(pe_st);
+            tc_fence_before();
+            mbar_arrive(smem_u32(&sh.p_ready[sub]));
+            sw.stop(pe_tile);
           }
-          if (q0 + BLK > s.len) {
-            // query rows past the sequence end are B rows of the dV / dK MMAs: clear them
-            const int r = wg * 64 + (row & 63);
-            zero_tile_half_row(sh.q[gt % KV_STAGES], s.len - q0, r, row >> 6);
-            zero_tile_half_row(sh.d_o[gt % KV_STAGES], s.len - q0, r, row >> 6);
-          }
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(smem_u32(&sh.p_ready[wg]));
           ++gt;
         }
       }
       if (!ok) break;
       // ---- accumulators leave TMEM: group 0 writes dK, group 1 writes dV, 64 columns at a time
+      sw.start();
       ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.acc_full), it & 1, abort_flag, a.status, WAIT_EPILOGUE));
+      sw.stop(pe_wacc);
       if (!ok) break;
       tc_fence_after();
+      sw.start();
       const float scal = per_token ? 1.f : row_scale(a, 0);
       const float sc = n < s.len ? (wg == 0 ? 0.5f * a.alpha * scal : scal) : 0.f;
       const long long out_rs = wg == 0 ? a.dk_rs : a.dv_rs;
       unsigned short* out0 = (wg == 0 ? reinterpret_cast<unsigned short*>(a.dk) : reinterpret_cast<unsigned short*>(a.dv)) +
                              (s.start + n0) * out_rs + head * HEAD_DIM;
       const uint32_t acc_addr = tmem + lane_addr + (wg == 0 ? KV_DK : KV_DV);
-#pragma unroll
-      for (int round = 0; round < 2; ++round) {
+      {
+        // Round 0 is staged first; the second half of the accumulator is pulled into registers
+        // (which frees TMEM for the next item's MMAs) before any global store is issued.
         uint32_t ov0[32], ov1[32];
-        tmem_ld32(acc_addr + round * 64, ov0);
-        tmem_ld32(acc_addr + round * 64 + 32, ov1);
+        tmem_ld32(acc_addr, ov0);
+        tmem_ld32(acc_addr + 32, ov1);
         tmem_wait_ld(ov0);
         tmem_wait_ld(ov1);
-        if (round == 1) {
-          tc_fence_before();
-          mbar_arrive(smem_u32(&sh.acc_empty));
-        }
-        group_barrier(wg);  // the previous copy out of the staging buffer has finished
+        group_barrier(wg);  // the previous item's copy out of the staging buffer has finished
+        stage_row64<IS_BF16>(stage, row, ov0, ov1, sc);
+        tmem_ld32(acc_addr + 64, ov0);
+        tmem_ld32(acc_addr + 96, ov1);
+        tmem_wait_ld(ov0);
+        tmem_wait_ld(ov1);
+        tc_fence_before();
+        mbar_arrive(smem_u32(&sh.acc_empty));
+        group_barrier(wg);
+        store_staged64(stage, out0, out_rs, s.len - n0, row);
+        group_barrier(wg);
         stage_row64<IS_BF16>(stage, row, ov0, ov1, sc);
         group_barrier(wg);
-        store_staged64(stage, out0 + round * 64, out_rs, s.len - n0, row);
+        store_staged64(stage, out0 + 64, out_rs, s.len - n0, row);
       }
+      sw.stop(pe_drain);
       ++it;
+    }
+    sw_total.stop(pe_total);
+    if (PROF && (threadIdx.x == 128 || threadIdx.x == 256)) {
+      atomicAdd(prof + PB_EPI_TOTAL, (int)(pe_total >> 6)); atomicAdd(prof + PB_EPI_WAIT_S, (int)(pe_ws >> 6));
+      atomicAdd(prof + PB_EPI_WAIT_ACC, (int)(pe_wacc >> 6)); atomicAdd(prof + PB_EPI_TILE, (int)(pe_tile >> 6));
+      atomicAdd(prof + PB_EPI_DRAIN, (int)(pe_drain >> 6)); atomicAdd(prof + PB_EPI_LD, (int)(pe_ld >> 6));
+      atomicAdd(prof + PB_EPI_ST, (int)(pe_st >> 6));
     }
   }
 
@@ -748,11 +822,12 @@ cudaError_t tc_backward(const KernelArgs& a, int dtype, void* workspace, cudaStr
     return cudaErrorInvalidValue;
   cudaError_t e = launch_prep(a, bf16, ws, w, true, st);
   if (e != cudaSuccess) return e;
-  long long grid = w.max_items < sm_count() ? w.max_items : sm_count();
-  if (grid < 1) grid = 1;
+  const int grid = main_grid(w);
   {
     const size_t smem = sizeof(DkvShared) + 1024;
-    auto kern = bf16 ? hstu_bwd_dkv_tc<true> : hstu_bwd_dkv_tc<false>;
+    static const bool profile = getenv("B200_HSTU_PROFILE") != nullptr;
+    auto kern = profile ? (bf16 ? hstu_bwd_dkv_tc<true, true> : hstu_bwd_dkv_tc<false, true>)
+                        : (bf16 ? hstu_bwd_dkv_tc<true, false> : hstu_bwd_dkv_tc<false, false>);
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     kern<<<static_cast<unsigned>(grid), BWD_THREADS, smem, st>>>(maps, a, ws, w.off_items);

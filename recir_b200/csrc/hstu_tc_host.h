@@ -12,6 +12,8 @@ namespace tc {
 // box = 64 columns x 128 rows, 128-byte swizzle, zero fill outside the matrix.
 bool make_map(CUtensorMap* m, const void* base, long long rows, long long width, long long row_stride, bool bf16);
 int sm_count();
+// Grid of the persistent kernels (also the stride with which CTAs walk the work list).
+int main_grid(const WorkspaceLayout& w);
 // Builds the work list in the workspace and zeroes the output rows no sequence owns.
 cudaError_t launch_prep(const KernelArgs& a, bool bf16, int* ws, const WorkspaceLayout& w, bool backward,
                         cudaStream_t st);
