@@ -288,18 +288,15 @@ def main():
     value = flops_step * args.steps / (ms_total * 1e-3) / 1e12
 
     # ------------------------------------------------------------ end to end (host buffers)
+    # Public host-memory API: chunks of whole sequences stream through copy-in / compute / copy-out
+    # streams (recir_b200.HostPipeline), so both PCIe directions overlap with the kernels.
     out_host = {k: torch.empty_like(host[k]).pin_memory() for k in ("q", "k", "v", "do")}
-    dd = {k: torch.empty_like(d[k]) for k in d}
+    pipe = recir_b200.HostPipeline(local["off"], local["nt"], H, D, D, torch.bfloat16, batch.max_seq_len,
+                                   batch.alpha, n_chunks=8, device=dev)
 
     def step_e2e():
-        for k_ in ("q", "k", "v", "do"):
-            dd[k_].copy_(host[k_], non_blocking=True)
-        o = torch.ops.recir.b200_hstu_attention_fwd(dd["q"], dd["k"], dd["v"], *args_op)
-        dq, dk, dv = torch.ops.recir.b200_hstu_attention_bwd(dd["do"], dd["q"], dd["k"], dd["v"], *args_op)
-        out_host["do"].copy_(o, non_blocking=True)
-        out_host["q"].copy_(dq, non_blocking=True)
-        out_host["k"].copy_(dk, non_blocking=True)
-        out_host["v"].copy_(dv, non_blocking=True)
+        pipe.run(host["q"], host["k"], host["v"], host["do"], out_host["do"], out_host["q"], out_host["k"],
+                 out_host["v"])
 
     for _ in range(3):
         step_e2e()

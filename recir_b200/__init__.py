@@ -5,5 +5,6 @@ Importing this package registers the ``recir::b200_*`` operators; the kernels li
 """
 from .ops import hstu_attention, hstu_attention_backward, validate_inputs  # noqa: F401
 from . import sharding, workload  # noqa: F401
+from .host_api import HostPipeline  # noqa: F401
 
-__all__ = ["hstu_attention", "hstu_attention_backward", "validate_inputs", "sharding", "workload"]
+__all__ = ["hstu_attention", "hstu_attention_backward", "validate_inputs", "sharding", "workload", "HostPipeline"]

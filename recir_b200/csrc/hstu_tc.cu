@@ -186,6 +186,17 @@ struct TensorMaps {
 enum { PF_MMA_TOTAL = 0, PF_MMA_KFULL, PF_MMA_PREADY, PF_MMA_VFULL, PF_MMA_ITEM, PF_EPI_TOTAL, PF_EPI_SFULL,
        PF_EPI_OFULL, PF_EPI_PARTIAL, PF_EPI_FULL, PF_N_PARTIAL, PF_N_FULL, PF_PROD_WAIT, PF_PROD_TOTAL };
 
+// Event trace (PROF only): CTA 0 records 32-bit clock samples into status[16 + slot]; the
+// profiling caller passes a status buffer large enough (16 + TRACE_SLOTS ints).
+constexpr int TRACE_SLOTS = 8192;
+template <bool PROF>
+__device__ __forceinline__ void trace_event(int* status, int slot_base, int idx, int ev, int n_ev) {
+  if (PROF && status != nullptr && blockIdx.x == 0) {
+    const int slot = slot_base + idx * n_ev + ev;
+    if (slot < TRACE_SLOTS) status[16 + slot] = static_cast<int>(clock64());
+  }
+}
+
 template <bool PROF>
 struct Stopwatch {
   long long t;
@@ -242,7 +253,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
   const uint32_t tmem = sh.tmem_base;
 
   // warps 0-3 (producer, MMA issuer, two idle) give registers to the eight epilogue warps
-  if (warp < 4) setmaxnreg_dec<120>(); else setmaxnreg_inc<184>();
+  if (warp < 4) setmaxnreg_dec<152>(); else setmaxnreg_inc<168>();
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer / tile scheduler
@@ -360,6 +371,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
           good = wait_all(&sh.v_full[vs], vph);
           sw.stop(pf[PF_MMA_VFULL]);
           if (!good) return false;
+          if (lane == 0) trace_event<PROF>(a.status, 0, pg, 2, 4);
           tc_fence_after();
           const uint32_t p_tmem = tmem + (sb ? TMEM_S1 : TMEM_S0);
           const uint32_t v_lo = v_lo0 + vs * (TILE_BYTES >> 4);
@@ -375,6 +387,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
             tc_commit(smem_u32(&sh.v_empty[vs]));
           }
           __syncwarp();
+          if (lane == 0) trace_event<PROF>(a.status, 0, pg, 3, 4);
           ++n_pv;
           return true;
         };
@@ -385,6 +398,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
           sw.stop(pf[PF_MMA_KFULL]);
           if (!ok) break;
           last = sh.meta[g & (META_RING - 1)] & 1;
+          if (lane == 0) trace_event<PROF>(a.status, 0, g, 0, 4);
           tc_fence_after();
           const uint32_t s_tmem = tmem + ((g & 1) ? TMEM_S1 : TMEM_S0);
           const uint32_t k_lo = k_lo0 + ks * (TILE_BYTES >> 4);
@@ -399,6 +413,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
             tc_commit(smem_u32(&sh.s_full[g & 1]));
           }
           __syncwarp();
+          if (lane == 0) trace_event<PROF>(a.status, 0, g, 1, 4);
           if (have_prev) ok = issue_pv(prev_g, prev_vs, prev_vph);
           prev_g = g; prev_vs = vs_cur; prev_vph = vph_cur;
           have_prev = true;
@@ -446,39 +461,34 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
       if (!ok) return false;
       tc_fence_after();
       const uint32_t o_addr = tmem + lane_addr + (ob ? TMEM_O1 : TMEM_O0) + wg * 64;
-      uint32_t ov0[32], ov1[32];
-      tmem_ld32(o_addr, ov0);
-      tmem_ld32(o_addr + 32, ov1);
-      tmem_wait_ld(ov0);
-      tmem_wait_ld(ov1);
-      tc_fence_before();
-      mbar_arrive(smem_u32(&sh.o_empty[ob]));
+      // Rows are handed to global memory through shared memory so that a warp writes whole
+      // 128-byte row segments (4 rows per instruction) instead of 32 scattered 16-byte pieces.
+      // Each group stages and writes its own 64 columns, 32 at a time (one register block);
+      // chunk index XOR (row & 7) keeps both the row-wise writes and the segment-wise reads free
+      // of avoidable bank conflicts.
       {
-        // Rows are handed to global memory through shared memory so that a warp writes whole
-        // 128-byte row segments (4 rows per instruction) instead of 32 scattered 16-byte pieces.
-        // Each group stages and writes its own 64 columns; chunk index XOR (row & 7) keeps both
-        // the row-wise writes and the segment-wise reads free of avoidable bank conflicts.
         const float sc = d_m0 + row < d_len ? row_scale(a, d_start + d_m0 + row) : 0.f;
         const int tid_wg = row;  // 0..127 inside the group
         asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");  // previous item's reads are done
         unsigned char* my_row = sh.o_stage + row * 256;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 x;
-          x.x = pack2<IS_BF16>(__uint_as_float(ov0[8 * j + 0]) * sc, __uint_as_float(ov0[8 * j + 1]) * sc);
-          x.y = pack2<IS_BF16>(__uint_as_float(ov0[8 * j + 2]) * sc, __uint_as_float(ov0[8 * j + 3]) * sc);
-          x.z = pack2<IS_BF16>(__uint_as_float(ov0[8 * j + 4]) * sc, __uint_as_float(ov0[8 * j + 5]) * sc);
-          x.w = pack2<IS_BF16>(__uint_as_float(ov0[8 * j + 6]) * sc, __uint_as_float(ov0[8 * j + 7]) * sc);
-          *reinterpret_cast<uint4*>(my_row + (((wg * 8 + j) ^ (row & 7)) << 4)) = x;
-        }
+        for (int h = 0; h < 2; ++h) {
+          uint32_t ov[32];
+          tmem_ld32(o_addr + h * 32, ov);
+          tmem_wait_ld(ov);
+          if (h == 1) {
+            tc_fence_before();
+            mbar_arrive(smem_u32(&sh.o_empty[ob]));
+          }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 x;
-          x.x = pack2<IS_BF16>(__uint_as_float(ov1[8 * j + 0]) * sc, __uint_as_float(ov1[8 * j + 1]) * sc);
-          x.y = pack2<IS_BF16>(__uint_as_float(ov1[8 * j + 2]) * sc, __uint_as_float(ov1[8 * j + 3]) * sc);
-          x.z = pack2<IS_BF16>(__uint_as_float(ov1[8 * j + 4]) * sc, __uint_as_float(ov1[8 * j + 5]) * sc);
-          x.w = pack2<IS_BF16>(__uint_as_float(ov1[8 * j + 6]) * sc, __uint_as_float(ov1[8 * j + 7]) * sc);
-          *reinterpret_cast<uint4*>(my_row + (((wg * 8 + 4 + j) ^ (row & 7)) << 4)) = x;
+          for (int j = 0; j < 4; ++j) {
+            uint4 x;
+            x.x = pack2<IS_BF16>(__uint_as_float(ov[8 * j + 0]) * sc, __uint_as_float(ov[8 * j + 1]) * sc);
+            x.y = pack2<IS_BF16>(__uint_as_float(ov[8 * j + 2]) * sc, __uint_as_float(ov[8 * j + 3]) * sc);
+            x.z = pack2<IS_BF16>(__uint_as_float(ov[8 * j + 4]) * sc, __uint_as_float(ov[8 * j + 5]) * sc);
+            x.w = pack2<IS_BF16>(__uint_as_float(ov[8 * j + 6]) * sc, __uint_as_float(ov[8 * j + 7]) * sc);
+            *reinterpret_cast<uint4*>(my_row + (((wg * 8 + h * 4 + j) ^ (row & 7)) << 4)) = x;
+          }
         }
         asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");  // the group's half tile is staged
         const int chunk = tid_wg & 7;
@@ -513,64 +523,97 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
       const RowMask rm = row_mask(m, s, a.mask);
       const BlockRange kr = key_blocks_for_query_block(m0, s, a.mask);
       const int cnt = kr.count();
-      // 32 candidate key blocks are classified at a time, one per lane
-      for (int base = 0; base < cnt && ok; base += 32) {
-        int my_cls = TILE_SKIP;
-        if (base + lane < cnt) my_cls = classify_tile(m0, kr.at(base + lane) * BLK, s, a.mask, true);
-        uint32_t todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
-        const uint32_t full_bits = __ballot_sync(0xffffffffu, my_cls == TILE_FULL);
-        while (todo != 0u && ok) {
-          const int bit = __ffs(todo) - 1;
-          todo &= todo - 1;
-          const int n0 = kr.at(base + bit) * BLK;
-          const int cls = ((full_bits >> bit) & 1u) ? TILE_FULL : TILE_PARTIAL;
-          // both groups work on every key tile: group wg owns score columns [64 wg, 64 wg + 64)
-          const uint32_t sb = g & 1, ph = (g >> 1) & 1;
-          sw.start();
-          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[sb]), ph, abort_flag, a.status, WAIT_EPILOGUE));
-          sw.stop(pf_sfull);
-          if (!ok) break;
-          sw.start();
-          tc_fence_after();
-          sw.stop(pf_fence);
-          sw.start();
-          const uint32_t s_addr = tmem + lane_addr + (sb ? TMEM_S1 : TMEM_S0) + wg * 64;
-          const uint32_t p_addr = s_addr;  // P (32 columns) goes over the group's own score columns
-          uint32_t sa[32], sb2[32], pk[16];
-          tmem_ld32(s_addr, sa);
-          tmem_ld32(s_addr + 32, sb2);
-          if (cls == TILE_FULL) {
-            tmem_wait_ld(sa);
-            tmem_wait_ld(sb2);
-            silu_chunk<IS_BF16, false>(sa, pk, c1, 0u);
-            tmem_st16(p_addr, pk);
-            silu_chunk<IS_BF16, false>(sb2, pk, c1, 0u);
-            tmem_st16(p_addr + 16, pk);
-          } else {
-            const unsigned long long bits = row_mask_bits64(rm, n0 + wg * 64);
-            tmem_wait_ld(sa);
-            tmem_wait_ld(sb2);
-            silu_chunk<IS_BF16, true>(sa, pk, c1, static_cast<uint32_t>(bits));
-            tmem_st16(p_addr, pk);
-            silu_chunk<IS_BF16, true>(sb2, pk, c1, static_cast<uint32_t>(bits >> 32));
-            tmem_st16(p_addr + 16, pk);
-          }
-          if (n0 + BLK > s.len) {
-            // Key rows past the end of the sequence belong to someone else (or to nobody) and may
-            // hold anything, NaN included; their P columns are exact zeros, but 0 * NaN is NaN,
-            // so the V rows themselves are cleared before the MMA reads the tile.
-            const uint32_t vs = g % NUM_V_STAGES, vph = (g / NUM_V_STAGES) & 1;
-            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.v_full[vs]), vph, abort_flag, a.status, WAIT_EPILOGUE));
-            if (!ok) break;
-            zero_tile_half_row(sh.v[vs], s.len - n0, row, wg);
-          }
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(smem_u32(&sh.p_ready[sb]));
-          if (cls == TILE_FULL) { sw.stop(pf_fullt); ++n_fullt; } else { sw.stop(pf_part); ++n_part; }
-          ++g;
-          if (drain_pending) { sw.start(); ok = drain_o(); sw.stop(pf_drain); }
+      // Kept key blocks of this item, in order; 32 candidates are classified at a time (one per lane).
+      int base_next = 0, cur_base = 0;
+      uint32_t todo = 0u, full_bits = 0u;
+      auto next_tile = [&](int& n0_out, bool& full_out) -> bool {
+        while (todo == 0u) {
+          if (base_next >= cnt) return false;
+          cur_base = base_next;
+          base_next += 32;
+          int my_cls = TILE_SKIP;
+          if (cur_base + lane < cnt) my_cls = classify_tile(m0, kr.at(cur_base + lane) * BLK, s, a.mask, true);
+          todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+          full_bits = __ballot_sync(0xffffffffu, my_cls == TILE_FULL);
         }
+        const int bit = __ffs(todo) - 1;
+        todo &= todo - 1;
+        n0_out = kr.at(cur_base + bit) * BLK;
+        full_out = (full_bits >> bit) & 1u;
+        return true;
+      };
+      auto s_addr_of = [&](uint32_t tile) -> uint32_t {
+        return tmem + lane_addr + ((tile & 1) ? TMEM_S1 : TMEM_S0) + wg * 64;
+      };
+      auto wait_scores = [&](uint32_t tile) -> bool {
+        sw.start();
+        const bool r = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[tile & 1]), (tile >> 1) & 1, abort_flag,
+                                                         a.status, WAIT_EPILOGUE));
+        sw.stop(pf_sfull);
+        if (r) tc_fence_after();
+        return r;
+      };
+      // Both groups work on every key tile: group wg owns score columns [64 wg, 64 wg + 64), handled
+      // as two 32-column chunks.  The chunk loads run ahead of the math: the second chunk is
+      // fetched while the first is processed, and the first chunk of the NEXT tile is fetched
+      // before this tile's P is handed to the MMA warp.
+      uint32_t sa[32], sb2[32], pk[16];
+      int n0 = 0, n0_next = 0;
+      bool full = false, full_next = false;
+      bool have = next_tile(n0, full);
+      if (have) {
+        if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 0, 6);
+        ok = wait_scores(g);
+        if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 1, 6);
+        if (ok) tmem_ld32(s_addr_of(g), sa);
+      }
+      while (have && ok) {
+        const bool have_next = next_tile(n0_next, full_next);
+        const uint32_t s_addr = s_addr_of(g);
+        const uint32_t sb = g & 1;
+        sw.start();
+        tmem_wait_ld(sa);
+        tmem_ld32(s_addr + 32, sb2);
+        if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 2, 6);
+        if (full) {
+          silu_chunk<IS_BF16, false>(sa, pk, c1, 0u);
+          tmem_st16(s_addr, pk);  // P (16 columns per chunk) goes over the group's own score columns
+          tmem_wait_ld(sb2);
+          silu_chunk<IS_BF16, false>(sb2, pk, c1, 0u);
+          tmem_st16(s_addr + 16, pk);
+        } else {
+          const unsigned long long bits = row_mask_bits64(rm, n0 + wg * 64);
+          silu_chunk<IS_BF16, true>(sa, pk, c1, static_cast<uint32_t>(bits));
+          tmem_st16(s_addr, pk);
+          tmem_wait_ld(sb2);
+          silu_chunk<IS_BF16, true>(sb2, pk, c1, static_cast<uint32_t>(bits >> 32));
+          tmem_st16(s_addr + 16, pk);
+        }
+        if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 3, 6);
+        if (n0 + BLK > s.len) {
+          // Key rows past the end of the sequence belong to someone else (or to nobody) and may
+          // hold anything, NaN included; their P columns are exact zeros, but 0 * NaN is NaN,
+          // so the V rows themselves are cleared before the MMA reads the tile.
+          const uint32_t vs = g % NUM_V_STAGES, vph = (g / NUM_V_STAGES) & 1;
+          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.v_full[vs]), vph, abort_flag, a.status, WAIT_EPILOGUE));
+          if (!ok) break;
+          zero_tile_half_row(sh.v[vs], s.len - n0, row, wg);
+        }
+        if (have_next) {
+          // scores of the next tile were issued before the MMA warp started waiting for this P
+          ok = wait_scores(g + 1);
+          if (!ok) break;
+          tmem_ld32(s_addr_of(g + 1), sa);
+        }
+        tmem_wait_st();
+        if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 4, 6);
+        tc_fence_before();
+        mbar_arrive(smem_u32(&sh.p_ready[sb]));
+        if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 5, 6);
+        if (full) { sw.stop(pf_fullt); ++n_fullt; } else { sw.stop(pf_part); ++n_part; }
+        ++g;
+        if (drain_pending) { sw.start(); ok = drain_o(); sw.stop(pf_drain); }
+        n0 = n0_next; full = full_next; have = have_next;
       }
       if (!ok) break;
       // hand the accumulator over: it is drained after the first key tile of the next item

@@ -59,6 +59,11 @@ template <bool IS_BF16, bool WANT_P>
 __device__ __forceinline__ void bwd_pair(uint32_t s0, uint32_t s1, uint32_t dp0, uint32_t dp1, float c1, uint32_t& p2,
                                          uint32_t& ds2) {
   const uint32_t u2 = pack2<IS_BF16>(c1 * __uint_as_float(s0), c1 * __uint_as_float(s1));
+#ifdef HSTU_EXPERIMENT_NO_MATH
+  if (WANT_P) p2 = u2;
+  ds2 = pack2<IS_BF16>(__uint_as_float(dp0), __uint_as_float(dp1));
+  return;
+#endif
   const uint32_t t2 = tanh2<IS_BF16>(u2);
   if (WANT_P) p2 = fma2<IS_BF16>(u2, t2, u2);
   const uint32_t w1 = add2<IS_BF16>(t2, one2<IS_BF16>());
