@@ -144,6 +144,33 @@ __device__ __forceinline__ SeqInfo load_seq_quiet(const KernelArgs& a, int b) {
   return r;
 }
 
+// Two-step variant for software-pipelined fetches: `load_seq_raw` only issues the loads (no
+// instruction consumes them), `finish_seq` turns them into a SeqInfo later.
+struct SeqRaw {
+  long long s, e, t;
+};
+__device__ __forceinline__ SeqRaw load_seq_raw(const KernelArgs& a, int b) {
+  SeqRaw r;
+  r.s = load_index(a.seq_offsets, a.offsets_i64, b);
+  r.e = load_index(a.seq_offsets, a.offsets_i64, b + 1);
+  r.t = a.num_targets != nullptr ? load_index(a.num_targets, a.targets_i64, b) : 0;
+  return r;
+}
+__device__ __forceinline__ SeqInfo finish_seq(const KernelArgs& a, const SeqRaw& raw) {
+  long long s = raw.s, e = raw.e, t = raw.t;
+  s = s < 0 ? 0 : (s > a.T ? a.T : s);
+  e = e < s ? s : (e > a.T ? a.T : e);
+  e = (e - s > 0x3fffffffLL) ? s + 0x3fffffffLL : e;
+  t = t < -0x3fffffffLL ? -0x3fffffffLL : (t > 0x3fffffffLL ? 0x3fffffffLL : t);
+  SeqInfo r;
+  r.start = s;
+  r.len = static_cast<int>(e - s);
+  r.has_targets = a.num_targets != nullptr;
+  r.hist = r.has_targets ? static_cast<int>(r.len - t) : r.len;
+  r.boundary = static_cast<int>(r.len - t) - a.mask.full;
+  return r;
+}
+
 __device__ __forceinline__ float row_scale(const KernelArgs& a, long long token) {
   if (a.scale_mode == 0) return a.inv_n;
   if (a.scale_mode == 1) return __ldg(a.attn_scale);

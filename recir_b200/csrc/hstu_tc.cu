@@ -582,11 +582,29 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
           silu_chunk<IS_BF16, false>(sb2, pk, c1, 0u);
           tmem_st16(s_addr + 16, pk);
         } else {
+          // A warp covers 32 consecutive rows, so on a diagonal tile most 32-column chunks are
+          // entirely kept or entirely dropped for the whole warp: vote, and only the chunks that
+          // straddle the mask boundary pay for per-element masking; dropped chunks skip the math.
           const unsigned long long bits = row_mask_bits64(rm, n0 + wg * 64);
-          silu_chunk<IS_BF16, true>(sa, pk, c1, static_cast<uint32_t>(bits));
+          const uint32_t b0 = static_cast<uint32_t>(bits), b1 = static_cast<uint32_t>(bits >> 32);
+          if (__all_sync(0xffffffffu, b0 == 0xffffffffu)) {
+            silu_chunk<IS_BF16, false>(sa, pk, c1, 0u);
+          } else if (__all_sync(0xffffffffu, b0 == 0u)) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[i] = 0u;
+          } else {
+            silu_chunk<IS_BF16, true>(sa, pk, c1, b0);
+          }
           tmem_st16(s_addr, pk);
           tmem_wait_ld(sb2);
-          silu_chunk<IS_BF16, true>(sb2, pk, c1, static_cast<uint32_t>(bits >> 32));
+          if (__all_sync(0xffffffffu, b1 == 0xffffffffu)) {
+            silu_chunk<IS_BF16, false>(sb2, pk, c1, 0u);
+          } else if (__all_sync(0xffffffffu, b1 == 0u)) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[i] = 0u;
+          } else {
+            silu_chunk<IS_BF16, true>(sb2, pk, c1, b1);
+          }
           tmem_st16(s_addr + 16, pk);
         }
         if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 3, 6);

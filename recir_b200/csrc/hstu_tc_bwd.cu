@@ -38,6 +38,15 @@ constexpr int META_RING = 16;
 // Optional cycle accounting (PROF): per-role wait/busy cycles, summed over CTAs into workspace ints 2..15.
 enum { PB_MMA_TOTAL = 0, PB_MMA_WAIT_LOAD, PB_MMA_WAIT_P, PB_MMA_WAIT_ACC, PB_MMA_WAIT_ITEM, PB_EPI_TOTAL,
        PB_EPI_WAIT_S, PB_EPI_WAIT_ACC, PB_EPI_TILE, PB_EPI_DRAIN, PB_EPI_LD, PB_EPI_ST, PB_PROD_WAIT, PB_PROD_TOTAL };
+constexpr int TRACE_SLOTS = 8192;
+template <bool PROF>
+__device__ __forceinline__ void trace_event(int* status, int slot_base, int idx, int ev, int n_ev) {
+  if (PROF && status != nullptr && blockIdx.x == 0) {
+    const int slot = slot_base + idx * n_ev + ev;
+    if (slot < TRACE_SLOTS) status[16 + slot] = static_cast<int>(clock64());
+  }
+}
+
 template <bool PROF>
 struct Stopwatch {
   long long t;
@@ -344,14 +353,20 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
     unsigned char* stage = sh.stage + wg * HALF_TILE_BYTES;
     uint32_t gt = 0, it = 0;
     bool ok = true;
-    int2 w_next = items[blockIdx.x];
-    SeqInfo s_next = load_seq_quiet(a, w_next.x & 0xffff);
+    // Work items are fetched two steps ahead (list entry) and one step ahead (sequence offsets), and
+    // nothing touches the loaded registers before the step that needs them, so the global-memory
+    // latency never sits on this loop's critical path.
+    const int grid_stride = static_cast<int>(gridDim.x);
+    int2 w_cur = items[blockIdx.x];
+    SeqRaw raw_cur = load_seq_raw(a, w_cur.x & 0xffff);
+    int2 w_ahead = items[min(static_cast<int>(blockIdx.x) + grid_stride, total_items - 1)];
     for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-      const int2 w = w_next;
-      const SeqInfo s = s_next;
-      if (item + static_cast<int>(gridDim.x) < total_items) {
-        w_next = items[item + gridDim.x];
-        s_next = load_seq_quiet(a, w_next.x & 0xffff);
+      const int2 w = w_cur;
+      const SeqInfo s = finish_seq(a, raw_cur);
+      if (item + grid_stride < total_items) {
+        w_cur = w_ahead;
+        raw_cur = load_seq_raw(a, w_ahead.x & 0xffff);
+        w_ahead = items[min(item + 2 * grid_stride, total_items - 1)];
       }
       const int head = w.x >> 16, qblk = w.y;
       const int m0 = qblk * BLK, m = m0 + row;
@@ -402,10 +417,16 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
             tmem_ld32(dp_addr, dpv);
             tmem_wait_ld(sv);
             tmem_wait_ld(dpv);
-            if (full) {
+            // on partial tiles most 32-column chunks are all-kept or all-dropped for a whole warp
+            // (32 consecutive rows): vote, mask per element only where the boundary crosses
+            const uint32_t hb = full ? 0xffffffffu
+                                     : static_cast<uint32_t>(row_mask_bits64(rm, n0 + sub * 64) >> (32 * wg));
+            if (__all_sync(0xffffffffu, hb == 0xffffffffu)) {
               bwd_chunk<IS_BF16, false, false>(sv, dpv, unused, pk, c1, 0u);
+            } else if (__all_sync(0xffffffffu, hb == 0u)) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) pk[i] = 0u;
             } else {
-              const uint32_t hb = static_cast<uint32_t>(row_mask_bits64(rm, n0 + sub * 64) >> (32 * wg));
               bwd_chunk<IS_BF16, false, true>(sv, dpv, unused, pk, c1, hb);
             }
             tmem_st16(dp_addr, pk);  // dS (16 columns) over the group's own dP columns
@@ -607,6 +628,7 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
         const bool g2 = n_acc != 0 || wait_all(&sh.acc_empty, (it & 1) ^ 1);
         sw.stop(pf[PB_MMA_WAIT_ACC]);
         if (!g2) return false;
+        if (lane == 0) trace_event<PROF>(a.status, 0, 2 * pgt + psub, 1, 4);
         tc_fence_after();
         const uint32_t don_lo = don_lo0 + pst * (TILE_BYTES >> 4) + psub * (SUBTILE_BYTES >> 4);
         const uint32_t qn_lo = qn_lo0 + pst * (TILE_BYTES >> 4) + psub * (SUBTILE_BYTES >> 4);
@@ -623,10 +645,12 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
           if (psub == 1) tc_commit(smem_u32(&sh.qd_empty[pst]));
         }
         __syncwarp();
+        if (lane == 0) trace_event<PROF>(a.status, 0, 2 * pgt + psub, 2, 4);
         ++n_acc;
         return true;
       };
       bool last = false;
+      if (lane == 0) trace_event<PROF>(a.status, 0, 2 * gt, 3, 4);  // item start (kv tiles landed)
       while (!last && ok) {
         sw.start();
         ok = wait_all(&sh.qd_full[st], ph);
@@ -649,6 +673,7 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
             tc_commit(smem_u32(&sh.s_full[sub]));
           }
           __syncwarp();
+          if (lane == 0) trace_event<PROF>(a.status, 0, 2 * gt + sub, 0, 4);
           if (have_prev) ok = issue_acc(prev_gt, prev_sub, prev_st);
           prev_gt = gt; prev_sub = sub; prev_st = st; have_prev = true;
         }
@@ -680,14 +705,20 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
     long long pe_total = 0, pe_ws = 0, pe_wacc = 0, pe_tile = 0, pe_drain = 0, pe_ld = 0, pe_st = 0;
     Stopwatch<PROF> sw_total, sw, sw2;
     sw_total.start();
-    int2 w_next = items[blockIdx.x];
-    SeqInfo s_next = load_seq_quiet(a, w_next.x & 0xffff);
+    // Work items are fetched two steps ahead (list entry) and one step ahead (sequence offsets), and
+    // nothing touches the loaded registers before the step that needs them, so the global-memory
+    // latency never sits on this loop's critical path.
+    const int grid_stride = static_cast<int>(gridDim.x);
+    int2 w_cur = items[blockIdx.x];
+    SeqRaw raw_cur = load_seq_raw(a, w_cur.x & 0xffff);
+    int2 w_ahead = items[min(static_cast<int>(blockIdx.x) + grid_stride, total_items - 1)];
     for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-      const int2 w = w_next;
-      const SeqInfo s = s_next;
-      if (item + static_cast<int>(gridDim.x) < total_items) {
-        w_next = items[item + gridDim.x];
-        s_next = load_seq_quiet(a, w_next.x & 0xffff);
+      const int2 w = w_cur;
+      const SeqInfo s = finish_seq(a, raw_cur);
+      if (item + grid_stride < total_items) {
+        w_cur = w_ahead;
+        raw_cur = load_seq_raw(a, w_ahead.x & 0xffff);
+        w_ahead = items[min(item + 2 * grid_stride, total_items - 1)];
       }
       const int head = w.x >> 16;
       const int kvblk = (s.len + BLK - 1) / BLK - 1 - w.y;
@@ -707,9 +738,11 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
           const bool full = (full_bits >> bit) & 1u;
           // both groups work on every 64-column half tile: group wg owns its columns [32 wg, 32 wg + 32)
           for (int sub = 0; sub < 2 && ok; ++sub) {
+            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 0, 6);
             sw.start();
             ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[sub]), gt & 1, abort_flag, a.status, WAIT_EPILOGUE));
             sw.stop(pe_ws);
+            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 1, 6);
             if (!ok) break;
             tc_fence_after();
             sw.start();
@@ -723,10 +756,15 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
             tmem_wait_ld(sv);
             tmem_wait_ld(dpv);
             sw2.stop(pe_ld);
-            if (full) {
+            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 2, 6);
+            const uint32_t hb = full ? 0xffffffffu
+                                     : static_cast<uint32_t>(col_mask_bits64(cm, s.len, mbase) >> (32 * wg));
+            if (__all_sync(0xffffffffu, hb == 0xffffffffu)) {
               bwd_chunk<IS_BF16, true, false>(sv, dpv, pp, pd, c1, 0u);
+            } else if (__all_sync(0xffffffffu, hb == 0u)) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) { pp[i] = 0u; pd[i] = 0u; }
             } else {
-              const uint32_t hb = static_cast<uint32_t>(col_mask_bits64(cm, s.len, mbase) >> (32 * wg));
               bwd_chunk<IS_BF16, true, true>(sv, dpv, pp, pd, c1, hb);
             }
             if (per_token) {  // one scale per query token = per column here (masked entries stay zero)
@@ -735,6 +773,7 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
             }
             tmem_st16(st_addr, pp);  // P^T and dS^T (16 columns each) over the group's own score columns
             tmem_st16(dp_addr, pd);
+            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 3, 6);
             if (q0 + BLK > s.len && wg == 0) {
               // query rows past the sequence end are B rows of the dV / dK MMAs: clear them
               const int r = sub * 64 + (row & 63);
@@ -746,6 +785,7 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
             sw2.stop(pe_st);
             tc_fence_before();
             mbar_arrive(smem_u32(&sh.p_ready[sub]));
+            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 4, 6);
             sw.stop(pe_tile);
           }
           ++gt;
@@ -789,6 +829,7 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
         store_staged64(stage, out0 + 64, out_rs, s.len - n0, row);
       }
       sw.stop(pe_drain);
+      if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt, 5, 6);  // drain finished (before half tile 2*gt)
       ++it;
     }
     sw_total.stop(pe_total);

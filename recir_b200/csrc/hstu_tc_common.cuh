@@ -222,8 +222,8 @@ __device__ __forceinline__ void zero_tile_rows(unsigned char* tile, int first_ba
     const uint4 z = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
     for (int i = 0; i < 8; ++i) { r0[i] = z; r1[i] = z; }
+    sm100::fence_proxy_async();
   }
-  sm100::fence_proxy_async();
 }
 // Same for one 64-column half (`half` = 0 or 1) of the row.
 __device__ __forceinline__ void zero_tile_half_row(unsigned char* tile, int first_bad, int row, int half) {
@@ -232,8 +232,8 @@ __device__ __forceinline__ void zero_tile_half_row(unsigned char* tile, int firs
     const uint4 z = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
     for (int i = 0; i < 8; ++i) r[i] = z;
+    sm100::fence_proxy_async();
   }
-  sm100::fence_proxy_async();
 }
 #endif
 
