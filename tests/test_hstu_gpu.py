@@ -253,3 +253,45 @@ def test_host_pipeline_matches_direct_call():
     g = torch.ops.recir.b200_hstu_attention_bwd(d(bt.dout), d(bt.q), d(bt.k), d(bt.v), *a)
     for got, ref in zip(outs, (o, *g)):
         assert torch.equal(got, ref.cpu())
+
+
+def test_long_window_config_tensor_core_vs_cuda_core_and_oracle():
+    """Long skewed sequences with a 1024-token sliding window and the contextual flag (the
+    third benchmark configuration, first 6 sequences): both kernel families must agree, and the
+    shortest sequence is checked against the oracle."""
+    bt = workload.config3(batch=6)
+    d = lambda x: None if x is None else x.to(DEV)
+    kw = bt.op_kwargs()
+    a = (d(bt.seq_offsets), kw["max_seq_len"], kw["alpha"], True, d(bt.num_targets), kw["contextual_seq_len"],
+         kw["max_attn_len"], None, 0)
+    q, k, v, do = d(bt.q), d(bt.k), d(bt.v), d(bt.dout)
+    o = torch.ops.recir.b200_hstu_attention_fwd(q, k, v, *a)
+    g = torch.ops.recir.b200_hstu_attention_bwd(do, q, k, v, *a)
+    ops.set_force_simt(True)
+    try:
+        o2 = torch.ops.recir.b200_hstu_attention_fwd(q, k, v, *a)
+        g2 = torch.ops.recir.b200_hstu_attention_bwd(do, q, k, v, *a)
+    finally:
+        ops.set_force_simt(False)
+    for x, y in zip((o, *g), (o2, *g2)):
+        assert torch.isfinite(x.float()).all()
+        assert rel_l2(x.float(), y.float()) <= 6e-3
+    b = int(np.argmin(bt.lengths))
+    s, e = int(bt.seq_offsets[b]), int(bt.seq_offsets[b + 1])
+    f = lambda x: x[s:e].float().numpy()
+    okw = dict(max_seq_len=kw["max_seq_len"], alpha=kw["alpha"], causal=True, max_attn_len=kw["max_attn_len"],
+               contextual_seq_len=kw["contextual_seq_len"], num_targets=np.array([int(bt.num_targets[b])]))
+    ro = hstu_oracle.hstu_attention_fwd(f(bt.q), f(bt.k), f(bt.v), np.array([0, e - s]), **okw)
+    rg = hstu_oracle.hstu_attention_bwd(f(bt.dout), f(bt.q), f(bt.k), f(bt.v), np.array([0, e - s]), **okw)
+    for got, ref in ((o, ro), (g[0], rg[0]), (g[1], rg[1]), (g[2], rg[2])):
+        assert rel_l2(got[s:e].float(), ref) <= 6e-3
+
+
+def test_per_token_attn_scale_on_tensor_core_path():
+    q, k, v, do, off, kw = _jagged_case(21, [300, 140, 520], [10, 0, 77])
+    g = torch.Generator().manual_seed(5)
+    kw["attn_scale"] = torch.rand(q.shape[0], generator=g) + 0.25
+    ro, rdq, rdk, rdv = _oracle(q, k, v, do, off, kw)
+    o, dq, dk, dv = _gpu(q, k, v, do, off, kw)
+    for got, ref in ((o, ro), (dq, rdq), (dk, rdk), (dv, rdv)):
+        assert rel_l2(got.float(), ref) <= 6e-3
