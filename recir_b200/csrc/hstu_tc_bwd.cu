@@ -175,13 +175,16 @@ __device__ __forceinline__ void group_barrier(int wg) { asm volatile("bar.sync %
 // ------------------------------------------------------------------------------------
 // dQ pass
 // ------------------------------------------------------------------------------------
-constexpr int DQ_STAGES = 3;
+constexpr int DQ_STAGES = 2;
 constexpr int DQ_QA = 0, DQ_DOA = 64, DQ_S0 = 128, DQ_DP0 = 256, DQ_ACC = 384;  // S1 = S0 + 64, DP1 = DP0 + 64
 
 struct DqShared {
   unsigned char k[DQ_STAGES][TILE_BYTES];
   unsigned char v[DQ_STAGES][TILE_BYTES];
+  unsigned char q[TILE_BYTES];    // Q and dO tiles of the NEXT work item (TMA), copied row by row into
+  unsigned char d_o[TILE_BYTES];  // TMEM when that item starts
   unsigned char stage[TILE_BYTES];
+  unsigned long long qd_full, qd_empty;
   unsigned long long k_full[DQ_STAGES], k_empty[DQ_STAGES];
   unsigned long long v_full[DQ_STAGES], v_empty[DQ_STAGES];
   unsigned long long a_ready, s_full[2], ds_ready[2], acc_full, acc_empty;
@@ -190,7 +193,7 @@ struct DqShared {
   int abort_flag;
 };
 
-template <bool IS_BF16>
+template <bool IS_BF16, bool PROF>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
 hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __restrict__ ws, long long off_items) {
   extern __shared__ unsigned char smem_raw[];
@@ -208,6 +211,8 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
       mbar_init(smem_u32(&sh.v_full[i]), 1); mbar_init(smem_u32(&sh.v_empty[i]), 1);
     }
     mbar_init(smem_u32(&sh.a_ready), 256);
+    mbar_init(smem_u32(&sh.qd_full), 1);
+    mbar_init(smem_u32(&sh.qd_empty), 256);
     for (int i = 0; i < 2; ++i) { mbar_init(smem_u32(&sh.s_full[i]), 1); mbar_init(smem_u32(&sh.ds_ready[i]), 256); }
     mbar_init(smem_u32(&sh.acc_full), 1);
     mbar_init(smem_u32(&sh.acc_empty), 256);
@@ -226,8 +231,11 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer / tile scheduler
-    if (lane == 0) { prefetch_tensormap(&maps.k); prefetch_tensormap(&maps.v); }
-    uint32_t gt = 0, st = 0, ph = 0;
+    if (lane == 0) {
+      prefetch_tensormap(&maps.k); prefetch_tensormap(&maps.v);
+      prefetch_tensormap(&maps.q); prefetch_tensormap(&maps.d_o);
+    }
+    uint32_t gt = 0, st = 0, ph = 0, pit = 0;
     bool ok = true;
     auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_PRODUCER));
@@ -237,6 +245,22 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
       const int b = w.x & 0xffff, head = w.x >> 16, qblk = w.y;
       const SeqInfo s = load_seq(a, b);
       const int m0 = qblk * BLK, col0 = head * HEAD_DIM;
+      {
+        // Q and dO rows of this item: the buffer is free as soon as the previous item's rows have
+        // been copied into TMEM, i.e. early in the previous item, so this load is a prefetch
+        const int qrow = static_cast<int>(s.start) + m0;
+        ok = wait_all(&sh.qd_empty, (pit & 1) ^ 1);
+        if (!ok) break;
+        if (elect_one()) {
+          mbar_arrive_expect_tx(smem_u32(&sh.qd_full), 2 * TILE_BYTES);
+          tma_load_2d(smem_u32(sh.q), &maps.q, smem_u32(&sh.qd_full), col0, qrow);
+          tma_load_2d(smem_u32(sh.q) + HALF_TILE_BYTES, &maps.q, smem_u32(&sh.qd_full), col0 + 64, qrow);
+          tma_load_2d(smem_u32(sh.d_o), &maps.d_o, smem_u32(&sh.qd_full), col0, qrow);
+          tma_load_2d(smem_u32(sh.d_o) + HALF_TILE_BYTES, &maps.d_o, smem_u32(&sh.qd_full), col0 + 64, qrow);
+        }
+        __syncwarp();
+        ++pit;
+      }
       const BlockRange kr = key_blocks_for_query_block(m0, s, a.mask);
       const int cnt = kr.count();
       // the last candidate (diagonal block, or last block of the sequence) is never skipped
@@ -293,6 +317,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
       auto issue_acc = [&](uint32_t pgt, uint32_t psub, uint32_t pst) -> bool {
         if (!wait_all(&sh.ds_ready[psub], pgt & 1)) return false;
         if (n_acc == 0 && !wait_all(&sh.acc_empty, (it & 1) ^ 1)) return false;
+        if (lane == 0) trace_event<PROF>(a.status, 0, 2 * pgt + psub, 2, 4);
         tc_fence_after();
         const uint32_t kn_lo = kn_lo0 + pst * (TILE_BYTES >> 4) + psub * (SUBTILE_BYTES >> 4);
         const uint32_t ds_tmem = tmem + DQ_DP0 + psub * 64;
@@ -305,6 +330,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
           if (psub == 1) tc_commit(smem_u32(&sh.k_empty[pst]));
         }
         __syncwarp();
+        if (lane == 0) trace_event<PROF>(a.status, 0, 2 * pgt + psub, 3, 4);
         ++n_acc;
         return true;
       };
@@ -314,6 +340,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
         if (ok) ok = wait_all(&sh.v_full[st], ph);
         if (!ok) break;
         last = sh.meta[gt & (META_RING - 1)] & 1;
+        if (lane == 0) trace_event<PROF>(a.status, 0, 2 * gt, 0, 4);
         tc_fence_after();
         for (uint32_t sub = 0; sub < 2 && ok; ++sub) {
           const uint32_t k_lo = k_lo0 + st * (TILE_BYTES >> 4) + sub * (SUBTILE_BYTES >> 4);
@@ -331,6 +358,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
             if (sub == 1) tc_commit(smem_u32(&sh.v_empty[st]));
           }
           __syncwarp();
+          if (lane == 0) trace_event<PROF>(a.status, 0, 2 * gt + sub, 1, 4);
           if (have_prev) ok = issue_acc(prev_gt, prev_sub, prev_st);
           prev_gt = gt; prev_sub = sub; prev_st = st; have_prev = true;
         }
@@ -370,24 +398,28 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
       }
       const int head = w.x >> 16, qblk = w.y;
       const int m0 = qblk * BLK, m = m0 + row;
-      // ---- A operands straight from global memory into TMEM: group 0 loads Q, group 1 loads dO
-      // (the previous item's MMAs are complete: both groups waited for its accumulator)
+      // ---- A operands: the item's Q and dO tiles were prefetched into shared memory by TMA; group 0
+      // copies its Q row, group 1 its dO row into TMEM (rows past the sequence end as zeros).
+      // The previous item's MMAs are complete: both groups waited for its accumulator.
       {
-        const unsigned short* src = wg == 0
-            ? reinterpret_cast<const unsigned short*>(a.q) + (s.start + m) * a.q_rs + head * HEAD_DIM
-            : reinterpret_cast<const unsigned short*>(a.d_o) + (s.start + m) * a.do_rs + head * HEAD_DIM;
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.qd_full), it & 1, abort_flag, a.status, WAIT_EPILOGUE));
+        if (!ok) break;
+        const unsigned char* tile = wg == 0 ? sh.q : sh.d_o;
         const uint32_t dst = tmem + lane_addr + (wg == 0 ? DQ_QA : DQ_DOA);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 4; ++c) {  // 4 x 16 TMEM columns = 4 x 32 elements; box = c / 2, chunks (c % 2) * 4 ..
           uint32_t r[16];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            uint4 x = make_uint4(0u, 0u, 0u, 0u);
-            if (m < s.len) x = __ldg(reinterpret_cast<const uint4*>(src) + c * 4 + j);
+            const int chunk = (c & 1) * 4 + j;  // 16-byte chunk inside the 128-byte box row
+            uint4 x = *reinterpret_cast<const uint4*>(tile + (c >> 1) * HALF_TILE_BYTES + row * 128 +
+                                                      ((chunk ^ (row & 7)) << 4));
+            if (m >= s.len) x = make_uint4(0u, 0u, 0u, 0u);
             r[4 * j + 0] = x.x; r[4 * j + 1] = x.y; r[4 * j + 2] = x.z; r[4 * j + 3] = x.w;
           }
           tmem_st16(dst + c * 16, r);
         }
+        mbar_arrive(smem_u32(&sh.qd_empty));  // the tile has been read: the next item's may land
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(smem_u32(&sh.a_ready));
@@ -407,7 +439,9 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
           const bool full = (full_bits >> bit) & 1u;
           // both groups work on every 64-column half tile: group wg owns its columns [32 wg, 32 wg + 32)
           for (int sub = 0; sub < 2 && ok; ++sub) {
+            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 0, 6);
             ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[sub]), gt & 1, abort_flag, a.status, WAIT_EPILOGUE));
+            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 1, 6);
             if (!ok) break;
             tc_fence_after();
             const uint32_t s_addr = tmem + lane_addr + DQ_S0 + sub * 64 + wg * 32;
@@ -417,6 +451,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
             tmem_ld32(dp_addr, dpv);
             tmem_wait_ld(sv);
             tmem_wait_ld(dpv);
+            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 2, 6);
             // on partial tiles most 32-column chunks are all-kept or all-dropped for a whole warp
             // (32 consecutive rows): vote, mask per element only where the boundary crosses
             const uint32_t hb = full ? 0xffffffffu
@@ -430,6 +465,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
               bwd_chunk<IS_BF16, false, true>(sv, dpv, unused, pk, c1, hb);
             }
             tmem_st16(dp_addr, pk);  // dS (16 columns) over the group's own dP columns
+            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 3, 6);
             if (n0 + BLK > s.len && wg == 0) {
               // key rows past the sequence end feed the dQ MMA as B rows: clear them (0 * NaN = NaN)
               zero_tile_half_row(sh.k[gt % DQ_STAGES], s.len - n0, sub * 64 + (row & 63), row >> 6);
@@ -437,6 +473,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(smem_u32(&sh.ds_ready[sub]));
+            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 4, 6);
           }
           ++gt;
         }
@@ -459,6 +496,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
       group_barrier(wg);
       store_staged64(stage, reinterpret_cast<unsigned short*>(a.dq) + (s.start + m0) * a.dq_rs + head * HEAD_DIM + wg * 64,
                      a.dq_rs, s.len - m0, row);
+      if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt, 5, 6);
       ++it;
     }
   }
@@ -880,7 +918,9 @@ cudaError_t tc_backward(const KernelArgs& a, int dtype, void* workspace, cudaStr
   }
   {
     const size_t smem = sizeof(DqShared) + 1024;
-    auto kern = bf16 ? hstu_bwd_dq_tc<true> : hstu_bwd_dq_tc<false>;
+    static const bool profile = getenv("B200_HSTU_PROFILE_DQ") != nullptr;
+    auto kern = profile ? (bf16 ? hstu_bwd_dq_tc<true, true> : hstu_bwd_dq_tc<false, true>)
+                        : (bf16 ? hstu_bwd_dq_tc<true, false> : hstu_bwd_dq_tc<false, false>);
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     kern<<<static_cast<unsigned>(grid), BWD_THREADS, smem, st>>>(maps, a, ws, w.off_items);
