@@ -36,6 +36,10 @@ import torch
 METRIC = "hstu_attn_fwd_bwd_useful_tflops"
 UNIT = "TFLOP/s"
 NOMINAL_BF16_TFLOPS = 2250.0
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from the committed ncu capture of the same
+# B/H/D and length distribution (profiles/tc_kernels_cfg1_ncu_full.md), and that capture's token count.
+NCU_CFG1_DRAM_BYTES = {"hstu_fwd_tc": 618.5e6, "hstu_bwd_dkv_tc": 820.6e6, "hstu_bwd_dq_tc": 795.4e6}
+NCU_CFG1_TOKENS = 78262
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -273,18 +277,30 @@ def main():
     barrier()
     launches = ops.launch_counter - launches0
     ms_total = max_over_ranks(ev0.elapsed_time(ev1))
-    # per-pass device time (same stream), for the roofline of the dominant pass
-    fe = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-    fwd_ms, bwd_ms = [], []
-    for _ in range(max(5, min(args.steps, 20))):
-        fe[0].record()
-        torch.ops.recir.b200_hstu_attention_fwd(d["q"], d["k"], d["v"], *args_op)
-        fe[1].record()
-        torch.ops.recir.b200_hstu_attention_bwd(d["do"], d["q"], d["k"], d["v"], *args_op)
-        fe[2].record()
-        torch.cuda.synchronize()
-        fwd_ms.append(fe[0].elapsed_time(fe[1]))
-        bwd_ms.append(fe[1].elapsed_time(fe[2]))
+    # per-kernel device time (same stream), for the roofline of the dominant kernel: each pass is
+    # issued `reps` times back to back between two events so that the host's launch latency does not
+    # sit inside the measurement; the backward kernels also run one at a time (C-ABI flag).
+    def time_pass(fn, reps=10, rounds=5):
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        out = []
+        for r in range(rounds + 1):
+            e[0].record()
+            for _ in range(reps):
+                fn()
+            e[1].record()
+            torch.cuda.synchronize()
+            if r > 0:
+                out.append(e[0].elapsed_time(e[1]) / reps)
+        return out
+
+    run_fwd = lambda: torch.ops.recir.b200_hstu_attention_fwd(d["q"], d["k"], d["v"], *args_op)
+    run_bwd = lambda: torch.ops.recir.b200_hstu_attention_bwd(d["do"], d["q"], d["k"], d["v"], *args_op)
+    fwd_ms, bwd_ms = time_pass(run_fwd), time_pass(run_bwd)
+    ops.set_backward_passes(dkv=True, dq=False)
+    dkv_ms = time_pass(run_bwd)
+    ops.set_backward_passes(dkv=False, dq=True)
+    dq_ms = time_pass(run_bwd)
+    ops.set_backward_passes(True, True)
     value = flops_step * args.steps / (ms_total * 1e-3) / 1e12
 
     # ------------------------------------------------------------ end to end (host buffers)
@@ -325,15 +341,32 @@ def main():
         p = _lib.B200HstuParams()
         fwd_med, bwd_med = float(np.median(fwd_ms)), float(np.median(bwd_ms))
         local_pairs = pairs_global / world  # token-balanced shards of one distribution
-        dom_is_bwd = bwd_med >= fwd_med
-        dom_flops = workload.useful_flops(local_pairs, H, D, D, backward=dom_is_bwd, forward=not dom_is_bwd)
-        dom_ms = bwd_med if dom_is_bwd else fwd_med
+        # One launch of each main kernel: useful flops (2*D per kept pair per GEMM: forward 2 GEMMs,
+        # dK/dV pass 4 -- S, dP, dV, dK -- and the dQ pass 1; its recomputed S and dP count as overhead)
+        # over the kernel's own device time.
+        gemm = 2.0 * local_pairs * H * D
+        kernels = {
+            "hstu_fwd_tc": (2 * gemm, fwd_med, NCU_CFG1_DRAM_BYTES["hstu_fwd_tc"]),
+            "hstu_bwd_dkv_tc": (4 * gemm, float(np.median(dkv_ms)), NCU_CFG1_DRAM_BYTES["hstu_bwd_dkv_tc"]),
+            "hstu_bwd_dq_tc": (1 * gemm, float(np.median(dq_ms)), NCU_CFG1_DRAM_BYTES["hstu_bwd_dq_tc"]),
+        }
+        dom = max(kernels, key=lambda k: kernels[k][1])
+        dom_flops, dom_ms, dom_traffic = kernels[dom]
         achieved = dom_flops / (dom_ms * 1e-3) / 1e12
         peak = peaks["bf16_tflops"]
+        local_tokens = T_global / world
         roofline = {
-            "bound": "tensor", "kernel": "backward pass (dK/dV + dQ kernels)" if dom_is_bwd else "forward kernel",
+            "bound": "tensor", "kernel": dom,
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-            "peak_source": f"{peaks['_source']} burst bf16 GEMM", "traffic": None,
+            "peak_source": f"{peaks['_source']} burst bf16 GEMM",
+            # DRAM bytes of one launch from the ncu capture of the same shapes at T=78262 tokens,
+            # scaled by tokens (traffic grows with the token count at a fixed length distribution)
+            "traffic": dom_traffic * local_tokens / NCU_CFG1_TOKENS,
+            # fwd: q,k,v read + o written; dK/dV pass: q,k,v,dO read + dk,dv written; dQ pass: q,k,v,dO read + dq written
+            "algorithmic_bytes": {"hstu_fwd_tc": 4, "hstu_bwd_dkv_tc": 6, "hstu_bwd_dq_tc": 5}[dom]
+            * local_tokens * H * D * 2,
+            "per_kernel_ms": {k: v[1] for k, v in kernels.items()},
+            "per_kernel_tflops": {k: v[0] / (v[1] * 1e-3) / 1e12 for k, v in kernels.items()},
             "fwd_ms": fwd_med, "bwd_ms": bwd_med,
             "fwd_tflops": workload.useful_flops(local_pairs, H, D, D, backward=False) / (fwd_med * 1e-3) / 1e12,
             "bwd_tflops": workload.useful_flops(local_pairs, H, D, D, backward=True, forward=False) / (bwd_med * 1e-3) / 1e12,

@@ -52,6 +52,8 @@ extern "C" {
 #define B200_HSTU_FLAG_TARGETS_I64 0x4u     /* num_targets is int64 (else int32) */
 #define B200_HSTU_FLAG_SCALE_PER_TOKEN 0x8u /* attn_scale has T values (else 1) */
 #define B200_HSTU_FLAG_FORCE_SIMT 0x10u     /* use the plain CUDA-core kernels (cross-check path) */
+#define B200_HSTU_FLAG_BWD_SKIP_DQ 0x20u    /* backward: run only the dK/dV pass (dq is left untouched) */
+#define B200_HSTU_FLAG_BWD_SKIP_DKV 0x40u   /* backward: run only the dQ pass (dk, dv are left untouched) */
 
 /* error codes */
 #define B200_HSTU_OK 0

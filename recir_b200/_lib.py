@@ -16,6 +16,8 @@ FLAG_OFFSETS_I64 = 0x2
 FLAG_TARGETS_I64 = 0x4
 FLAG_SCALE_PER_TOKEN = 0x8
 FLAG_FORCE_SIMT = 0x10
+FLAG_BWD_SKIP_DQ = 0x20
+FLAG_BWD_SKIP_DKV = 0x40
 
 EXPORTS = (
     "b200_hstu_fwd", "b200_hstu_bwd", "b200_hstu_workspace_bytes", "b200_hstu_uses_tensor_cores",

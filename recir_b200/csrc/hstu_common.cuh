@@ -85,6 +85,7 @@ struct KernelArgs {
   long long q_rs, k_rs, v_rs, o_rs, do_rs, dq_rs, dk_rs, dv_rs;
   int B, H, Dqk, Dv;
   int offsets_i64, targets_i64, scale_mode;  // scale_mode: 0 = 1/N, 1 = scalar, 2 = per token
+  int skip_dq, skip_dkv;                     // backward: leave one of the two passes out (timing aid)
   float alpha;
   float inv_n;
   MaskOpts mask;

@@ -297,8 +297,8 @@ cudaError_t launch_bwd_t(const KernelArgs& a, int max_seq_len, cudaStream_t st) 
   e = cudaFuncSetAttribute(simt_kv_major<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2);
   if (e != cudaSuccess) return e;
   dim3 grid(grid_x(a, max_seq_len), a.H, a.B);
-  simt_kv_major<T><<<grid, THREADS, sm2, st>>>(a);
-  simt_q_major<T, 1><<<grid, THREADS, sm1, st>>>(a);
+  if (!a.skip_dkv) simt_kv_major<T><<<grid, THREADS, sm2, st>>>(a);
+  if (!a.skip_dq) simt_q_major<T, 1><<<grid, THREADS, sm1, st>>>(a);
   return cudaGetLastError();
 }
 

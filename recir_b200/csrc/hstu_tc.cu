@@ -99,6 +99,21 @@ __global__ void __launch_bounds__(1024) build_block_index(KernelArgs a, int* ws,
     ws[0] = start[0] + cnt[0] * a.H;
     ws[1] = cnt[0];
   }
+  // chunk_base[c] = items owned by the first c * chunk_seqs sequences of the sorted order:
+  // sequence i has more than j blocks iff i < cnt[j], so its block count is #{j : cnt[j] > i}
+  int* chunk_base = ws + w.off_chunk;
+  const int n_seq = cnt[0];
+  const int n_chunks = (n_seq + w.chunk_seqs - 1) / w.chunk_seqs;
+  for (int c = tid; c <= n_chunks; c += blockDim.x) {
+    const long long lim = min((long long)c * w.chunk_seqs, (long long)n_seq);
+    long long sum = 0;
+    for (long long j = 0; j < w.nbins; ++j) {
+      const int v = cnt[j];
+      if (v == 0) break;
+      sum += v < lim ? v : lim;
+    }
+    chunk_base[c] = static_cast<int>(sum * a.H);
+  }
 }
 
 // One thread per work item: find its block index by bisection over start[], then decode.
@@ -112,7 +127,7 @@ __global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, W
                                                         T* z2, long long rs2, int w2) {
   const int* sorted = ws + w.off_sorted;
   const int* cnt = ws + w.off_cnt;
-  const int* start = ws + w.off_start;
+  const int* chunk_base = ws + w.off_chunk;
   int2* items = reinterpret_cast<int2*>(ws + w.off_items);
   const int total = ws[0];
   const long long gtid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
@@ -121,17 +136,36 @@ __global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, W
     const long long round = slot / stride, c = slot - round * stride;
     const long long round_size = (total - round * stride < stride) ? (total - round * stride) : stride;
     const long long p = round * stride + ((round & 1) ? (round_size - 1 - c) : c);  // rank in the sorted order
-    // start[] is non-increasing in j; find the smallest j with start[j] <= p
-    long long lo = 0, hi = w.nbins - 1;
+    // Rank p -> item.  The sorted sequences are cut into chunks of chunk_seqs; the list is
+    // chunk-major, and inside a chunk block-index-major (highest block index = most expensive
+    // first), then sequence, then head.  All items that read the same K/V (or Q/dO) rows are
+    // therefore close together in the list and run at about the same time, which is what
+    // keeps those rows in L2 between their readers.
+    const int n_seq = ws[1];
+    const int n_chunks = (n_seq + w.chunk_seqs - 1) / w.chunk_seqs;
+    int lo = 0, hi = n_chunks - 1;
     while (lo < hi) {
-      const long long mid = (lo + hi) >> 1;
-      if (start[mid] <= p) hi = mid; else lo = mid + 1;
+      const int mid = (lo + hi + 1) >> 1;
+      if (chunk_base[mid] <= p) lo = mid; else hi = mid - 1;
     }
-    const int j = static_cast<int>(lo);
-    const int r = static_cast<int>(p - start[j]);
-    const int i = r / a.H, head = r - i * a.H;
+    const int first = lo * w.chunk_seqs;
+    const int n_c = min(w.chunk_seqs, n_seq - first);
+    long long r = p - chunk_base[lo];
+    // highest block index present in the chunk: largest j with cnt[j] > first
+    long long jl = 0, jh = w.nbins - 1;
+    while (jl < jh) {
+      const long long mid = (jl + jh + 1) >> 1;
+      if (cnt[mid] > first) jl = mid; else jh = mid - 1;
+    }
+    int j = static_cast<int>(jl);
+    for (; j > 0; --j) {
+      const long long nj = (long long)min(cnt[j] - first, n_c) * a.H;
+      if (r < nj) break;
+      r -= nj;
+    }
+    const int i = static_cast<int>(r / a.H), head = static_cast<int>(r - (long long)i * a.H);
     int2 it;
-    it.x = (i < cnt[j]) ? (sorted[i] | (head << 16)) : -1;
+    it.x = (first + i < n_seq) ? (sorted[first + i] | (head << 16)) : -1;
     it.y = j;
     items[slot] = it;
   }
@@ -180,6 +214,7 @@ struct FwdShared {
 
 struct TensorMaps {
   CUtensorMap q, k, v;
+  CUtensorMap o;  // output (bulk stores of whole 128-row blocks)
 };
 
 // Optional cycle accounting (PROF): per-role wait/busy cycles, summed over CTAs into 14 ints.
@@ -461,16 +496,18 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
       if (!ok) return false;
       tc_fence_after();
       const uint32_t o_addr = tmem + lane_addr + (ob ? TMEM_O1 : TMEM_O0) + wg * 64;
-      // Rows are handed to global memory through shared memory so that a warp writes whole
-      // 128-byte row segments (4 rows per instruction) instead of 32 scattered 16-byte pieces.
-      // Each group stages and writes its own 64 columns, 32 at a time (one register block);
-      // chunk index XOR (row & 7) keeps both the row-wise writes and the segment-wise reads free
-      // of avoidable bank conflicts.
+      // Rows are handed to global memory through shared memory.  Each group stages its own 64
+      // columns as a 128-row half tile in the 128-byte-swizzled box layout (16-byte chunk index
+      // XOR (row & 7)).  A whole block then leaves as one bulk tensor store per group, which runs
+      // in the background; the ragged last block of a sequence is copied out by the threads
+      // (8 lanes write one 128-byte row segment, a warp 4 rows per instruction).
       {
         const float sc = d_m0 + row < d_len ? row_scale(a, d_start + d_m0 + row) : 0.f;
         const int tid_wg = row;  // 0..127 inside the group
-        asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");  // previous item's reads are done
-        unsigned char* my_row = sh.o_stage + row * 256;
+        unsigned char* half = sh.o_stage + wg * HALF_TILE_BYTES;
+        if (tid_wg == 0) bulk_wait_read_all();  // the previous item's store has read the staging buffer
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
+        unsigned char* my_row = half + row * 128;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           uint32_t ov[32];
@@ -487,20 +524,29 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
             x.y = pack2<IS_BF16>(__uint_as_float(ov[8 * j + 2]) * sc, __uint_as_float(ov[8 * j + 3]) * sc);
             x.z = pack2<IS_BF16>(__uint_as_float(ov[8 * j + 4]) * sc, __uint_as_float(ov[8 * j + 5]) * sc);
             x.w = pack2<IS_BF16>(__uint_as_float(ov[8 * j + 6]) * sc, __uint_as_float(ov[8 * j + 7]) * sc);
-            *reinterpret_cast<uint4*>(my_row + (((wg * 8 + h * 4 + j) ^ (row & 7)) << 4)) = x;
+            *reinterpret_cast<uint4*>(my_row + (((h * 4 + j) ^ (row & 7)) << 4)) = x;
           }
         }
-        asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");  // the group's half tile is staged
-        const int chunk = tid_wg & 7;
-        unsigned short* obase = reinterpret_cast<unsigned short*>(a.o) + (d_start + d_m0) * a.o_rs + d_head * HEAD_DIM +
-                                wg * 64 + chunk * 8;
         const int rows_valid = d_len - d_m0;
+        if (rows_valid >= BLK) {
+          fence_proxy_async();
+          asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");  // the group's half tile is staged
+          if (tid_wg == 0) {
+            tma_store_2d(&maps.o, smem_u32(half), d_head * HEAD_DIM + wg * 64, static_cast<int>(d_start) + d_m0);
+            bulk_commit();
+          }
+        } else {
+          asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");  // the group's half tile is staged
+          const int chunk = tid_wg & 7;
+          unsigned short* obase = reinterpret_cast<unsigned short*>(a.o) + (d_start + d_m0) * a.o_rs + d_head * HEAD_DIM +
+                                  wg * 64 + chunk * 8;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int r = i * 16 + (tid_wg >> 3);
-          if (r < rows_valid) {
-            const uint4 x = *reinterpret_cast<const uint4*>(sh.o_stage + r * 256 + (((wg * 8 + chunk) ^ (r & 7)) << 4));
-            *reinterpret_cast<uint4*>(obase + static_cast<long long>(r) * a.o_rs) = x;
+          for (int i = 0; i < 8; ++i) {
+            const int r = i * 16 + (tid_wg >> 3);
+            if (r < rows_valid) {
+              const uint4 x = *reinterpret_cast<const uint4*>(half + r * 128 + ((chunk ^ (r & 7)) << 4));
+              *reinterpret_cast<uint4*>(obase + static_cast<long long>(r) * a.o_rs) = x;
+            }
           }
         }
       }
@@ -640,6 +686,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
       ++it;
     }
     if (ok && drain_pending) ok = drain_o();
+    if (row == 0) bulk_wait_all();  // shared memory must outlive the stores that read it
     sw_total.stop(pf_total);
     if (prof_thread) {
       atomicAdd(prof + PF_EPI_TOTAL, (int)(pf_total >> 6)); atomicAdd(prof + PF_EPI_SFULL, (int)(pf_sfull >> 6));
@@ -720,7 +767,9 @@ int sm_count() {
 }
 
 template <typename T>
-static cudaError_t launch_prep_t(const KernelArgs& a, int* ws, const WorkspaceLayout& w, bool backward, cudaStream_t st) {
+static cudaError_t launch_prep_t(const KernelArgs& a, int* ws, const WorkspaceLayout& w_in, bool backward, cudaStream_t st) {
+  WorkspaceLayout w = w_in;
+  if (const char* e = getenv("B200_HSTU_CHUNK")) w.chunk_seqs = atoi(e) > 0 ? atoi(e) : w.chunk_seqs;
   build_block_index<<<1, 1024, 0, st>>>(a, ws, w);
   const int blocks = sm_count() * 2;
   const int stride = main_grid(w);
@@ -778,7 +827,7 @@ cudaError_t tc_forward(const KernelArgs& a, int dtype, void* workspace, cudaStre
   TensorMaps maps;
   const long long width = (long long)a.H * HEAD_DIM;
   if (!make_map(&maps.q, a.q, a.T, width, a.q_rs, bf16) || !make_map(&maps.k, a.k, a.T, width, a.k_rs, bf16) ||
-      !make_map(&maps.v, a.v, a.T, width, a.v_rs, bf16))
+      !make_map(&maps.v, a.v, a.T, width, a.v_rs, bf16) || !make_map(&maps.o, a.o, a.T, width, a.o_rs, bf16))
     return cudaErrorInvalidValue;
   cudaError_t e = launch_prep(a, bf16, ws, w, false, st);
   if (e != cudaSuccess) return e;

@@ -56,6 +56,7 @@ struct Stopwatch {
 
 struct MapsBwd {
   CUtensorMap q, k, v, d_o;
+  CUtensorMap dq, dk, dv;  // outputs (bulk stores of whole 128-row blocks)
 };
 
 // low-word offset (16-byte units) of k-step kk inside a K-major tile: 32 bytes inside a
@@ -491,14 +492,28 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
       tc_fence_before();
       mbar_arrive(smem_u32(&sh.acc_empty));
       const float sc = m < s.len ? 0.5f * a.alpha * row_scale(a, s.start + m) : 0.f;
-      group_barrier(wg);  // previous item's staged rows have been copied out
-      stage_row64<IS_BF16>(stage, row, ov0, ov1, sc);
+      // A whole 128-row block leaves as one bulk tensor store per group (the staging layout is the
+      // 128-byte-swizzled box layout), which runs in the background; the ragged last block of a
+      // sequence is copied out by the threads, row by row.
+      if (row == 0) bulk_wait_read_all();  // the previous item's store has read the staging buffer
       group_barrier(wg);
-      store_staged64(stage, reinterpret_cast<unsigned short*>(a.dq) + (s.start + m0) * a.dq_rs + head * HEAD_DIM + wg * 64,
-                     a.dq_rs, s.len - m0, row);
+      stage_row64<IS_BF16>(stage, row, ov0, ov1, sc);
+      if (m0 + BLK <= s.len) {
+        fence_proxy_async();
+        group_barrier(wg);
+        if (row == 0) {
+          tma_store_2d(&maps.dq, smem_u32(stage), head * HEAD_DIM + wg * 64, static_cast<int>(s.start) + m0);
+          bulk_commit();
+        }
+      } else {
+        group_barrier(wg);
+        store_staged64(stage, reinterpret_cast<unsigned short*>(a.dq) + (s.start + m0) * a.dq_rs + head * HEAD_DIM + wg * 64,
+                       a.dq_rs, s.len - m0, row);
+      }
       if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt, 5, 6);
       ++it;
     }
+    if (row == 0) bulk_wait_all();  // shared memory must outlive the stores that read it
   }
 
   tc_fence_before();
@@ -851,7 +866,8 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
         tmem_ld32(acc_addr + 32, ov1);
         tmem_wait_ld(ov0);
         tmem_wait_ld(ov1);
-        group_barrier(wg);  // the previous item's copy out of the staging buffer has finished
+        if (row == 0) bulk_wait_read_all();  // the previous item's stores have read the staging buffer
+        group_barrier(wg);
         stage_row64<IS_BF16>(stage, row, ov0, ov1, sc);
         tmem_ld32(acc_addr + 64, ov0);
         tmem_ld32(acc_addr + 96, ov1);
@@ -859,17 +875,40 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
         tmem_wait_ld(ov1);
         tc_fence_before();
         mbar_arrive(smem_u32(&sh.acc_empty));
-        group_barrier(wg);
-        store_staged64(stage, out0, out_rs, s.len - n0, row);
-        group_barrier(wg);
-        stage_row64<IS_BF16>(stage, row, ov0, ov1, sc);
-        group_barrier(wg);
-        store_staged64(stage, out0 + 64, out_rs, s.len - n0, row);
+        if (n0 + BLK <= s.len) {
+          // whole 128-row block: two bulk tensor stores per group (64 columns each) run in the
+          // background; the second waits until the first has read the staging buffer
+          const CUtensorMap* omap = wg == 0 ? &maps.dk : &maps.dv;
+          const int orow = static_cast<int>(s.start) + n0, ocol = head * HEAD_DIM;
+          fence_proxy_async();
+          group_barrier(wg);
+          if (row == 0) {
+            tma_store_2d(omap, smem_u32(stage), ocol, orow);
+            bulk_commit();
+            bulk_wait_read_all();
+          }
+          group_barrier(wg);
+          stage_row64<IS_BF16>(stage, row, ov0, ov1, sc);
+          fence_proxy_async();
+          group_barrier(wg);
+          if (row == 0) {
+            tma_store_2d(omap, smem_u32(stage), ocol + 64, orow);
+            bulk_commit();
+          }
+        } else {
+          group_barrier(wg);
+          store_staged64(stage, out0, out_rs, s.len - n0, row);
+          group_barrier(wg);
+          stage_row64<IS_BF16>(stage, row, ov0, ov1, sc);
+          group_barrier(wg);
+          store_staged64(stage, out0 + 64, out_rs, s.len - n0, row);
+        }
       }
       sw.stop(pe_drain);
       if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt, 5, 6);  // drain finished (before half tile 2*gt)
       ++it;
     }
+    if (row == 0) bulk_wait_all();  // shared memory must outlive the stores that read it
     sw_total.stop(pe_total);
     if (PROF && (threadIdx.x == 128 || threadIdx.x == 256)) {
       atomicAdd(prof + PB_EPI_TOTAL, (int)(pe_total >> 6)); atomicAdd(prof + PB_EPI_WAIT_S, (int)(pe_ws >> 6));
@@ -902,12 +941,14 @@ cudaError_t tc_backward(const KernelArgs& a, int dtype, void* workspace, cudaStr
   MapsBwd maps;
   const long long width = (long long)a.H * HEAD_DIM;
   if (!make_map(&maps.q, a.q, a.T, width, a.q_rs, bf16) || !make_map(&maps.k, a.k, a.T, width, a.k_rs, bf16) ||
-      !make_map(&maps.v, a.v, a.T, width, a.v_rs, bf16) || !make_map(&maps.d_o, a.d_o, a.T, width, a.do_rs, bf16))
+      !make_map(&maps.v, a.v, a.T, width, a.v_rs, bf16) || !make_map(&maps.d_o, a.d_o, a.T, width, a.do_rs, bf16) ||
+      !make_map(&maps.dq, a.dq, a.T, width, a.dq_rs, bf16) || !make_map(&maps.dk, a.dk, a.T, width, a.dk_rs, bf16) ||
+      !make_map(&maps.dv, a.dv, a.T, width, a.dv_rs, bf16))
     return cudaErrorInvalidValue;
   cudaError_t e = launch_prep(a, bf16, ws, w, true, st);
   if (e != cudaSuccess) return e;
   const int grid = main_grid(w);
-  {
+  if (!a.skip_dkv) {
     const size_t smem = sizeof(DkvShared) + 1024;
     static const bool profile = getenv("B200_HSTU_PROFILE") != nullptr;
     auto kern = profile ? (bf16 ? hstu_bwd_dkv_tc<true, true> : hstu_bwd_dkv_tc<false, true>)
@@ -916,7 +957,7 @@ cudaError_t tc_backward(const KernelArgs& a, int dtype, void* workspace, cudaStr
     if (e != cudaSuccess) return e;
     kern<<<static_cast<unsigned>(grid), BWD_THREADS, smem, st>>>(maps, a, ws, w.off_items);
   }
-  {
+  if (!a.skip_dq) {
     const size_t smem = sizeof(DqShared) + 1024;
     static const bool profile = getenv("B200_HSTU_PROFILE_DQ") != nullptr;
     auto kern = profile ? (bf16 ? hstu_bwd_dq_tc<true, true> : hstu_bwd_dq_tc<false, true>)

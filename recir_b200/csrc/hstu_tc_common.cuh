@@ -23,7 +23,8 @@ constexpr int HEAD_DIM = 128;
 //                items[2 * max_items] : (seq | head << 16, block index) per work item
 struct WorkspaceLayout {
   long long nbins, max_items;
-  long long off_sorted, off_hist, off_cnt, off_start, off_items, total_ints;
+  long long off_sorted, off_hist, off_cnt, off_start, off_chunk, off_items, total_ints;
+  int chunk_seqs;  // sequences per locality chunk of the work list
 };
 
 HSTU_HD WorkspaceLayout workspace_layout(long long T, int B, int H) {
@@ -34,7 +35,9 @@ HSTU_HD WorkspaceLayout workspace_layout(long long T, int B, int H) {
   w.off_hist = w.off_sorted + B;
   w.off_cnt = w.off_hist + w.nbins;
   w.off_start = w.off_cnt + w.nbins;
-  w.off_items = (w.off_start + w.nbins + 1) & ~1LL;  // int2 alignment
+  w.off_chunk = w.off_start + w.nbins;
+  w.off_items = (w.off_chunk + B + 2 + 1) & ~1LL;  // int2 alignment
+  w.chunk_seqs = 16;
   w.total_ints = w.off_items + 2 * w.max_items;
   return w;
 }

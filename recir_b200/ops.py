@@ -45,6 +45,8 @@ _LIBDEF.define(
 
 # Set by tests/benchmarks that want the CUDA-core cross-check kernels instead of the tensor-core ones.
 _force_simt = False
+# Extra C-ABI flags for the backward (benchmark timing of one pass at a time).
+_bwd_extra_flags = 0
 # Kernel launches issued through this module since import (launch accounting for the benchmark).
 launch_counter = 0
 
@@ -52,6 +54,12 @@ launch_counter = 0
 def set_force_simt(flag: bool) -> None:
     global _force_simt
     _force_simt = bool(flag)
+
+
+def set_backward_passes(dkv: bool = True, dq: bool = True) -> None:
+    """Timing aid: leave one of the two backward passes out (its outputs stay unwritten)."""
+    global _bwd_extra_flags
+    _bwd_extra_flags = (0 if dkv else _lib.FLAG_BWD_SKIP_DKV) | (0 if dq else _lib.FLAG_BWD_SKIP_DQ)
 
 
 # ---------------------------------------------------------------------------
@@ -200,6 +208,7 @@ def _bwd_cuda(dout, q, k, v, seq_offsets, max_seq_len, alpha, causal, num_target
     with torch.cuda.device(q.device):
         keep = _fill(p, q, k, v, seq_offsets, max_seq_len, alpha, causal, num_targets,
                      contextual_seq_len, max_attn_len, attn_scale, full_attn_size)
+        p.flags |= _bwd_extra_flags
         p.d_o = dout.data_ptr()
         p.do_row_stride = dout.stride(0)
         p.dq, p.dk, p.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()

@@ -295,3 +295,18 @@ def test_per_token_attn_scale_on_tensor_core_path():
     o, dq, dk, dv = _gpu(q, k, v, do, off, kw)
     for got, ref in ((o, ro), (dq, rdq), (dk, rdk), (dv, rdv)):
         assert rel_l2(got.float(), ref) <= 6e-3
+
+
+def test_backward_passes_can_run_one_at_a_time():
+    """The two C-ABI flags that leave one backward pass out (used to time each kernel alone) must
+    not change what the remaining pass writes."""
+    c = golden_case("multi_tile")
+    _, dq, dk, dv = _run(c, torch.bfloat16)
+    try:
+        ops.set_backward_passes(dkv=True, dq=False)
+        _, _, dk1, dv1 = _run(c, torch.bfloat16)
+        ops.set_backward_passes(dkv=False, dq=True)
+        _, dq2, _, _ = _run(c, torch.bfloat16)
+    finally:
+        ops.set_backward_passes(True, True)
+    assert torch.equal(dk, dk1) and torch.equal(dv, dv1) and torch.equal(dq, dq2)
