@@ -138,3 +138,46 @@ def test_no_cpu_implementation():
     off = torch.tensor([0, 3, 5])
     with pytest.raises((NotImplementedError, RuntimeError)):
         recir_b200.hstu_attention(q, q, q, off, 4)
+
+
+def test_batch_dim_rule_and_swap_helper():
+    """The token axis stays the batch axis on the forward output and on each gradient taken out of
+    the functional backward (recir/compiler/batch_dim.py:309-330)."""
+    from recir_b200 import graph
+
+    mode = FakeTensorMode(allow_non_fake_inputs=True)
+    q, k, v, off, nt = _fake_inputs(mode)
+
+    def step(q, k, v):
+        q = q.detach().requires_grad_(True)
+        o, _aux = torch.ops.recir_b200_test.source_ragged_attention(
+            8, 0.5, q, k, v, off, "lower_triangular", nt, None, 0, 0, 0, 0)
+        o2 = torch.ops.recir.b200_hstu_attention_fwd(q, k, v, off, 8, 0.5, True, nt, 0, 0, None, 0)
+        (dq,) = torch.autograd.grad(o2.sum(), (q,))
+        return o, dq
+
+    with mode:
+        gm = make_fx(step, tracing_mode="fake")(q, k, v)
+    src = torch.ops.recir_b200_test.source_ragged_attention.default
+    assert graph.swap_ops(gm, graph.swap_table(source_fwd=src)) == 1
+    seen = {"fwd": 0, "bwd": 0, "grad": 0, "aux": 0}
+    for node in gm.graph.nodes:
+        if node.op != "call_function":
+            continue
+        bd = graph.output_batch_dim(node, 0)
+        name = str(node.target)
+        if name in graph.FORWARD_OPS:
+            assert bd == 0
+            seen["fwd"] += 1
+        elif name in graph.BACKWARD_OPS:
+            assert bd == 0
+            seen["bwd"] += 1
+        elif node.target is operator.getitem and str(node.args[0].target) in graph.BACKWARD_OPS:
+            assert bd == 0
+            seen["grad"] += 1
+        elif node.target is operator.getitem and str(node.args[0].target) == graph.FORWARD_OPS[1]:
+            assert bd == (0 if node.args[1] == 0 else None)
+            seen["aux"] += 1
+        else:
+            assert bd is None
+    assert seen["fwd"] == 2 and seen["bwd"] == 1 and seen["grad"] >= 1 and seen["aux"] >= 1
