@@ -116,10 +116,10 @@ __global__ void __launch_bounds__(1024) build_block_index(KernelArgs a, int* ws,
   }
 }
 
-// One thread per work item: find its block index by bisection over start[], then decode.
-// The list is sorted by descending cost; CTA c of a grid of `stride` CTAs walks entries c,
-// c + stride, ...  Every other round of `stride` entries is stored mirrored, so that no CTA
-// always receives the most expensive item of its round (serpentine deal).
+// One thread per work-list entry: decode its rank into (sequence, head, block index).
+// `stride` is the grid of the main kernels: CTA c starts with entry c and claims further entries
+// from a cursor, so the list only has to be in a good ORDER (expensive items early, items that
+// share K/V or Q/dO rows close together); no static deal is needed.
 // Also zeroes the output rows no sequence owns (rows at or past the last offset).
 template <typename T>
 __global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, WorkspaceLayout w, int stride, T* z0,
@@ -133,9 +133,7 @@ __global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, W
   const long long gtid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   const long long gsz = (long long)gridDim.x * blockDim.x;
   for (long long slot = gtid; slot < total; slot += gsz) {
-    const long long round = slot / stride, c = slot - round * stride;
-    const long long round_size = (total - round * stride < stride) ? (total - round * stride) : stride;
-    const long long p = round * stride + ((round & 1) ? (round_size - 1 - c) : c);  // rank in the sorted order
+    const long long p = slot;  // rank in the list order
     // Rank p -> item.  The sorted sequences are cut into chunks of chunk_seqs; the list is
     // chunk-major, and inside a chunk block-index-major (highest block index = most expensive
     // first), then sequence, then head.  All items that read the same K/V (or Q/dO) rows are
@@ -168,6 +166,11 @@ __global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, W
     it.x = (first + i < n_seq) ? (sorted[first + i] | (head << 16)) : -1;
     it.y = j;
     items[slot] = it;
+  }
+  if (gtid == 0) {
+    // CTA c starts with entry c; the rest of the list is claimed dynamically from these cursors
+    ws[WS_CURSOR0] = stride;
+    ws[WS_CURSOR1] = stride;
   }
   // tail rows
   long long first = load_index(a.seq_offsets, a.offsets_i64, a.B);
@@ -208,6 +211,7 @@ struct FwdShared {
   unsigned long long s_full[2], p_ready[2];
   unsigned long long o_full[2], o_empty[2];
   int meta[META_RING];  // per key tile, written by the producer: bit 0 = last tile of its item
+  ItemRing ring;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -265,6 +269,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
 
   if (threadIdx.x == 0) {
     sh.abort_flag = 0;
+    item_ring_init(sh.ring);
     mbar_init(smem_u32(&sh.q_full), 1);
     mbar_init(smem_u32(&sh.q_empty), 1);
     for (int i = 0; i < NUM_K_STAGES; ++i) { mbar_init(smem_u32(&sh.k_full[i]), 1); mbar_init(smem_u32(&sh.k_empty[i]), 1); }
@@ -310,10 +315,10 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
         sw.stop(pf_wait);
         return r;
       };
-      for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-        const int2 w = items[item];
-        const int b = w.x & 0xffff, head = w.x >> 16, qblk = w.y;
-        const SeqInfo s = load_seq(a, b);
+      int2 w;
+      SeqInfo s;
+      for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, ok, abort_flag, a.status, WAIT_PRODUCER); ++n_item) {
+        const int head = w.x >> 16, qblk = w.y;
         const int m0 = qblk * BLK;
         const int row0 = static_cast<int>(s.start) + m0;
         const int col0 = head * HEAD_DIM;
@@ -385,7 +390,9 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
       auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
         return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_MMA));
       };
-      for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
+      int2 w_unused;
+      SeqInfo s_unused;
+      for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w_unused, s_unused, ok, abort_flag, a.status, WAIT_MMA); ++n_item) {
         const uint32_t ob = it & 1;
         const uint32_t o_tmem = tmem + (ob ? TMEM_O1 : TMEM_O0);
         sw.start();
@@ -469,6 +476,9 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
       if (PROF && lane == 0)
         for (int i = 0; i < 5; ++i) atomicAdd(prof + i, (int)(pf[i] >> 6));
     }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ work-item scheduler
+    run_item_scheduler(sh.ring, a, items, total_items, ws + WS_CURSOR0, abort_flag);
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue groups
     const int wg = (warp - 4) >> 2;                 // 0 or 1
@@ -553,16 +563,9 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
       drain_pending = false;
       return true;
     };
-    int2 w_next = items[blockIdx.x];
-    SeqInfo s_next = load_seq(a, w_next.x & 0xffff);
-    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-      const int2 w = w_next;
-      const SeqInfo s = s_next;
-      if (item + static_cast<int>(gridDim.x) < total_items) {
-        // fetch the next item's description now; it is needed only after this item's tiles
-        w_next = items[item + gridDim.x];
-        s_next = load_seq_quiet(a, w_next.x & 0xffff);
-      }
+    int2 w;
+    SeqInfo s;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, ok, abort_flag, a.status, WAIT_EPILOGUE); ++n_item) {
       const int head = w.x >> 16, qblk = w.y;
       const int m0 = qblk * BLK;
       const int m = m0 + row;

@@ -190,13 +190,14 @@ struct DqShared {
   unsigned long long v_full[DQ_STAGES], v_empty[DQ_STAGES];
   unsigned long long a_ready, s_full[2], ds_ready[2], acc_full, acc_empty;
   int meta[META_RING];
+  ItemRing ring;
   uint32_t tmem_base;
   int abort_flag;
 };
 
 template <bool IS_BF16, bool PROF>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
-hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __restrict__ ws, long long off_items) {
+hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restrict__ ws, long long off_items) {
   extern __shared__ unsigned char smem_raw[];
   DqShared& sh = *reinterpret_cast<DqShared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -207,6 +208,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
 
   if (threadIdx.x == 0) {
     sh.abort_flag = 0;
+    item_ring_init(sh.ring);
     for (int i = 0; i < DQ_STAGES; ++i) {
       mbar_init(smem_u32(&sh.k_full[i]), 1); mbar_init(smem_u32(&sh.k_empty[i]), 1);
       mbar_init(smem_u32(&sh.v_full[i]), 1); mbar_init(smem_u32(&sh.v_empty[i]), 1);
@@ -241,10 +243,10 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
     auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_PRODUCER));
     };
-    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-      const int2 w = items[item];
-      const int b = w.x & 0xffff, head = w.x >> 16, qblk = w.y;
-      const SeqInfo s = load_seq(a, b);
+    int2 w;
+    SeqInfo s;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, ok, abort_flag, a.status, WAIT_PRODUCER); ++n_item) {
+      const int head = w.x >> 16, qblk = w.y;
       const int m0 = qblk * BLK, col0 = head * HEAD_DIM;
       {
         // Q and dO rows of this item: the buffer is free as soon as the previous item's rows have
@@ -309,7 +311,9 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
     auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_MMA));
     };
-    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
+    int2 w_unused;
+    SeqInfo s_unused;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w_unused, s_unused, ok, abort_flag, a.status, WAIT_MMA); ++n_item) {
       ok = wait_all(&sh.a_ready, it & 1);
       if (!ok) break;
       tc_fence_after();
@@ -373,6 +377,9 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
       __syncwarp();
       ++it;
     }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ work-item scheduler
+    run_item_scheduler(sh.ring, a, items, total_items, ws + WS_CURSOR1, abort_flag);
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue groups
     const int wg = (warp - 4) >> 2;
@@ -382,21 +389,9 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, const int* __
     unsigned char* stage = sh.stage + wg * HALF_TILE_BYTES;
     uint32_t gt = 0, it = 0;
     bool ok = true;
-    // Work items are fetched two steps ahead (list entry) and one step ahead (sequence offsets), and
-    // nothing touches the loaded registers before the step that needs them, so the global-memory
-    // latency never sits on this loop's critical path.
-    const int grid_stride = static_cast<int>(gridDim.x);
-    int2 w_cur = items[blockIdx.x];
-    SeqRaw raw_cur = load_seq_raw(a, w_cur.x & 0xffff);
-    int2 w_ahead = items[min(static_cast<int>(blockIdx.x) + grid_stride, total_items - 1)];
-    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-      const int2 w = w_cur;
-      const SeqInfo s = finish_seq(a, raw_cur);
-      if (item + grid_stride < total_items) {
-        w_cur = w_ahead;
-        raw_cur = load_seq_raw(a, w_ahead.x & 0xffff);
-        w_ahead = items[min(item + 2 * grid_stride, total_items - 1)];
-      }
+    int2 w;
+    SeqInfo s;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, ok, abort_flag, a.status, WAIT_EPILOGUE); ++n_item) {
       const int head = w.x >> 16, qblk = w.y;
       const int m0 = qblk * BLK, m = m0 + row;
       // ---- A operands: the item's Q and dO tiles were prefetched into shared memory by TMA; group 0
@@ -544,6 +539,7 @@ struct DkvShared {
   unsigned long long qd_full[KV_STAGES], qd_empty[KV_STAGES];
   unsigned long long s_full[2], p_ready[2], acc_full, acc_empty;
   int meta[META_RING];
+  ItemRing ring;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -562,6 +558,7 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
 
   if (threadIdx.x == 0) {
     sh.abort_flag = 0;
+    item_ring_init(sh.ring);
     mbar_init(smem_u32(&sh.kv_full), 1);
     mbar_init(smem_u32(&sh.kv_empty), 1);
     for (int i = 0; i < KV_STAGES; ++i) { mbar_init(smem_u32(&sh.qd_full[i]), 1); mbar_init(smem_u32(&sh.qd_empty[i]), 1); }
@@ -592,10 +589,10 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
     auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_PRODUCER));
     };
-    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-      const int2 w = items[item];
-      const int b = w.x & 0xffff, head = w.x >> 16;
-      const SeqInfo s = load_seq(a, b);
+    int2 w;
+    SeqInfo s;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, ok, abort_flag, a.status, WAIT_PRODUCER); ++n_item) {
+      const int head = w.x >> 16;
       const int kvblk = (s.len + BLK - 1) / BLK - 1 - w.y;
       const int n0 = kvblk * BLK, col0 = head * HEAD_DIM;
       const int krow = static_cast<int>(s.start) + n0;
@@ -664,7 +661,9 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
     auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_MMA));
     };
-    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
+    int2 w_unused;
+    SeqInfo s_unused;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w_unused, s_unused, ok, abort_flag, a.status, WAIT_MMA); ++n_item) {
       sw.start();
       ok = wait_all(&sh.kv_full, it & 1);
       sw.stop(pf[PB_MMA_WAIT_ITEM]);
@@ -745,6 +744,9 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
     sw_total.stop(pf[PB_MMA_TOTAL]);
     if (PROF && lane == 0)
       for (int i = 0; i < 5; ++i) atomicAdd(prof + i, (int)(pf[i] >> 6));
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ work-item scheduler
+    run_item_scheduler(sh.ring, a, items, total_items, ws + WS_CURSOR0, abort_flag);
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue groups
     const int wg = (warp - 4) >> 2;
@@ -758,21 +760,9 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
     long long pe_total = 0, pe_ws = 0, pe_wacc = 0, pe_tile = 0, pe_drain = 0, pe_ld = 0, pe_st = 0;
     Stopwatch<PROF> sw_total, sw, sw2;
     sw_total.start();
-    // Work items are fetched two steps ahead (list entry) and one step ahead (sequence offsets), and
-    // nothing touches the loaded registers before the step that needs them, so the global-memory
-    // latency never sits on this loop's critical path.
-    const int grid_stride = static_cast<int>(gridDim.x);
-    int2 w_cur = items[blockIdx.x];
-    SeqRaw raw_cur = load_seq_raw(a, w_cur.x & 0xffff);
-    int2 w_ahead = items[min(static_cast<int>(blockIdx.x) + grid_stride, total_items - 1)];
-    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-      const int2 w = w_cur;
-      const SeqInfo s = finish_seq(a, raw_cur);
-      if (item + grid_stride < total_items) {
-        w_cur = w_ahead;
-        raw_cur = load_seq_raw(a, w_ahead.x & 0xffff);
-        w_ahead = items[min(item + 2 * grid_stride, total_items - 1)];
-      }
+    int2 w;
+    SeqInfo s;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, ok, abort_flag, a.status, WAIT_EPILOGUE); ++n_item) {
       const int head = w.x >> 16;
       const int kvblk = (s.len + BLK - 1) / BLK - 1 - w.y;
       const int n0 = kvblk * BLK, n = n0 + row;

@@ -31,16 +31,19 @@ HSTU_HD WorkspaceLayout workspace_layout(long long T, int B, int H) {
   WorkspaceLayout w;
   w.nbins = (T + BLK - 1) / BLK + 2;
   w.max_items = (long long)H * (T / BLK + B);
-  w.off_sorted = 16;
+  w.off_sorted = 32;  // ints 0..31: totals, profiling counters, work-list cursors (WS_CURSOR0/1)
   w.off_hist = w.off_sorted + B;
   w.off_cnt = w.off_hist + w.nbins;
   w.off_start = w.off_cnt + w.nbins;
   w.off_chunk = w.off_start + w.nbins;
   w.off_items = (w.off_chunk + B + 2 + 1) & ~1LL;  // int2 alignment
-  w.chunk_seqs = 16;
+  w.chunk_seqs = 8;
   w.total_ints = w.off_items + 2 * w.max_items;
   return w;
 }
+
+// Workspace header slots: next unclaimed work-list entry, one cursor per main kernel of a call.
+constexpr int WS_CURSOR0 = 16, WS_CURSOR1 = 17;
 
 enum TileClass { TILE_SKIP = 0, TILE_PARTIAL = 1, TILE_FULL = 2 };
 
@@ -237,6 +240,76 @@ __device__ __forceinline__ void zero_tile_half_row(unsigned char* tile, int firs
     for (int i = 0; i < 8; ++i) r[i] = z;
     sm100::fence_proxy_async();
   }
+}
+// ------------------------------------------------------------------ work-item ring
+// Work items are handed out dynamically: one otherwise idle warp of every CTA (the scheduler)
+// claims the next entry of the work list with an atomic add on a cursor in the workspace,
+// reads the entry and the sequence it belongs to, and publishes both through a two-slot ring in
+// shared memory.  The producer warp, the MMA warp and the eight epilogue warps each take every
+// item from the ring (copying the slot into registers and releasing it at once), so none of
+// them touches global memory to find out what to do next, and a CTA that finishes early simply
+// claims more.  The first item of a CTA is entry blockIdx.x; the cursor starts at gridDim.x.
+struct ItemSlot {
+  int2 w;     // (sequence | head << 16, block index); w.x < 0: the list is exhausted
+  SeqInfo s;
+};
+constexpr int ITEM_RING = 2;
+constexpr int ITEM_CONSUMERS = 10;  // producer warp, MMA warp, eight epilogue warps
+enum { WAIT_SCHEDULER = 104 };
+struct ItemRing {
+  ItemSlot slot[ITEM_RING];
+  unsigned long long full[ITEM_RING], empty[ITEM_RING];
+};
+
+__device__ __forceinline__ void item_ring_init(ItemRing& r) {
+  for (int i = 0; i < ITEM_RING; ++i) {
+    sm100::mbar_init(sm100::smem_u32(&r.full[i]), 1);
+    sm100::mbar_init(sm100::smem_u32(&r.empty[i]), ITEM_CONSUMERS);
+  }
+}
+
+// Body of the scheduler warp (all 32 lanes call it; lane 0 does the work).
+__device__ __forceinline__ void run_item_scheduler(ItemRing& r, const KernelArgs& a, const int2* items, int total,
+                                                   int* cursor, volatile int* abort_flag) {
+  const int lane = threadIdx.x & 31;
+  int idx = blockIdx.x;
+  for (uint32_t n = 0;; ++n) {
+    const uint32_t sl = n % ITEM_RING, par = ((n / ITEM_RING) & 1) ^ 1;
+    if (!__all_sync(0xffffffffu, sm100::mbar_wait(sm100::smem_u32(&r.empty[sl]), par, abort_flag, a.status, WAIT_SCHEDULER)))
+      return;
+    const bool have = idx < total;
+    if (lane == 0) {
+      ItemSlot it;
+      it.w = make_int2(-1, 0);
+      it.s.start = 0; it.s.len = 0; it.s.hist = 0; it.s.has_targets = 0; it.s.boundary = 0;
+      if (have) {
+        it.w = items[idx];
+        it.s = load_seq(a, it.w.x & 0xffff);
+      }
+      r.slot[sl] = it;
+      sm100::mbar_arrive(sm100::smem_u32(&r.full[sl]));  // release: the slot is written before the arrival
+    }
+    __syncwarp();
+    if (!have) return;
+    if (lane == 0) idx = atomicAdd(cursor, 1);
+    idx = __shfl_sync(0xffffffffu, idx, 0);
+  }
+}
+
+// Takes item n from the ring (whole warp).  Returns false when the list is exhausted or a wait
+// gave up (then `ok` is cleared as well).
+__device__ __forceinline__ bool next_item(ItemRing& r, uint32_t n, int2& w, SeqInfo& s, bool& ok,
+                                          volatile int* abort_flag, int* status, int code) {
+  const uint32_t sl = n % ITEM_RING, par = (n / ITEM_RING) & 1;
+  if (!__all_sync(0xffffffffu, sm100::mbar_wait(sm100::smem_u32(&r.full[sl]), par, abort_flag, status, code))) {
+    ok = false;
+    return false;
+  }
+  w = r.slot[sl].w;
+  s = r.slot[sl].s;
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) sm100::mbar_arrive(sm100::smem_u32(&r.empty[sl]));
+  return w.x >= 0;
 }
 #endif
 
