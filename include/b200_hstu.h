@@ -139,6 +139,10 @@ int b200_hstu_launch_count(const B200HstuParams* params, int pass);
 int b200_hstu_fwd_static_scratch(const B200HstuParams* params, void* cuda_stream);
 
 const char* b200_hstu_strerror(int code);
+/* Name and text of the CUDA runtime error behind the calling thread's most recent
+ * B200_HSTU_ELAUNCH result ("" if there was none).  The pointer stays valid until the thread's
+ * next failing call.  No counterpart in the reference. */
+const char* b200_hstu_last_cuda_error(void);
 int b200_hstu_version(void);
 /* sizeof(B200HstuParams) as this library was compiled (for foreign-language bindings). */
 size_t b200_hstu_params_size(void);

@@ -24,7 +24,7 @@ EXPORTS = (
     "b200_hstu_launch_count", "b200_hstu_strerror", "b200_hstu_version", "b200_hstu_params_size",
     "b200_hstu_debug_keep", "b200_hstu_debug_classify_tile", "b200_hstu_debug_key_blocks",
     "b200_hstu_debug_query_blocks", "b200_hstu_fwd_static_scratch", "b200_hstu_debug_row_mask",
-    "b200_hstu_debug_col_mask",
+    "b200_hstu_debug_col_mask", "b200_hstu_last_cuda_error",
 )
 STATIC_SCRATCH_BYTES = 4 << 20
 
@@ -91,6 +91,8 @@ def load() -> ctypes.CDLL:
     lib.b200_hstu_launch_count.restype = ctypes.c_int
     lib.b200_hstu_strerror.argtypes = [ctypes.c_int]
     lib.b200_hstu_strerror.restype = ctypes.c_char_p
+    lib.b200_hstu_last_cuda_error.argtypes = []
+    lib.b200_hstu_last_cuda_error.restype = ctypes.c_char_p
     lib.b200_hstu_version.argtypes = []
     lib.b200_hstu_version.restype = ctypes.c_int
     lib.b200_hstu_params_size.argtypes = []
@@ -114,4 +116,9 @@ def load() -> ctypes.CDLL:
 
 
 def strerror(code: int) -> str:
-    return load().b200_hstu_strerror(code).decode()
+    msg = load().b200_hstu_strerror(code).decode()
+    if code == -5:
+        detail = load().b200_hstu_last_cuda_error().decode()
+        if detail:
+            msg += f" ({detail})"
+    return msg

@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <string.h>
 
+#include <stdio.h>
+
 #include <mutex>
 
 #include "hstu_common.cuh"
@@ -75,6 +77,13 @@ int validate(const B200HstuParams* p, int pass, KernelArgs* a) {
 
 }  // namespace
 
+static thread_local char g_last_cuda_error[192] = "";
+static thread_local const char* g_error_stage = "";
+
+namespace hstu {
+void set_error_stage(const char* what) { g_error_stage = what; }
+}  // namespace hstu
+
 extern "C" {
 
 int b200_hstu_version(void) { return B200_HSTU_ABI_VERSION; }
@@ -118,6 +127,17 @@ int b200_hstu_launch_count(const B200HstuParams* p, int pass) {
   return pass == 0 ? 2 : 3;
 }
 
+
+static int launch_result(cudaError_t e) {
+  if (e == cudaSuccess) return B200_HSTU_OK;
+  snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s: %s [%s]", cudaGetErrorName(e), cudaGetErrorString(e),
+           g_error_stage);
+  return B200_HSTU_ELAUNCH;
+}
+
+const char* b200_hstu_last_cuda_error(void) { return g_last_cuda_error; }
+
+
 static int run(const B200HstuParams* p, int pass, void* stream) {
   KernelArgs a;
   const int rc = validate(p, pass, &a);
@@ -134,7 +154,7 @@ static int run(const B200HstuParams* p, int pass, void* stream) {
     e = pass == 0 ? hstu::simt_forward(a, p->dtype, p->max_seq_len, st)
                   : hstu::simt_backward(a, p->dtype, p->max_seq_len, st);
   }
-  return e == cudaSuccess ? B200_HSTU_OK : B200_HSTU_ELAUNCH;
+  return launch_result(e);
 }
 
 static void mask_query(const B200HstuMaskQuery* mq, hstu::SeqInfo* s, hstu::MaskOpts* o) {
@@ -237,7 +257,7 @@ int b200_hstu_fwd_static_scratch(const B200HstuParams* p, void* stream) {
   } else {
     e = hstu::simt_forward(a, p->dtype, p->max_seq_len, st);  // needs no scratch at all
   }
-  return e == cudaSuccess ? B200_HSTU_OK : B200_HSTU_ELAUNCH;
+  return launch_result(e);
 }
 int b200_hstu_bwd(const B200HstuParams* p, void* stream) { return run(p, 1, stream); }
 

@@ -6,6 +6,10 @@
 
 namespace hstu {
 
+// Names the step a launch function is in; a failing call reports it through
+// b200_hstu_last_cuda_error().  `what` must be a string literal.
+void set_error_stage(const char* what);
+
 // CUDA-core kernels (hstu_simt.cu): zero the unowned tail rows, then run the pass.
 cudaError_t simt_forward(const KernelArgs& a, int dtype, int max_seq_len, cudaStream_t st);
 cudaError_t simt_backward(const KernelArgs& a, int dtype, int max_seq_len, cudaStream_t st);

@@ -16,6 +16,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <stdio.h>
 #include <stdlib.h>
 
 #include <mutex>
@@ -736,10 +737,36 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// Tensor-map encoding is a driver call and fails with CUDA_ERROR_INVALID_CONTEXT on a thread that
+// has no current context yet (a fresh worker thread, e.g. an autograd thread whose first CUDA work
+// is this library).  If none is current, the primary context of the device that owns `device_ptr`
+// is made current (cudaSetDevice initialises and binds it).
+bool ensure_current_context(const void* device_ptr) {
+  typedef CUresult (*GetCurrentFn)(CUcontext*);
+  static GetCurrentFn get_current = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrentFn>(p);
+  });
+  CUcontext ctx = nullptr;
+  if (get_current && get_current(&ctx) == CUDA_SUCCESS && ctx != nullptr) return true;
+  cudaPointerAttributes at;
+  int dev = 0;
+  if (cudaPointerGetAttributes(&at, device_ptr) == cudaSuccess && at.type == cudaMemoryTypeDevice) dev = at.device;
+  return cudaSetDevice(dev) == cudaSuccess;
+}
+
 // [rows, H*128] 16-bit matrix, box = 64 columns x 128 rows, 128-byte swizzle, zero fill out of range.
 bool make_map(CUtensorMap* m, const void* base, long long rows, long long width, long long row_stride, bool bf16) {
   EncodeTiledFn fn = encode_fn();
-  if (!fn) return false;
+  if (!fn) {
+    set_error_stage("tensor map: cuTensorMapEncodeTiled entry point not found");
+    return false;
+  }
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride) * 2};
   cuuint32_t box[2] = {64, BLK};
@@ -748,6 +775,12 @@ bool make_map(CUtensorMap* m, const void* base, long long rows, long long width,
                         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    static thread_local char why[160];
+    snprintf(why, sizeof(why), "tensor map: CUresult %d for base %p rows %lld width %lld row stride %lld", (int)r, base, rows,
+             width, row_stride);
+    set_error_stage(why);
+  }
   return r == CUDA_SUCCESS;
 }
 
@@ -829,11 +862,15 @@ cudaError_t tc_forward(const KernelArgs& a, int dtype, void* workspace, cudaStre
   int* ws = reinterpret_cast<int*>(workspace);
   TensorMaps maps;
   const long long width = (long long)a.H * HEAD_DIM;
+  set_error_stage("forward: tensor maps");
+  if (!ensure_current_context(a.q)) return cudaErrorInvalidValue;
   if (!make_map(&maps.q, a.q, a.T, width, a.q_rs, bf16) || !make_map(&maps.k, a.k, a.T, width, a.k_rs, bf16) ||
       !make_map(&maps.v, a.v, a.T, width, a.v_rs, bf16) || !make_map(&maps.o, a.o, a.T, width, a.o_rs, bf16))
     return cudaErrorInvalidValue;
+  set_error_stage("forward: work-list kernels");
   cudaError_t e = launch_prep(a, bf16, ws, w, false, st);
   if (e != cudaSuccess) return e;
+  set_error_stage("forward: main kernel");
   const size_t smem = sizeof(FwdShared) + 1024;
   static const bool profile = getenv("B200_HSTU_PROFILE") != nullptr;  // cycle accounting into workspace ints 2..15
   auto kern = profile ? (bf16 ? hstu_fwd_tc<true, true> : hstu_fwd_tc<false, true>)

@@ -930,15 +930,19 @@ cudaError_t tc_backward(const KernelArgs& a, int dtype, void* workspace, cudaStr
   int* ws = reinterpret_cast<int*>(workspace);
   MapsBwd maps;
   const long long width = (long long)a.H * HEAD_DIM;
+  set_error_stage("backward: tensor maps");
+  if (!ensure_current_context(a.q)) return cudaErrorInvalidValue;
   if (!make_map(&maps.q, a.q, a.T, width, a.q_rs, bf16) || !make_map(&maps.k, a.k, a.T, width, a.k_rs, bf16) ||
       !make_map(&maps.v, a.v, a.T, width, a.v_rs, bf16) || !make_map(&maps.d_o, a.d_o, a.T, width, a.do_rs, bf16) ||
       !make_map(&maps.dq, a.dq, a.T, width, a.dq_rs, bf16) || !make_map(&maps.dk, a.dk, a.T, width, a.dk_rs, bf16) ||
       !make_map(&maps.dv, a.dv, a.T, width, a.dv_rs, bf16))
     return cudaErrorInvalidValue;
+  set_error_stage("backward: work-list kernels");
   cudaError_t e = launch_prep(a, bf16, ws, w, true, st);
   if (e != cudaSuccess) return e;
   const int grid = main_grid(w);
   if (!a.skip_dkv) {
+    set_error_stage("backward: dK/dV kernel");
     const size_t smem = sizeof(DkvShared) + 1024;
     static const bool profile = getenv("B200_HSTU_PROFILE") != nullptr;
     auto kern = profile ? (bf16 ? hstu_bwd_dkv_tc<true, true> : hstu_bwd_dkv_tc<false, true>)
@@ -948,6 +952,7 @@ cudaError_t tc_backward(const KernelArgs& a, int dtype, void* workspace, cudaStr
     kern<<<static_cast<unsigned>(grid), BWD_THREADS, smem, st>>>(maps, a, ws, w.off_items);
   }
   if (!a.skip_dq) {
+    set_error_stage("backward: dQ kernel");
     const size_t smem = sizeof(DqShared) + 1024;
     static const bool profile = getenv("B200_HSTU_PROFILE_DQ") != nullptr;
     auto kern = profile ? (bf16 ? hstu_bwd_dq_tc<true, true> : hstu_bwd_dq_tc<false, true>)

@@ -10,6 +10,8 @@ namespace tc {
 
 // Tensor map over a [rows, width] 16-bit matrix with the given row stride (elements):
 // box = 64 columns x 128 rows, 128-byte swizzle, zero fill outside the matrix.
+// Makes sure the calling thread has a current CUDA context (needed by the tensor-map encoder).
+bool ensure_current_context(const void* device_ptr);
 bool make_map(CUtensorMap* m, const void* base, long long rows, long long width, long long row_stride, bool bf16);
 int sm_count();
 // Grid of the persistent kernels (also the stride with which CTAs walk the work list).

@@ -310,3 +310,35 @@ def test_backward_passes_can_run_one_at_a_time():
     finally:
         ops.set_backward_passes(True, True)
     assert torch.equal(dk, dk1) and torch.equal(dv, dv1) and torch.equal(dq, dq2)
+
+
+def test_first_call_on_a_fresh_thread_and_in_a_fresh_process():
+    """Tensor-map encoding needs a current CUDA context on the calling thread; a worker thread whose
+    first CUDA work is this library (an autograd thread in a new process) has none until the library
+    binds the device's primary context itself."""
+    import subprocess
+    import sys
+    import threading
+
+    c = golden_case("multi_tile")
+    want = _run(c, torch.bfloat16)
+    got = {}
+
+    def work():
+        got["r"] = _run(c, torch.bfloat16)
+
+    t = threading.Thread(target=work)
+    t.start()
+    t.join()
+    assert all(torch.equal(a, b) for a, b in zip(got["r"], want))
+    # new process: the first backward runs on the autograd engine's thread
+    code = ("import torch, recir_b200\n"
+            "q = (torch.randn(300, 2, 128) * 0.5).to(torch.bfloat16).cuda().requires_grad_(True)\n"
+            "off = torch.tensor([0, 300], device='cuda')\n"
+            "o = recir_b200.hstu_attention(q, q.detach(), q.detach(), off, 300)\n"
+            "o.backward(torch.ones_like(o))\n"
+            "torch.cuda.synchronize()\n"
+            "assert torch.isfinite(q.grad.float()).all()\n"
+            "print('fresh-process ok')\n")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "fresh-process ok" in r.stdout, r.stderr[-2000:]
