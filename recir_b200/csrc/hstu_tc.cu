@@ -665,7 +665,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
           const uint32_t vs = g % NUM_V_STAGES, vph = (g / NUM_V_STAGES) & 1;
           ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.v_full[vs]), vph, abort_flag, a.status, WAIT_EPILOGUE));
           if (!ok) break;
-          zero_tile_half_row(sh.v[vs], s.len - n0, row, wg);
+          zero_box_rows(sh.v[vs] + wg * HALF_TILE_BYTES, s.len - n0, BLK, row, 128);
         }
         if (have_next) {
           // scores of the next tile were issued before the MMA warp started waiting for this P

@@ -464,7 +464,8 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
             if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 3, 6);
             if (n0 + BLK > s.len && wg == 0) {
               // key rows past the sequence end feed the dQ MMA as B rows: clear them (0 * NaN = NaN)
-              zero_tile_half_row(sh.k[gt % DQ_STAGES], s.len - n0, sub * 64 + (row & 63), row >> 6);
+              const int first_bad = s.len - n0, lo = first_bad > sub * 64 ? first_bad : sub * 64;
+              zero_box_rows(sh.k[gt % DQ_STAGES] + (row >> 6) * HALF_TILE_BYTES, lo, sub * 64 + 64, row & 63, 64);
             }
             tmem_wait_st();
             tc_fence_before();
@@ -819,9 +820,9 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
             if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 3, 6);
             if (q0 + BLK > s.len && wg == 0) {
               // query rows past the sequence end are B rows of the dV / dK MMAs: clear them
-              const int r = sub * 64 + (row & 63);
-              zero_tile_half_row(sh.q[gt % KV_STAGES], s.len - q0, r, row >> 6);
-              zero_tile_half_row(sh.d_o[gt % KV_STAGES], s.len - q0, r, row >> 6);
+              const int first_bad = s.len - q0, lo = first_bad > sub * 64 ? first_bad : sub * 64;
+              zero_box_rows(sh.q[gt % KV_STAGES] + (row >> 6) * HALF_TILE_BYTES, lo, sub * 64 + 64, row & 63, 64);
+              zero_box_rows(sh.d_o[gt % KV_STAGES] + (row >> 6) * HALF_TILE_BYTES, lo, sub * 64 + 64, row & 63, 64);
             }
             sw2.start();
             tmem_wait_st();

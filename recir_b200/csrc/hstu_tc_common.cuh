@@ -217,30 +217,21 @@ __device__ __forceinline__ uint32_t silu_pair(uint32_t s0, uint32_t s1, float c1
   return sm100::fma2<IS_BF16>(u2, sm100::tanh2<IS_BF16>(u2), u2);
 }
 
-// Clears row `row` of a 128x128 16-bit tile (two 64-column boxes, 128 bytes per box row) if it
-// lies at or past `first_bad`, and makes the write visible to the async proxy (TMA / MMA).
-// The swizzle only permutes 16-byte chunks inside a 128-byte row, so whole rows can be cleared
-// without knowing it.
-__device__ __forceinline__ void zero_tile_rows(unsigned char* tile, int first_bad, int row) {
-  if (row >= first_bad) {
-    uint4* r0 = reinterpret_cast<uint4*>(tile + row * 128);
-    uint4* r1 = reinterpret_cast<uint4*>(tile + HALF_TILE_BYTES + row * 128);
-    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) { r0[i] = z; r1[i] = z; }
-    sm100::fence_proxy_async();
-  }
+// Clears rows [row_lo, row_hi) of one 64-column box of a tile (128 bytes per box row, rows
+// contiguous in shared memory) and makes the write visible to the async proxy (TMA / MMA).
+// `nthreads` threads with ids `tid` write consecutive 16-byte chunks, so a warp store covers 512
+// contiguous bytes (no bank conflicts; a thread-per-row version was 32-way conflicted and cost
+// thousands of cycles per ragged tile).  The 128-byte swizzle only permutes chunks inside a row,
+// so whole rows can be cleared without knowing it.
+__device__ __forceinline__ void zero_box_rows(unsigned char* box, int row_lo, int row_hi, int tid, int nthreads) {
+  if (row_lo < 0) row_lo = 0;
+  if (row_lo >= row_hi) return;
+  uint4* p = reinterpret_cast<uint4*>(box);
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  for (int c = row_lo * 8 + tid; c < row_hi * 8; c += nthreads) p[c] = z;
+  sm100::fence_proxy_async();
 }
-// Same for one 64-column half (`half` = 0 or 1) of the row.
-__device__ __forceinline__ void zero_tile_half_row(unsigned char* tile, int first_bad, int row, int half) {
-  if (row >= first_bad) {
-    uint4* r = reinterpret_cast<uint4*>(tile + half * HALF_TILE_BYTES + row * 128);
-    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) r[i] = z;
-    sm100::fence_proxy_async();
-  }
-}
+
 // ------------------------------------------------------------------ work-item ring
 // Work items are handed out dynamically: one otherwise idle warp of every CTA (the scheduler)
 // claims the next entry of the work list with an atomic add on a cursor in the workspace,
