@@ -318,7 +318,8 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
       };
       int2 w;
       SeqInfo s;
-      for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, ok, abort_flag, a.status, WAIT_PRODUCER); ++n_item) {
+      uint32_t todo0 = 0u, full0 = 0u;
+      for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, todo0, full0, ok, abort_flag, a.status, WAIT_PRODUCER); ++n_item) {
         const int head = w.x >> 16, qblk = w.y;
         const int m0 = qblk * BLK;
         const int row0 = static_cast<int>(s.start) + m0;
@@ -337,9 +338,12 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
         // 32 candidate key blocks are classified at a time, one per lane; the last candidate of an
         // item (the diagonal block, or the last block of the sequence) is never skipped
         for (int base = 0; base < cnt && ok; base += 32) {
-          int my_cls = TILE_SKIP;
-          if (base + lane < cnt) my_cls = classify_tile(m0, kr.at(base + lane) * BLK, s, a.mask, true);
-          uint32_t todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+          uint32_t todo = todo0;  // the scheduler warp classified the first 32 candidates
+          if (base > 0) {
+            int my_cls = TILE_SKIP;
+            if (base + lane < cnt) my_cls = classify_tile(m0, kr.at(base + lane) * BLK, s, a.mask, true);
+            todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+          }
           while (todo != 0u && ok) {
             const int bit = __ffs(todo) - 1;
             todo &= todo - 1;
@@ -393,7 +397,8 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
       };
       int2 w_unused;
       SeqInfo s_unused;
-      for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w_unused, s_unused, ok, abort_flag, a.status, WAIT_MMA); ++n_item) {
+      uint32_t t_unused = 0u, f_unused = 0u;
+      for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w_unused, s_unused, t_unused, f_unused, ok, abort_flag, a.status, WAIT_MMA); ++n_item) {
         const uint32_t ob = it & 1;
         const uint32_t o_tmem = tmem + (ob ? TMEM_O1 : TMEM_O0);
         sw.start();
@@ -479,7 +484,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
     }
   } else if (warp == 2) {
     // ------------------------------------------------------------------ work-item scheduler
-    run_item_scheduler(sh.ring, a, items, total_items, ws + WS_CURSOR0, abort_flag);
+    run_item_scheduler<false>(sh.ring, a, items, total_items, ws + WS_CURSOR0, abort_flag);
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue groups
     const int wg = (warp - 4) >> 2;                 // 0 or 1
@@ -566,7 +571,8 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
     };
     int2 w;
     SeqInfo s;
-    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, ok, abort_flag, a.status, WAIT_EPILOGUE); ++n_item) {
+    uint32_t todo0 = 0u, full0 = 0u;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, todo0, full0, ok, abort_flag, a.status, WAIT_EPILOGUE); ++n_item) {
       const int head = w.x >> 16, qblk = w.y;
       const int m0 = qblk * BLK;
       const int m = m0 + row;
@@ -581,10 +587,15 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
           if (base_next >= cnt) return false;
           cur_base = base_next;
           base_next += 32;
-          int my_cls = TILE_SKIP;
-          if (cur_base + lane < cnt) my_cls = classify_tile(m0, kr.at(cur_base + lane) * BLK, s, a.mask, true);
-          todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
-          full_bits = __ballot_sync(0xffffffffu, my_cls == TILE_FULL);
+          if (cur_base == 0) {  // classified by the scheduler warp
+            todo = todo0;
+            full_bits = full0;
+          } else {
+            int my_cls = TILE_SKIP;
+            if (cur_base + lane < cnt) my_cls = classify_tile(m0, kr.at(cur_base + lane) * BLK, s, a.mask, true);
+            todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+            full_bits = __ballot_sync(0xffffffffu, my_cls == TILE_FULL);
+          }
         }
         const int bit = __ffs(todo) - 1;
         todo &= todo - 1;

@@ -245,7 +245,8 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
     };
     int2 w;
     SeqInfo s;
-    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, ok, abort_flag, a.status, WAIT_PRODUCER); ++n_item) {
+    uint32_t todo0 = 0u, full0 = 0u;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, todo0, full0, ok, abort_flag, a.status, WAIT_PRODUCER); ++n_item) {
       const int head = w.x >> 16, qblk = w.y;
       const int m0 = qblk * BLK, col0 = head * HEAD_DIM;
       {
@@ -268,9 +269,12 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
       const int cnt = kr.count();
       // the last candidate (diagonal block, or last block of the sequence) is never skipped
       for (int base = 0; base < cnt && ok; base += 32) {
-        int my_cls = TILE_SKIP;
-        if (base + lane < cnt) my_cls = classify_tile(m0, kr.at(base + lane) * BLK, s, a.mask, true);
-        uint32_t todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+        uint32_t todo = todo0;  // the scheduler warp classified the first 32 candidates
+        if (base > 0) {
+          int my_cls = TILE_SKIP;
+          if (base + lane < cnt) my_cls = classify_tile(m0, kr.at(base + lane) * BLK, s, a.mask, true);
+          todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+        }
         while (todo != 0u && ok) {
           const int bit = __ffs(todo) - 1;
           todo &= todo - 1;
@@ -313,7 +317,8 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
     };
     int2 w_unused;
     SeqInfo s_unused;
-    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w_unused, s_unused, ok, abort_flag, a.status, WAIT_MMA); ++n_item) {
+    uint32_t t_unused = 0u, f_unused = 0u;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w_unused, s_unused, t_unused, f_unused, ok, abort_flag, a.status, WAIT_MMA); ++n_item) {
       ok = wait_all(&sh.a_ready, it & 1);
       if (!ok) break;
       tc_fence_after();
@@ -379,7 +384,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
     }
   } else if (warp == 2) {
     // ------------------------------------------------------------------ work-item scheduler
-    run_item_scheduler(sh.ring, a, items, total_items, ws + WS_CURSOR1, abort_flag);
+    run_item_scheduler<false>(sh.ring, a, items, total_items, ws + WS_CURSOR1, abort_flag);
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue groups
     const int wg = (warp - 4) >> 2;
@@ -391,7 +396,8 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
     bool ok = true;
     int2 w;
     SeqInfo s;
-    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, ok, abort_flag, a.status, WAIT_EPILOGUE); ++n_item) {
+    uint32_t todo0 = 0u, full0 = 0u;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, todo0, full0, ok, abort_flag, a.status, WAIT_EPILOGUE); ++n_item) {
       const int head = w.x >> 16, qblk = w.y;
       const int m0 = qblk * BLK, m = m0 + row;
       // ---- A operands: the item's Q and dO tiles were prefetched into shared memory by TMA; group 0
@@ -424,10 +430,13 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
       const BlockRange kr = key_blocks_for_query_block(m0, s, a.mask);
       const int cnt = kr.count();
       for (int base = 0; base < cnt && ok; base += 32) {
-        int my_cls = TILE_SKIP;
-        if (base + lane < cnt) my_cls = classify_tile(m0, kr.at(base + lane) * BLK, s, a.mask, true);
-        uint32_t todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
-        const uint32_t full_bits = __ballot_sync(0xffffffffu, my_cls == TILE_FULL);
+        uint32_t todo = todo0, full_bits = full0;  // the scheduler warp classified the first 32 candidates
+        if (base > 0) {
+          int my_cls = TILE_SKIP;
+          if (base + lane < cnt) my_cls = classify_tile(m0, kr.at(base + lane) * BLK, s, a.mask, true);
+          todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+          full_bits = __ballot_sync(0xffffffffu, my_cls == TILE_FULL);
+        }
         while (todo != 0u && ok) {
           const int bit = __ffs(todo) - 1;
           todo &= todo - 1;
@@ -592,7 +601,8 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
     };
     int2 w;
     SeqInfo s;
-    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, ok, abort_flag, a.status, WAIT_PRODUCER); ++n_item) {
+    uint32_t todo0 = 0u, full0 = 0u;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, todo0, full0, ok, abort_flag, a.status, WAIT_PRODUCER); ++n_item) {
       const int head = w.x >> 16;
       const int kvblk = (s.len + BLK - 1) / BLK - 1 - w.y;
       const int n0 = kvblk * BLK, col0 = head * HEAD_DIM;
@@ -610,17 +620,20 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
       const BlockRange qr = query_blocks_for_key_block(n0, s, a.mask);
       const int cnt = qr.count();
       // first pass: how many query blocks are kept (to flag the last one for the MMA warp)
-      int n_tiles = 0;
-      for (int base = 0; base < cnt; base += 32) {
+      int n_tiles = __popc(todo0);  // the scheduler warp classified the first 32 candidates
+      for (int base = 32; base < cnt; base += 32) {
         int my_cls = TILE_SKIP;
         if (base + lane < cnt) my_cls = classify_tile(qr.at(base + lane) * BLK, n0, s, a.mask);
         n_tiles += __popc(__ballot_sync(0xffffffffu, my_cls != TILE_SKIP));
       }
       int emitted = 0;
       for (int base = 0; base < cnt && ok; base += 32) {
-        int my_cls = TILE_SKIP;
-        if (base + lane < cnt) my_cls = classify_tile(qr.at(base + lane) * BLK, n0, s, a.mask);
-        uint32_t todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+        uint32_t todo = todo0;
+        if (base > 0) {
+          int my_cls = TILE_SKIP;
+          if (base + lane < cnt) my_cls = classify_tile(qr.at(base + lane) * BLK, n0, s, a.mask);
+          todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+        }
         while (todo != 0u && ok) {
           const int bit = __ffs(todo) - 1;
           todo &= todo - 1;
@@ -664,7 +677,8 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
     };
     int2 w_unused;
     SeqInfo s_unused;
-    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w_unused, s_unused, ok, abort_flag, a.status, WAIT_MMA); ++n_item) {
+    uint32_t t_unused = 0u, f_unused = 0u;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w_unused, s_unused, t_unused, f_unused, ok, abort_flag, a.status, WAIT_MMA); ++n_item) {
       sw.start();
       ok = wait_all(&sh.kv_full, it & 1);
       sw.stop(pf[PB_MMA_WAIT_ITEM]);
@@ -747,7 +761,7 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
       for (int i = 0; i < 5; ++i) atomicAdd(prof + i, (int)(pf[i] >> 6));
   } else if (warp == 2) {
     // ------------------------------------------------------------------ work-item scheduler
-    run_item_scheduler(sh.ring, a, items, total_items, ws + WS_CURSOR0, abort_flag);
+    run_item_scheduler<true>(sh.ring, a, items, total_items, ws + WS_CURSOR0, abort_flag);
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ epilogue groups
     const int wg = (warp - 4) >> 2;
@@ -763,7 +777,8 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
     sw_total.start();
     int2 w;
     SeqInfo s;
-    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, ok, abort_flag, a.status, WAIT_EPILOGUE); ++n_item) {
+    uint32_t todo0 = 0u, full0 = 0u;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, todo0, full0, ok, abort_flag, a.status, WAIT_EPILOGUE); ++n_item) {
       const int head = w.x >> 16;
       const int kvblk = (s.len + BLK - 1) / BLK - 1 - w.y;
       const int n0 = kvblk * BLK, n = n0 + row;
@@ -771,10 +786,13 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
       const BlockRange qr = query_blocks_for_key_block(n0, s, a.mask);
       const int cnt = qr.count();
       for (int base = 0; base < cnt && ok; base += 32) {
-        int my_cls = TILE_SKIP;
-        if (base + lane < cnt) my_cls = classify_tile(qr.at(base + lane) * BLK, n0, s, a.mask);
-        uint32_t todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
-        const uint32_t full_bits = __ballot_sync(0xffffffffu, my_cls == TILE_FULL);
+        uint32_t todo = todo0, full_bits = full0;  // the scheduler warp classified the first 32 candidates
+        if (base > 0) {
+          int my_cls = TILE_SKIP;
+          if (base + lane < cnt) my_cls = classify_tile(qr.at(base + lane) * BLK, n0, s, a.mask);
+          todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+          full_bits = __ballot_sync(0xffffffffu, my_cls == TILE_FULL);
+        }
         while (todo != 0u && ok) {
           const int bit = __ffs(todo) - 1;
           todo &= todo - 1;

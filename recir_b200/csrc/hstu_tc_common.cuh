@@ -243,6 +243,7 @@ __device__ __forceinline__ void zero_box_rows(unsigned char* box, int row_lo, in
 struct ItemSlot {
   int2 w;     // (sequence | head << 16, block index); w.x < 0: the list is exhausted
   SeqInfo s;
+  uint32_t todo, full;  // classes of the item's first 32 candidate tiles: bit i = not skipped / fully kept
 };
 constexpr int ITEM_RING = 2;
 constexpr int ITEM_CONSUMERS = 10;  // producer warp, MMA warp, eight epilogue warps
@@ -259,7 +260,26 @@ __device__ __forceinline__ void item_ring_init(ItemRing& r) {
   }
 }
 
-// Body of the scheduler warp (all 32 lanes call it; lane 0 does the work).
+// Class of candidate tile i of an item.  KEY_MAJOR = false: the item is a query block and the
+// candidates are its key blocks (forward, dQ pass; query rows past the sequence end do not
+// matter); true: the item is a key block and the candidates are its query blocks (dK/dV pass).
+template <bool KEY_MAJOR>
+__device__ __forceinline__ int item_tile_class(const int2& w, const SeqInfo& s, const MaskOpts& o, int i, int* count) {
+  if (!KEY_MAJOR) {
+    const int m0 = w.y * BLK;
+    const BlockRange kr = key_blocks_for_query_block(m0, s, o);
+    *count = kr.count();
+    return i < kr.count() ? classify_tile(m0, kr.at(i) * BLK, s, o, true) : TILE_SKIP;
+  }
+  const int n0 = ((s.len + BLK - 1) / BLK - 1 - w.y) * BLK;
+  const BlockRange qr = query_blocks_for_key_block(n0, s, o);
+  *count = qr.count();
+  return i < qr.count() ? classify_tile(qr.at(i) * BLK, n0, s, o) : TILE_SKIP;
+}
+
+// Body of the scheduler warp (all 32 lanes call it): lane 0 claims and reads the item, every
+// lane classifies one of its first 32 candidate tiles, so that the other warps do not repeat it.
+template <bool KEY_MAJOR>
 __device__ __forceinline__ void run_item_scheduler(ItemRing& r, const KernelArgs& a, const int2* items, int total,
                                                    int* cursor, volatile int* abort_flag) {
   const int lane = threadIdx.x & 31;
@@ -269,14 +289,28 @@ __device__ __forceinline__ void run_item_scheduler(ItemRing& r, const KernelArgs
     if (!__all_sync(0xffffffffu, sm100::mbar_wait(sm100::smem_u32(&r.empty[sl]), par, abort_flag, a.status, WAIT_SCHEDULER)))
       return;
     const bool have = idx < total;
-    if (lane == 0) {
-      ItemSlot it;
-      it.w = make_int2(-1, 0);
-      it.s.start = 0; it.s.len = 0; it.s.hist = 0; it.s.has_targets = 0; it.s.boundary = 0;
-      if (have) {
+    ItemSlot it;
+    it.w = make_int2(-1, 0);
+    it.s.start = 0; it.s.len = 0; it.s.hist = 0; it.s.has_targets = 0; it.s.boundary = 0;
+    it.todo = 0u; it.full = 0u;
+    if (have) {
+      if (lane == 0) {
         it.w = items[idx];
         it.s = load_seq(a, it.w.x & 0xffff);
       }
+      it.w.x = __shfl_sync(0xffffffffu, it.w.x, 0);
+      it.w.y = __shfl_sync(0xffffffffu, it.w.y, 0);
+      it.s.start = __shfl_sync(0xffffffffu, it.s.start, 0);
+      it.s.len = __shfl_sync(0xffffffffu, it.s.len, 0);
+      it.s.hist = __shfl_sync(0xffffffffu, it.s.hist, 0);
+      it.s.has_targets = __shfl_sync(0xffffffffu, it.s.has_targets, 0);
+      it.s.boundary = __shfl_sync(0xffffffffu, it.s.boundary, 0);
+      int count = 0;
+      const int cls = item_tile_class<KEY_MAJOR>(it.w, it.s, a.mask, lane, &count);
+      it.todo = __ballot_sync(0xffffffffu, cls != TILE_SKIP);
+      it.full = __ballot_sync(0xffffffffu, cls == TILE_FULL);
+    }
+    if (lane == 0) {
       r.slot[sl] = it;
       sm100::mbar_arrive(sm100::smem_u32(&r.full[sl]));  // release: the slot is written before the arrival
     }
@@ -289,8 +323,8 @@ __device__ __forceinline__ void run_item_scheduler(ItemRing& r, const KernelArgs
 
 // Takes item n from the ring (whole warp).  Returns false when the list is exhausted or a wait
 // gave up (then `ok` is cleared as well).
-__device__ __forceinline__ bool next_item(ItemRing& r, uint32_t n, int2& w, SeqInfo& s, bool& ok,
-                                          volatile int* abort_flag, int* status, int code) {
+__device__ __forceinline__ bool next_item(ItemRing& r, uint32_t n, int2& w, SeqInfo& s, uint32_t& todo0,
+                                          uint32_t& full0, bool& ok, volatile int* abort_flag, int* status, int code) {
   const uint32_t sl = n % ITEM_RING, par = (n / ITEM_RING) & 1;
   if (!__all_sync(0xffffffffu, sm100::mbar_wait(sm100::smem_u32(&r.full[sl]), par, abort_flag, status, code))) {
     ok = false;
@@ -298,6 +332,8 @@ __device__ __forceinline__ bool next_item(ItemRing& r, uint32_t n, int2& w, SeqI
   }
   w = r.slot[sl].w;
   s = r.slot[sl].s;
+  todo0 = r.slot[sl].todo;
+  full0 = r.slot[sl].full;
   __syncwarp();
   if ((threadIdx.x & 31) == 0) sm100::mbar_arrive(sm100::smem_u32(&r.empty[sl]));
   return w.x >= 0;
