@@ -1,0 +1,64 @@
+/* C ABI of the row-wise STU-layer kernels that sit either side of the attention operator:
+ * the weighted layer norm (optionally SiLU-gated) in front of the u/v/q/k projection, and the
+ * layer-norm * gate stage (with optional concatenation and row-wise fp8 quantisation) behind it.
+ *
+ * Reference semantics (CPU, ATen): recir/ops/kjt_split_per_feature.cpp
+ *   weightedLayerNorm          :197-244  schema generative_recommenders::triton_weighted_layer_norm_fwd (:724-727)
+ *   layerNormMulQuantized      :558-600  schema ..._triton_layer_norm_mul_dropout_quantization_fwd_impl (:744-747)
+ *   quantizeFp8Rowwise         :492-501
+ * The reference ignores dropout_ratio / training / seed on this path; so does this library.
+ *
+ * Same conventions as b200_hstu.h: plain pointers and sizes, caller-owned buffers, nothing is
+ * allocated or synchronised, launches go to the given stream, results are negative on error
+ * (B200_HSTU_E* codes of b200_hstu.h).
+ */
+#ifndef B200_STU_ROWWISE_H
+#define B200_STU_ROWWISE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_ROWWISE_FLAG_SWISH 0x1u        /* layer norm: y = sigmoid(ln(x)) * x            (is_swish) */
+#define B200_ROWWISE_FLAG_STATS_IN 0x2u     /* layer norm: use mean_in / rstd_in instead of computing them */
+#define B200_ROWWISE_FLAG_SILU_U 0x4u       /* mul: the concatenated copy of u is silu(u)     (silu_u) */
+#define B200_ROWWISE_FLAG_CONCAT_U 0x8u     /* mul: output row = [u' | ...]                   (concat_u) */
+#define B200_ROWWISE_FLAG_CONCAT_X 0x10u    /* mul: output row = [... | x | ...]              (concat_x) */
+#define B200_ROWWISE_FLAG_ACT_SILU 0x20u    /* mul: gate = silu(u)      (mul_u_activation_type == "silu") */
+#define B200_ROWWISE_FLAG_ACT_SIGMOID 0x40u /* mul: gate = sigmoid(u)   (mul_u_activation_type == "sigmoid") */
+
+typedef struct B200RowwiseParams {
+  uint32_t struct_size; /* sizeof(B200RowwiseParams) */
+  uint32_t flags;
+  int32_t dtype;        /* B200_HSTU_F32 / _BF16 / _F16: element type of x, u, weight, bias, y */
+  float eps;
+  int64_t rows, cols;   /* x is [rows, cols]; cols a multiple of 8, at most 2048 */
+  int64_t x_row_stride, u_row_stride, y_row_stride, q8_row_stride; /* in elements */
+  const void* x;        /* [rows, cols] */
+  const void* u;        /* [rows, cols] (mul only) */
+  const void* weight;   /* [cols] or NULL (then bias must be NULL too; layer norm only) */
+  const void* bias;     /* [cols] or NULL */
+  const float* mean_in; /* [rows] with FLAG_STATS_IN */
+  const float* rstd_in;
+  void* y;              /* layer norm: [rows, cols]; mul: [rows, parts*cols] or NULL (save_y == false) */
+  float* mean;          /* [rows] */
+  float* rstd;          /* [rows] */
+  float* scale;         /* mul: [rows] row scale of the fp8 copy, or NULL (no fp8 copy) */
+  void* q8;             /* mul: [rows, parts*cols] float8 e4m3 (1 byte each), or NULL */
+} B200RowwiseParams;
+
+/* y = ln(x) * weight + bias (or plain ln(x)), optionally sigmoid(y) * x; writes mean and rstd. */
+int b200_stu_layer_norm_fwd(const B200RowwiseParams* p, void* stream);
+/* out row = [u' | x | ln(x) * gate(u)] (the first two parts are optional); optionally also its
+ * row-wise fp8 copy: scale = max(|row|, 1e-12) / 448, q8 = clamp(row / scale, +-448) as e4m3. */
+int b200_stu_layer_norm_mul_fwd(const B200RowwiseParams* p, void* stream);
+/* Number of column blocks of the mul output: 1 + concat_u + concat_x. */
+int b200_stu_layer_norm_mul_parts(uint32_t flags);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

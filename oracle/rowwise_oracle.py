@@ -1,0 +1,113 @@
+"""CPU restatement (numpy) of the reference's row-wise STU-layer operators.
+
+TEST INFRASTRUCTURE ONLY: imported by tests, never by the product path.
+
+* ``weighted_layer_norm``      -- ``weightedLayerNorm``, recir/ops/kjt_split_per_feature.cpp:197-244
+* ``layer_norm_mul_quantized`` -- ``layerNormMulQuantized``, :558-600, with
+  ``quantizeFp8Rowwise``, :492-501
+
+The reference computes statistics and the normalisation in float32 and materialises some
+intermediates in the input dtype (the normalised rows returned by ``weightedLayerNorm``, silu(u),
+sigmoid(u), the product); ``dtype`` names that element type ("float32", "bfloat16", "float16") and
+the same roundings are applied here.  Inputs and outputs are float32 arrays holding values that
+are representable in ``dtype``; the fp8 copy is returned as e4m3 bytes (uint8).
+
+Pinned against golden vectors produced by the reference's compiled operators
+(tests/golden/rowwise_golden.npz, generator tests/golden/make_rowwise_golden.py).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def round_to(x, dtype: str):
+    """float32 -> dtype -> float32 (round to nearest even), i.e. what materialising a tensor does."""
+    x = np.asarray(x, dtype=np.float32)
+    if dtype == "float32":
+        return x
+    if dtype == "float16":
+        return x.astype(np.float16).astype(np.float32)
+    if dtype == "bfloat16":
+        b = x.view(np.uint32).astype(np.uint64)
+        rounded = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16
+        out = (rounded & 0xFFFFFFFF).astype(np.uint32).view(np.float32)
+        return np.where(np.isnan(x), x, out)
+    raise ValueError(dtype)
+
+
+def _sigmoid(x):
+    x = np.asarray(x, dtype=np.float32)
+    return (np.float32(1) / (np.float32(1) + np.exp(-x, dtype=np.float32))).astype(np.float32)
+
+
+def weighted_layer_norm(x, weight, bias, eps, dtype="float32", mean=None, rstd=None, is_swish=False):
+    """Returns (y, mean, rstd); kjt_split_per_feature.cpp:220-243."""
+    xf = np.asarray(x, dtype=np.float32)
+    if mean is None or rstd is None:
+        mean = xf.mean(axis=1, dtype=np.float32)
+        centered = xf - mean[:, None]
+        rstd = (np.float32(1) / np.sqrt((centered * centered).mean(axis=1, dtype=np.float32) + np.float32(eps))).astype(np.float32)
+    else:
+        mean = np.asarray(mean, dtype=np.float32).copy()
+        rstd = np.asarray(rstd, dtype=np.float32).copy()
+    n = (xf - mean[:, None]) * rstd[:, None]
+    if weight is not None:
+        n = n * np.asarray(weight, dtype=np.float32) + np.asarray(bias, dtype=np.float32)
+    if is_swish:
+        n = _sigmoid(n) * xf
+    return round_to(n, dtype), mean, rstd
+
+
+def e4m3_encode(v):
+    """float32 (|v| <= 448) -> float8 e4m3fn byte, round to nearest even."""
+    v = np.asarray(v, dtype=np.float32)
+    sign = (np.signbit(v)).astype(np.uint8) << 7
+    m = np.abs(v).astype(np.float64)
+    out = np.zeros(v.shape, dtype=np.uint8)
+    sub = m < 2.0 ** -6
+    q_sub = np.rint(m / 2.0 ** -9).astype(np.int64)  # 0..8; 8 is the smallest normal, same encoding
+    e = np.floor(np.log2(np.where(m > 0, m, 1.0))).astype(np.int64)
+    frac = m / np.exp2(e.astype(np.float64)) - 1.0
+    q = np.rint(frac * 8.0).astype(np.int64)
+    e = np.where(q == 8, e + 1, e)
+    q = np.where(q == 8, 0, q)
+    code = ((e + 7) << 3) | q
+    code = np.minimum(code, 0x7E)  # 448 is the largest finite value
+    out = np.where(sub, q_sub, code).astype(np.uint8)
+    return (out | sign).astype(np.uint8)
+
+
+def quantize_fp8_rowwise(values):
+    """(scale [rows], e4m3 bytes); kjt_split_per_feature.cpp:492-501."""
+    vf = np.asarray(values, dtype=np.float32)
+    amax = np.abs(vf).max(axis=1) if vf.shape[1] else np.zeros(vf.shape[0], np.float32)
+    scale = (np.maximum(amax, np.float32(1e-12)) / np.float32(448.0)).astype(np.float32)
+    q = np.clip(vf / scale[:, None], np.float32(-448.0), np.float32(448.0)).astype(np.float32)
+    return scale, e4m3_encode(q)
+
+
+def layer_norm_mul_quantized(x, u, weight, bias, eps, dtype="float32", silu_u=False, concat_u=False,
+                             concat_x=False, mul_u_activation="none"):
+    """Returns (combined, mean, rstd, scale, q8); kjt_split_per_feature.cpp:573-599."""
+    normalized, mean, rstd = weighted_layer_norm(x, weight, bias, eps, dtype)
+    uf = np.asarray(u, dtype=np.float32)
+
+    def silu_t(t):
+        return round_to(t * round_to(_sigmoid(t), dtype), dtype)
+
+    if mul_u_activation == "silu":
+        gate = silu_t(uf)
+    elif mul_u_activation == "sigmoid":
+        gate = round_to(_sigmoid(uf), dtype)
+    else:
+        gate = uf
+    multiplied = round_to(normalized * gate, dtype)
+    parts = []
+    if concat_u:
+        parts.append(silu_t(uf) if silu_u else uf)
+    if concat_x:
+        parts.append(np.asarray(x, dtype=np.float32))
+    parts.append(multiplied)
+    combined = np.concatenate(parts, axis=1)
+    scale, q8 = quantize_fp8_rowwise(combined)
+    return combined, mean, rstd, scale, q8

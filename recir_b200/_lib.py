@@ -25,6 +25,8 @@ EXPORTS = (
     "b200_hstu_debug_keep", "b200_hstu_debug_classify_tile", "b200_hstu_debug_key_blocks",
     "b200_hstu_debug_query_blocks", "b200_hstu_fwd_static_scratch", "b200_hstu_debug_row_mask",
     "b200_hstu_debug_col_mask", "b200_hstu_last_cuda_error",
+    # include/b200_stu_rowwise.h
+    "b200_stu_layer_norm_fwd", "b200_stu_layer_norm_mul_fwd", "b200_stu_layer_norm_mul_parts",
 )
 STATIC_SCRATCH_BYTES = 4 << 20
 
@@ -60,6 +62,27 @@ class B200HstuParams(ctypes.Structure):
         ("max_seq_len", ctypes.c_int32), ("max_attn_len", ctypes.c_int32),
         ("contextual_seq_len", ctypes.c_int32), ("full_attn_size", ctypes.c_int32),
         ("alpha", ctypes.c_float),
+    ]
+
+
+# flags of include/b200_stu_rowwise.h
+ROWWISE_SWISH, ROWWISE_STATS_IN, ROWWISE_SILU_U, ROWWISE_CONCAT_U = 0x1, 0x2, 0x4, 0x8
+ROWWISE_CONCAT_X, ROWWISE_ACT_SILU, ROWWISE_ACT_SIGMOID = 0x10, 0x20, 0x40
+
+
+class B200RowwiseParams(ctypes.Structure):
+    """Mirror of ``struct B200RowwiseParams`` (include/b200_stu_rowwise.h)."""
+
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32), ("flags", ctypes.c_uint32),
+        ("dtype", ctypes.c_int32), ("eps", ctypes.c_float),
+        ("rows", ctypes.c_int64), ("cols", ctypes.c_int64),
+        ("x_row_stride", ctypes.c_int64), ("u_row_stride", ctypes.c_int64),
+        ("y_row_stride", ctypes.c_int64), ("q8_row_stride", ctypes.c_int64),
+        ("x", ctypes.c_void_p), ("u", ctypes.c_void_p), ("weight", ctypes.c_void_p), ("bias", ctypes.c_void_p),
+        ("mean_in", ctypes.c_void_p), ("rstd_in", ctypes.c_void_p),
+        ("y", ctypes.c_void_p), ("mean", ctypes.c_void_p), ("rstd", ctypes.c_void_p),
+        ("scale", ctypes.c_void_p), ("q8", ctypes.c_void_p),
     ]
 
 
@@ -109,6 +132,12 @@ def load() -> ctypes.CDLL:
     lib.b200_hstu_debug_key_blocks.restype = None
     lib.b200_hstu_debug_query_blocks.argtypes = [MQ, ctypes.c_int, ctypes.POINTER(ctypes.c_int32 * 3)]
     lib.b200_hstu_debug_query_blocks.restype = None
+    RP = ctypes.POINTER(B200RowwiseParams)
+    for fn in (lib.b200_stu_layer_norm_fwd, lib.b200_stu_layer_norm_mul_fwd):
+        fn.argtypes = [RP, ctypes.c_void_p]
+        fn.restype = ctypes.c_int
+    lib.b200_stu_layer_norm_mul_parts.argtypes = [ctypes.c_uint32]
+    lib.b200_stu_layer_norm_mul_parts.restype = ctypes.c_int
     if lib.b200_hstu_params_size() != ctypes.sizeof(B200HstuParams):
         raise RuntimeError("B200HstuParams layout mismatch between Python binding and library")
     _lib = lib

@@ -1,0 +1,329 @@
+// Row-wise STU-layer kernels either side of the attention operator (HBM-bound):
+//   layer norm (optionally affine, optionally SiLU-gated: y = sigmoid(ln(x)) * x), and
+//   layer norm * gate(u) with optional [u' | x | .] concatenation and row-wise fp8 quantisation.
+// Reference semantics: recir/ops/kjt_split_per_feature.cpp:197-244 (weightedLayerNorm),
+// :558-600 (layerNormMulQuantized), :492-501 (quantizeFp8Rowwise).  All statistics and the
+// normalisation run in fp32; wherever the reference materialises an intermediate tensor in the
+// input dtype (the normalised rows, silu(u), the product) the value is rounded to that dtype here
+// too, so 16-bit results agree with the reference to the last bit except where its vectorised
+// exp differs from expf in the last fp32 bit.
+//
+// One warp owns one row: a lane reads 16-byte vectors (8 elements; 32 bytes for fp32) strided by
+// 32 lanes, so every warp load is one contiguous 512-byte segment; the row stays in registers
+// between the statistics pass and the output pass, i.e. x is read from HBM exactly once.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/b200_hstu.h"
+#include "../../include/b200_stu_rowwise.h"
+#include "hstu_launch.h"
+
+namespace hstu {
+namespace rowwise {
+namespace {
+
+constexpr int WARPS_PER_BLOCK = 8;
+
+template <typename T> struct Vec8;  // 8 consecutive elements
+template <> struct Vec8<float> { float4 a, b; };
+template <> struct Vec8<__nv_bfloat16> { uint4 v; };
+template <> struct Vec8<__half> { uint4 v; };
+
+template <typename T> __device__ __forceinline__ void load8(const T* p, float (&f)[8]);
+template <> __device__ __forceinline__ void load8<float>(const float* p, float (&f)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+template <> __device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&f)[8]) {
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+template <> __device__ __forceinline__ void load8<__half>(const __half* p, float (&f)[8]) {
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+  const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 x = __half22float2(h[i]);
+    f[2 * i] = x.x; f[2 * i + 1] = x.y;
+  }
+}
+
+template <typename T> __device__ __forceinline__ void store8(T* p, const float (&f)[8]);
+template <> __device__ __forceinline__ void store8<float>(float* p, const float (&f)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+}
+template <> __device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* p, const float (&f)[8]) {
+  uint4 v;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint4*>(p) = v;
+}
+template <> __device__ __forceinline__ void store8<__half>(__half* p, const float (&f)[8]) {
+  uint4 v;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint4*>(p) = v;
+}
+
+// value -> element type -> value (what materialising a tensor in the input dtype does)
+template <typename T> __device__ __forceinline__ float round_to(float x);
+template <> __device__ __forceinline__ float round_to<float>(float x) { return x; }
+template <> __device__ __forceinline__ float round_to<__nv_bfloat16>(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+template <> __device__ __forceinline__ float round_to<__half>(float x) { return __half2float(__float2half_rn(x)); }
+
+__device__ __forceinline__ float sigmoidf(float x) { return 1.f / (1.f + expf(-x)); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+struct Args {
+  const void* x; const void* u; const void* weight; const void* bias;
+  const float* mean_in; const float* rstd_in;
+  void* y; float* mean; float* rstd; float* scale; unsigned char* q8;
+  long long rows, x_rs, u_rs, y_rs, q8_rs;
+  int cols; unsigned flags; float eps;
+};
+
+// Loads the row into registers and returns (mean, rstd) the way the reference computes them:
+// mean first, then the mean of squared deviations (kjt_split_per_feature.cpp:223-226).
+template <typename T, int VPL>
+__device__ __forceinline__ void row_stats(const T* xr, int nv, int lane, float (&xv)[VPL][8], float cols, float eps,
+                                          float& mean, float& rstd) {
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int v = lane + 32 * j;
+    if (v < nv) {
+      load8<T>(xr + 8 * v, xv[j]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += xv[j][i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xv[j][i] = 0.f;
+    }
+  }
+  mean = warp_sum(s) / cols;
+  float q = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j)
+    if (lane + 32 * j < nv) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { const float d = xv[j][i] - mean; q += d * d; }
+    }
+  rstd = rsqrtf(warp_sum(q) / cols + eps);
+}
+
+template <typename T, int VPL>
+__global__ void __launch_bounds__(WARPS_PER_BLOCK * 32) layer_norm_kernel(Args a) {
+  const int lane = threadIdx.x & 31;
+  const long long row = static_cast<long long>(blockIdx.x) * WARPS_PER_BLOCK + (threadIdx.x >> 5);
+  if (row >= a.rows) return;
+  const int nv = a.cols >> 3;
+  const T* xr = reinterpret_cast<const T*>(a.x) + row * a.x_rs;
+  T* yr = reinterpret_cast<T*>(a.y) + row * a.y_rs;
+  float xv[VPL][8];
+  float mean, rstd;
+  row_stats<T, VPL>(xr, nv, lane, xv, static_cast<float>(a.cols), a.eps, mean, rstd);
+  if (a.flags & B200_ROWWISE_FLAG_STATS_IN) { mean = a.mean_in[row]; rstd = a.rstd_in[row]; }
+  if (lane == 0) { a.mean[row] = mean; a.rstd[row] = rstd; }
+  const bool affine = a.weight != nullptr, swish = (a.flags & B200_ROWWISE_FLAG_SWISH) != 0;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int v = lane + 32 * j;
+    if (v >= nv) continue;
+    float w[8], b[8], o[8];
+    if (affine) {
+      load8<T>(reinterpret_cast<const T*>(a.weight) + 8 * v, w);
+      load8<T>(reinterpret_cast<const T*>(a.bias) + 8 * v, b);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float n = (xv[j][i] - mean) * rstd;
+      if (affine) n = n * w[i] + b[i];
+      if (swish) n = sigmoidf(n) * xv[j][i];
+      o[i] = n;
+    }
+    store8<T>(yr + 8 * v, o);
+  }
+}
+
+__device__ __forceinline__ unsigned char to_e4m3(float v) {
+  return static_cast<unsigned char>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+}
+
+template <typename T, int VPL>
+__global__ void __launch_bounds__(WARPS_PER_BLOCK * 32) layer_norm_mul_kernel(Args a) {
+  const int lane = threadIdx.x & 31;
+  const long long row = static_cast<long long>(blockIdx.x) * WARPS_PER_BLOCK + (threadIdx.x >> 5);
+  if (row >= a.rows) return;
+  const int nv = a.cols >> 3;
+  const T* xr = reinterpret_cast<const T*>(a.x) + row * a.x_rs;
+  const T* ur = reinterpret_cast<const T*>(a.u) + row * a.u_rs;
+  float xv[VPL][8], mv[VPL][8];
+  float mean, rstd;
+  row_stats<T, VPL>(xr, nv, lane, xv, static_cast<float>(a.cols), a.eps, mean, rstd);
+  if (lane == 0) { a.mean[row] = mean; a.rstd[row] = rstd; }
+  const bool cat_u = (a.flags & B200_ROWWISE_FLAG_CONCAT_U) != 0, cat_x = (a.flags & B200_ROWWISE_FLAG_CONCAT_X) != 0;
+  const bool silu_u = (a.flags & B200_ROWWISE_FLAG_SILU_U) != 0;
+  const int act = (a.flags & B200_ROWWISE_FLAG_ACT_SILU) ? 1 : ((a.flags & B200_ROWWISE_FLAG_ACT_SIGMOID) ? 2 : 0);
+  const int off_x = cat_u ? a.cols : 0, off_m = off_x + (cat_x ? a.cols : 0);
+  T* yr = a.y ? reinterpret_cast<T*>(a.y) + row * a.y_rs : nullptr;
+  // silu(u) as the reference materialises it: sigmoid rounded to the dtype, then the product rounded
+  auto silu_t = [](float u) { return round_to<T>(u * round_to<T>(sigmoidf(u))); };
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int v = lane + 32 * j;
+    if (v >= nv) continue;
+    float w[8], b[8], uu[8], ou[8];
+    load8<T>(reinterpret_cast<const T*>(a.weight) + 8 * v, w);
+    load8<T>(reinterpret_cast<const T*>(a.bias) + 8 * v, b);
+    load8<T>(ur + 8 * v, uu);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float n = round_to<T>((xv[j][i] - mean) * rstd * w[i] + b[i]);
+      const float gate = act == 1 ? silu_t(uu[i]) : (act == 2 ? round_to<T>(sigmoidf(uu[i])) : uu[i]);
+      mv[j][i] = round_to<T>(n * gate);
+      ou[i] = silu_u ? silu_t(uu[i]) : uu[i];
+      amax = fmaxf(amax, fabsf(mv[j][i]));
+      if (cat_u) amax = fmaxf(amax, fabsf(ou[i]));
+      if (cat_x) amax = fmaxf(amax, fabsf(xv[j][i]));
+    }
+    if (yr) {
+      if (cat_u) store8<T>(yr + 8 * v, ou);
+      if (cat_x) store8<T>(yr + off_x + 8 * v, xv[j]);
+      store8<T>(yr + off_m + 8 * v, mv[j]);
+    }
+  }
+  if (a.q8 == nullptr) return;
+  // row-wise fp8 copy (kjt_split_per_feature.cpp:492-501)
+  amax = warp_max(amax);
+  const float scale = fmaxf(amax, 1e-12f) / 448.f;
+  if (lane == 0) a.scale[row] = scale;
+  unsigned char* qr = a.q8 + row * a.q8_rs;
+  auto quant8 = [&](unsigned char* dst, const float (&f)[8]) {
+    uint2 pk;
+    unsigned char* b8 = reinterpret_cast<unsigned char*>(&pk);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) b8[i] = to_e4m3(fminf(fmaxf(f[i] / scale, -448.f), 448.f));
+    *reinterpret_cast<uint2*>(dst) = pk;
+  };
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int v = lane + 32 * j;
+    if (v >= nv) continue;
+    if (cat_u) {
+      float uu[8], ou[8];
+      load8<T>(ur + 8 * v, uu);  // second read of u: served by L1/L2
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ou[i] = silu_u ? silu_t(uu[i]) : uu[i];
+      quant8(qr + 8 * v, ou);
+    }
+    if (cat_x) quant8(qr + off_x + 8 * v, xv[j]);
+    quant8(qr + off_m + 8 * v, mv[j]);
+  }
+}
+
+int check(const B200RowwiseParams* p, bool mul, Args* a) {
+  if (p == nullptr) return B200_HSTU_EINVAL;
+  if (p->struct_size != sizeof(B200RowwiseParams)) return B200_HSTU_EVERSION;
+  if (p->dtype != B200_HSTU_F32 && p->dtype != B200_HSTU_BF16 && p->dtype != B200_HSTU_F16) return B200_HSTU_EUNSUPPORTED;
+  if (p->rows < 0 || p->cols <= 0) return B200_HSTU_EINVAL;
+  if (p->cols % 8 != 0 || p->cols > 2048) return B200_HSTU_EUNSUPPORTED;
+  const int esz = p->dtype == B200_HSTU_F32 ? 4 : 2;
+  const int parts = mul ? b200_stu_layer_norm_mul_parts(p->flags) : 1;
+  auto bad_ptr = [&](const void* q) { return reinterpret_cast<uintptr_t>(q) % 16 != 0; };
+  if (p->rows > 0) {
+    if (!p->x || !p->mean || !p->rstd) return B200_HSTU_EINVAL;
+    if (p->x_row_stride < p->cols || p->x_row_stride % 8 != 0 || bad_ptr(p->x)) return p->x_row_stride < p->cols ? B200_HSTU_EINVAL : B200_HSTU_EALIGN;
+    if ((p->weight == nullptr) != (p->bias == nullptr)) return B200_HSTU_EINVAL;
+    if (p->weight && (bad_ptr(p->weight) || bad_ptr(p->bias))) return B200_HSTU_EALIGN;
+    if (!mul) {
+      if (!p->y) return B200_HSTU_EINVAL;
+      if ((p->flags & B200_ROWWISE_FLAG_SWISH) && !p->weight) return B200_HSTU_EINVAL;  // as the reference (:205-207)
+      if ((p->flags & B200_ROWWISE_FLAG_STATS_IN) && (!p->mean_in || !p->rstd_in)) return B200_HSTU_EINVAL;
+    } else {
+      if (!p->u || !p->weight) return B200_HSTU_EINVAL;
+      if (p->u_row_stride < p->cols || p->u_row_stride % 8 != 0 || bad_ptr(p->u)) return p->u_row_stride < p->cols ? B200_HSTU_EINVAL : B200_HSTU_EALIGN;
+      if ((p->q8 == nullptr) != (p->scale == nullptr)) return B200_HSTU_EINVAL;
+      if (!p->y && !p->q8) return B200_HSTU_EINVAL;
+      if (p->q8 && (p->q8_row_stride < parts * p->cols || p->q8_row_stride % 8 != 0 || reinterpret_cast<uintptr_t>(p->q8) % 8 != 0))
+        return p->q8_row_stride < parts * p->cols ? B200_HSTU_EINVAL : B200_HSTU_EALIGN;
+    }
+    if (p->y && (p->y_row_stride < parts * p->cols || p->y_row_stride % 8 != 0 || bad_ptr(p->y)))
+      return p->y_row_stride < parts * p->cols ? B200_HSTU_EINVAL : B200_HSTU_EALIGN;
+    (void)esz;
+  }
+  a->x = p->x; a->u = p->u; a->weight = p->weight; a->bias = p->bias;
+  a->mean_in = p->mean_in; a->rstd_in = p->rstd_in;
+  a->y = p->y; a->mean = p->mean; a->rstd = p->rstd; a->scale = p->scale; a->q8 = static_cast<unsigned char*>(p->q8);
+  a->rows = p->rows; a->x_rs = p->x_row_stride; a->u_rs = p->u_row_stride; a->y_rs = p->y_row_stride; a->q8_rs = p->q8_row_stride;
+  a->cols = static_cast<int>(p->cols); a->flags = p->flags; a->eps = p->eps;
+  return B200_HSTU_OK;
+}
+
+template <typename T, bool MUL>
+cudaError_t launch_t(const Args& a, cudaStream_t st) {
+  const unsigned grid = static_cast<unsigned>((a.rows + WARPS_PER_BLOCK - 1) / WARPS_PER_BLOCK);
+  const int vpl = (a.cols / 8 + 31) / 32;  // vectors per lane
+#define B200_ROWWISE_LAUNCH(V)                                                                 \
+  if (MUL) layer_norm_mul_kernel<T, V><<<grid, WARPS_PER_BLOCK * 32, 0, st>>>(a);               \
+  else layer_norm_kernel<T, V><<<grid, WARPS_PER_BLOCK * 32, 0, st>>>(a)
+  if (vpl <= 1) { B200_ROWWISE_LAUNCH(1); }
+  else if (vpl <= 2) { B200_ROWWISE_LAUNCH(2); }
+  else if (vpl <= 4) { B200_ROWWISE_LAUNCH(4); }
+  else { B200_ROWWISE_LAUNCH(8); }
+#undef B200_ROWWISE_LAUNCH
+  return cudaGetLastError();
+}
+
+template <bool MUL>
+int run(const B200RowwiseParams* p, void* stream) {
+  Args a;
+  const int rc = check(p, MUL, &a);
+  if (rc != B200_HSTU_OK) return rc;
+  if (a.rows == 0) return B200_HSTU_OK;
+  set_error_stage(MUL ? "layer norm * gate kernel" : "layer norm kernel");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = p->dtype == B200_HSTU_F32    ? launch_t<float, MUL>(a, st)
+                  : p->dtype == B200_HSTU_BF16 ? launch_t<__nv_bfloat16, MUL>(a, st)
+                                               : launch_t<__half, MUL>(a, st);
+  return e == cudaSuccess ? B200_HSTU_OK : B200_HSTU_ELAUNCH;
+}
+
+}  // namespace
+}  // namespace rowwise
+}  // namespace hstu
+
+extern "C" {
+int b200_stu_layer_norm_mul_parts(uint32_t flags) {
+  return 1 + ((flags & B200_ROWWISE_FLAG_CONCAT_U) ? 1 : 0) + ((flags & B200_ROWWISE_FLAG_CONCAT_X) ? 1 : 0);
+}
+int b200_stu_layer_norm_fwd(const B200RowwiseParams* p, void* stream) { return hstu::rowwise::run<false>(p, stream); }
+int b200_stu_layer_norm_mul_fwd(const B200RowwiseParams* p, void* stream) { return hstu::rowwise::run<true>(p, stream); }
+}

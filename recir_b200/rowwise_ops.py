@@ -1,0 +1,164 @@
+"""``torch.library`` operators for the row-wise STU-layer kernels either side of the attention.
+
+Positionally identical to the reference's operators, so the same node-retargeting swap applies
+(``recir/lowering/op_swap.py:78-97``):
+
+* ``recir::b200_weighted_layer_norm_fwd`` -- schema of
+  ``generative_recommenders::triton_weighted_layer_norm_fwd``
+  (``recir/ops/kjt_split_per_feature.cpp:724-727``, semantics ``:197-244``);
+* ``recir::b200_layer_norm_mul_dropout_quantization_fwd`` -- schema of
+  ``generative_recommenders::_triton_layer_norm_mul_dropout_quantization_fwd_impl``
+  (``:744-747``, semantics ``:558-600``).  Like the reference's CPU operator it applies no dropout
+  (``dropout_ratio``, ``training`` and ``seed`` are accepted and ignored).
+
+Forward only (the reference differentiates its composites through ATen; a fused backward is not
+built).  CUDA tensors only; there is no CPU implementation.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .ops import _check, _DTYPES
+
+_LIBDEF = torch.library.Library("recir", "FRAGMENT")
+_LIBDEF.define(
+    "b200_weighted_layer_norm_fwd(Tensor x, Tensor? weight, Tensor? bias, float eps, Tensor? mean=None, "
+    "Tensor? rstd=None, bool is_swish=False) -> (Tensor, Tensor, Tensor)")
+_LIBDEF.define(
+    "b200_layer_norm_mul_dropout_quantization_fwd(Tensor x, Tensor u, Tensor weight, Tensor bias, float eps, "
+    "float dropout_ratio, bool training, bool silu_u, bool concat_u, bool concat_x, str mul_u_activation_type, "
+    "int seed, bool save_y, int BLOCK_D) -> (Tensor, Tensor, Tensor, Tensor, Tensor)")
+
+# Kernel launches issued through this module since import.
+launch_counter = 0
+
+
+def _rows2d(t: torch.Tensor) -> torch.Tensor:
+    return t if t.stride(1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0 else t.contiguous()
+
+
+def _validate(x, weight, bias):
+    # messages of recir/ops/kjt_split_per_feature.cpp:205-218
+    if x.dim() != 2:
+        raise ValueError("x must be two-dimensional")
+    if x.dtype not in _DTYPES:
+        raise ValueError(f"unsupported dtype {x.dtype}: expected float32, bfloat16 or float16")
+    if weight is not None:
+        if bias is None:
+            raise ValueError("bias is required when weight is provided")
+        if weight.dim() != 1 or weight.numel() != x.shape[1]:
+            raise ValueError("weight must match the feature dimension")
+        if bias.dim() != 1 or bias.numel() != x.shape[1]:
+            raise ValueError("bias must match the feature dimension")
+    if x.shape[1] % 8 != 0 or x.shape[1] > 2048:
+        raise ValueError("the feature dimension must be a multiple of 8 and at most 2048")
+
+
+def _params(x, weight, bias, eps):
+    p = _lib.B200RowwiseParams()
+    p.struct_size = ctypes.sizeof(p)
+    p.dtype = _DTYPES[x.dtype]
+    p.eps = float(eps)
+    p.rows, p.cols = x.shape
+    p.x, p.x_row_stride = x.data_ptr(), x.stride(0)
+    keep = [x]
+    if weight is not None:
+        w, b = weight.to(x.dtype).contiguous(), bias.to(x.dtype).contiguous()
+        keep += [w, b]
+        p.weight, p.bias = w.data_ptr(), b.data_ptr()
+    return p, keep
+
+
+def _layer_norm_cuda(x, weight, bias, eps, mean=None, rstd=None, is_swish=False):
+    global launch_counter
+    _validate(x, weight, bias)
+    if is_swish and weight is None:
+        raise ValueError("is_swish requires learnable layer normalization")
+    x = _rows2d(x)
+    y = torch.empty_like(x, memory_format=torch.contiguous_format)
+    mean_out = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+    rstd_out = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+    if x.shape[0] == 0:
+        return y, mean_out, rstd_out
+    p, keep = _params(x, weight, bias, eps)
+    if mean is not None and rstd is not None:
+        if mean.numel() != x.shape[0] or rstd.numel() != x.shape[0]:
+            raise ValueError("mean and rstd must match the row count")
+        m_in, r_in = mean.to(torch.float32).contiguous(), rstd.to(torch.float32).contiguous()
+        keep += [m_in, r_in]
+        p.mean_in, p.rstd_in = m_in.data_ptr(), r_in.data_ptr()
+        p.flags |= _lib.ROWWISE_STATS_IN
+    if is_swish:
+        p.flags |= _lib.ROWWISE_SWISH
+    p.y, p.y_row_stride = y.data_ptr(), y.stride(0)
+    p.mean, p.rstd = mean_out.data_ptr(), rstd_out.data_ptr()
+    with torch.cuda.device(x.device):
+        rc = _lib.load().b200_stu_layer_norm_fwd(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    _check(rc, "b200_stu_layer_norm_fwd")
+    launch_counter += 1
+    del keep
+    return y, mean_out, rstd_out
+
+
+def _mul_flags(silu_u, concat_u, concat_x, act):
+    if act not in ("none", "silu", "sigmoid"):
+        raise ValueError(f"unknown mul_u_activation_type {act!r}")
+    return ((_lib.ROWWISE_SILU_U if silu_u else 0) | (_lib.ROWWISE_CONCAT_U if concat_u else 0)
+            | (_lib.ROWWISE_CONCAT_X if concat_x else 0)
+            | (_lib.ROWWISE_ACT_SILU if act == "silu" else (_lib.ROWWISE_ACT_SIGMOID if act == "sigmoid" else 0)))
+
+
+def _layer_norm_mul_cuda(x, u, weight, bias, eps, dropout_ratio, training, silu_u, concat_u, concat_x,
+                         mul_u_activation_type, seed, save_y, BLOCK_D):
+    global launch_counter
+    _validate(x, weight, bias)
+    if u.shape != x.shape or u.dtype != x.dtype:
+        raise ValueError("u must have the shape and dtype of x")
+    x, u = _rows2d(x), _rows2d(u)
+    flags = _mul_flags(silu_u, concat_u, concat_x, mul_u_activation_type)
+    parts = 1 + int(bool(concat_u)) + int(bool(concat_x))
+    rows, cols = x.shape
+    dev = x.device
+    y = torch.empty((rows, parts * cols), dtype=x.dtype, device=dev) if save_y else torch.empty((0,), dtype=x.dtype, device=dev)
+    mean = torch.empty(rows, dtype=torch.float32, device=dev)
+    rstd = torch.empty(rows, dtype=torch.float32, device=dev)
+    scale = torch.empty(rows, dtype=torch.float32, device=dev)
+    q8 = torch.empty((rows, parts * cols), dtype=torch.float8_e4m3fn, device=dev)
+    if rows == 0:
+        return y, mean, rstd, scale, q8
+    p, keep = _params(x, weight, bias, eps)
+    p.flags = flags
+    p.u, p.u_row_stride = u.data_ptr(), u.stride(0)
+    if save_y:
+        p.y, p.y_row_stride = y.data_ptr(), y.stride(0)
+    p.mean, p.rstd, p.scale = mean.data_ptr(), rstd.data_ptr(), scale.data_ptr()
+    p.q8, p.q8_row_stride = q8.data_ptr(), q8.stride(0)
+    with torch.cuda.device(dev):
+        rc = _lib.load().b200_stu_layer_norm_mul_fwd(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    _check(rc, "b200_stu_layer_norm_mul_fwd")
+    launch_counter += 1
+    del keep
+    return y, mean, rstd, scale, q8
+
+
+def _layer_norm_fake(x, weight, bias, eps, mean=None, rstd=None, is_swish=False):
+    return (torch.empty_like(x, memory_format=torch.contiguous_format),
+            x.new_empty((x.shape[0],), dtype=torch.float32), x.new_empty((x.shape[0],), dtype=torch.float32))
+
+
+def _layer_norm_mul_fake(x, u, weight, bias, eps, dropout_ratio, training, silu_u, concat_u, concat_x,
+                         mul_u_activation_type, seed, save_y, BLOCK_D):
+    parts = 1 + int(bool(concat_u)) + int(bool(concat_x))
+    rows, cols = x.shape
+    y = x.new_empty((rows, parts * cols)) if save_y else x.new_empty((0,))
+    stat = lambda: x.new_empty((rows,), dtype=torch.float32)  # noqa: E731
+    return y, stat(), stat(), stat(), x.new_empty((rows, parts * cols), dtype=torch.float8_e4m3fn)
+
+
+_LIBDEF.impl("b200_weighted_layer_norm_fwd", _layer_norm_cuda, "CUDA")
+_LIBDEF.impl("b200_layer_norm_mul_dropout_quantization_fwd", _layer_norm_mul_cuda, "CUDA")
+torch.library.register_fake("recir::b200_weighted_layer_norm_fwd", _layer_norm_fake)
+torch.library.register_fake("recir::b200_layer_norm_mul_dropout_quantization_fwd", _layer_norm_mul_fake)

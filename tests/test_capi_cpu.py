@@ -15,9 +15,13 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def _header_functions():
-    text = open(os.path.join(ROOT, "include", "b200_hstu.h")).read()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(b200_hstu_[a-z0-9_]+)\s*\(", text)))
+    """Every function declared in include/*.h."""
+    names = set()
+    for header in ("b200_hstu.h", "b200_stu_rowwise.h"):
+        text = open(os.path.join(ROOT, "include", header)).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names |= set(re.findall(r"\b(b200_(?:hstu|stu)_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)
 
 
 def test_library_loads_and_exports_every_declared_symbol():
@@ -25,7 +29,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     names = _header_functions()
     assert len(names) >= 12
     for n in names:
-        assert hasattr(lib, n), f"{n} declared in include/b200_hstu.h but not exported"
+        assert hasattr(lib, n), f"{n} declared in include/*.h but not exported"
     assert set(names) == set(_lib.EXPORTS)
 
 
@@ -147,3 +151,21 @@ def test_row_and_column_interval_masks_equal_the_keep_rule(seed):
         got = (ids == diag) | ((ids >= a_lo) & (ids < a_hi)) | (ids >= b_lo)
         want = keep[:, n] if n < L else np.zeros(L, bool)
         assert (got == want).all(), (n, list(out))
+
+
+def test_rowwise_params_validation_without_a_gpu():
+    """Argument checks of the row-wise entry points run on the host before any launch."""
+    lib = _lib.load()
+    p = _lib.B200RowwiseParams()
+    assert lib.b200_stu_layer_norm_fwd(ctypes.byref(p), None) == -6  # struct_size mismatch
+    p.struct_size = ctypes.sizeof(p)
+    p.dtype, p.rows, p.cols = _lib.BF16, 4, 20
+    assert lib.b200_stu_layer_norm_fwd(ctypes.byref(p), None) == -2  # cols not a multiple of 8
+    p.cols = 4096
+    assert lib.b200_stu_layer_norm_fwd(ctypes.byref(p), None) == -2  # too wide
+    p.cols = 64
+    assert lib.b200_stu_layer_norm_fwd(ctypes.byref(p), None) == -1  # null pointers
+    assert lib.b200_stu_layer_norm_mul_parts(0) == 1
+    assert lib.b200_stu_layer_norm_mul_parts(_lib.ROWWISE_CONCAT_U | _lib.ROWWISE_CONCAT_X) == 3
+    p.rows = 0
+    assert lib.b200_stu_layer_norm_fwd(ctypes.byref(p), None) == 0  # nothing to do, nothing launched

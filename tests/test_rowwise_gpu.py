@@ -1,0 +1,130 @@
+"""GPU parity of the row-wise STU kernels (through the torch operators -> C ABI) against the golden
+vectors made by the reference's compiled operators and against the numpy restatement.
+
+Tolerances (floating point): float32 results within 2e-6 absolute of O(1) values; 16-bit results
+equal to the reference up to one unit in the last place on at most 0.1 % of the elements (the
+reference's vectorised exp and this kernel's expf can differ in the last float32 bit before a
+rounding); fp8 codes identical except for such boundary cases (at most 0.2 %), never by more than
+one code."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import recir_b200  # noqa: F401
+from oracle import rowwise_oracle as ro
+
+pytestmark = pytest.mark.gpu
+GOLD = np.load(os.path.join(os.path.dirname(__file__), "golden", "rowwise_golden.npz"))
+LN = sorted({k.split("/")[0] for k in GOLD.files if k.startswith("ln_")})
+MUL = sorted({k.split("/")[0] for k in GOLD.files if k.startswith("mul_")})
+DT = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}
+ULP = {"float32": 2e-6, "bfloat16": 2.0 ** -7, "float16": 2.0 ** -10}
+
+
+def _t(a, dt=None):
+    t = torch.as_tensor(np.asarray(a))
+    return (t.to(DT[dt]) if dt else t).cuda()
+
+
+def _close(got, want, dtype, what):
+    got, want = got.float().cpu().numpy().astype(np.float64), np.asarray(want, np.float64)
+    assert got.shape == want.shape, what
+    if got.size == 0:
+        return
+    tol = ULP[dtype] * np.maximum(np.abs(want), 1.0 if dtype == "float32" else 1e-3)
+    bad = np.abs(got - want) > tol
+    assert bad.mean() <= 1e-3, f"{what}: {bad.sum()} of {bad.size} beyond one ulp"
+    assert np.abs(got - want).max() <= 4 * tol.max(), what
+
+
+def _codes_close(got, want, what):
+    got, want = got.view(torch.uint8).cpu().numpy(), np.asarray(want)
+    assert got.shape == want.shape, what
+    diff = got != want
+    assert diff.mean() <= 2e-3, f"{what}: {diff.sum()} of {diff.size} fp8 codes differ"
+    if diff.any():
+        assert np.abs((got & 0x7F).astype(np.int16) - (want & 0x7F).astype(np.int16))[diff].max() <= 1, what
+
+
+@pytest.mark.parametrize("name", LN)
+def test_layer_norm_matches_reference_golden(name):
+    dt, affine, swish, stats_in = GOLD[f"{name}/cfg"]
+    x = _t(GOLD[f"{name}/x"], dt)
+    w = _t(GOLD[f"{name}/w"], dt) if affine == "1" else None
+    b = _t(GOLD[f"{name}/b"], dt) if affine == "1" else None
+    m_in = _t(GOLD[f"{name}/mean_in"]) if stats_in == "1" else None
+    r_in = _t(GOLD[f"{name}/rstd_in"]) if stats_in == "1" else None
+    y, mean, rstd = torch.ops.recir.b200_weighted_layer_norm_fwd(x, w, b, 1e-5, m_in, r_in, swish == "1")
+    torch.cuda.synchronize()
+    _close(y, GOLD[f"{name}/y"], dt, "y")
+    _close(mean, GOLD[f"{name}/mean"], "float32", "mean")
+    _close(rstd, GOLD[f"{name}/rstd"], "float32", "rstd")
+
+
+@pytest.mark.parametrize("name", MUL)
+def test_layer_norm_mul_matches_reference_golden(name):
+    dt, silu_u, cat_u, cat_x, act = GOLD[f"{name}/cfg"]
+    args = [_t(GOLD[f"{name}/{k}"], dt) for k in ("x", "u", "w", "b")]
+    y, mean, rstd, scale, q8 = torch.ops.recir.b200_layer_norm_mul_dropout_quantization_fwd(
+        *args, 1e-5, 0.0, False, silu_u == "1", cat_u == "1", cat_x == "1", str(act), 0, True, 0)
+    torch.cuda.synchronize()
+    _close(y, GOLD[f"{name}/y"], dt, "y")
+    _close(mean, GOLD[f"{name}/mean"], "float32", "mean")
+    _close(rstd, GOLD[f"{name}/rstd"], "float32", "rstd")
+    _close(scale, GOLD[f"{name}/scale"], "float32", "scale")
+    _codes_close(q8, GOLD[f"{name}/q8"], "q8")
+    # save_y == False: no y, same fp8 copy
+    y2, _, _, scale2, q82 = torch.ops.recir.b200_layer_norm_mul_dropout_quantization_fwd(
+        *args, 1e-5, 0.0, False, silu_u == "1", cat_u == "1", cat_x == "1", str(act), 0, False, 0)
+    assert y2.numel() == 0 and torch.equal(q82.view(torch.uint8), q8.view(torch.uint8)) and torch.equal(scale2, scale)
+
+
+def test_full_size_rows_against_the_oracle_and_strided_input():
+    """Benchmark-sized rows (embedding 512, bf16): a sample of rows against the numpy restatement,
+    every row through row-wise invariants, and a strided (column-sliced) input."""
+    g = torch.Generator().manual_seed(3)
+    rows, cols = 78262, 512
+    big = (torch.randn(rows, 2 * cols, generator=g) * 1.3).to(torch.bfloat16).cuda()
+    x, u = big[:, :cols], big[:, cols:]  # row stride 1024: two column slices of one buffer
+    w = (torch.randn(cols, generator=g) * 0.5 + 1).to(torch.bfloat16).cuda()
+    b = (torch.randn(cols, generator=g) * 0.2).to(torch.bfloat16).cuda()
+    y, mean, rstd = torch.ops.recir.b200_weighted_layer_norm_fwd(x, w, b, 1e-6, None, None, True)
+    ym, _, _, scale, q8 = torch.ops.recir.b200_layer_norm_mul_dropout_quantization_fwd(
+        x, u, w, b, 1e-6, 0.0, False, True, True, False, "silu", 0, True, 0)
+    torch.cuda.synchronize()
+    sel = torch.arange(0, rows, 997)
+    f = lambda t: t[sel.to(t.device)].float().cpu().numpy()
+    ry, rm, rr = ro.weighted_layer_norm(f(x), w.float().cpu().numpy(), b.float().cpu().numpy(), 1e-6, "bfloat16",
+                                        is_swish=True)
+    _close(y[sel.cuda()], ry, "bfloat16", "y sample")
+    _close(mean[sel.cuda()], rm, "float32", "mean sample")
+    ryy, _, _, rs, rq = ro.layer_norm_mul_quantized(f(x), f(u), w.float().cpu().numpy(), b.float().cpu().numpy(), 1e-6,
+                                                    "bfloat16", silu_u=True, concat_u=True, mul_u_activation="silu")
+    _close(ym[sel.cuda()], ryy, "bfloat16", "mul sample")
+    _close(scale[sel.cuda()], rs, "float32", "scale sample")
+    _codes_close(q8[sel.cuda()], rq, "q8 sample")
+    # invariants over every row: statistics against torch, the fp8 copy spans its full range in each row
+    xf = x.float()
+    assert torch.allclose(mean, xf.mean(1), atol=1e-5)
+    assert torch.allclose(rstd, torch.rsqrt(xf.var(1, unbiased=False) + 1e-6), rtol=1e-4)
+    assert int((q8.view(torch.uint8) & 0x7F).max(dim=1).values.min()) == 0x7E
+
+
+def test_validation_and_fake_kernels():
+    x = torch.zeros(4, 20, device="cuda")
+    with pytest.raises(ValueError, match="multiple of 8"):
+        torch.ops.recir.b200_weighted_layer_norm_fwd(x, None, None, 1e-5, None, None, False)
+    x = torch.zeros(4, 16, device="cuda")
+    with pytest.raises(ValueError, match="is_swish requires"):
+        torch.ops.recir.b200_weighted_layer_norm_fwd(x, None, None, 1e-5, None, None, True)
+    with pytest.raises(ValueError, match="bias is required"):
+        torch.ops.recir.b200_weighted_layer_norm_fwd(x, torch.ones(16, device="cuda"), None, 1e-5, None, None, False)
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    with FakeTensorMode():
+        xf = torch.empty(6, 32, dtype=torch.bfloat16, device="cuda")
+        wf = torch.empty(32, dtype=torch.bfloat16, device="cuda")
+        out = torch.ops.recir.b200_layer_norm_mul_dropout_quantization_fwd(
+            xf, xf, wf, wf, 1e-5, 0.0, False, True, True, True, "silu", 0, True, 0)
+    assert out[0].shape == (6, 96) and out[4].dtype == torch.float8_e4m3fn and out[3].shape == (6,)

@@ -1,0 +1,69 @@
+"""The numpy restatement of the reference's row-wise STU operators against golden vectors made by
+the reference's own compiled operators (tests/golden/make_rowwise_golden.py)."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import rowwise_oracle as ro
+
+GOLD = np.load(os.path.join(os.path.dirname(__file__), "golden", "rowwise_golden.npz"))
+LN = sorted({k.split("/")[0] for k in GOLD.files if k.startswith("ln_")})
+MUL = sorted({k.split("/")[0] for k in GOLD.files if k.startswith("mul_")})
+# one unit in the last place of the case's dtype, relative
+ULP = {"float32": 2e-6, "bfloat16": 2.0 ** -7, "float16": 2.0 ** -10}
+
+
+def _close(got, want, dtype, what):
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    assert got.shape == want.shape, what
+    if got.size == 0:
+        return
+    # float32: results are sums of O(1) terms, so the error is absolute; 16-bit: one last-place flip
+    tol = ULP[dtype] * np.maximum(np.abs(want), 1.0 if dtype == "float32" else 1e-3)
+    bad = np.abs(got - want) > tol
+    # the restatement reproduces the reference's roundings: at most a stray last-place flip
+    assert bad.mean() <= 1e-3, f"{what}: {bad.sum()} of {bad.size} beyond one ulp"
+    assert np.abs(got - want).max() <= 4 * tol.max(), what
+
+
+@pytest.mark.parametrize("name", LN)
+def test_layer_norm_matches_reference(name):
+    dt, affine, swish, stats_in = GOLD[f"{name}/cfg"]
+    x = GOLD[f"{name}/x"]
+    w = GOLD[f"{name}/w"] if affine == "1" else None
+    b = GOLD[f"{name}/b"] if affine == "1" else None
+    kw = dict(mean=GOLD[f"{name}/mean_in"], rstd=GOLD[f"{name}/rstd_in"]) if stats_in == "1" else {}
+    y, mean, rstd = ro.weighted_layer_norm(x, w, b, 1e-5, dt, is_swish=swish == "1", **kw)
+    _close(y, GOLD[f"{name}/y"], dt, "y")
+    _close(mean, GOLD[f"{name}/mean"], "float32", "mean")
+    _close(rstd, GOLD[f"{name}/rstd"], "float32", "rstd")
+
+
+@pytest.mark.parametrize("name", MUL)
+def test_layer_norm_mul_matches_reference(name):
+    dt, silu_u, cat_u, cat_x, act = GOLD[f"{name}/cfg"]
+    y, mean, rstd, scale, q8 = ro.layer_norm_mul_quantized(
+        GOLD[f"{name}/x"], GOLD[f"{name}/u"], GOLD[f"{name}/w"], GOLD[f"{name}/b"], 1e-5, dt,
+        silu_u=silu_u == "1", concat_u=cat_u == "1", concat_x=cat_x == "1", mul_u_activation=act)
+    _close(y, GOLD[f"{name}/y"], dt, "y")
+    _close(mean, GOLD[f"{name}/mean"], "float32", "mean")
+    _close(rstd, GOLD[f"{name}/rstd"], "float32", "rstd")
+    _close(scale, GOLD[f"{name}/scale"], "float32", "scale")
+    want = GOLD[f"{name}/q8"]
+    assert q8.shape == want.shape
+    # e4m3 codes: identical except where the value sat within rounding noise of a code boundary
+    diff = q8.astype(np.int16) != want.astype(np.int16)
+    assert diff.mean() <= 2e-3, f"{diff.sum()} of {diff.size} fp8 codes differ"
+    mag = np.abs((q8 & 0x7F).astype(np.int16) - (want & 0x7F).astype(np.int16))
+    assert mag.max() <= 1 and ((q8 ^ want) & 0x80)[mag > 0].sum() == 0 or diff.sum() == 0
+
+
+def test_e4m3_known_codes():
+    # float8 e4m3fn: bias 7, 3 mantissa bits, subnormal step 2^-9, largest finite 448 = 0x7E
+    vals = np.array([0.0, 2.0 ** -9, 2.0 ** -6, 1.0, 1.5, 448.0, -448.0, -1.0, 0.0625 * 1.125], np.float32)
+    want = np.array([0x00, 0x01, 0x08, 0x38, 0x3C, 0x7E, 0xFE, 0xB8, 0x19], np.uint8)
+    assert (ro.e4m3_encode(vals) == want).all()
+    # ties go to the even code: halfway between 1.0 (0x38) and 1.125 (0x39) -> 0x38
+    assert ro.e4m3_encode(np.array([1.0625], np.float32))[0] == 0x38
+    assert ro.e4m3_encode(np.array([1.1875], np.float32))[0] == 0x3A
