@@ -46,6 +46,8 @@ def main():
 
     el = args.rows * cols
     cases = {
+        "layer_norm_affine": (lambda: torch.ops.recir.b200_weighted_layer_norm_fwd(x, w, b, 1e-6, None, None, False),
+                              2 * el * 2 + 8 * args.rows),
         "layer_norm_swish": (lambda: torch.ops.recir.b200_weighted_layer_norm_fwd(x, w, b, 1e-6, None, None, True),
                              2 * el * 2 + 8 * args.rows),
         "layer_norm_mul_silu (y only counted)": (
