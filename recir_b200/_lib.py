@@ -27,6 +27,8 @@ EXPORTS = (
     "b200_hstu_debug_col_mask", "b200_hstu_last_cuda_error",
     # include/b200_stu_rowwise.h
     "b200_stu_layer_norm_fwd", "b200_stu_layer_norm_mul_fwd", "b200_stu_layer_norm_mul_parts",
+    # include/b200_stu_jagged.h
+    "b200_stu_jagged_copy",
 )
 STATIC_SCRATCH_BYTES = 4 << 20
 
@@ -86,6 +88,26 @@ class B200RowwiseParams(ctypes.Structure):
     ]
 
 
+# modes of include/b200_stu_jagged.h
+JAGGED_TO_PADDED_DENSE, DENSE_TO_JAGGED, JAGGED_CONCAT, JAGGED_SPLIT_LEFT, JAGGED_SPLIT_RIGHT = range(5)
+JAGGED_OFFSETS_I64 = 0x1
+
+
+class B200JaggedParams(ctypes.Structure):
+    """Mirror of ``struct B200JaggedParams`` (include/b200_stu_jagged.h)."""
+
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32), ("flags", ctypes.c_uint32),
+        ("mode", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("num_seqs", ctypes.c_int64), ("padded_len", ctypes.c_int64), ("dst_rows", ctypes.c_int64),
+        ("src0_rows", ctypes.c_int64), ("src1_rows", ctypes.c_int64), ("row_bytes", ctypes.c_int64),
+        ("dst_row_stride", ctypes.c_int64), ("src0_row_stride", ctypes.c_int64), ("src1_row_stride", ctypes.c_int64),
+        ("src0", ctypes.c_void_p), ("src1", ctypes.c_void_p), ("dst", ctypes.c_void_p),
+        ("offsets0", ctypes.c_void_p), ("offsets1", ctypes.c_void_p),
+        ("pad", ctypes.c_ubyte * 16),
+    ]
+
+
 _lib = None
 
 
@@ -138,6 +160,8 @@ def load() -> ctypes.CDLL:
         fn.restype = ctypes.c_int
     lib.b200_stu_layer_norm_mul_parts.argtypes = [ctypes.c_uint32]
     lib.b200_stu_layer_norm_mul_parts.restype = ctypes.c_int
+    lib.b200_stu_jagged_copy.argtypes = [ctypes.POINTER(B200JaggedParams), ctypes.c_void_p]
+    lib.b200_stu_jagged_copy.restype = ctypes.c_int
     if lib.b200_hstu_params_size() != ctypes.sizeof(B200HstuParams):
         raise RuntimeError("B200HstuParams layout mismatch between Python binding and library")
     _lib = lib

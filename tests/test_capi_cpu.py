@@ -17,7 +17,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def _header_functions():
     """Every function declared in include/*.h."""
     names = set()
-    for header in ("b200_hstu.h", "b200_stu_rowwise.h"):
+    for header in ("b200_hstu.h", "b200_stu_rowwise.h", "b200_stu_jagged.h"):
         text = open(os.path.join(ROOT, "include", header)).read()
         text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
         names |= set(re.findall(r"\b(b200_(?:hstu|stu)_[a-z0-9_]+)\s*\(", text))
@@ -169,3 +169,18 @@ def test_rowwise_params_validation_without_a_gpu():
     assert lib.b200_stu_layer_norm_mul_parts(_lib.ROWWISE_CONCAT_U | _lib.ROWWISE_CONCAT_X) == 3
     p.rows = 0
     assert lib.b200_stu_layer_norm_fwd(ctypes.byref(p), None) == 0  # nothing to do, nothing launched
+
+
+def test_jagged_params_validation_without_a_gpu():
+    lib = _lib.load()
+    p = _lib.B200JaggedParams()
+    assert lib.b200_stu_jagged_copy(ctypes.byref(p), None) == -6  # struct_size mismatch
+    p.struct_size = ctypes.sizeof(p)
+    p.mode, p.row_bytes = 7, 16
+    assert lib.b200_stu_jagged_copy(ctypes.byref(p), None) == -1  # unknown mode
+    p.mode, p.row_bytes = _lib.JAGGED_CONCAT, 3
+    assert lib.b200_stu_jagged_copy(ctypes.byref(p), None) == -1  # odd row size
+    p.row_bytes, p.dst_rows = 16, 0
+    assert lib.b200_stu_jagged_copy(ctypes.byref(p), None) == 0   # nothing to write, nothing launched
+    p.dst_rows, p.num_seqs = 4, 2
+    assert lib.b200_stu_jagged_copy(ctypes.byref(p), None) == -1  # null pointers
