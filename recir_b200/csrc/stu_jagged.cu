@@ -2,9 +2,11 @@
 // Reference: recir/ops/jagged_ops.py:29-66 (jagged_to_padded_dense), :69-109 (dense_to_jagged),
 // :218-250 (concat_2d_jagged), :253-277 (split_2d_jagged).  Byte copies, so any element type.
 //
-// One warp per destination row: lane 0 finds the source row (a binary search over the B + 1
-// offsets where the rule needs the sequence of a packed position), the warp copies the row in
-// 16-byte pieces (2-byte pieces for rows or pointers that are not 16-byte aligned).
+// A warp takes one destination row at a time (persistent CTAs, rows strided over all warps): lane 0
+// finds the source row (a binary search over the B + 1 offsets where the rule needs the sequence
+// of a packed position), the warp copies the row in 16-byte pieces (2-byte pieces for rows or
+// pointers that are not 16-byte aligned).  When they fit, the offsets are copied to shared memory
+// once per CTA so that the searches do not wait on global memory.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -44,9 +46,11 @@ __device__ __forceinline__ long long upper_bound(F f, long long first, long long
 }
 
 // Source of destination row r: which = 0 (src0), 1 (src1), 2 (padding pattern), 3 (zeros).
-__device__ __forceinline__ void locate(const Args& a, long long r, int& which, long long& src) {
-  auto o0 = [&](long long i) { return off_at(a.off0, a.i64, i); };
-  auto o1 = [&](long long i) { return off_at(a.off1, a.i64, i); };
+template <bool SMEM>
+__device__ __forceinline__ void locate(const Args& a, const long long* sm0, const long long* sm1, long long r, int& which,
+                                       long long& src) {
+  auto o0 = [&](long long i) { return SMEM ? sm0[i] : off_at(a.off0, a.i64, i); };
+  auto o1 = [&](long long i) { return SMEM ? sm1[i] : off_at(a.off1, a.i64, i); };
   which = 0;
   src = 0;
   switch (a.mode) {
@@ -93,32 +97,41 @@ __device__ __forceinline__ void locate(const Args& a, long long r, int& which, l
   }
 }
 
-template <bool VEC16>
+template <bool VEC16, bool SMEM>
 __global__ void __launch_bounds__(WARPS_PER_BLOCK * 32) jagged_copy_kernel(Args a) {
+  extern __shared__ long long sm_off[];
+  const long long* sm0 = sm_off;
+  const long long* sm1 = sm_off + (a.B + 1);
+  if (SMEM) {
+    for (long long i = threadIdx.x; i <= a.B; i += blockDim.x) {
+      sm_off[i] = off_at(a.off0, a.i64, i);
+      if (a.off1) sm_off[a.B + 1 + i] = off_at(a.off1, a.i64, i);
+    }
+    __syncthreads();
+  }
   const int lane = threadIdx.x & 31;
-  const long long r = static_cast<long long>(blockIdx.x) * WARPS_PER_BLOCK + (threadIdx.x >> 5);
-  if (r >= a.dst_rows) return;
-  int which = 0;
-  long long src = 0;
-  if (lane == 0) locate(a, r, which, src);
-  which = __shfl_sync(0xffffffffu, which, 0);
-  src = __shfl_sync(0xffffffffu, src, 0);
-  unsigned char* d = a.dst + r * a.dst_rs;
-  const unsigned char* s = which == 0 ? a.src0 + src * a.src0_rs : (which == 1 ? a.src1 + src * a.src1_rs : nullptr);
-  if (VEC16) {
-    const long long nv = a.row_bytes >> 4;
-    const uint4 fill = which == 2 ? a.pad : make_uint4(0u, 0u, 0u, 0u);
-    for (long long v = lane; v < nv; v += 32)
-      reinterpret_cast<uint4*>(d)[v] = s ? __ldg(reinterpret_cast<const uint4*>(s) + v) : fill;
-  } else {
-    const long long nv = a.row_bytes >> 1;
-    const unsigned short fill = which == 2 ? static_cast<unsigned short>(a.pad.x & 0xffffu) : static_cast<unsigned short>(0);
-    // 4-byte elements are written as two 2-byte halves of the padding pattern
-    for (long long v = lane; v < nv; v += 32) {
-      unsigned short x = fill;
-      if (s) x = reinterpret_cast<const unsigned short*>(s)[v];
-      else if (which == 2) x = reinterpret_cast<const unsigned short*>(&a.pad)[v & 7];
-      reinterpret_cast<unsigned short*>(d)[v] = x;
+  const long long warps = static_cast<long long>(gridDim.x) * WARPS_PER_BLOCK;
+  for (long long r = static_cast<long long>(blockIdx.x) * WARPS_PER_BLOCK + (threadIdx.x >> 5); r < a.dst_rows; r += warps) {
+    int which = 0;
+    long long src = 0;
+    if (lane == 0) locate<SMEM>(a, sm0, sm1, r, which, src);
+    which = __shfl_sync(0xffffffffu, which, 0);
+    src = __shfl_sync(0xffffffffu, src, 0);
+    unsigned char* d = a.dst + r * a.dst_rs;
+    const unsigned char* s = which == 0 ? a.src0 + src * a.src0_rs : (which == 1 ? a.src1 + src * a.src1_rs : nullptr);
+    if (VEC16) {
+      const long long nv = a.row_bytes >> 4;
+      const uint4 fill = which == 2 ? a.pad : make_uint4(0u, 0u, 0u, 0u);
+      for (long long v = lane; v < nv; v += 32)
+        reinterpret_cast<uint4*>(d)[v] = s ? __ldg(reinterpret_cast<const uint4*>(s) + v) : fill;
+    } else {
+      const long long nv = a.row_bytes >> 1;
+      for (long long v = lane; v < nv; v += 32) {
+        unsigned short x = 0;
+        if (s) x = reinterpret_cast<const unsigned short*>(s)[v];
+        else if (which == 2) x = reinterpret_cast<const unsigned short*>(&a.pad)[v & 7];  // 2-byte pieces of the pattern
+        reinterpret_cast<unsigned short*>(d)[v] = x;
+      }
     }
   }
 }
@@ -161,9 +174,19 @@ extern "C" int b200_stu_jagged_copy(const B200JaggedParams* p, void* stream) {
   a.mode = p->mode; a.i64 = (p->flags & B200_JAGGED_FLAG_OFFSETS_I64) ? 1 : 0;
   a.pad = *reinterpret_cast<const uint4*>(p->pad);
   hstu::set_error_stage("jagged row copy kernel");
-  const unsigned grid = static_cast<unsigned>((a.dst_rows + WARPS_PER_BLOCK - 1) / WARPS_PER_BLOCK);
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long want = (a.dst_rows + WARPS_PER_BLOCK - 1) / WARPS_PER_BLOCK, cap = static_cast<long long>(sms) * 8;
+  const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
+  const size_t smem = static_cast<size_t>(a.B + 1) * sizeof(long long) * (two_offsets ? 2 : 1);
+  const bool use_smem = smem <= 40 * 1024 && want > cap;  // worth it only when a CTA handles many rows
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (vec) jagged_copy_kernel<true><<<grid, WARPS_PER_BLOCK * 32, 0, st>>>(a);
-  else jagged_copy_kernel<false><<<grid, WARPS_PER_BLOCK * 32, 0, st>>>(a);
+  if (use_smem) {
+    if (vec) jagged_copy_kernel<true, true><<<grid, WARPS_PER_BLOCK * 32, smem, st>>>(a);
+    else jagged_copy_kernel<false, true><<<grid, WARPS_PER_BLOCK * 32, smem, st>>>(a);
+  } else {
+    if (vec) jagged_copy_kernel<true, false><<<grid, WARPS_PER_BLOCK * 32, 0, st>>>(a);
+    else jagged_copy_kernel<false, false><<<grid, WARPS_PER_BLOCK * 32, 0, st>>>(a);
+  }
   return cudaGetLastError() == cudaSuccess ? B200_HSTU_OK : B200_HSTU_ELAUNCH;
 }

@@ -161,7 +161,9 @@ def _j2d_setup(ctx, inputs, output):
 
 def _j2d_backward(ctx, grad):
     g, _ = torch.ops.recir.b200_dense_to_jagged(grad.contiguous(), ctx.offsets, ctx.total)
-    return g, None, None, None
+    # trailing arguments left at their defaults are not passed on by the dispatcher, so the number of
+    # non-tensor slots varies with the call
+    return (g, [None] * len(ctx.offsets)) + (None,) * (len(ctx.needs_input_grad) - 2)
 
 
 def _d2j_setup(ctx, inputs, output):
@@ -170,7 +172,8 @@ def _d2j_setup(ctx, inputs, output):
 
 
 def _d2j_backward(ctx, grad, _grad_offsets):
-    return torch.ops.recir.b200_jagged_to_padded_dense(grad.contiguous(), ctx.offsets, [ctx.n], 0.0), None, None
+    g = torch.ops.recir.b200_jagged_to_padded_dense(grad.contiguous(), ctx.offsets, [ctx.n], 0.0)
+    return (g, [None] * len(ctx.offsets)) + (None,) * (len(ctx.needs_input_grad) - 2)
 
 
 def _concat_setup(ctx, inputs, output):
