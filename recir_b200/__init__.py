@@ -4,7 +4,7 @@ Importing this package registers the ``recir::b200_*`` operators; the kernels li
 ``libb200_hstu.so`` (C ABI in ``include/b200_hstu.h``), built by ``python -m recir_b200.build``.
 """
 from .ops import hstu_attention, hstu_attention_backward, validate_inputs  # noqa: F401
-from . import jagged_ops, rowwise_ops, sharding, workload  # noqa: F401
+from . import embed_ops, jagged_ops, rowwise_ops, sharding, workload  # noqa: F401
 from .host_api import HostPipeline  # noqa: F401
 
 __all__ = ["hstu_attention", "hstu_attention_backward", "validate_inputs", "sharding", "workload", "HostPipeline"]

@@ -29,6 +29,8 @@ EXPORTS = (
     "b200_stu_layer_norm_fwd", "b200_stu_layer_norm_mul_fwd", "b200_stu_layer_norm_mul_parts",
     # include/b200_stu_jagged.h
     "b200_stu_jagged_copy",
+    # include/b200_stu_embed.h
+    "b200_stu_add_ts_pos_emb",
 )
 STATIC_SCRATCH_BYTES = 4 << 20
 
@@ -108,6 +110,27 @@ class B200JaggedParams(ctypes.Structure):
     ]
 
 
+# flags of include/b200_stu_embed.h
+EMBED_OFFSETS_I64, EMBED_LENGTHS_I64, EMBED_INTERLEAVE, EMBED_SQRT, EMBED_TABLES_F32 = 0x1, 0x2, 0x4, 0x8, 0x10
+
+
+class B200EmbedParams(ctypes.Structure):
+    """Mirror of ``struct B200EmbedParams`` (include/b200_stu_embed.h)."""
+
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32), ("flags", ctypes.c_uint32),
+        ("dtype", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("rows", ctypes.c_int64), ("cols", ctypes.c_int64), ("num_seqs", ctypes.c_int64),
+        ("pos_rows", ctypes.c_int64), ("ts_cols", ctypes.c_int64), ("max_contextual_seq_len", ctypes.c_int64),
+        ("x_row_stride", ctypes.c_int64), ("out_row_stride", ctypes.c_int64),
+        ("pos_row_stride", ctypes.c_int64), ("ts_table_row_stride", ctypes.c_int64),
+        ("x", ctypes.c_void_p), ("pos_table", ctypes.c_void_p), ("ts_table", ctypes.c_void_p),
+        ("timestamps", ctypes.c_void_p), ("seq_offsets", ctypes.c_void_p), ("seq_lengths", ctypes.c_void_p),
+        ("num_targets", ctypes.c_void_p), ("out", ctypes.c_void_p),
+        ("pos_index", ctypes.c_void_p), ("ts_index", ctypes.c_void_p),
+    ]
+
+
 _lib = None
 
 
@@ -160,6 +183,8 @@ def load() -> ctypes.CDLL:
         fn.restype = ctypes.c_int
     lib.b200_stu_layer_norm_mul_parts.argtypes = [ctypes.c_uint32]
     lib.b200_stu_layer_norm_mul_parts.restype = ctypes.c_int
+    lib.b200_stu_add_ts_pos_emb.argtypes = [ctypes.POINTER(B200EmbedParams), ctypes.c_void_p]
+    lib.b200_stu_add_ts_pos_emb.restype = ctypes.c_int
     lib.b200_stu_jagged_copy.argtypes = [ctypes.POINTER(B200JaggedParams), ctypes.c_void_p]
     lib.b200_stu_jagged_copy.restype = ctypes.c_int
     if lib.b200_hstu_params_size() != ctypes.sizeof(B200HstuParams):

@@ -1,4 +1,4 @@
-"""Time the jagged marshalling kernels on the current GPU and print their HBM throughput.
+"""Time the jagged marshalling kernels and the embedding add on the current GPU and print their HBM throughput.
 
     python -m recir_b200.run_jagged --batch 1024
 
@@ -55,6 +55,15 @@ def main():
         "split_2d_jagged": (lambda: ops.b200_split_2d_jagged(x, hist_off, tgt_off, left.shape[0], right.shape[0]), 2 * T * row),
         "concat_2d_jagged": (lambda: ops.b200_concat_2d_jagged(left, hist_off, right, tgt_off), 2 * T * row),
     }
+    # position + timestamp embedding add: x read, out written, two table rows per token (L2-resident tables)
+    g = torch.Generator().manual_seed(0)
+    pos_t = torch.randn(n + 8, args.cols, generator=g).to(torch.bfloat16).to(dev)
+    ts_t = torch.randn(2049, args.cols, generator=g).to(torch.bfloat16).to(dev)
+    stamps = (torch.cumsum(torch.exp(torch.rand(b, n, generator=g) * 12.0).to(torch.int64), dim=1) + 1_600_000_000).to(dev)
+    lens_d, tg_d = lengths.to(dev), torch.as_tensor(tg).to(dev)
+    cases["add_ts_pos_emb"] = (
+        lambda: ops.b200_add_ts_pos_emb_fwd(x, off, pos_t, ts_t, stamps, lens_d, tg_d, n, 0, False, "sqrt"),
+        2 * T * row + 8 * T + 8 * T)
     out = {"B": b, "T": T, "N": n, "cols": args.cols, "dtype": "bf16"}
     for name, (fn, nbytes) in cases.items():
         ms = timed(fn)
