@@ -32,6 +32,8 @@ _LIBDEF.define(
     "float dropout_ratio, bool training, bool silu_u, bool concat_u, bool concat_x, str mul_u_activation_type, "
     "int seed, bool save_y, int BLOCK_D) -> (Tensor, Tensor, Tensor, Tensor, Tensor)")
 
+_LIBDEF.define("b200_addmm_fwd(Tensor x, Tensor w, Tensor y) -> Tensor")
+
 # Kernel launches issued through this module since import.
 launch_counter = 0
 
@@ -162,3 +164,24 @@ _LIBDEF.impl("b200_weighted_layer_norm_fwd", _layer_norm_cuda, "CUDA")
 _LIBDEF.impl("b200_layer_norm_mul_dropout_quantization_fwd", _layer_norm_mul_cuda, "CUDA")
 torch.library.register_fake("recir::b200_weighted_layer_norm_fwd", _layer_norm_fake)
 torch.library.register_fake("recir::b200_layer_norm_mul_dropout_quantization_fwd", _layer_norm_mul_fake)
+
+
+def _addmm_cuda(x, w, y):
+    """The u/v/q/k and output projections of an STU layer: ``y + x @ w``.  A plain GEMM, handed to the
+    vendor library (``generative_recommenders::triton_addmm_fwd``,
+    ``recir/ops/kjt_split_per_feature.cpp:246-262``, does the same with ``at::addmm``)."""
+    if x.dim() != 2 or w.dim() != 2:
+        raise ValueError("x and weight must be two-dimensional")
+    if x.shape[1] != w.shape[0]:
+        raise ValueError("x and weight dimensions are incompatible")
+    if not ((y.dim() == 1 and y.shape[0] == w.shape[1]) or (y.dim() == 2 and y.shape[1] == w.shape[1])):
+        raise ValueError("bias dimensions are incompatible with the output")
+    return torch.addmm(y, x, w)
+
+
+def _addmm_fake(x, w, y):
+    return x.new_empty((x.shape[0], w.shape[1]))
+
+
+_LIBDEF.impl("b200_addmm_fwd", _addmm_cuda, "CUDA")
+torch.library.register_fake("recir::b200_addmm_fwd", _addmm_fake)

@@ -128,3 +128,13 @@ def test_validation_and_fake_kernels():
         out = torch.ops.recir.b200_layer_norm_mul_dropout_quantization_fwd(
             xf, xf, wf, wf, 1e-5, 0.0, False, True, True, True, "silu", 0, True, 0)
     assert out[0].shape == (6, 96) and out[4].dtype == torch.float8_e4m3fn and out[3].shape == (6,)
+
+
+def test_addmm_operator_is_the_library_gemm():
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(300, 64, generator=g).to(torch.bfloat16).cuda()
+    w = torch.randn(64, 96, generator=g).to(torch.bfloat16).cuda()
+    for y in (torch.randn(96, generator=g).to(torch.bfloat16).cuda(), torch.randn(300, 96, generator=g).to(torch.bfloat16).cuda()):
+        assert torch.equal(torch.ops.recir.b200_addmm_fwd(x, w, y), torch.addmm(y, x, w))
+    with pytest.raises(ValueError, match="incompatible"):
+        torch.ops.recir.b200_addmm_fwd(x, w[:32], y)
