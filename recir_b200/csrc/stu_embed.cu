@@ -1,8 +1,8 @@
 // Position + timestamp embedding add (HBM-bound gather-add).
 // Reference: addTimestampPositionEmbeddings, recir/ops/kjt_split_per_feature.cpp:307-428.
-// One warp per token (persistent CTAs): lane 0 finds the token's sequence (binary search over the
-// offsets, cached in shared memory when they fit), computes the position index and the time bucket,
-// the warp adds the two table rows to the token's row.  The bucket arithmetic follows the
+// Persistent CTAs; a warp takes 32 tokens at a time: each lane finds one token's sequence (binary search
+// over the offsets, cached in shared memory when they fit) and computes its position index and time
+// bucket, then the warp adds the two table rows to each token's row in turn.  The bucket arithmetic follows the
 // reference step by step in float32 (int64 difference -> float, max with 1e-6, division by 60,
 // log or sqrt, truncation, clamp to [0, 2048]); the sum of the two table rows is rounded to the
 // tables' dtype and then to x's dtype before it is added, as the reference's tensor ops do.
@@ -84,9 +84,13 @@ __global__ void __launch_bounds__(WARPS_PER_BLOCK * 32) add_ts_pos_emb_kernel(Ar
   const int lane = threadIdx.x & 31;
   const int nv = a.cols >> 3;
   const long long warps = static_cast<long long>(gridDim.x) * WARPS_PER_BLOCK;
-  for (long long r = static_cast<long long>(blockIdx.x) * WARPS_PER_BLOCK + (threadIdx.x >> 5); r < a.rows; r += warps) {
-    int pos = 0, tsb = 0, owned = 0;
-    if (lane == 0) {
+  // A warp takes 32 consecutive tokens at a time: every lane resolves one token's sequence, position
+  // index and time bucket (in parallel), then the warp processes the 32 rows one by one.
+  for (long long r0 = (static_cast<long long>(blockIdx.x) * WARPS_PER_BLOCK + (threadIdx.x >> 5)) * 32; r0 < a.rows;
+       r0 += warps * 32) {
+    int my_pos = 0, my_tsb = 0, my_owned = 0;
+    const long long r = r0 + lane;
+    if (r < a.rows) {
       // sequence of packed row r: the last b with offsets[b] <= r (empty sequences are skipped)
       long long lo = 0, hi = a.B;
       while (lo < hi) {
@@ -94,7 +98,7 @@ __global__ void __launch_bounds__(WARPS_PER_BLOCK * 32) add_ts_pos_emb_kernel(Ar
         if (off(mid + 1) <= r) lo = mid + 1; else hi = mid;
       }
       if (lo < a.B && off(lo) <= r) {
-        owned = 1;
+        my_owned = 1;
         const long long b = lo, i = r - off(b);
         const long long L = at_i(a.len, a.len64, b);
         long long high = L;
@@ -102,32 +106,34 @@ __global__ void __launch_bounds__(WARPS_PER_BLOCK * 32) add_ts_pos_emb_kernel(Ar
         long long p = high - (i < high ? i : high) + a.C;  // kjt_split_per_feature.cpp:376-377
         if (p > a.P - 1) p = a.P - 1;
         if (i < a.C) p = i;
-        pos = static_cast<int>(p);
+        my_pos = static_cast<int>(p);
         const long long* row = a.stamps + b * a.S;
         float d = static_cast<float>(row[L - 1] - row[i]);  // :385-389
         d = fmaxf(d, 1e-6f) / 60.0f;
         d = a.use_sqrt ? sqrtf(d) : logf(d);
         long long q = static_cast<long long>(d);  // truncation toward zero
-        tsb = static_cast<int>(q < 0 ? 0 : (q > 2048 ? 2048 : q));
+        my_tsb = static_cast<int>(q < 0 ? 0 : (q > 2048 ? 2048 : q));
+        a.pos_idx[r] = my_pos;  // coalesced: one index per lane
+        a.ts_idx[r] = my_tsb;
       }
     }
-    pos = __shfl_sync(0xffffffffu, pos, 0);
-    tsb = __shfl_sync(0xffffffffu, tsb, 0);
-    owned = __shfl_sync(0xffffffffu, owned, 0);
-    if (!owned) continue;  // rows past the last offset are not touched, as in the reference
-    if (lane == 0) { a.pos_idx[r] = pos; a.ts_idx[r] = tsb; }
-    const X* xr = reinterpret_cast<const X*>(a.x) + r * a.x_rs;
-    X* orow = reinterpret_cast<X*>(a.out) + r * a.out_rs;
-    const TAB* pr = reinterpret_cast<const TAB*>(a.pos) + static_cast<long long>(pos) * a.pos_rs;
-    const TAB* tr = reinterpret_cast<const TAB*>(a.ts) + static_cast<long long>(tsb) * a.ts_rs;
-    for (int v = lane; v < nv; v += 32) {
-      float xv[8], pv[8], tv[8], o[8];
-      load8<X>(xr + 8 * v, xv);
-      load8<TAB>(pr + 8 * v, pv);
-      load8<TAB>(tr + 8 * v, tv);
+    const int count = a.rows - r0 < 32 ? static_cast<int>(a.rows - r0) : 32;
+    for (int k = 0; k < count; ++k) {
+      const int pos = __shfl_sync(0xffffffffu, my_pos, k), tsb = __shfl_sync(0xffffffffu, my_tsb, k);
+      if (!__shfl_sync(0xffffffffu, my_owned, k)) continue;  // rows past the last offset are not touched
+      const X* xr = reinterpret_cast<const X*>(a.x) + (r0 + k) * a.x_rs;
+      X* orow = reinterpret_cast<X*>(a.out) + (r0 + k) * a.out_rs;
+      const TAB* pr = reinterpret_cast<const TAB*>(a.pos) + static_cast<long long>(pos) * a.pos_rs;
+      const TAB* tr = reinterpret_cast<const TAB*>(a.ts) + static_cast<long long>(tsb) * a.ts_rs;
+      for (int v = lane; v < nv; v += 32) {
+        float xv[8], pv[8], tv[8], o[8];
+        load8<X>(xr + 8 * v, xv);
+        load8<TAB>(pr + 8 * v, pv);
+        load8<TAB>(tr + 8 * v, tv);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = xv[i] + round_to<X>(round_to<TAB>(pv[i] + tv[i]));
-      store8<X>(orow + 8 * v, o);
+        for (int i = 0; i < 8; ++i) o[i] = xv[i] + round_to<X>(round_to<TAB>(pv[i] + tv[i]));
+        store8<X>(orow + 8 * v, o);
+      }
     }
   }
 }
@@ -167,10 +173,11 @@ extern "C" int b200_stu_add_ts_pos_emb(const B200EmbedParams* p, void* stream) {
   const bool tab32 = p->dtype == B200_HSTU_F32 || (p->flags & B200_EMBED_FLAG_TABLES_F32);
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const long long want = (a.rows + WARPS_PER_BLOCK - 1) / WARPS_PER_BLOCK, cap = static_cast<long long>(sms) * 8;
+  const long long per_block = static_cast<long long>(WARPS_PER_BLOCK) * 32;  // tokens one CTA takes per round
+  const long long want = (a.rows + per_block - 1) / per_block, cap = static_cast<long long>(sms) * 8;
   const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
   const size_t smem = static_cast<size_t>(a.B + 1) * sizeof(long long);
-  const bool use_smem = smem <= 40 * 1024 && want > cap;
+  const bool use_smem = smem <= 40 * 1024 && a.rows >= 16 * (a.B + 1);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   hstu::set_error_stage("position/timestamp embedding kernel");
 #define B200_EMBED_LAUNCH(X, TAB)                                                                   \

@@ -2,9 +2,9 @@
 // Reference: recir/ops/jagged_ops.py:29-66 (jagged_to_padded_dense), :69-109 (dense_to_jagged),
 // :218-250 (concat_2d_jagged), :253-277 (split_2d_jagged).  Byte copies, so any element type.
 //
-// A warp takes one destination row at a time (persistent CTAs, rows strided over all warps): lane 0
-// finds the source row (a binary search over the B + 1 offsets where the rule needs the sequence
-// of a packed position), the warp copies the row in 16-byte pieces (2-byte pieces for rows or
+// Persistent CTAs; a warp takes 32 consecutive destination rows at a time: each lane finds the source
+// of one row (a binary search over the B + 1 offsets where the rule needs the sequence of a packed
+// position), then the warp copies the rows one by one in 16-byte pieces (2-byte pieces for rows or
 // pointers that are not 16-byte aligned).  When they fit, the offsets are copied to shared memory
 // once per CTA so that the searches do not wait on global memory.
 #include <cuda_runtime.h>
@@ -111,26 +111,33 @@ __global__ void __launch_bounds__(WARPS_PER_BLOCK * 32) jagged_copy_kernel(Args 
   }
   const int lane = threadIdx.x & 31;
   const long long warps = static_cast<long long>(gridDim.x) * WARPS_PER_BLOCK;
-  for (long long r = static_cast<long long>(blockIdx.x) * WARPS_PER_BLOCK + (threadIdx.x >> 5); r < a.dst_rows; r += warps) {
-    int which = 0;
-    long long src = 0;
-    if (lane == 0) locate<SMEM>(a, sm0, sm1, r, which, src);
-    which = __shfl_sync(0xffffffffu, which, 0);
-    src = __shfl_sync(0xffffffffu, src, 0);
-    unsigned char* d = a.dst + r * a.dst_rs;
-    const unsigned char* s = which == 0 ? a.src0 + src * a.src0_rs : (which == 1 ? a.src1 + src * a.src1_rs : nullptr);
-    if (VEC16) {
-      const long long nv = a.row_bytes >> 4;
-      const uint4 fill = which == 2 ? a.pad : make_uint4(0u, 0u, 0u, 0u);
-      for (long long v = lane; v < nv; v += 32)
-        reinterpret_cast<uint4*>(d)[v] = s ? __ldg(reinterpret_cast<const uint4*>(s) + v) : fill;
-    } else {
-      const long long nv = a.row_bytes >> 1;
-      for (long long v = lane; v < nv; v += 32) {
-        unsigned short x = 0;
-        if (s) x = reinterpret_cast<const unsigned short*>(s)[v];
-        else if (which == 2) x = reinterpret_cast<const unsigned short*>(&a.pad)[v & 7];  // 2-byte pieces of the pattern
-        reinterpret_cast<unsigned short*>(d)[v] = x;
+  // A warp takes 32 consecutive destination rows at a time: every lane resolves the source of one
+  // row (the searches run in parallel instead of one after the other), then the warp copies the
+  // rows one by one.
+  for (long long r0 = (static_cast<long long>(blockIdx.x) * WARPS_PER_BLOCK + (threadIdx.x >> 5)) * 32; r0 < a.dst_rows;
+       r0 += warps * 32) {
+    int my_which = 3;
+    long long my_src = 0;
+    if (r0 + lane < a.dst_rows) locate<SMEM>(a, sm0, sm1, r0 + lane, my_which, my_src);
+    const int count = a.dst_rows - r0 < 32 ? static_cast<int>(a.dst_rows - r0) : 32;
+    for (int k = 0; k < count; ++k) {
+      const int which = __shfl_sync(0xffffffffu, my_which, k);
+      const long long src = __shfl_sync(0xffffffffu, my_src, k);
+      unsigned char* d = a.dst + (r0 + k) * a.dst_rs;
+      const unsigned char* s = which == 0 ? a.src0 + src * a.src0_rs : (which == 1 ? a.src1 + src * a.src1_rs : nullptr);
+      if (VEC16) {
+        const long long nv = a.row_bytes >> 4;
+        const uint4 fill = which == 2 ? a.pad : make_uint4(0u, 0u, 0u, 0u);
+        for (long long v = lane; v < nv; v += 32)
+          reinterpret_cast<uint4*>(d)[v] = s ? __ldg(reinterpret_cast<const uint4*>(s) + v) : fill;
+      } else {
+        const long long nv = a.row_bytes >> 1;
+        for (long long v = lane; v < nv; v += 32) {
+          unsigned short x = 0;
+          if (s) x = reinterpret_cast<const unsigned short*>(s)[v];
+          else if (which == 2) x = reinterpret_cast<const unsigned short*>(&a.pad)[v & 7];  // 2-byte pieces of the pattern
+          reinterpret_cast<unsigned short*>(d)[v] = x;
+        }
       }
     }
   }
@@ -176,10 +183,11 @@ extern "C" int b200_stu_jagged_copy(const B200JaggedParams* p, void* stream) {
   hstu::set_error_stage("jagged row copy kernel");
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const long long want = (a.dst_rows + WARPS_PER_BLOCK - 1) / WARPS_PER_BLOCK, cap = static_cast<long long>(sms) * 8;
+  const long long per_block = static_cast<long long>(WARPS_PER_BLOCK) * 32;  // rows one CTA takes per round
+  const long long want = (a.dst_rows + per_block - 1) / per_block, cap = static_cast<long long>(sms) * 8;
   const unsigned grid = static_cast<unsigned>(want < cap ? want : cap);
   const size_t smem = static_cast<size_t>(a.B + 1) * sizeof(long long) * (two_offsets ? 2 : 1);
-  const bool use_smem = smem <= 40 * 1024 && want > cap;  // worth it only when a CTA handles many rows
+  const bool use_smem = smem <= 40 * 1024 && a.dst_rows >= 16 * (a.B + 1);  // worth it only when a CTA handles many rows
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (use_smem) {
     if (vec) jagged_copy_kernel<true, true><<<grid, WARPS_PER_BLOCK * 32, smem, st>>>(a);
