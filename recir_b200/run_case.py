@@ -46,6 +46,16 @@ def main():
     ap.add_argument("--simt", action="store_true", help="use the CUDA-core kernels")
     args = ap.parse_args()
 
+    # under torchrun (one process per GPU) every rank takes its token-balanced shard of the
+    # configuration; rank 0 then reports the slowest rank (max over ranks) and global tokens/s
+    import os
+    dist_run = int(os.environ.get("WORLD_SIZE", "1")) > 1
+    if dist_run:
+        import torch.distributed as dist
+        args.rank, args.world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl", device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
+
     bt = make_batch(args.config, args.batch, args.rank, args.world)
     dev = torch.device("cuda")
     q, k, v, do = (x.to(dev) for x in (bt.q, bt.k, bt.v, bt.dout))
@@ -82,7 +92,21 @@ def main():
             times.append(e0.elapsed_time(e1))
         med = float(np.median(times))
         res[name] = {"ms_median": med, "ms_min": float(min(times)), "useful_tflops": fl / (med * 1e-3) / 1e12}
-    print(json.dumps(res))
+    if dist_run:
+        keys = [k for k in ("fwd", "bwd") if k in res]
+        t = torch.tensor([res[k]["ms_median"] for k in keys] + [float(bt.total_tokens)], dtype=torch.float64, device=dev)
+        tmax, tsum = t.clone(), t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+        if args.rank == 0:
+            step_ms = float(tmax[:-1].sum())
+            print(json.dumps({"config": bt.name, "world": args.world, "T_global": int(tsum[-1].item()),
+                              "ms_max_over_ranks": {k: float(tmax[i]) for i, k in enumerate(keys)},
+                              "tokens_per_s": float(tsum[-1].item()) / (step_ms * 1e-3), "rank0": res}))
+        dist.barrier()
+        dist.destroy_process_group()
+    else:
+        print(json.dumps(res))
 
 
 if __name__ == "__main__":
