@@ -46,11 +46,12 @@ typedef struct B200RowwiseParams {
   void* y;              /* layer norm: [rows, cols]; mul: [rows, parts*cols] or NULL (save_y == false) */
   float* mean;          /* [rows] */
   float* rstd;          /* [rows] */
-  float* scale;         /* mul: [rows] row scale of the fp8 copy, or NULL (no fp8 copy) */
-  void* q8;             /* mul: [rows, parts*cols] float8 e4m3 (1 byte each), or NULL */
+  float* scale;         /* [rows] row scale of the fp8 copy, or NULL (no fp8 copy) */
+  void* q8;             /* float8 e4m3 copy of y (1 byte each): [rows, cols] (layer norm) / [rows, parts*cols] (mul), or NULL */
 } B200RowwiseParams;
 
-/* y = ln(x) * weight + bias (or plain ln(x)), optionally sigmoid(y) * x; writes mean and rstd. */
+/* y = ln(x) * weight + bias (or plain ln(x)), optionally sigmoid(y) * x; writes mean and rstd, and
+ * optionally the row-wise fp8 copy of y (weightedLayerNormQuantized, :504-531). */
 int b200_stu_layer_norm_fwd(const B200RowwiseParams* p, void* stream);
 /* out row = [u' | x | ln(x) * gate(u)] (the first two parts are optional); optionally also its
  * row-wise fp8 copy: scale = max(|row|, 1e-12) / 448, q8 = clamp(row / scale, +-448) as e4m3. */

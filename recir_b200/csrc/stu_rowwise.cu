@@ -105,6 +105,11 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// two values -> two e4m3 bytes (round to nearest even, saturating), low byte = first value
+__device__ __forceinline__ unsigned short to_e4m3x2(float a, float b) {
+  return static_cast<unsigned short>(__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3));
+}
+
 struct Args {
   const void* x; const void* u; const void* weight; const void* bias;
   const float* mean_in; const float* rstd_in;
@@ -153,7 +158,7 @@ __device__ __forceinline__ void load_row(const T* xr, int nv, int lane, float (&
 // RPW rows per warp: the loads of all of a warp's rows are issued before the first reduction, which
 // doubles the bytes in flight per SM for narrow rows (one 1 KB row per warp does not cover the
 // HBM latency at full bandwidth).
-template <typename T, int VPL, int RPW>
+template <typename T, int VPL, int RPW, bool FP8>
 __global__ void __launch_bounds__(WARPS_PER_BLOCK * 32) layer_norm_kernel(Args a) {
   const int lane = threadIdx.x & 31;
   const long long row0 = (static_cast<long long>(blockIdx.x) * WARPS_PER_BLOCK + (threadIdx.x >> 5)) * RPW;
@@ -186,11 +191,12 @@ __global__ void __launch_bounds__(WARPS_PER_BLOCK * 32) layer_norm_kernel(Args a
     if (a.flags & B200_ROWWISE_FLAG_STATS_IN) { mean[r] = a.mean_in[row]; rstd[r] = a.rstd_in[row]; }
     if (lane == 0) { a.mean[row] = mean[r]; a.rstd[row] = rstd[r]; }
     T* yr = reinterpret_cast<T*>(a.y) + row * a.y_rs;
+    float amax = 0.f;
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int v = lane + 32 * j;
       if (v >= nv) continue;
-      float w[8], b[8], o[8];
+      float w[8], b[8];
       if (affine) {
         load8<T>(reinterpret_cast<const T*>(a.weight) + 8 * v, w);
         load8<T>(reinterpret_cast<const T*>(a.bias) + 8 * v, b);
@@ -200,16 +206,32 @@ __global__ void __launch_bounds__(WARPS_PER_BLOCK * 32) layer_norm_kernel(Args a
         float n = (xv[r][j][i] - mean[r]) * rstd[r];
         if (affine) n = n * w[i] + b[i];
         if (swish) n = sigmoid_t<T>(n) * xv[r][j][i];
-        o[i] = n;
+        xv[r][j][i] = n;  // the row now holds the output
+        if (FP8) amax = fmaxf(amax, fabsf(round_to<T>(n)));
       }
-      store8<T>(yr + 8 * v, o);
+      store8<T>(yr + 8 * v, xv[r][j]);
+    }
+    if (!FP8) continue;
+    // optional row-wise fp8 copy of the output as stored (kjt_split_per_feature.cpp:492-501, :504-531)
+    amax = warp_max(amax);
+    const float scale = fmaxf(amax, 1e-12f) / 448.f;
+    if (lane == 0) a.scale[row] = scale;
+    const float inv_scale = 1.f / scale;
+    unsigned char* qr = a.q8 + row * a.q8_rs;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int v = lane + 32 * j;
+      if (v >= nv) continue;
+      uint2 pk;
+      unsigned short* b16 = reinterpret_cast<unsigned short*>(&pk);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float f0 = round_to<T>(xv[r][j][2 * i]), f1 = round_to<T>(xv[r][j][2 * i + 1]);
+        b16[i] = sizeof(T) == 4 ? to_e4m3x2(f0 / scale, f1 / scale) : to_e4m3x2(f0 * inv_scale, f1 * inv_scale);
+      }
+      *reinterpret_cast<uint2*>(qr + 8 * v) = pk;
     }
   }
-}
-
-// two values -> two e4m3 bytes (round to nearest even, saturating), low byte = first value
-__device__ __forceinline__ unsigned short to_e4m3x2(float a, float b) {
-  return static_cast<unsigned short>(__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3));
 }
 
 template <typename T, int VPL>
@@ -440,6 +462,9 @@ int check(const B200RowwiseParams* p, bool mul, Args* a) {
       if (!p->y) return B200_HSTU_EINVAL;
       if ((p->flags & B200_ROWWISE_FLAG_SWISH) && !p->weight) return B200_HSTU_EINVAL;  // as the reference (:205-207)
       if ((p->flags & B200_ROWWISE_FLAG_STATS_IN) && (!p->mean_in || !p->rstd_in)) return B200_HSTU_EINVAL;
+      if ((p->q8 == nullptr) != (p->scale == nullptr)) return B200_HSTU_EINVAL;
+      if (p->q8 && (p->q8_row_stride < p->cols || p->q8_row_stride % 8 != 0 || reinterpret_cast<uintptr_t>(p->q8) % 8 != 0))
+        return p->q8_row_stride < p->cols ? B200_HSTU_EINVAL : B200_HSTU_EALIGN;
     } else {
       if (!p->u || !p->weight) return B200_HSTU_EINVAL;
       if (p->u_row_stride < p->cols || p->u_row_stride % 8 != 0 || bad_ptr(p->u)) return p->u_row_stride < p->cols ? B200_HSTU_EINVAL : B200_HSTU_EALIGN;
@@ -476,7 +501,8 @@ cudaError_t launch_t(const Args& a, cudaStream_t st) {
   };
 #define B200_ROWWISE_LAUNCH(V, R)                                                              \
   if (MUL) launch_mul<T, V>(a, grid_for(1), st);                                                \
-  else layer_norm_kernel<T, V, R><<<grid_for(R), WARPS_PER_BLOCK * 32, 0, st>>>(a)
+  else if (a.q8) layer_norm_kernel<T, V, R, true><<<grid_for(R), WARPS_PER_BLOCK * 32, 0, st>>>(a);  \
+  else layer_norm_kernel<T, V, R, false><<<grid_for(R), WARPS_PER_BLOCK * 32, 0, st>>>(a)
   // one row per warp measured fastest at every width (more rows per warp: 0.88 ms against 0.78 ms on
   // 1.65 M rows of 512 bf16): the kernel is balanced between HBM, MUFU and issue slots, not latency-bound
   if (vpl <= 1) { B200_ROWWISE_LAUNCH(1, 1); }

@@ -6,6 +6,9 @@ Positionally identical to the reference's operators, so the same node-retargetin
 * ``recir::b200_weighted_layer_norm_fwd`` -- schema of
   ``generative_recommenders::triton_weighted_layer_norm_fwd``
   (``recir/ops/kjt_split_per_feature.cpp:724-727``, semantics ``:197-244``);
+* ``recir::b200_weighted_layer_norm_quantization_fwd`` -- schema of
+  ``generative_recommenders::_triton_weighted_layer_norm_quantization_fwd_impl`` (``:740-743``,
+  semantics ``:504-531``): the layer norm plus the row-wise fp8 copy of its output;
 * ``recir::b200_layer_norm_mul_dropout_quantization_fwd`` -- schema of
   ``generative_recommenders::_triton_layer_norm_mul_dropout_quantization_fwd_impl``
   (``:744-747``, semantics ``:558-600``).  Like the reference's CPU operator it applies no dropout
@@ -33,6 +36,9 @@ _LIBDEF.define(
     "int seed, bool save_y, int BLOCK_D) -> (Tensor, Tensor, Tensor, Tensor, Tensor)")
 
 _LIBDEF.define("b200_addmm_fwd(Tensor x, Tensor w, Tensor y) -> Tensor")
+_LIBDEF.define(
+    "b200_weighted_layer_norm_quantization_fwd(Tensor x, Tensor weight, Tensor bias, float eps, Tensor mean, Tensor rstd, "
+    "int BLOCK_D) -> (Tensor, Tensor, Tensor, Tensor, Tensor)")
 
 # Kernel launches issued through this module since import.
 launch_counter = 0
@@ -74,7 +80,7 @@ def _params(x, weight, bias, eps):
     return p, keep
 
 
-def _layer_norm_cuda(x, weight, bias, eps, mean=None, rstd=None, is_swish=False):
+def _layer_norm_cuda(x, weight, bias, eps, mean=None, rstd=None, is_swish=False, _fp8=False):
     global launch_counter
     _validate(x, weight, bias)
     if is_swish and weight is None:
@@ -83,9 +89,13 @@ def _layer_norm_cuda(x, weight, bias, eps, mean=None, rstd=None, is_swish=False)
     y = torch.empty_like(x, memory_format=torch.contiguous_format)
     mean_out = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
     rstd_out = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+    scale = torch.empty(x.shape[0], dtype=torch.float32, device=x.device) if _fp8 else None
+    q8 = torch.empty(x.shape, dtype=torch.float8_e4m3fn, device=x.device) if _fp8 else None
     if x.shape[0] == 0:
-        return y, mean_out, rstd_out
+        return (y, mean_out, rstd_out, scale, q8) if _fp8 else (y, mean_out, rstd_out)
     p, keep = _params(x, weight, bias, eps)
+    if _fp8:
+        p.scale, p.q8, p.q8_row_stride = scale.data_ptr(), q8.data_ptr(), q8.stride(0)
     if mean is not None and rstd is not None:
         if mean.numel() != x.shape[0] or rstd.numel() != x.shape[0]:
             raise ValueError("mean and rstd must match the row count")
@@ -102,7 +112,14 @@ def _layer_norm_cuda(x, weight, bias, eps, mean=None, rstd=None, is_swish=False)
     _check(rc, "b200_stu_layer_norm_fwd")
     launch_counter += 1
     del keep
-    return y, mean_out, rstd_out
+    return (y, mean_out, rstd_out, scale, q8) if _fp8 else (y, mean_out, rstd_out)
+
+
+def _layer_norm_quant_cuda(x, weight, bias, eps, mean, rstd, BLOCK_D):
+    """``generative_recommenders::_triton_weighted_layer_norm_quantization_fwd_impl``
+    (``recir/ops/kjt_split_per_feature.cpp:504-531``): empty ``mean`` / ``rstd`` mean "compute them"."""
+    given = mean.numel() != 0 and rstd.numel() != 0
+    return _layer_norm_cuda(x, weight, bias, eps, mean if given else None, rstd if given else None, False, _fp8=True)
 
 
 def _mul_flags(silu_u, concat_u, concat_x, act):
@@ -160,6 +177,14 @@ def _layer_norm_mul_fake(x, u, weight, bias, eps, dropout_ratio, training, silu_
     return y, stat(), stat(), stat(), x.new_empty((rows, parts * cols), dtype=torch.float8_e4m3fn)
 
 
+def _layer_norm_quant_fake(x, weight, bias, eps, mean, rstd, BLOCK_D):
+    stat = lambda: x.new_empty((x.shape[0],), dtype=torch.float32)  # noqa: E731
+    return (torch.empty_like(x, memory_format=torch.contiguous_format), stat(), stat(), stat(),
+            x.new_empty(x.shape, dtype=torch.float8_e4m3fn))
+
+
+_LIBDEF.impl("b200_weighted_layer_norm_quantization_fwd", _layer_norm_quant_cuda, "CUDA")
+torch.library.register_fake("recir::b200_weighted_layer_norm_quantization_fwd", _layer_norm_quant_fake)
 _LIBDEF.impl("b200_weighted_layer_norm_fwd", _layer_norm_cuda, "CUDA")
 _LIBDEF.impl("b200_layer_norm_mul_dropout_quantization_fwd", _layer_norm_mul_cuda, "CUDA")
 torch.library.register_fake("recir::b200_weighted_layer_norm_fwd", _layer_norm_fake)

@@ -74,6 +74,16 @@ def main():
             out[f"{name}/mean_in"], out[f"{name}/rstd_in"] = mean.numpy(), rstd.numpy()
         out[f"{name}/y"], out[f"{name}/mean"], out[f"{name}/rstd"] = y.float().numpy(), m.numpy(), r.numpy()
         out[f"{name}/cfg"] = np.array([dt, str(int(affine)), str(int(swish)), str(int(stats_in))])
+    for name, rows, cols, dt in (("lnq_f32", 5, 24, "float32"), ("lnq_bf16", 7, 512, "bfloat16"), ("lnq_f16", 4, 264, "float16")):
+        x = (torch.randn(rows, cols, generator=g) * 1.5 + 0.3).to(DT[dt])
+        w = (torch.randn(cols, generator=g) * 0.5 + 1.0).to(DT[dt])
+        b = (torch.randn(cols, generator=g) * 0.2).to(DT[dt])
+        empty = torch.empty(0)
+        y, m, r, scale, q8 = gr._triton_weighted_layer_norm_quantization_fwd_impl(x, w, b, 1e-5, empty, empty, 0)
+        out[f"{name}/x"], out[f"{name}/w"], out[f"{name}/b"] = x.float().numpy(), w.float().numpy(), b.float().numpy()
+        out[f"{name}/y"], out[f"{name}/mean"], out[f"{name}/rstd"] = y.float().numpy(), m.numpy(), r.numpy()
+        out[f"{name}/scale"], out[f"{name}/q8"] = scale.numpy(), q8.view(torch.uint8).numpy()
+        out[f"{name}/cfg"] = np.array([dt])
     for name, rows, cols, dt, silu_u, cat_u, cat_x, act in mul_cases():
         x = (torch.randn(rows, cols, generator=g) * 1.5 + 0.3).to(DT[dt])
         u = (torch.randn(rows, cols, generator=g) * 2.0).to(DT[dt])

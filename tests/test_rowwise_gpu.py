@@ -81,6 +81,24 @@ def test_layer_norm_mul_matches_reference_golden(name):
     assert y2.numel() == 0 and torch.equal(q82.view(torch.uint8), q8.view(torch.uint8)) and torch.equal(scale2, scale)
 
 
+LNQ = sorted({k.split("/")[0] for k in GOLD.files if k.startswith("lnq_")})
+
+
+@pytest.mark.parametrize("name", LNQ)
+def test_quantized_layer_norm_matches_reference_golden(name):
+    dt = str(GOLD[f"{name}/cfg"][0])
+    x, w, b = (_t(GOLD[f"{name}/{k}"], dt) for k in ("x", "w", "b"))
+    empty = torch.empty(0, device="cuda")
+    y, mean, rstd, scale, q8 = torch.ops.recir.b200_weighted_layer_norm_quantization_fwd(x, w, b, 1e-5, empty, empty, 0)
+    torch.cuda.synchronize()
+    _close(y, GOLD[f"{name}/y"], dt, "y")
+    _close(mean, GOLD[f"{name}/mean"], "float32", "mean")
+    _close(scale, GOLD[f"{name}/scale"], "float32", "scale")
+    _codes_close(q8, GOLD[f"{name}/q8"], "q8")
+    y2, m2, r2 = torch.ops.recir.b200_weighted_layer_norm_fwd(x, w, b, 1e-5, None, None, False)
+    assert torch.equal(y2, y) and torch.equal(m2, mean) and torch.equal(r2, rstd)
+
+
 def test_full_size_rows_against_the_oracle_and_strided_input():
     """Benchmark-sized rows (embedding 512, bf16): a sample of rows against the numpy restatement,
     every row through row-wise invariants, and a strided (column-sliced) input."""

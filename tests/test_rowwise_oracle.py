@@ -59,6 +59,20 @@ def test_layer_norm_mul_matches_reference(name):
     assert mag.max() <= 1 and ((q8 ^ want) & 0x80)[mag > 0].sum() == 0 or diff.sum() == 0
 
 
+LNQ = sorted({k.split("/")[0] for k in GOLD.files if k.startswith("lnq_")})
+
+
+@pytest.mark.parametrize("name", LNQ)
+def test_quantized_layer_norm_matches_reference(name):
+    dt = str(GOLD[f"{name}/cfg"][0])
+    y, mean, rstd = ro.weighted_layer_norm(GOLD[f"{name}/x"], GOLD[f"{name}/w"], GOLD[f"{name}/b"], 1e-5, dt)
+    scale, q8 = ro.quantize_fp8_rowwise(y)
+    _close(y, GOLD[f"{name}/y"], dt, "y")
+    _close(scale, GOLD[f"{name}/scale"], "float32", "scale")
+    diff = q8 != GOLD[f"{name}/q8"]
+    assert diff.mean() <= 2e-3
+
+
 def test_e4m3_known_codes():
     # float8 e4m3fn: bias 7, 3 mantissa bits, subnormal step 2^-9, largest finite 448 = 0x7E
     vals = np.array([0.0, 2.0 ** -9, 2.0 ** -6, 1.0, 1.5, 448.0, -448.0, -1.0, 0.0625 * 1.125], np.float32)
