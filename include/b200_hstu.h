@@ -143,6 +143,11 @@ const char* b200_hstu_strerror(int code);
  * B200_HSTU_ELAUNCH result ("" if there was none).  The pointer stays valid until the thread's
  * next failing call.  No counterpart in the reference. */
 const char* b200_hstu_last_cuda_error(void);
+/* Self-test of the bounded waits inside the tensor-core kernels: launches a one-warp kernel that waits
+ * (limit_ns, at most 1e8) on a barrier nothing completes; the wait gives up, stores `code` in
+ * status[1] (device int32[4], zeroed by the caller) and counts in status[2]; the kernel then ends
+ * normally and the context stays usable.  No counterpart in the reference. */
+int b200_hstu_debug_bounded_wait(int32_t* status, int code, uint64_t limit_ns, void* stream);
 int b200_hstu_version(void);
 /* sizeof(B200HstuParams) as this library was compiled (for foreign-language bindings). */
 size_t b200_hstu_params_size(void);

@@ -24,7 +24,7 @@ EXPORTS = (
     "b200_hstu_launch_count", "b200_hstu_strerror", "b200_hstu_version", "b200_hstu_params_size",
     "b200_hstu_debug_keep", "b200_hstu_debug_classify_tile", "b200_hstu_debug_key_blocks",
     "b200_hstu_debug_query_blocks", "b200_hstu_fwd_static_scratch", "b200_hstu_debug_row_mask",
-    "b200_hstu_debug_col_mask", "b200_hstu_last_cuda_error",
+    "b200_hstu_debug_col_mask", "b200_hstu_last_cuda_error", "b200_hstu_debug_bounded_wait",
     # include/b200_stu_rowwise.h
     "b200_stu_layer_norm_fwd", "b200_stu_layer_norm_mul_fwd", "b200_stu_layer_norm_mul_parts",
     # include/b200_stu_jagged.h
@@ -161,6 +161,8 @@ def load() -> ctypes.CDLL:
     lib.b200_hstu_strerror.restype = ctypes.c_char_p
     lib.b200_hstu_last_cuda_error.argtypes = []
     lib.b200_hstu_last_cuda_error.restype = ctypes.c_char_p
+    lib.b200_hstu_debug_bounded_wait.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_uint64, ctypes.c_void_p]
+    lib.b200_hstu_debug_bounded_wait.restype = ctypes.c_int
     lib.b200_hstu_version.argtypes = []
     lib.b200_hstu_version.restype = ctypes.c_int
     lib.b200_hstu_params_size.argtypes = []

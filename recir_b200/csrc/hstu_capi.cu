@@ -10,6 +10,7 @@
 #include "hstu_common.cuh"
 #include "hstu_launch.h"
 #include "hstu_tc_common.cuh"
+#include "hstu_tc_host.h"
 
 using hstu::KernelArgs;
 
@@ -260,5 +261,11 @@ int b200_hstu_fwd_static_scratch(const B200HstuParams* p, void* stream) {
   return launch_result(e);
 }
 int b200_hstu_bwd(const B200HstuParams* p, void* stream) { return run(p, 1, stream); }
+
+int b200_hstu_debug_bounded_wait(int32_t* status, int code, uint64_t limit_ns, void* stream) {
+  if (status == nullptr || limit_ns == 0 || limit_ns > 100000000ull) return B200_HSTU_EINVAL;  // at most 0.1 s
+  hstu::set_error_stage("bounded-wait probe");
+  return launch_result(hstu::tc::launch_bounded_wait_probe(status, code, limit_ns, static_cast<cudaStream_t>(stream)));
+}
 
 }  // extern "C"

@@ -835,6 +835,27 @@ cudaError_t launch_prep(const KernelArgs& a, bool bf16, int* ws, const Workspace
   return bf16 ? launch_prep_t<__nv_bfloat16>(a, ws, w, backward, st) : launch_prep_t<__half>(a, ws, w, backward, st);
 }
 
+// Exercises the bounded wait that every pipeline wait of the tensor-core kernels goes through: one warp
+// waits on a barrier that nothing will ever complete, with a limit of `limit_ns`; the wait must give up,
+// record `code` in status[1] and let the kernel finish normally.
+__global__ void bounded_wait_probe(int* status, int code, unsigned long long limit_ns) {
+  __shared__ unsigned long long bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    sm100::mbar_init(sm100::smem_u32(&bar), 1);
+    sm100::fence_barrier_init();
+  }
+  __syncthreads();
+  const bool ok = sm100::mbar_wait(sm100::smem_u32(&bar), 0u, &abort_flag, status, code, limit_ns);
+  if (!ok && threadIdx.x == 0) atomicAdd(status + 2, 1);  // how many probes saw the wait give up
+}
+
+cudaError_t launch_bounded_wait_probe(int* status, int code, unsigned long long limit_ns, cudaStream_t st) {
+  bounded_wait_probe<<<1, 32, 0, st>>>(status, code, limit_ns);
+  return cudaGetLastError();
+}
+
 }  // namespace tc
 
 bool tc_supported(const B200HstuParams& p, const KernelArgs& a, int pass) {

@@ -20,5 +20,8 @@ int main_grid(const WorkspaceLayout& w);
 cudaError_t launch_prep(const KernelArgs& a, bool bf16, int* ws, const WorkspaceLayout& w, bool backward,
                         cudaStream_t st);
 
+// Launches the bounded-wait self-test kernel (see b200_hstu_debug_bounded_wait).
+cudaError_t launch_bounded_wait_probe(int* status, int code, unsigned long long limit_ns, cudaStream_t st);
+
 }  // namespace tc
 }  // namespace hstu

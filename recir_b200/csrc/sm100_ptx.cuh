@@ -59,10 +59,10 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
   return t;
 }
 
-// Bounded wait: gives up after ~2 s (or as soon as another thread of the CTA gave up),
-// records `code` in status[1] and raises the CTA-wide abort flag.  Returns false on abort.
+// Bounded wait: gives up after `limit_ns` (2 s by default; or as soon as another thread of the CTA
+// gave up), records `code` in status[1] and raises the CTA-wide abort flag.  Returns false on abort.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
-                                          int code) {
+                                          int code, unsigned long long limit_ns = 2000000000ull) {
   if (mbar_try_wait(bar, parity)) return true;
   unsigned long long t0 = 0;
   for (uint32_t i = 1;; ++i) {
@@ -71,7 +71,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
       if (*abort_flag) return false;
       const unsigned long long now = globaltimer_ns();
       if (t0 == 0) t0 = now;
-      if (now - t0 > 2000000000ull) {
+      if (now - t0 > limit_ns) {
         *abort_flag = 1;
         if (status) atomicCAS(status + 1, 0, code);
         return false;

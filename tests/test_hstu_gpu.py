@@ -365,3 +365,29 @@ def test_scheduler_and_work_list_on_irregular_batches(seed, B, lo, hi, H):
         if hi_r > lo_r:
             assert rel_l2(a[0][lo_r:hi_r].float(), b[0][lo_r:hi_r].float()) <= 1e-2
             assert rel_l2(a[2][lo_r:hi_r].float(), b[2][lo_r:hi_r].float()) <= 1e-2
+
+
+def test_bounded_wait_gives_up_and_leaves_the_context_usable():
+    """Every pipeline wait of the tensor-core kernels is bounded.  The library's self-test kernel waits
+    (2 ms limit) on a barrier that nothing completes: it must report the given code in status[1], end
+    normally, and the next operator call on the same context must still be correct."""
+    from recir_b200 import _lib
+
+    lib = _lib.load()
+    status = torch.zeros(4, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = lib.b200_hstu_debug_bounded_wait(status.data_ptr(), 199, 2_000_000, stream)
+    assert rc == 0, _lib.strerror(rc)
+    torch.cuda.synchronize()
+    got = status.cpu().tolist()
+    assert got[1] == 199 and got[2] == 1, got
+    # limits above 0.1 s and missing buffers are refused on the host
+    assert lib.b200_hstu_debug_bounded_wait(status.data_ptr(), 1, 10**9, stream) < 0
+    assert lib.b200_hstu_debug_bounded_wait(None, 1, 1000, stream) < 0
+
+    c = golden_case("multi_tile")
+    o, dq, dk, dv = _run(c, dtype=torch.bfloat16)
+    o32, *_ = _run(c)
+    n = int(c["offsets"][-1])
+    assert max_abs(o32[:n], c["o"]) <= 2e-3
+    assert rel_l2(o.float()[:n], c["o"]) <= 2e-2 and rel_l2(dk.float()[:n], c["dk"]) <= 2e-2
