@@ -13,6 +13,7 @@
 //   warps 8-11  epilogue group 1   } alpha / SiLU / mask, write P (16-bit) back over S
 // The output scale (1/N or attn_scale) is a per-query-row factor, so it is applied once
 // when O leaves TMEM, not per score.
+#define SM100_OUTLINE_WAIT_SLOW_PATH  // one shared copy of the wait loop: see sm100_ptx.cuh
 #include <cuda.h>
 #include <cuda_runtime.h>
 

@@ -61,9 +61,20 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 
 // Bounded wait: gives up after `limit_ns` (2 s by default; or as soon as another thread of the CTA
 // gave up), records `code` in status[1] and raises the CTA-wide abort flag.  Returns false on abort.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
-                                          int code, unsigned long long limit_ns = 2000000000ull) {
-  if (mbar_try_wait(bar, parity)) return true;
+//
+// A kernel has dozens of waits.  A translation unit that defines SM100_OUTLINE_WAIT_SLOW_PATH before
+// including this header gets ONE shared, non-inlined copy of the spin loop instead of one per call
+// site: that shrinks the kernel by several KB and lets the warps that spin at the same time share
+// instruction-cache lines.  It pays in the forward kernel (whose short items are bound by
+// instruction fetch); in the backward kernels the call's register constraints cost more than the
+// smaller footprint gains, so they keep the inlined loop.
+#ifdef SM100_OUTLINE_WAIT_SLOW_PATH
+#define SM100_WAIT_SLOW_ATTR static __device__ __noinline__
+#else
+#define SM100_WAIT_SLOW_ATTR __device__ __forceinline__
+#endif
+SM100_WAIT_SLOW_ATTR bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                         int code, unsigned long long limit_ns) {
   unsigned long long t0 = 0;
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -78,6 +89,13 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
       }
     }
   }
+}
+#undef SM100_WAIT_SLOW_ATTR
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                          int code, unsigned long long limit_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, abort_flag, status, code, limit_ns);
 }
 
 // Register reallocation between warpgroups (all four warps of a warpgroup must execute it).

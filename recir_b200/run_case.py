@@ -4,7 +4,10 @@
 
 Configurations: cfg0 (smoke shape, fp32), cfg1 (B=64, H=4, D=128 bf16), cfg3 (long skewed
 sequences, sliding window + contextual prefix), cfg4 (one layer of the Zipf batch, optionally
-the shard of one rank).  ``--passes`` is ``fwd``, ``bwd`` or ``both``.  This is also the
+the shard of one rank).  ``--passes`` is ``fwd``, ``bwd`` or ``both``.  ``--buckets`` (cfg4 only)
+times each sequence-length bucket of the Zipf batch as a batch of its own, repeated to at least
+64k tokens so that its tensors exceed the L2, and reports useful TFLOP/s and algorithmic GB/s per
+bucket: short sequences sit on the HBM roofline, long ones on the tensor-core roofline.  This is also the
 command profilers are pointed at: it launches nothing but the library's kernels after the
 inputs have been copied to the device.
 """
@@ -34,6 +37,72 @@ def make_batch(name: str, batch: int | None, rank: int, world: int):
     raise SystemExit(f"unknown config {name}")
 
 
+BUCKETS = ((32, 128), (128, 256), (256, 512), (512, 1024), (1024, 2048), (2048, 4225))
+
+
+def bucket_batch(lo: int, hi: int, min_tokens: int = 65536):
+    """The cfg4 sequences with lo <= length < hi: repeated until the batch holds min_tokens tokens, or cut
+    after the first 4 * min_tokens tokens when the bucket holds more."""
+    hist, tg = workload.config4_lengths(1024)
+    lengths = hist + tg
+    sel = np.nonzero((lengths >= lo) & (lengths < hi))[0]
+    if sel.size == 0:
+        return None, 0
+    n = sel.size
+    over = np.nonzero(np.cumsum(lengths[sel]) >= 4 * min_tokens)[0]
+    if over.size:
+        sel = sel[: int(over[0]) + 1]
+    reps = max(1, -(-min_tokens // int(lengths[sel].sum())))
+    sel_r = np.tile(sel, reps)
+    return workload.config4_layer(lengths[sel_r], tg[sel_r], layer=0), int(n)
+
+
+def measure(bt, passes: str, iters: int, warmup: int, calls: int = 1) -> dict:
+    """Times the forward and/or backward operator call on one batch with CUDA events.  With calls > 1
+    each sample is that many calls issued back to back, divided by their number, so that the host's
+    launch latency hides behind the previous call's kernels."""
+    dev = torch.device("cuda")
+    q, k, v, do = (x.to(dev) for x in (bt.q, bt.k, bt.v, bt.dout))
+    off = bt.seq_offsets.to(dev)
+    nt = None if bt.num_targets is None else bt.num_targets.to(dev)
+    a = (off, bt.max_seq_len, bt.alpha, bt.causal, nt, bt.contextual_seq_len, bt.max_attn_len, None,
+         bt.full_attn_size)
+    H, Dq, Dv = q.shape[1], q.shape[2], v.shape[2]
+    pairs = workload.total_kept_pairs(bt)
+
+    def fwd():
+        return torch.ops.recir.b200_hstu_attention_fwd(q, k, v, *a)
+
+    def bwd():
+        return torch.ops.recir.b200_hstu_attention_bwd(do, q, k, v, *a)
+
+    res = {"config": bt.name, "T": bt.total_tokens, "B": len(bt.lengths), "H": H, "D": Dq,
+           "kept_pairs_per_head": pairs}
+    for name, fn, fl, by in (
+            ("fwd", fwd, workload.useful_flops(pairs, H, Dq, Dv, False),
+             workload.algorithmic_bytes(bt.total_tokens, H, Dq, Dv, q.element_size(), False)),
+            ("bwd", bwd, workload.useful_flops(pairs, H, Dq, Dv, True, forward=False),
+             workload.algorithmic_bytes(bt.total_tokens, H, Dq, Dv, q.element_size(), True, forward=False))):
+        if passes not in (name, "both"):
+            continue
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(iters):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(calls):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1) / calls)
+        med = float(np.median(times))
+        res[name] = {"ms_median": med, "ms_min": float(min(times)), "useful_tflops": fl / (med * 1e-3) / 1e12,
+                     "algorithmic_gbs": by / (med * 1e-3) / 1e9}
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--config", default="cfg1")
@@ -44,7 +113,23 @@ def main():
     ap.add_argument("--rank", type=int, default=0)
     ap.add_argument("--world", type=int, default=1)
     ap.add_argument("--simt", action="store_true", help="use the CUDA-core kernels")
+    ap.add_argument("--calls", type=int, default=1, help="calls issued back to back per timed sample")
+    ap.add_argument("--buckets", action="store_true", help="cfg4: one measurement per sequence-length bucket")
+    ap.add_argument("--bucket", default=None, help="cfg4: only the bucket LO:HI (lengths LO <= L < HI)")
     args = ap.parse_args()
+
+    if args.buckets or args.bucket:
+        out = []
+        only = tuple(int(x) for x in args.bucket.split(":")) if args.bucket else None
+        for lo, hi in ((only,) if only else BUCKETS):
+            bt, n = bucket_batch(lo, hi)
+            if bt is None:
+                continue
+            r = measure(bt, args.passes, args.iters, args.warmup, args.calls)
+            r.update(bucket=[lo, hi], seqs_in_cfg4=n, mean_length=bt.total_tokens / len(bt.lengths))
+            out.append(r)
+        print(json.dumps({"config": "cfg4 length buckets", "buckets": out}))
+        return
 
     # under torchrun (one process per GPU) every rank takes its token-balanced shard of the
     # configuration; rank 0 then reports the slowest rank (max over ranks) and global tokens/s
@@ -58,40 +143,8 @@ def main():
 
     bt = make_batch(args.config, args.batch, args.rank, args.world)
     dev = torch.device("cuda")
-    q, k, v, do = (x.to(dev) for x in (bt.q, bt.k, bt.v, bt.dout))
-    off = bt.seq_offsets.to(dev)
-    nt = None if bt.num_targets is None else bt.num_targets.to(dev)
-    a = (off, bt.max_seq_len, bt.alpha, bt.causal, nt, bt.contextual_seq_len, bt.max_attn_len, None,
-         bt.full_attn_size)
     ops.set_force_simt(args.simt)
-    H, Dq, Dv = q.shape[1], q.shape[2], v.shape[2]
-    pairs = workload.total_kept_pairs(bt)
-
-    def fwd():
-        return torch.ops.recir.b200_hstu_attention_fwd(q, k, v, *a)
-
-    def bwd():
-        return torch.ops.recir.b200_hstu_attention_bwd(do, q, k, v, *a)
-
-    res = {"config": bt.name, "T": bt.total_tokens, "B": len(bt.lengths), "H": H, "D": Dq,
-           "kept_pairs_per_head": pairs}
-    for name, fn, fl in (("fwd", fwd, workload.useful_flops(pairs, H, Dq, Dv, False)),
-                         ("bwd", bwd, workload.useful_flops(pairs, H, Dq, Dv, True, forward=False))):
-        if args.passes not in (name, "both"):
-            continue
-        for _ in range(args.warmup):
-            fn()
-        torch.cuda.synchronize()
-        times = []
-        for _ in range(args.iters):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            fn()
-            e1.record()
-            torch.cuda.synchronize()
-            times.append(e0.elapsed_time(e1))
-        med = float(np.median(times))
-        res[name] = {"ms_median": med, "ms_min": float(min(times)), "useful_tflops": fl / (med * 1e-3) / 1e12}
+    res = measure(bt, args.passes, args.iters, args.warmup, args.calls)
     if dist_run:
         keys = [k for k in ("fwd", "bwd") if k in res]
         t = torch.tensor([res[k]["ms_median"] for k in keys] + [float(bt.total_tokens)], dtype=torch.float64, device=dev)
