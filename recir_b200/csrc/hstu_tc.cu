@@ -245,6 +245,13 @@ struct Stopwatch {
   __device__ __forceinline__ void stop(long long& acc) { if (PROF) acc += clock64() - t; }
 };
 
+// Tile class for candidates past the first 32 of an item (sequences longer than 32 blocks only; the
+// scheduler warp classifies the first 32): kept out of line so that this rarely executed code does not
+// sit in the middle of the per-item paths.
+static __device__ __noinline__ int classify_tile_cold(int m0, int n0, SeqInfo s, MaskOpts o) {
+  return classify_tile(m0, n0, s, o, true);
+}
+
 // One 32-column chunk of scores -> 16 packed 16-bit pairs of P; `bits` = kept columns of the chunk.
 template <bool IS_BF16, bool MASKED>
 __device__ __forceinline__ void silu_chunk(const uint32_t (&sv)[32], uint32_t (&pk)[16], float c1, uint32_t bits) {
@@ -342,7 +349,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
           uint32_t todo = todo0;  // the scheduler warp classified the first 32 candidates
           if (base > 0) {
             int my_cls = TILE_SKIP;
-            if (base + lane < cnt) my_cls = classify_tile(m0, kr.at(base + lane) * BLK, s, a.mask, true);
+            if (base + lane < cnt) my_cls = classify_tile_cold(m0, kr.at(base + lane) * BLK, s, a.mask);
             todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
           }
           while (todo != 0u && ok) {
@@ -573,7 +580,11 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
     int2 w;
     SeqInfo s;
     uint32_t todo0 = 0u, full0 = 0u;
-    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, todo0, full0, ok, abort_flag, a.status, WAIT_EPILOGUE); ++n_item) {
+    // The loop runs once more after the last item (have_item == false, no tiles) so that the final
+    // accumulator is drained by the same copy of the drain code as all the others.
+    for (uint32_t n_item = 0; ok; ++n_item) {
+      const bool have_item = next_item(sh.ring, n_item, w, s, todo0, full0, ok, abort_flag, a.status, WAIT_EPILOGUE);
+      if (!ok) break;
       const int head = w.x >> 16, qblk = w.y;
       const int m0 = qblk * BLK;
       const int m = m0 + row;
@@ -593,7 +604,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
             full_bits = full0;
           } else {
             int my_cls = TILE_SKIP;
-            if (cur_base + lane < cnt) my_cls = classify_tile(m0, kr.at(cur_base + lane) * BLK, s, a.mask, true);
+            if (cur_base + lane < cnt) my_cls = classify_tile_cold(m0, kr.at(cur_base + lane) * BLK, s, a.mask);
             todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
             full_bits = __ballot_sync(0xffffffffu, my_cls == TILE_FULL);
           }
@@ -622,86 +633,88 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
       uint32_t sa[32], sb2[32], pk[16];
       int n0 = 0, n0_next = 0;
       bool full = false, full_next = false;
-      bool have = next_tile(n0, full);
+      bool have = have_item && next_tile(n0, full);
       if (have) {
         if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 0, 6);
         ok = wait_scores(g);
         if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 1, 6);
         if (ok) tmem_ld32(s_addr_of(g), sa);
       }
-      while (have && ok) {
-        const bool have_next = next_tile(n0_next, full_next);
-        const uint32_t s_addr = s_addr_of(g);
-        const uint32_t sb = g & 1;
-        sw.start();
-        tmem_wait_ld(sa);
-        tmem_ld32(s_addr + 32, sb2);
-        if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 2, 6);
-        if (full) {
-          silu_chunk<IS_BF16, false>(sa, pk, c1, 0u);
-          tmem_st16(s_addr, pk);  // P (16 columns per chunk) goes over the group's own score columns
-          tmem_wait_ld(sb2);
-          silu_chunk<IS_BF16, false>(sb2, pk, c1, 0u);
-          tmem_st16(s_addr + 16, pk);
-        } else {
-          // A warp covers 32 consecutive rows, so on a diagonal tile most 32-column chunks are
-          // entirely kept or entirely dropped for the whole warp: vote, and only the chunks that
-          // straddle the mask boundary pay for per-element masking; dropped chunks skip the math.
-          const unsigned long long bits = row_mask_bits64(rm, n0 + wg * 64);
-          const uint32_t b0 = static_cast<uint32_t>(bits), b1 = static_cast<uint32_t>(bits >> 32);
-          if (__all_sync(0xffffffffu, b0 == 0xffffffffu)) {
+      while ((have || (!have_item && drain_pending)) && ok) {
+        bool have_next = false;
+        if (have) {
+          have_next = next_tile(n0_next, full_next);
+          const uint32_t s_addr = s_addr_of(g);
+          const uint32_t sb = g & 1;
+          sw.start();
+          tmem_wait_ld(sa);
+          tmem_ld32(s_addr + 32, sb2);
+          if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 2, 6);
+          if (full) {
             silu_chunk<IS_BF16, false>(sa, pk, c1, 0u);
-          } else if (__all_sync(0xffffffffu, b0 == 0u)) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) pk[i] = 0u;
-          } else {
-            silu_chunk<IS_BF16, true>(sa, pk, c1, b0);
-          }
-          tmem_st16(s_addr, pk);
-          tmem_wait_ld(sb2);
-          if (__all_sync(0xffffffffu, b1 == 0xffffffffu)) {
+            tmem_st16(s_addr, pk);  // P (16 columns per chunk) goes over the group's own score columns
+            tmem_wait_ld(sb2);
             silu_chunk<IS_BF16, false>(sb2, pk, c1, 0u);
-          } else if (__all_sync(0xffffffffu, b1 == 0u)) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) pk[i] = 0u;
+            tmem_st16(s_addr + 16, pk);
           } else {
-            silu_chunk<IS_BF16, true>(sb2, pk, c1, b1);
+            // A warp covers 32 consecutive rows, so on a diagonal tile most 32-column chunks are
+            // entirely kept or entirely dropped for the whole warp: vote, and only the chunks that
+            // straddle the mask boundary pay for per-element masking; dropped chunks skip the math.
+            const unsigned long long bits = row_mask_bits64(rm, n0 + wg * 64);
+            const uint32_t b0 = static_cast<uint32_t>(bits), b1 = static_cast<uint32_t>(bits >> 32);
+            if (__all_sync(0xffffffffu, b0 == 0xffffffffu)) {
+              silu_chunk<IS_BF16, false>(sa, pk, c1, 0u);
+            } else if (__all_sync(0xffffffffu, b0 == 0u)) {
+  #pragma unroll
+              for (int i = 0; i < 16; ++i) pk[i] = 0u;
+            } else {
+              silu_chunk<IS_BF16, true>(sa, pk, c1, b0);
+            }
+            tmem_st16(s_addr, pk);
+            tmem_wait_ld(sb2);
+            if (__all_sync(0xffffffffu, b1 == 0xffffffffu)) {
+              silu_chunk<IS_BF16, false>(sb2, pk, c1, 0u);
+            } else if (__all_sync(0xffffffffu, b1 == 0u)) {
+  #pragma unroll
+              for (int i = 0; i < 16; ++i) pk[i] = 0u;
+            } else {
+              silu_chunk<IS_BF16, true>(sb2, pk, c1, b1);
+            }
+            tmem_st16(s_addr + 16, pk);
           }
-          tmem_st16(s_addr + 16, pk);
+          if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 3, 6);
+          if (n0 + BLK > s.len) {
+            // Key rows past the end of the sequence belong to someone else (or to nobody) and may
+            // hold anything, NaN included; their P columns are exact zeros, but 0 * NaN is NaN,
+            // so the V rows themselves are cleared before the MMA reads the tile.
+            const uint32_t vs = g % NUM_V_STAGES, vph = (g / NUM_V_STAGES) & 1;
+            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.v_full[vs]), vph, abort_flag, a.status, WAIT_EPILOGUE));
+            if (!ok) break;
+            zero_box_rows(sh.v[vs] + wg * HALF_TILE_BYTES, s.len - n0, BLK, row, 128);
+          }
+          if (have_next) {
+            // scores of the next tile were issued before the MMA warp started waiting for this P
+            ok = wait_scores(g + 1);
+            if (!ok) break;
+            tmem_ld32(s_addr_of(g + 1), sa);
+          }
+          tmem_wait_st();
+          if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 4, 6);
+          tc_fence_before();
+          mbar_arrive(smem_u32(&sh.p_ready[sb]));
+          if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 5, 6);
+          if (full) { sw.stop(pf_fullt); ++n_fullt; } else { sw.stop(pf_part); ++n_part; }
+          ++g;
         }
-        if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 3, 6);
-        if (n0 + BLK > s.len) {
-          // Key rows past the end of the sequence belong to someone else (or to nobody) and may
-          // hold anything, NaN included; their P columns are exact zeros, but 0 * NaN is NaN,
-          // so the V rows themselves are cleared before the MMA reads the tile.
-          const uint32_t vs = g % NUM_V_STAGES, vph = (g / NUM_V_STAGES) & 1;
-          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.v_full[vs]), vph, abort_flag, a.status, WAIT_EPILOGUE));
-          if (!ok) break;
-          zero_box_rows(sh.v[vs] + wg * HALF_TILE_BYTES, s.len - n0, BLK, row, 128);
-        }
-        if (have_next) {
-          // scores of the next tile were issued before the MMA warp started waiting for this P
-          ok = wait_scores(g + 1);
-          if (!ok) break;
-          tmem_ld32(s_addr_of(g + 1), sa);
-        }
-        tmem_wait_st();
-        if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 4, 6);
-        tc_fence_before();
-        mbar_arrive(smem_u32(&sh.p_ready[sb]));
-        if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 5, 6);
-        if (full) { sw.stop(pf_fullt); ++n_fullt; } else { sw.stop(pf_part); ++n_part; }
-        ++g;
         if (drain_pending) { sw.start(); ok = drain_o(); sw.stop(pf_drain); }
         n0 = n0_next; full = full_next; have = have_next;
       }
-      if (!ok) break;
+      if (!ok || !have_item) break;
       // hand the accumulator over: it is drained after the first key tile of the next item
       d_start = s.start; d_len = s.len; d_m0 = m0; d_head = head; d_it = it;
       drain_pending = true;
       ++it;
     }
-    if (ok && drain_pending) ok = drain_o();
     if (row == 0) bulk_wait_all();  // shared memory must outlive the stores that read it
     sw_total.stop(pf_total);
     if (prof_thread) {
