@@ -38,7 +38,7 @@ UNIT = "TFLOP/s"
 NOMINAL_BF16_TFLOPS = 2250.0
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from the committed ncu capture of the same
 # B/H/D and length distribution (profiles/tc_kernels_cfg1_ncu_full.md), and that capture's token count.
-NCU_CFG1_DRAM_BYTES = {"hstu_fwd_tc": 312.0e6, "hstu_bwd_dkv_tc": 471.7e6, "hstu_bwd_dq_tc": 406.0e6}
+NCU_CFG1_DRAM_BYTES = {"hstu_fwd_tc": 315.6e6, "hstu_bwd_dkv_tc": 471.1e6, "hstu_bwd_dq_tc": 405.8e6}
 NCU_CFG1_TOKENS = 78262
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
