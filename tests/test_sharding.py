@@ -52,3 +52,23 @@ def test_gather_rows_matches_offsets():
     x = torch.arange(9).view(9, 1, 1)
     got = sharding.gather_rows(x, offs, [3, 0])
     assert got.flatten().tolist() == [5, 6, 7, 8, 0, 1, 2]
+
+
+def test_length_buckets_of_the_zipf_batch_partition_it():
+    """The per-length-bucket runner covers every sequence of the Zipf batch exactly once, keeps each
+    batch's lengths inside its bucket and repeats / cuts buckets to the advertised token range."""
+    from recir_b200 import run_case
+
+    hist, tg = workload.config4_lengths(1024)
+    lengths = hist + tg
+    seen = 0
+    for lo, hi in run_case.BUCKETS:
+        bt, n = run_case.bucket_batch(lo, hi, min_tokens=4096)
+        assert n == int(((lengths >= lo) & (lengths < hi)).sum())
+        seen += n
+        got = np.diff(bt.seq_offsets.numpy())
+        assert got.min() >= lo and got.max() < hi
+        assert 4096 <= bt.total_tokens <= 4 * 4096 + hi
+        assert bt.q.shape == (bt.total_tokens, 4, 128)
+        assert (bt.num_targets.numpy() < got).all()
+    assert seen == 1024
