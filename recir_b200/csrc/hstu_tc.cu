@@ -41,46 +41,71 @@ __device__ __forceinline__ int blocks_of(const KernelArgs& a, int b) {
   return (s.len + BLK - 1) / BLK;
 }
 
-// out[j] = sum_{i > j} in[i] for j in [0, n): exclusive suffix sum, one CTA of 1024 threads.
-__device__ void suffix_sum_exclusive(const int* in, int* out, long long n, int* sh /*1024*/) {
-  const int tid = threadIdx.x, nt = blockDim.x;
+// out[j] = sum_{i > j} in[i] for j in [0, n): exclusive suffix sum, one CTA of up to 1024 threads (whole
+// warps).  Every thread sums a contiguous chunk; the per-thread totals are scanned with warp shuffles
+// (two block barriers instead of the twenty of a shared-memory scan).
+__device__ void suffix_sum_exclusive(const int* in, int* out, long long n, int* sh /*>= 64 ints*/) {
+  const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5, nwarps = nt >> 5;
   const long long chunk = (n + nt - 1) / nt;
   const long long beg = (long long)tid * chunk;
   long long end = beg + chunk;
   if (end > n) end = n;
   int local = 0;
   for (long long i = beg; i < end; ++i) local += in[i];
-  sh[tid] = local;
-  __syncthreads();
-  // inclusive suffix scan over the per-thread totals (Hillis-Steele)
-  for (int off = 1; off < nt; off <<= 1) {
-    int v = (tid + off < nt) ? sh[tid + off] : 0;
-    __syncthreads();
-    sh[tid] += v;
-    __syncthreads();
+  // v = sum over the lanes >= this one of the warp
+  int v = local;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int t = __shfl_down_sync(0xffffffffu, v, off);
+    if (lane + off < 32) v += t;
   }
-  int run = (tid + 1 < nt) ? sh[tid + 1] : 0;  // sum of everything owned by later threads
+  if (lane == 0) sh[warp] = v;
   __syncthreads();
+  if (warp == 0) {
+    int t = lane < nwarps ? sh[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int u = __shfl_down_sync(0xffffffffu, t, off);
+      if (lane + off < 32) t += u;
+    }
+    sh[32 + lane] = t;  // sum of the totals of warps >= lane
+  }
+  __syncthreads();
+  int run = (v - local) + (warp + 1 < nwarps ? sh[32 + warp + 1] : 0);  // everything owned by later threads
   for (long long i = end - 1; i >= beg; --i) {
-    const int v = in[i];
+    const int x = in[i];
     out[i] = run;
-    run += v;
+    run += x;
   }
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(1024) build_block_index(KernelArgs a, int* ws, WorkspaceLayout w) {
+// The three per-block-count tables (histogram, suffix counts, starts) live in shared memory when they
+// fit (tables_in_smem; 3 * nbins ints of dynamic shared memory), so that the dozen dependent phases of
+// this single-CTA kernel pay shared-memory instead of global-memory latency; the suffix counts are
+// copied to the workspace at the end for build_work_items.
+__global__ void __launch_bounds__(1024) build_block_index(KernelArgs a, int* ws, WorkspaceLayout w, int tables_in_smem) {
   __shared__ int sh[1024];
+  extern __shared__ int tab[];
   int* sorted = ws + w.off_sorted;
-  int* hist = ws + w.off_hist;
-  int* cnt = ws + w.off_cnt;
-  int* start = ws + w.off_start;
+  int* hist = tables_in_smem ? tab : ws + w.off_hist;
+  int* cnt = tables_in_smem ? tab + w.nbins : ws + w.off_cnt;
+  int* start = tables_in_smem ? tab + 2 * w.nbins : ws + w.off_start;
   const int tid = threadIdx.x;
   for (long long i = tid; i < w.nbins; i += blockDim.x) hist[i] = 0;
+  // block count of the first sequence of this thread stays in a register for the second pass
+  long long nb_first = 0;
+  if (tid < a.B) {
+    nb_first = blocks_of(a, tid);
+    if (nb_first > w.nbins - 1) nb_first = w.nbins - 1;  // cannot happen for offsets within [0, T]
+  }
   __syncthreads();
   for (int b = tid; b < a.B; b += blockDim.x) {
-    long long nb = blocks_of(a, b);
-    if (nb > w.nbins - 1) nb = w.nbins - 1;  // cannot happen for offsets within [0, T]
+    long long nb = nb_first;
+    if (b != tid) {
+      nb = blocks_of(a, b);
+      if (nb > w.nbins - 1) nb = w.nbins - 1;
+    }
     atomicAdd(&hist[nb], 1);
   }
   __syncthreads();
@@ -88,8 +113,11 @@ __global__ void __launch_bounds__(1024) build_block_index(KernelArgs a, int* ws,
   for (long long i = tid; i < w.nbins; i += blockDim.x) hist[i] = 0;  // reuse as fill counters
   __syncthreads();
   for (int b = tid; b < a.B; b += blockDim.x) {
-    long long nb = blocks_of(a, b);
-    if (nb > w.nbins - 1) nb = w.nbins - 1;
+    long long nb = nb_first;
+    if (b != tid) {
+      nb = blocks_of(a, b);
+      if (nb > w.nbins - 1) nb = w.nbins - 1;
+    }
     if (nb > 0) sorted[cnt[nb] + atomicAdd(&hist[nb], 1)] = b;
   }
   __syncthreads();
@@ -116,6 +144,14 @@ __global__ void __launch_bounds__(1024) build_block_index(KernelArgs a, int* ws,
     }
     chunk_base[c] = static_cast<int>(sum * a.H);
   }
+  if (tables_in_smem) {
+    int* g_cnt = ws + w.off_cnt;
+    int* g_start = ws + w.off_start;
+    for (long long i = tid; i < w.nbins; i += blockDim.x) {
+      g_cnt[i] = cnt[i];
+      g_start[i] = start[i];
+    }
+  }
 }
 
 // One thread per work-list entry: decode its rank into (sequence, head, block index).
@@ -124,7 +160,8 @@ __global__ void __launch_bounds__(1024) build_block_index(KernelArgs a, int* ws,
 // share K/V or Q/dO rows close together); no static deal is needed.
 // Also zeroes the output rows no sequence owns (rows at or past the last offset).
 template <typename T>
-__global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, WorkspaceLayout w, int stride, T* z0,
+__global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, WorkspaceLayout w, int stride,
+                                                        int tables_in_smem, T* z0,
                                                         long long rs0, int w0, T* z1, long long rs1, int w1,
                                                         T* z2, long long rs2, int w2) {
   const int* sorted = ws + w.off_sorted;
@@ -132,6 +169,19 @@ __global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, W
   const int* chunk_base = ws + w.off_chunk;
   int2* items = reinterpret_cast<int2*>(ws + w.off_items);
   const int total = ws[0];
+  // the two tables every thread searches are copied to shared memory first when they fit
+  // (tables_in_smem: nbins + n_chunks + 1 ints of dynamic shared memory)
+  extern __shared__ int tab[];
+  if (tables_in_smem) {
+    const int n_chunks1 = (ws[1] + w.chunk_seqs - 1) / w.chunk_seqs + 1;
+    int* s_cnt = tab;
+    int* s_chunk = tab + w.nbins;
+    for (long long i = threadIdx.x; i < w.nbins; i += blockDim.x) s_cnt[i] = cnt[i];
+    for (int i = threadIdx.x; i < n_chunks1; i += blockDim.x) s_chunk[i] = chunk_base[i];
+    __syncthreads();
+    cnt = s_cnt;
+    chunk_base = s_chunk;
+  }
   const long long gtid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   const long long gsz = (long long)gridDim.x * blockDim.x;
   for (long long slot = gtid; slot < total; slot += gsz) {
@@ -831,14 +881,20 @@ template <typename T>
 static cudaError_t launch_prep_t(const KernelArgs& a, int* ws, const WorkspaceLayout& w_in, bool backward, cudaStream_t st) {
   WorkspaceLayout w = w_in;
   if (const char* e = getenv("B200_HSTU_CHUNK")) w.chunk_seqs = atoi(e) > 0 ? atoi(e) : w.chunk_seqs;
-  build_block_index<<<1, 1024, 0, st>>>(a, ws, w);
+  // tables in shared memory when they fit under the default 48 KB (next to 4 KB of static shared memory)
+  const long long index_ints = 3 * w.nbins;
+  const int index_smem = index_ints <= 10240 ? 1 : 0;
+  build_block_index<<<1, 1024, index_smem ? index_ints * sizeof(int) : 0, st>>>(a, ws, w, index_smem);
   const int blocks = sm_count() * 2;
   const int stride = main_grid(w);
+  const long long item_ints = w.nbins + (a.B + w.chunk_seqs - 1) / w.chunk_seqs + 1;
+  const int item_smem = item_ints <= 10240 ? 1 : 0;
+  const size_t item_bytes = item_smem ? item_ints * sizeof(int) : 0;
   if (!backward)
-    build_work_items<T><<<blocks, 256, 0, st>>>(a, ws, w, stride, reinterpret_cast<T*>(a.o), a.o_rs, a.H * a.Dv,
+    build_work_items<T><<<blocks, 256, item_bytes, st>>>(a, ws, w, stride, item_smem, reinterpret_cast<T*>(a.o), a.o_rs, a.H * a.Dv,
                                                 (T*)nullptr, 0, 0, (T*)nullptr, 0, 0);
   else
-    build_work_items<T><<<blocks, 256, 0, st>>>(a, ws, w, stride, reinterpret_cast<T*>(a.dq), a.dq_rs, a.H * a.Dqk,
+    build_work_items<T><<<blocks, 256, item_bytes, st>>>(a, ws, w, stride, item_smem, reinterpret_cast<T*>(a.dq), a.dq_rs, a.H * a.Dqk,
                                                 reinterpret_cast<T*>(a.dk), a.dk_rs, a.H * a.Dqk,
                                                 reinterpret_cast<T*>(a.dv), a.dv_rs, a.H * a.Dv);
   return cudaGetLastError();
