@@ -197,6 +197,45 @@ def test_linearity_in_v_and_dout_full_size_config():
         assert rel_l2(got[s:e].float(), ref) <= 6e-3
 
 
+def _full_size_batches():
+    from recir_b200 import sharding
+    hist, tg = workload.config4_lengths(1024)
+    lengths = hist + tg
+    mine = sharding.token_balanced_partition(lengths, 8)[0]
+    return {"cfg3": lambda: workload.config3(),
+            "cfg4_shard": lambda: workload.config4_layer(lengths[mine], tg[mine], layer=0)}
+
+
+@pytest.mark.parametrize("name", ["cfg3", "cfg4_shard"])
+def test_sequences_are_independent_at_full_size(name):
+    """Size-independent property on the full long-window shape (32 sequences up to 8 k tokens, H=8) and
+    on one rank's shard of the Zipf batch (128 sequences, about 200 k tokens): running the first and
+    the second half of the sequences as two batches gives bit-identical rows to running them together
+    (no sequence sees another one, and the dynamic work distribution does not change any result)."""
+    bt = _full_size_batches()[name]()
+    d = lambda x: x.to(DEV)
+    q, k, v, do = d(bt.q), d(bt.k), d(bt.v), d(bt.dout)
+    off, nt = d(bt.seq_offsets), d(bt.num_targets)
+    tail = (bt.max_seq_len, bt.alpha, bt.causal)
+    opts = (bt.contextual_seq_len, bt.max_attn_len, None, bt.full_attn_size)
+
+    def run(lo, hi):  # sequences [lo, hi)
+        s, e = int(bt.seq_offsets[lo]), int(bt.seq_offsets[hi])
+        a = ((off[lo:hi + 1] - off[lo]).contiguous(), *tail, nt[lo:hi].contiguous(), *opts)
+        o = torch.ops.recir.b200_hstu_attention_fwd(q[s:e], k[s:e], v[s:e], *a)
+        g = torch.ops.recir.b200_hstu_attention_bwd(do[s:e], q[s:e], k[s:e], v[s:e], *a)
+        return (o, *g)
+
+    B = len(bt.lengths)
+    whole = run(0, B)
+    mid = int(bt.seq_offsets[B // 2])
+    first, second = run(0, B // 2), run(B // 2, B)
+    for w, a, b in zip(whole, first, second):
+        assert torch.isfinite(w.float()).all()
+        assert torch.equal(w[:mid], a) and torch.equal(w[mid:], b)
+    assert float(whole[0].float().abs().max()) > 0
+
+
 def test_autograd_through_the_operator():
     q, k, v, do, off, kw = _jagged_case(3, [150, 40], [6, 0], dtype=torch.float32, D=32)
     d = lambda x: x.to(DEV)
