@@ -202,7 +202,10 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
   DqShared& sh = *reinterpret_cast<DqShared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total_items = ws[0];
-  if (static_cast<int>(blockIdx.x) >= total_items) return;
+  if (static_cast<int>(blockIdx.x) >= total_items) {
+    grid_dependency_wait();  // see the end of the kernel
+    return;
+  }
   const int2* items = reinterpret_cast<const int2*>(ws + off_items);
   volatile int* abort_flag = &sh.abort_flag;
 
@@ -531,6 +534,10 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
+  // This kernel may have been started before the dK/dV kernel ahead of it in the stream finished
+  // (programmatic dependent launch): it must not complete first, or work queued behind it could see
+  // unfinished dK / dV.
+  grid_dependency_wait();
 }
 
 // ------------------------------------------------------------------------------------
@@ -561,6 +568,9 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
   DkvShared& sh = *reinterpret_cast<DkvShared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total_items = ws[0];
+  // The dQ kernel that follows in the stream reads nothing this kernel writes: let its CTAs start on
+  // the SMs that this kernel's CTAs leave, instead of after the last of them has finished.
+  grid_launch_dependents();
   if (static_cast<int>(blockIdx.x) >= total_items) return;
   const int2* items = reinterpret_cast<const int2*>(ws + off_items);
   volatile int* abort_flag = &sh.abort_flag;
@@ -978,7 +988,21 @@ cudaError_t tc_backward(const KernelArgs& a, int dtype, void* workspace, cudaStr
                         : (bf16 ? hstu_bwd_dq_tc<true, false> : hstu_bwd_dq_tc<false, false>);
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    kern<<<static_cast<unsigned>(grid), BWD_THREADS, smem, st>>>(maps, a, ws, w.off_items);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(BWD_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    // only behind the dK/dV kernel, whose output this kernel does not read
+    cfg.numAttrs = a.skip_dkv ? 0 : 1;
+    int* ws_arg = ws;
+    long long off_items = w.off_items;
+    e = cudaLaunchKernelEx(&cfg, kern, maps, a, ws_arg, off_items);
+    if (e != cudaSuccess) return e;
   }
   return cudaGetLastError();
 }

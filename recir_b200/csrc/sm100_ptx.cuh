@@ -98,6 +98,13 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   return mbar_wait_slow(bar, parity, abort_flag, status, code, limit_ns);
 }
 
+// Programmatic dependent launch.  A kernel launched with the programmatic-stream-serialisation
+// attribute may start while the kernel before it in the stream still runs, once every CTA of that kernel
+// has executed grid_launch_dependents() (or exited); grid_dependency_wait() blocks until the preceding
+// kernel has completed and its memory is visible (a no-op when there is no such dependency).
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Register reallocation between warpgroups (all four warps of a warpgroup must execute it).
 template <int N> __device__ __forceinline__ void setmaxnreg_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
