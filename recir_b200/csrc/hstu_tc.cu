@@ -87,6 +87,7 @@ __device__ void suffix_sum_exclusive(const int* in, int* out, long long n, int* 
 __global__ void __launch_bounds__(1024) build_block_index(KernelArgs a, int* ws, WorkspaceLayout w, int tables_in_smem) {
   __shared__ int sh[1024];
   extern __shared__ int tab[];
+  grid_launch_dependents();  // build_work_items may be made resident now; it waits for this kernel to finish
   int* sorted = ws + w.off_sorted;
   int* hist = tables_in_smem ? tab : ws + w.off_hist;
   int* cnt = tables_in_smem ? tab + w.nbins : ws + w.off_cnt;
@@ -164,6 +165,8 @@ __global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, W
                                                         int tables_in_smem, T* z0,
                                                         long long rs0, int w0, T* z1, long long rs1, int w1,
                                                         T* z2, long long rs2, int w2) {
+  grid_dependency_wait();    // build_block_index has finished and its tables are visible
+  grid_launch_dependents();  // the main kernel may be made resident; it waits for this kernel to finish
   const int* sorted = ws + w.off_sorted;
   const int* cnt = ws + w.off_cnt;
   const int* chunk_base = ws + w.off_chunk;
@@ -320,6 +323,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
   // dynamic shared memory is only guaranteed 16-byte aligned: round up to 1024
   FwdShared& sh = *reinterpret_cast<FwdShared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  grid_dependency_wait();  // launched as a dependent of build_work_items: the work list is complete from here on
   const int total_items = ws[0];
   if (static_cast<int>(blockIdx.x) >= total_items) return;  // uniform per CTA
   const int2* items = reinterpret_cast<const int2*>(ws + off_items);
@@ -891,13 +895,11 @@ static cudaError_t launch_prep_t(const KernelArgs& a, int* ws, const WorkspaceLa
   const int item_smem = item_ints <= 10240 ? 1 : 0;
   const size_t item_bytes = item_smem ? item_ints * sizeof(int) : 0;
   if (!backward)
-    build_work_items<T><<<blocks, 256, item_bytes, st>>>(a, ws, w, stride, item_smem, reinterpret_cast<T*>(a.o), a.o_rs, a.H * a.Dv,
-                                                (T*)nullptr, 0, 0, (T*)nullptr, 0, 0);
-  else
-    build_work_items<T><<<blocks, 256, item_bytes, st>>>(a, ws, w, stride, item_smem, reinterpret_cast<T*>(a.dq), a.dq_rs, a.H * a.Dqk,
-                                                reinterpret_cast<T*>(a.dk), a.dk_rs, a.H * a.Dqk,
-                                                reinterpret_cast<T*>(a.dv), a.dv_rs, a.H * a.Dv);
-  return cudaGetLastError();
+    return launch_dependent(build_work_items<T>, blocks, 256, item_bytes, st, true, a, ws, w, stride, item_smem,
+                            reinterpret_cast<T*>(a.o), a.o_rs, a.H * a.Dv, (T*)nullptr, 0, 0, (T*)nullptr, 0, 0);
+  return launch_dependent(build_work_items<T>, blocks, 256, item_bytes, st, true, a, ws, w, stride, item_smem,
+                          reinterpret_cast<T*>(a.dq), a.dq_rs, a.H * a.Dqk, reinterpret_cast<T*>(a.dk), a.dk_rs,
+                          a.H * a.Dqk, reinterpret_cast<T*>(a.dv), a.dv_rs, a.H * a.Dv);
 }
 
 cudaError_t launch_prep(const KernelArgs& a, bool bf16, int* ws, const WorkspaceLayout& w, bool backward,
@@ -979,7 +981,8 @@ cudaError_t tc_forward(const KernelArgs& a, int dtype, void* workspace, cudaStre
                       : (bf16 ? hstu_fwd_tc<true, false> : hstu_fwd_tc<false, false>);
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  kern<<<static_cast<unsigned>(main_grid(w)), FWD_THREADS, smem, st>>>(maps, a, ws, w.off_items);
+  e = launch_dependent(kern, static_cast<unsigned>(main_grid(w)), FWD_THREADS, smem, st, true, maps, a, ws, w.off_items);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

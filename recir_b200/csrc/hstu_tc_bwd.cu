@@ -568,8 +568,11 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
   DkvShared& sh = *reinterpret_cast<DkvShared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total_items = ws[0];
+  // Launched as a dependent of build_work_items: the work list is complete from here on.
+  grid_dependency_wait();
   // The dQ kernel that follows in the stream reads nothing this kernel writes: let its CTAs start on
-  // the SMs that this kernel's CTAs leave, instead of after the last of them has finished.
+  // the SMs that this kernel's CTAs leave, instead of after the last of them has finished.  (After the
+  // wait above, so that the dQ kernel cannot start before the work list is complete either.)
   grid_launch_dependents();
   if (static_cast<int>(blockIdx.x) >= total_items) return;
   const int2* items = reinterpret_cast<const int2*>(ws + off_items);
@@ -978,7 +981,8 @@ cudaError_t tc_backward(const KernelArgs& a, int dtype, void* workspace, cudaStr
                         : (bf16 ? hstu_bwd_dkv_tc<true, false> : hstu_bwd_dkv_tc<false, false>);
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    kern<<<static_cast<unsigned>(grid), BWD_THREADS, smem, st>>>(maps, a, ws, w.off_items);
+    e = launch_dependent(kern, static_cast<unsigned>(grid), BWD_THREADS, smem, st, true, maps, a, ws, w.off_items);
+    if (e != cudaSuccess) return e;
   }
   if (!a.skip_dq) {
     set_error_stage("backward: dQ kernel");
@@ -988,20 +992,9 @@ cudaError_t tc_backward(const KernelArgs& a, int dtype, void* workspace, cudaStr
                         : (bf16 ? hstu_bwd_dq_tc<true, false> : hstu_bwd_dq_tc<false, false>);
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(grid));
-    cfg.blockDim = dim3(BWD_THREADS);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    // only behind the dK/dV kernel, whose output this kernel does not read
-    cfg.numAttrs = a.skip_dkv ? 0 : 1;
-    int* ws_arg = ws;
-    long long off_items = w.off_items;
-    e = cudaLaunchKernelEx(&cfg, kern, maps, a, ws_arg, off_items);
+    // a dependent launch only behind the dK/dV kernel, whose output this kernel does not read; alone, it
+    // is an ordinary launch behind build_work_items
+    e = launch_dependent(kern, static_cast<unsigned>(grid), BWD_THREADS, smem, st, !a.skip_dkv, maps, a, ws, w.off_items);
     if (e != cudaSuccess) return e;
   }
   return cudaGetLastError();

@@ -20,6 +20,25 @@ int main_grid(const WorkspaceLayout& w);
 cudaError_t launch_prep(const KernelArgs& a, bool bf16, int* ws, const WorkspaceLayout& w, bool backward,
                         cudaStream_t st);
 
+// Launches `kern` so that it may be scheduled while the kernel before it in the stream still runs
+// (programmatic dependent launch): the kernel before must execute grid_launch_dependents(), and `kern`
+// must execute grid_dependency_wait() before it reads anything that kernel wrote.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_dependent(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t st,
+                                    bool dependent, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = dependent ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // Launches the bounded-wait self-test kernel (see b200_hstu_debug_bounded_wait).
 cudaError_t launch_bounded_wait_probe(int* status, int code, unsigned long long limit_ns, cudaStream_t st);
 
