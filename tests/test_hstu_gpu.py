@@ -430,3 +430,41 @@ def test_bounded_wait_gives_up_and_leaves_the_context_usable():
     n = int(c["offsets"][-1])
     assert max_abs(o32[:n], c["o"]) <= 2e-3
     assert rel_l2(o.float()[:n], c["o"]) <= 2e-2 and rel_l2(dk.float()[:n], c["dk"]) <= 2e-2
+
+
+def test_calls_can_be_captured_in_a_cuda_graph_and_replayed():
+    """The library neither allocates nor synchronises and launches only on the caller's stream (its
+    dependent launches included), so a forward + backward pair can be captured once and replayed;
+    replays on new input values give the same results as eager calls."""
+    c = golden_case("multi_tile")
+    kw = case_kwargs(c)
+    q, k, v, do = (_t(c[n], torch.bfloat16) for n in ("q", "k", "v", "do"))
+    off = _t(c["offsets"])
+    nt = None if kw["num_targets"] is None else _t(kw["num_targets"])
+    args = (off, kw["max_seq_len"], kw["alpha"], kw["causal"], nt, kw["contextual_seq_len"],
+            kw["max_attn_len"], None, kw["full_attn_size"])
+
+    def step():
+        o = torch.ops.recir.b200_hstu_attention_fwd(q, k, v, *args)
+        return (o, *torch.ops.recir.b200_hstu_attention_bwd(do, q, k, v, *args))
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        captured = step()
+    for scale in (1.0, 0.5):
+        q.copy_(_t(c["q"], torch.bfloat16) * scale)  # new values in the captured input buffers
+        graph.replay()
+        torch.cuda.synchronize()
+        got = [x.clone() for x in captured]
+        want = step()
+        torch.cuda.synchronize()
+        for g, w in zip(got, want):
+            assert torch.equal(g, w)
+    assert float(got[0].float().abs().max()) > 0
