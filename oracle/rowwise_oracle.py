@@ -111,3 +111,28 @@ def layer_norm_mul_quantized(x, u, weight, bias, eps, dtype="float32", silu_u=Fa
     combined = np.concatenate(parts, axis=1)
     scale, q8 = quantize_fp8_rowwise(combined)
     return combined, mean, rstd, scale, q8
+
+
+def e4m3_decode(code):
+    """float8 e4m3fn bytes -> float32 (exact)."""
+    c = np.asarray(code, dtype=np.uint8).astype(np.int64)
+    sign = np.where(c & 0x80, -1.0, 1.0)
+    e = (c >> 3) & 0xF
+    m = c & 0x7
+    normal = np.exp2((e - 7).astype(np.float64)) * (1.0 + m / 8.0)
+    sub = m * 2.0 ** -9
+    v = np.where(e == 0, sub, normal)
+    v = np.where((c & 0x7F) == 0x7F, np.nan, v)
+    return (sign * v).astype(np.float32)
+
+
+def fp8_rowwise_addmm(a_code, b_code, a_scale, b_scale, bias=None, dtype="float32"):
+    """``(a * a_scale[:, None]) @ (b * b_scale[:, None]).T + bias`` for e4m3 bytes ``a`` [M, K], ``b`` [N, K];
+    kjt_split_per_feature.cpp:533-556 (dequantise to float32, at::mm, add the bias in float32, cast).
+    The sum is taken in float64 here: the float32 summation order of a GEMM is not part of the contract."""
+    a = e4m3_decode(a_code) * np.asarray(a_scale, dtype=np.float32)[:, None]
+    b = e4m3_decode(b_code) * np.asarray(b_scale, dtype=np.float32)[:, None]
+    out = a.astype(np.float64) @ b.astype(np.float64).T
+    if bias is not None:
+        out = out + np.asarray(bias, dtype=np.float32).astype(np.float64)
+    return round_to(out.astype(np.float32), dtype)

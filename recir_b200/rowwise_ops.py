@@ -37,6 +37,9 @@ _LIBDEF.define(
 
 _LIBDEF.define("b200_addmm_fwd(Tensor x, Tensor w, Tensor y) -> Tensor")
 _LIBDEF.define(
+    "b200_fp8_rowwise_addmm_fwd(Tensor a, Tensor b, Tensor a_scale, Tensor b_scale, Tensor bias, bool has_bias, "
+    "bool bias_is_2d, ScalarType dot_out_dtype, bool allow_tf32, bool use_fast_accum) -> Tensor")
+_LIBDEF.define(
     "b200_weighted_layer_norm_quantization_fwd(Tensor x, Tensor weight, Tensor bias, float eps, Tensor mean, Tensor rstd, "
     "int BLOCK_D) -> (Tensor, Tensor, Tensor, Tensor, Tensor)")
 
@@ -210,3 +213,45 @@ def _addmm_fake(x, w, y):
 
 _LIBDEF.impl("b200_addmm_fwd", _addmm_cuda, "CUDA")
 torch.library.register_fake("recir::b200_addmm_fwd", _addmm_fake)
+
+
+def _fp8_rowwise_addmm_cuda(a, b, a_scale, b_scale, bias, has_bias, bias_is_2d, dot_out_dtype, allow_tf32,
+                            use_fast_accum):
+    """The projection behind the quantised layer-norm stage: ``(a * a_scale[:, None]) @ (b * b_scale[:, None]).T
+    + bias`` with ``a`` [M, K] and ``b`` [N, K] in float8 e4m3 and one float32 scale per row of each
+    (``generative_recommenders::_triton_fp8_rowwise_addmm_fwd_impl``,
+    ``recir/ops/kjt_split_per_feature.cpp:533-556``, which dequantises and calls ``at::mm``; it ignores
+    ``bias_is_2d``, ``allow_tf32`` and ``use_fast_accum``, and so does this).  A plain GEMM, handed to the
+    vendor library's fp8 path: the float8 products are exact and accumulate in float32, so only the
+    summation order differs from the reference."""
+    if a.dim() != 2 or b.dim() != 2:
+        raise ValueError("a and b must be two-dimensional")
+    if a.shape[1] != b.shape[1]:
+        raise ValueError("a and b dimensions are incompatible")
+    if a.dtype != torch.float8_e4m3fn or b.dtype != torch.float8_e4m3fn:
+        raise ValueError("a and b must be float8_e4m3fn")
+    if a_scale.numel() != a.shape[0] or b_scale.numel() != b.shape[0]:
+        raise ValueError("one scale per row of a and of b is required")
+    if a.shape[1] % 16 != 0 or b.shape[0] % 16 != 0:
+        raise ValueError("the reduction and output dimensions must be multiples of 16")
+    sa = a_scale.reshape(-1, 1).to(torch.float32).contiguous()
+    sb = b_scale.reshape(1, -1).to(torch.float32).contiguous()
+    # the library wants a row-major [M, K] and a column-major [K, N]: b.T of a contiguous [N, K] is that
+    a, bt = a.contiguous(), b.contiguous().t()
+    # Unscaled float32 sums from the library's fp8 GEMM, then row scale x column scale (+ bias) and the
+    # final rounding in one element-wise pass, as the reference rounds once.  (The library's own
+    # row-wise scaling writes 16-bit outputs only, and gave different values on small float16 cases.)
+    one = torch.ones((), dtype=torch.float32, device=a.device)
+    out = torch._scaled_mm(a, bt, scale_a=one, scale_b=one, out_dtype=torch.float32) * sa * sb
+    if has_bias:
+        out = out + bias.float()
+    return out.to(dot_out_dtype)
+
+
+def _fp8_rowwise_addmm_fake(a, b, a_scale, b_scale, bias, has_bias, bias_is_2d, dot_out_dtype, allow_tf32,
+                            use_fast_accum):
+    return a.new_empty((a.shape[0], b.shape[0]), dtype=dot_out_dtype)
+
+
+_LIBDEF.impl("b200_fp8_rowwise_addmm_fwd", _fp8_rowwise_addmm_cuda, "CUDA")
+torch.library.register_fake("recir::b200_fp8_rowwise_addmm_fwd", _fp8_rowwise_addmm_fake)

@@ -156,3 +156,45 @@ def test_addmm_operator_is_the_library_gemm():
         assert torch.equal(torch.ops.recir.b200_addmm_fwd(x, w, y), torch.addmm(y, x, w))
     with pytest.raises(ValueError, match="incompatible"):
         torch.ops.recir.b200_addmm_fwd(x, w[:32], y)
+
+
+FP8MM = np.load(os.path.join(os.path.dirname(__file__), "golden", "fp8_addmm_golden.npz"))
+
+
+@pytest.mark.parametrize("name", [str(n) for n in FP8MM["names"]])
+def test_fp8_rowwise_addmm_matches_reference_golden(name):
+    """The fp8 projection behind the quantised layer-norm stage, through the library's fp8 GEMM with
+    row-wise scales, against the reference operator's output on the same e4m3 operands."""
+    dt, has_bias = FP8MM[f"{name}/cfg"]
+    a = torch.as_tensor(FP8MM[f"{name}/a"]).cuda().view(torch.float8_e4m3fn)
+    b = torch.as_tensor(FP8MM[f"{name}/b"]).cuda().view(torch.float8_e4m3fn)
+    sa, sb = _t(FP8MM[f"{name}/a_scale"]), _t(FP8MM[f"{name}/b_scale"])
+    bias = _t(FP8MM[f"{name}/bias"], dt) if has_bias == "1" else torch.empty(0, device="cuda")
+    y = torch.ops.recir.b200_fp8_rowwise_addmm_fwd(a, b, sa, sb, bias, has_bias == "1", False, DT[dt], False, False)
+    assert y.dtype == DT[dt] and tuple(y.shape) == FP8MM[f"{name}/y"].shape
+    want = FP8MM[f"{name}/y"].astype(np.float64)
+    got = y.float().cpu().numpy().astype(np.float64)
+    tol = (1e-5 if dt == "float32" else 2 * ULP[dt]) * np.maximum(np.abs(want), float(np.abs(want).max()) * 1e-2)
+    assert (np.abs(got - want) <= tol).all(), float(np.abs(got - want).max())
+
+
+def test_fp8_rowwise_addmm_chained_behind_the_quantised_norm_stage():
+    """layer-norm x gate with fp8 copy -> fp8 projection, full STU width, against the oracle chain."""
+    g = torch.Generator().manual_seed(5)
+    rows, cols, n_out = 1024, 512, 256
+    x = (torch.randn(rows, cols, generator=g) * 1.5).to(torch.bfloat16).cuda()
+    u = (torch.randn(rows, cols, generator=g) * 2.0).to(torch.bfloat16).cuda()
+    w = (torch.randn(cols, generator=g) * 0.5 + 1.0).to(torch.bfloat16).cuda()
+    b = (torch.randn(cols, generator=g) * 0.2).to(torch.bfloat16).cuda()
+    wq = (torch.randn(n_out, cols, generator=g) * 30.0).clamp(-448, 448).to(torch.float8_e4m3fn).cuda()
+    ws = (torch.rand(n_out, generator=g) * 0.01 + 0.001).cuda()
+    y, mean, rstd, scale, q8 = torch.ops.recir.b200_layer_norm_mul_dropout_quantization_fwd(
+        x, u, w, b, 1e-5, 0.0, False, False, False, False, "silu", 0, True, 0)
+    out = torch.ops.recir.b200_fp8_rowwise_addmm_fwd(q8, wq, scale, ws, torch.empty(0, device="cuda"), False, False,
+                                                     torch.bfloat16, False, False)
+    want = ro.fp8_rowwise_addmm(q8.view(torch.uint8).cpu().numpy(), wq.view(torch.uint8).cpu().numpy(),
+                                scale.cpu().numpy(), ws.cpu().numpy(), None, "bfloat16")
+    _close(out, want, "bfloat16", "fp8 projection")
+    with pytest.raises(ValueError, match="float8"):
+        torch.ops.recir.b200_fp8_rowwise_addmm_fwd(y, wq, scale, ws, torch.empty(0, device="cuda"), False, False,
+                                                   torch.bfloat16, False, False)

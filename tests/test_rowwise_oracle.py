@@ -81,3 +81,27 @@ def test_e4m3_known_codes():
     # ties go to the even code: halfway between 1.0 (0x38) and 1.125 (0x39) -> 0x38
     assert ro.e4m3_encode(np.array([1.0625], np.float32))[0] == 0x38
     assert ro.e4m3_encode(np.array([1.1875], np.float32))[0] == 0x3A
+
+
+FP8MM = np.load(os.path.join(os.path.dirname(__file__), "golden", "fp8_addmm_golden.npz"))
+
+
+def test_e4m3_decode_inverts_encode_on_every_finite_code():
+    codes = np.array([c for c in range(256) if (c & 0x7F) != 0x7F], dtype=np.uint8)
+    vals = ro.e4m3_decode(codes)
+    assert np.isfinite(vals).all() and float(np.abs(vals).max()) == 448.0
+    back = ro.e4m3_encode(vals)
+    # +0 and -0 keep their sign bit; every other code round-trips exactly
+    assert np.array_equal(back, codes)
+
+
+@pytest.mark.parametrize("name", [str(n) for n in FP8MM["names"]])
+def test_fp8_rowwise_addmm_matches_reference(name):
+    dt, has_bias = FP8MM[f"{name}/cfg"]
+    bias = FP8MM[f"{name}/bias"] if has_bias == "1" else None
+    y = ro.fp8_rowwise_addmm(FP8MM[f"{name}/a"], FP8MM[f"{name}/b"], FP8MM[f"{name}/a_scale"],
+                             FP8MM[f"{name}/b_scale"], bias, dt)
+    want = FP8MM[f"{name}/y"].astype(np.float64)
+    # float32: the reference sums K products in float32 in its own order; 16-bit: one last-place flip
+    tol = (1e-5 if dt == "float32" else ULP[dt]) * np.maximum(np.abs(want), float(np.abs(want).max()) * 1e-2)
+    assert (np.abs(y.astype(np.float64) - want) <= tol).all()
