@@ -136,3 +136,19 @@ def fp8_rowwise_addmm(a_code, b_code, a_scale, b_scale, bias=None, dtype="float3
     if bias is not None:
         out = out + np.asarray(bias, dtype=np.float32).astype(np.float64)
     return round_to(out.astype(np.float32), dtype)
+
+
+def jagged_dense_bmm_add(seq_offsets, jagged, dense, bias, elementwise=False, dtype="float32"):
+    """``out[rows of b] = jagged[rows of b] @ dense[b] + bias[b]`` (``bias[row]`` when elementwise);
+    kjt_split_per_feature.cpp:262-305 (one addmm per sequence, concatenated).  Sums in float64: the
+    float32 summation order of a GEMM is not part of the contract."""
+    offs = np.asarray(seq_offsets, dtype=np.int64)
+    jag = np.asarray(jagged, dtype=np.float32).astype(np.float64)
+    den = np.asarray(dense, dtype=np.float32).astype(np.float64)
+    bia = np.asarray(bias, dtype=np.float32).astype(np.float64)
+    parts = []
+    for b in range(den.shape[0]):
+        s, e = int(offs[b]), int(offs[b + 1])
+        parts.append(jag[s:e] @ den[b] + (bia[s:e] if elementwise else bia[b]))
+    out = np.concatenate(parts, 0) if parts else np.zeros((0, den.shape[2]))
+    return round_to(out.astype(np.float32), dtype)

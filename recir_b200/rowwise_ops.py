@@ -43,6 +43,10 @@ _LIBDEF.define(
     "b200_weighted_layer_norm_quantization_fwd(Tensor x, Tensor weight, Tensor bias, float eps, Tensor mean, Tensor rstd, "
     "int BLOCK_D) -> (Tensor, Tensor, Tensor, Tensor, Tensor)")
 
+_LIBDEF.define(
+    "b200_jagged_dense_bmm_add_fwd(int max_seq_len, Tensor seq_offsets, Tensor jagged, Tensor dense, Tensor bias, "
+    "bool elementwise=False) -> (Tensor, int, int, int)")
+
 # Kernel launches issued through this module since import.
 launch_counter = 0
 
@@ -255,3 +259,51 @@ def _fp8_rowwise_addmm_fake(a, b, a_scale, b_scale, bias, has_bias, bias_is_2d, 
 
 _LIBDEF.impl("b200_fp8_rowwise_addmm_fwd", _fp8_rowwise_addmm_cuda, "CUDA")
 torch.library.register_fake("recir::b200_fp8_rowwise_addmm_fwd", _fp8_rowwise_addmm_fake)
+
+
+def _jagged_dense_bmm_add_cuda(max_seq_len, seq_offsets, jagged, dense, bias, elementwise=False):
+    """Rows of sequence ``b`` times that sequence's own matrix, plus a bias per sequence (or per row):
+    ``out[rows of b] = jagged[rows of b] @ dense[b] + bias[b]``
+    (``generative_recommenders::triton_jagged_dense_bmm_add_fwd``,
+    ``recir/ops/kjt_split_per_feature.cpp:262-305``, which loops over the sequences with ``at::addmm``).
+    One grouped GEMM of the vendor library over the jagged rows, no padding and no host read of the
+    offsets; bfloat16 only (the library's grouped GEMM: float32 accumulation, bfloat16 product, then the bias
+    is added in float32 and the sum rounded).  ``jagged.shape[0]`` must equal ``seq_offsets[-1]`` (not checked: that would need a
+    host read); rows past it would be left unspecified by the library and are returned as zeros."""
+    if jagged.dim() != 2:
+        raise ValueError("jagged must be two-dimensional")
+    if dense.dim() != 3:
+        raise ValueError("dense must be three-dimensional")
+    if seq_offsets.dim() != 1:
+        raise ValueError("sequence offsets must be one-dimensional")
+    B, K, N = dense.shape
+    if K != jagged.shape[1]:
+        raise ValueError("jagged and dense input dimensions are incompatible")
+    if seq_offsets.numel() != B + 1:
+        raise ValueError("sequence offsets size must match the dense batch size")
+    if tuple(bias.shape) != ((jagged.shape[0], N) if elementwise else (B, N)):
+        raise ValueError("bias dimensions are incompatible with the output")
+    if jagged.dtype != torch.bfloat16 or dense.dtype != torch.bfloat16:
+        raise ValueError(f"unsupported dtype {jagged.dtype}: the grouped GEMM takes bfloat16")
+    T = jagged.shape[0]
+    if T == 0 or B == 0:
+        return jagged.new_zeros((T, N)), B, K, N
+    ends = seq_offsets[1:].to(torch.int32)
+    prod = torch.nn.functional.grouped_mm(jagged.contiguous(), dense.contiguous(), offs=ends).float()
+    rows = torch.arange(T, device=jagged.device, dtype=ends.dtype)
+    seq = torch.searchsorted(ends, rows, right=True)  # sequence of every row; B for rows past the last offset
+    owned = (seq < B).unsqueeze(1)
+    if elementwise:
+        out = prod + bias.float()
+    else:
+        out = prod + bias.float()[seq.clamp(max=B - 1)]
+    return torch.where(owned, out, torch.zeros((), device=out.device)).to(jagged.dtype), B, K, N
+
+
+
+def _jagged_dense_bmm_add_fake(max_seq_len, seq_offsets, jagged, dense, bias, elementwise=False):
+    return jagged.new_empty((jagged.shape[0], dense.shape[2])), dense.shape[0], dense.shape[1], dense.shape[2]
+
+
+_LIBDEF.impl("b200_jagged_dense_bmm_add_fwd", _jagged_dense_bmm_add_cuda, "CUDA")
+torch.library.register_fake("recir::b200_jagged_dense_bmm_add_fwd", _jagged_dense_bmm_add_fake)

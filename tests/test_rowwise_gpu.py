@@ -198,3 +198,53 @@ def test_fp8_rowwise_addmm_chained_behind_the_quantised_norm_stage():
     with pytest.raises(ValueError, match="float8"):
         torch.ops.recir.b200_fp8_rowwise_addmm_fwd(y, wq, scale, ws, torch.empty(0, device="cuda"), False, False,
                                                    torch.bfloat16, False, False)
+
+
+JBMM = np.load(os.path.join(os.path.dirname(__file__), "golden", "jagged_bmm_golden.npz"))
+
+
+@pytest.mark.parametrize("name", [str(n) for n in JBMM["names"] if str(n).startswith("bf16")])
+def test_jagged_dense_bmm_add_matches_reference_golden(name):
+    """Per-sequence projection of jagged rows as one grouped GEMM of the library, against the reference
+    operator's output (bias per sequence and per row, empty sequences in the batch)."""
+    dt, elementwise = JBMM[f"{name}/cfg"]
+    offs = torch.as_tensor(JBMM[f"{name}/offsets"]).cuda()
+    jag, den, bias = (_t(JBMM[f"{name}/{k}"], dt) for k in ("jagged", "dense", "bias"))
+    y, B, K, N = torch.ops.recir.b200_jagged_dense_bmm_add_fwd(int(np.diff(JBMM[f"{name}/offsets"]).max()), offs, jag,
+                                                              den, bias, elementwise == "1")
+    assert (B, K, N) == tuple(den.shape) and y.dtype == DT[dt]
+    want = JBMM[f"{name}/y"].astype(np.float64)
+    got = y.float().cpu().numpy().astype(np.float64)
+    assert got.shape == want.shape
+    tol = 2 * ULP[dt] * np.maximum(np.abs(want), float(np.abs(want).max()) * 5e-2)
+    assert (np.abs(got - want) <= tol).all(), float(np.abs(got - want).max())
+
+
+def test_jagged_dense_bmm_add_on_a_zipf_batch_and_validation():
+    from recir_b200 import workload
+    hist, tg = workload.config4_lengths(64)
+    lengths = hist + tg
+    offs = torch.as_tensor(np.concatenate([[0], np.cumsum(lengths)])).cuda()
+    T, B, K, N = int(offs[-1]), 64, 128, 64
+    g = torch.Generator().manual_seed(3)
+    jag = torch.randn(T, K, generator=g).to(torch.bfloat16).cuda()
+    den = (torch.randn(B, K, N, generator=g) * 0.2).to(torch.bfloat16).cuda()
+    bias = torch.randn(B, N, generator=g).to(torch.bfloat16).cuda()
+    y, *_ = torch.ops.recir.b200_jagged_dense_bmm_add_fwd(int(lengths.max()), offs, jag, den, bias, False)
+    # the library's grouped GEMM writes the product in bfloat16 before the bias is added: restate that
+    prod = ro.jagged_dense_bmm_add(offs.cpu().numpy(), jag.float().cpu().numpy(), den.float().cpu().numpy(),
+                                   np.zeros((B, N), np.float32), False, "bfloat16")
+    seq = np.repeat(np.arange(B), lengths)
+    want = ro.round_to(prod + bias.float().cpu().numpy()[seq], "bfloat16")
+    got = y.float().cpu().numpy().astype(np.float64)
+    # a last-place flip of the bfloat16 product (summation order) moves the sum by one ulp of the product
+    tol = 2.0 ** -7 * np.maximum(np.abs(prod), np.abs(want)) + 1e-6
+    bad = np.abs(got - want) > tol
+    assert bad.mean() <= 1e-3 and np.abs(got - want).max() <= 4 * tol.max()
+    once = ro.jagged_dense_bmm_add(offs.cpu().numpy(), jag.float().cpu().numpy(), den.float().cpu().numpy(),
+                                   bias.float().cpu().numpy(), False, "float32")
+    assert np.abs(got - once).max() <= 2.0 ** -6 * float(np.abs(prod).max())  # against the single-rounding reference
+    with pytest.raises(ValueError, match="incompatible"):
+        torch.ops.recir.b200_jagged_dense_bmm_add_fwd(8, offs, jag, den[:, :64], bias, False)
+    with pytest.raises(ValueError, match="bfloat16"):
+        torch.ops.recir.b200_jagged_dense_bmm_add_fwd(8, offs, jag.float(), den.float(), bias.float(), False)

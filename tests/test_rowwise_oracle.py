@@ -105,3 +105,18 @@ def test_fp8_rowwise_addmm_matches_reference(name):
     # float32: the reference sums K products in float32 in its own order; 16-bit: one last-place flip
     tol = (1e-5 if dt == "float32" else ULP[dt]) * np.maximum(np.abs(want), float(np.abs(want).max()) * 1e-2)
     assert (np.abs(y.astype(np.float64) - want) <= tol).all()
+
+
+JBMM = np.load(os.path.join(os.path.dirname(__file__), "golden", "jagged_bmm_golden.npz"))
+
+
+@pytest.mark.parametrize("name", [str(n) for n in JBMM["names"]])
+def test_jagged_dense_bmm_add_matches_reference(name):
+    dt, elementwise = JBMM[f"{name}/cfg"]
+    y = ro.jagged_dense_bmm_add(JBMM[f"{name}/offsets"], JBMM[f"{name}/jagged"], JBMM[f"{name}/dense"],
+                                JBMM[f"{name}/bias"], elementwise == "1", dt)
+    want = JBMM[f"{name}/y"].astype(np.float64)
+    assert y.shape == want.shape
+    # float32: summation order; bfloat16: the reference rounds the product before the bias is added
+    tol = (1e-5 if dt == "float32" else 2 * ULP[dt]) * np.maximum(np.abs(want), float(np.abs(want).max()) * 5e-2)
+    assert (np.abs(y.astype(np.float64) - want) <= tol).all(), float(np.abs(y - want).max())
