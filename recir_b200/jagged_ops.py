@@ -25,6 +25,13 @@ _LIBDEF.define("b200_jagged_to_padded_dense(Tensor values, Tensor[] offsets, int
 _LIBDEF.define("b200_concat_2d_jagged(Tensor values_left, Tensor offsets_left, Tensor values_right, Tensor offsets_right) -> Tensor")
 _LIBDEF.define("b200_split_2d_jagged(Tensor values, Tensor offsets_left, Tensor offsets_right, SymInt seq_len_a, SymInt seq_len_b) -> (Tensor, Tensor)")
 
+_LIBDEF.define(
+    "b200_concat_2D_jagged_fwd_op(int max_seq_len, Tensor values_a, Tensor values_b, Tensor? offsets_a, "
+    "Tensor? offsets_b, bool is_replace, int n_prefix_from_right) -> Tensor")
+_LIBDEF.define(
+    "b200_split_2D_jagged_fwd_op(Tensor values, int max_seq_len, Tensor offsets_a, Tensor offsets_b, int seq_len_a, "
+    "int seq_len_b, bool is_dense_a, bool is_dense_b, int dense_size, int n_prefix_to_right, int B) -> (Tensor, Tensor)")
+
 launch_counter = 0
 
 
@@ -123,6 +130,111 @@ def _split_cuda(values, offsets_left, offsets_right, seq_len_a, seq_len_b):
     _launch(_lib.JAGGED_SPLIT_LEFT, left, values, None, offsets_left, offsets_right, n)
     _launch(_lib.JAGGED_SPLIT_RIGHT, right, values, None, offsets_left, offsets_right, n)
     return left, right
+
+
+def _uniform(batch: int, length: int, like: torch.Tensor) -> torch.Tensor:
+    return torch.arange(batch + 1, device=like.device, dtype=torch.int64) * int(length)
+
+
+def _gr_concat_cuda(max_seq_len, values_a, values_b, offsets_a, offsets_b, is_replace, n_prefix_from_right):
+    """``generative_recommenders::concat_2D_jagged_fwd_op`` (``recir/ops/kjt_split_per_feature.cpp:100-196``):
+    per sequence ``[b[:p], a, b[p:]]`` (``p = n_prefix_from_right``), or with ``is_replace`` the rows of
+    ``a`` with its last ``len(b)`` rows replaced by ``b``.  A side without offsets is dense ``[B, L, D]``, i.e.
+    jagged with uniform offsets.  Composed from the row-gather kernel's concat / split passes (one pass
+    for the plain form, two for the replace form, four with a prefix); like every operator here it reads
+    no offset on the host, so the per-sequence length checks of the reference (``:170-183``) are not made."""
+    if offsets_a is None and offsets_b is None:
+        raise ValueError("at least one input must be jagged")
+    p = int(n_prefix_from_right)
+    if p < 0:
+        raise ValueError(f"n_prefix_from_right must be non-negative, got {p}")
+    if is_replace and p != 0:
+        raise ValueError("n_prefix_from_right is not supported when is_replace is true")
+    if p != 0 and (offsets_a is None or offsets_b is None):
+        raise ValueError("n_prefix_from_right is only supported for two jagged inputs")
+    if values_a.dtype != values_b.dtype:
+        raise ValueError("values_a and values_b must have the same dtype")
+    if values_a.shape[-1] != values_b.shape[-1]:
+        raise ValueError("values_a and values_b must have the same embedding dimension")
+    if offsets_a is None:
+        if values_a.dim() != 3:
+            raise ValueError("dense values_a must be three-dimensional")
+        if offsets_b.numel() != values_a.shape[0] + 1:
+            raise ValueError("offsets_b size must match the dense batch size")
+        offsets_a = _uniform(values_a.shape[0], values_a.shape[1], values_a)
+    elif offsets_b is None:
+        if values_b.dim() != 3:
+            raise ValueError("dense values_b must be three-dimensional")
+        if offsets_a.numel() != values_b.shape[0] + 1:
+            raise ValueError("offsets_a size must match the dense batch size")
+        offsets_b = _uniform(values_b.shape[0], values_b.shape[1], values_b)
+    elif offsets_a.numel() != offsets_b.numel():
+        raise ValueError("offsets_a and offsets_b must have the same size")
+    (oa, ob), _ = _offsets(offsets_a, offsets_b)
+    batch = oa.shape[0] - 1
+    fa = values_a.reshape(-1, values_a.shape[-1])
+    fb = values_b.reshape(-1, values_b.shape[-1])
+    if is_replace:
+        keep = oa - ob  # rows of a that survive, as offsets
+        head, _tail = _split_cuda(fa, keep, ob, fa.shape[0] - fb.shape[0], fb.shape[0])
+        flat = _concat_cuda(head, keep, fb, ob)
+        return flat.reshape(values_a.shape) if values_a.dim() == 3 else flat
+    if p == 0:
+        return _concat_cuda(fa, oa, fb, ob)
+    op = _uniform(batch, p, fa).to(oa.dtype)
+    front, rest = _split_cuda(fb, op, ob - op, batch * p, fb.shape[0] - batch * p)
+    return _concat_cuda(_concat_cuda(front, op, fa, oa), op + oa, rest, ob - op)
+
+
+def _gr_split_cuda(values, max_seq_len, offsets_a, offsets_b, seq_len_a, seq_len_b, is_dense_a, is_dense_b,
+                   dense_size, n_prefix_to_right, B):
+    """``generative_recommenders::split_2D_jagged_fwd_op`` (``recir/ops/kjt_split_per_feature.cpp:430-489``),
+    the inverse of the concatenation above; a dense side has ``dense_size`` rows per sequence and comes
+    back as ``[B, dense_size, D]``."""
+    if values.dim() != 2:
+        raise ValueError("values must be two-dimensional")
+    batch, p = int(B), int(n_prefix_to_right)
+    oa = _uniform(batch, dense_size, values) if is_dense_a else offsets_a
+    ob = _uniform(batch, dense_size, values) if is_dense_b else offsets_b
+    (oa, ob), _ = _offsets(oa, ob)
+    rows_a = batch * int(dense_size) if is_dense_a else int(seq_len_a)
+    rows_b = batch * int(dense_size) if is_dense_b else int(seq_len_b)
+    if rows_a + rows_b != values.shape[0]:
+        raise ValueError("split lengths do not match values")
+    if p == 0:
+        a, b = _split_cuda(values, oa, ob, rows_a, rows_b)
+    else:
+        op = _uniform(batch, p, values).to(oa.dtype)
+        front_a, rest = _split_cuda(values, op + oa, ob - op, batch * p + rows_a, rows_b - batch * p)
+        front, a = _split_cuda(front_a, op, oa, batch * p, rows_a)
+        b = _concat_cuda(front, op, rest, ob - op)
+    if is_dense_a:
+        a = a.reshape(batch, int(dense_size), values.shape[1])
+    if is_dense_b:
+        b = b.reshape(batch, int(dense_size), values.shape[1])
+    return a, b
+
+
+_LIBDEF.impl("b200_concat_2D_jagged_fwd_op", _gr_concat_cuda, "CUDA")
+_LIBDEF.impl("b200_split_2D_jagged_fwd_op", _gr_split_cuda, "CUDA")
+
+
+@torch.library.register_fake("recir::b200_concat_2D_jagged_fwd_op")
+def _(max_seq_len, values_a, values_b, offsets_a, offsets_b, is_replace, n_prefix_from_right):
+    d = values_a.shape[-1]
+    if is_replace:
+        return values_a.new_empty(values_a.shape)
+    rows = values_a.reshape(-1, d).shape[0] + values_b.reshape(-1, d).shape[0]
+    return values_a.new_empty((rows, d))
+
+
+@torch.library.register_fake("recir::b200_split_2D_jagged_fwd_op")
+def _(values, max_seq_len, offsets_a, offsets_b, seq_len_a, seq_len_b, is_dense_a, is_dense_b, dense_size,
+      n_prefix_to_right, B):
+    d = values.shape[1]
+    a = values.new_empty((B, dense_size, d) if is_dense_a else (seq_len_a, d))
+    b = values.new_empty((B, dense_size, d) if is_dense_b else (seq_len_b, d))
+    return a, b
 
 
 _LIBDEF.impl("b200_jagged_to_padded_dense", _j2d_cuda, "CUDA")

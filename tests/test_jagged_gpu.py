@@ -109,3 +109,50 @@ def test_round_trips_at_benchmark_size_and_autograd():
     (cat * wc).sum().backward()
     gl, gr = ops.b200_split_2d_jagged(wc, hist_off[:3], tgt_off[:3], a.shape[0], b.shape[0])
     assert torch.equal(a.grad, gl) and torch.equal(b.grad, gr)
+
+
+GRJ = np.load(os.path.join(os.path.dirname(__file__), "golden", "gr_jagged_golden.npz"))
+
+
+@pytest.mark.parametrize("name", [str(n) for n in GRJ["names"]])
+def test_gr_concat_and_split_match_the_reference_golden(name):
+    """The concat / split operators with the schemas of generative_recommenders (dense sides, a prefix of
+    the right side moved to the front, the replace form), bit-exact against the reference operators."""
+    dense_a, dense_b, replace, p, batch, dense_size = (int(x) for x in GRJ[f"{name}/cfg"])
+    cu = lambda k: torch.as_tensor(GRJ[f"{name}/{k}"]).cuda()
+    oa = None if dense_a else cu("offsets_a")
+    ob = None if dense_b else cu("offsets_b")
+    a, b, cat = cu("a"), cu("b"), cu("cat")
+    got = torch.ops.recir.b200_concat_2D_jagged_fwd_op(16, a, b, oa, ob, bool(replace), p)
+    assert got.shape == cat.shape and torch.equal(got, cat)
+    if not replace:
+        dummy = torch.zeros(batch + 1, dtype=torch.int64, device="cuda")
+        sa, sb = torch.ops.recir.b200_split_2D_jagged_fwd_op(
+            cat, 16, dummy if dense_a else oa, dummy if dense_b else ob, 0 if dense_a else a.shape[0],
+            0 if dense_b else b.shape[0], bool(dense_a), bool(dense_b), dense_size, p, batch)
+        assert torch.equal(sa, a) and torch.equal(sb, b)
+
+
+def test_gr_concat_with_prefix_on_a_zipf_batch_against_the_oracle():
+    from oracle import jagged_oracle as jo
+    from recir_b200 import workload
+    hist, tg = workload.config4_lengths(96)
+    g = torch.Generator().manual_seed(9)
+    oa = torch.as_tensor(np.concatenate([[0], np.cumsum(hist)]))
+    ob = torch.as_tensor(np.concatenate([[0], np.cumsum(tg)]))
+    a = torch.randn(int(oa[-1]), 64, generator=g).to(torch.bfloat16)
+    b = torch.randn(int(ob[-1]), 64, generator=g).to(torch.bfloat16)
+    for replace, p in ((False, 0), (False, 3), (True, 0)):
+        if replace:  # the replaced tail must fit: whole sequences (history + targets) on the left
+            oa = torch.as_tensor(np.concatenate([[0], np.cumsum(hist + tg)]))
+            a = torch.randn(int(oa[-1]), 64, generator=g).to(torch.bfloat16)
+        got = torch.ops.recir.b200_concat_2D_jagged_fwd_op(4224, a.cuda(), b.cuda(), oa.cuda(), ob.cuda(), replace, p)
+        want = jo.gr_concat_2d_jagged(a.view(torch.int16).numpy(), b.view(torch.int16).numpy(), oa.numpy(), ob.numpy(),
+                                      replace, p)
+        assert np.array_equal(got.view(torch.int16).cpu().numpy(), want)
+        if not replace:
+            sa, sb = torch.ops.recir.b200_split_2D_jagged_fwd_op(got, 4224, oa.cuda(), ob.cuda(), a.shape[0], b.shape[0],
+                                                                 False, False, 0, p, 96)
+            assert torch.equal(sa.cpu(), a) and torch.equal(sb.cpu(), b)
+    with pytest.raises(ValueError, match="at least one input must be jagged"):
+        torch.ops.recir.b200_concat_2D_jagged_fwd_op(8, a.cuda(), b.cuda(), None, None, False, 0)
