@@ -87,7 +87,7 @@ typedef struct B200HstuParams {
   int64_t do_row_stride, dq_row_stride, dk_row_stride, dv_row_stride;
   int32_t B, H, Dqk, Dv;
   int32_t dtype;
-  int32_t max_seq_len; /* N: only used for the default 1/N scale */
+  int32_t max_seq_len; /* N: the default scale is 1/N; also sizes the locality chunks of the work list */
   int32_t max_attn_len;
   int32_t contextual_seq_len;
   int32_t full_attn_size;

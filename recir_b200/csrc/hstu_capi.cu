@@ -67,6 +67,7 @@ int validate(const B200HstuParams* p, int pass, KernelArgs* a) {
   a->scale_mode = p->attn_scale == nullptr ? 0 : ((p->flags & B200_HSTU_FLAG_SCALE_PER_TOKEN) ? 2 : 1);
   a->skip_dq = (p->flags & B200_HSTU_FLAG_BWD_SKIP_DQ) ? 1 : 0;
   a->skip_dkv = (p->flags & B200_HSTU_FLAG_BWD_SKIP_DKV) ? 1 : 0;
+  a->max_seq_len = static_cast<int>(p->max_seq_len > 0x3fffffff ? 0x3fffffff : p->max_seq_len);
   a->alpha = p->alpha;
   a->inv_n = 1.0f / static_cast<float>(p->max_seq_len);
   a->mask.causal = (p->flags & B200_HSTU_FLAG_CAUSAL) ? 1 : 0;

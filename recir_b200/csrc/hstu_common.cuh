@@ -86,6 +86,7 @@ struct KernelArgs {
   int B, H, Dqk, Dv;
   int offsets_i64, targets_i64, scale_mode;  // scale_mode: 0 = 1/N, 1 = scalar, 2 = per token
   int skip_dq, skip_dkv;                     // backward: leave one of the two passes out (timing aid)
+  int max_seq_len;                           // the caller's bound on sequence lengths (sizes locality chunks)
   float alpha;
   float inv_n;
   MaskOpts mask;
