@@ -3,18 +3,30 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N ... bench.py --gpus N ...
+    python bench.py --case NAME ...        (single-purpose runners, see bench_cases.py)
 
-One step = one forward + one backward of one STU-layer attention over one batch of
-synthetic jagged sequences.  At N=1 the batch is the single-layer train-step shape
-(B=64, H=4, D=128 bf16, history U[256,2048] + 64 targets: forward + backward with dO).
-At N>1 the global batch holds 64*N sequences of the same distribution, split across ranks
-by token-balanced sharding of whole sequences (no collective on the attention path), so
-the per-GPU work stays fixed ("weak" scaling).
+Headline (``value``): one step = one forward + one backward of one STU-layer attention over one
+batch of synthetic jagged sequences.  At N=1 the batch is the single-layer train-step shape
+(B=64, H=4, D=128 bf16, history U[256,2048] + 64 targets: forward + backward with dO).  At N>1
+the global batch holds 64*N sequences of the same distribution, split across ranks by
+token-balanced sharding of whole sequences (no collective on the attention path), so the per-GPU
+work stays fixed ("weak" scaling).
 
-Prints ONE JSON line on rank 0.  ``value`` is the whole-job useful (masked) TFLOP/s with
-inputs resident in HBM; ``e2e`` is the same metric with pinned host inputs copied in and
-results copied out inside the timed region; ``roofline`` is for the dominant kernel;
-``cpu_baseline`` is the reference operator on the host cores.
+The same JSON line also carries, measured in the same process:
+
+* ``stack8``    the 8-layer stack over the FIXED global batch of 1024 Zipf-length sequences, forward
+                through all layers then backward through all layers, token-balanced over the N ranks
+                (strong scaling: ``tokens_per_s`` at every N, per-rank times, imbalance);
+* ``long_window`` the long skewed sequences with a 1024-token window (N=1 only);
+* ``sustained`` the headline step looped for >= 2 s with the SM clock sampled meanwhile;
+* ``per_rank_ms`` every rank's own time for the headline region;
+* ``grad_check`` (N>1) per-sequence float64 checksums of dq, dk, dv of every rank's shard, exchanged
+                over NCCL and compared on rank 0 with the un-sharded run of the same global batch;
+* ``e2e``       the headline metric with pinned host inputs copied in and results copied out inside the
+                timed region, and the plain-copy floor for the same bytes;
+* ``roofline``  for the dominant kernel; ``cpu_baseline``: the reference operator on the host cores.
+
+Prints ONE JSON line on rank 0.
 """
 from __future__ import annotations
 
@@ -35,11 +47,14 @@ import torch
 
 METRIC = "hstu_attn_fwd_bwd_useful_tflops"
 UNIT = "TFLOP/s"
+WORKLOAD = "cfg2_stu_layer_fwd_bwd"
 NOMINAL_BF16_TFLOPS = 2250.0
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from the committed ncu capture of the same
-# B/H/D and length distribution (profiles/tc_kernels_cfg1_ncu_full.md), and that capture's token count.
+# B/H/D and length distribution (profiles/tc_kernels_cfg1_ncu_full.md names the build it was taken
+# from), and that capture's token count.
 NCU_CFG1_DRAM_BYTES = {"hstu_fwd_tc": 315.6e6, "hstu_bwd_dkv_tc": 471.1e6, "hstu_bwd_dq_tc": 405.8e6}
 NCU_CFG1_TOKENS = 78262
+NCU_CAPTURE = "profiles/tc_kernels_cfg1_ncu_full.md"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -62,14 +77,14 @@ class ClockSampler:
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index, self.rows, self.proc, self.thread = index, [], None, None
+    def __init__(self, index: int, period_ms: int = 20):
+        self.index, self.rows, self.proc, self.thread, self.period_ms = index, [], None, None, period_ms
 
     def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "20"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.period_ms)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -91,21 +106,25 @@ class ClockSampler:
             self.proc.kill()
         if self.thread is not None:
             self.thread.join(timeout=2)
-        sm, mx, reasons = [], [], set()
+        sm, mx, pw, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in self.rows:
             if len(r) < 7:
                 continue
             try:
-                sm.append(float(r[0])); mx.append(float(r[1]))
+                sm.append(float(r[0])); mx.append(float(r[1])); pw.append(float(r[2]))
             except ValueError:
                 continue
             for n, val in zip(names, r[3:7]):
                 if val.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "samples": len(sm), "reasons": sorted(reasons)}
+                "power_w_max": max(pw) if pw else None, "samples": len(sm), "reasons": sorted(reasons)}
 
+
+# --------------------------------------------------------------------------------------------------
+# workloads
+# --------------------------------------------------------------------------------------------------
 
 def build_global_batch(n_gpus: int):
     from recir_b200 import workload
@@ -124,81 +143,226 @@ def local_shard(batch, rank: int, world: int):
     return local, sharding.shard_summary(lengths, parts)
 
 
+def headline_config(world: int, H: int, D: int, T_global: int, pairs_global: int, shard_info) -> dict:
+    """The ``config`` object of the headline; both arms print the same keys."""
+    return {"workload": WORKLOAD, "B_global": 64 * world, "H": H, "D": D, "T_global": T_global,
+            "kept_pairs_per_head": pairs_global, "sharding": "token-balanced whole sequences, no collective",
+            "shard": shard_info, "l2": "inputs+outputs per step (~640 MB/GPU) exceed the 126 MB L2"}
+
+
+# --------------------------------------------------------------------------------------------------
+# the reference operator on the host cores (reference arm and cpu_baseline leg: ONE procedure)
+# --------------------------------------------------------------------------------------------------
+
+class ReferenceSample:
+    """A bounded sample of the N=1 headline batch for the reference's CPU operator: every 4th sequence by
+    sorted length (16 of 64), bf16, forward + backward through autograd, all host threads."""
+
+    def __init__(self):
+        from oracle import ref_op
+        from recir_b200 import workload
+        self.ref_op = ref_op
+        self.cores = os.cpu_count() or 1
+        torch.set_num_threads(self.cores)
+        self.batch = batch = build_global_batch(1)
+        order = np.argsort(batch.lengths, kind="stable")
+        self.sel = [int(i) for i in order[1::4]]
+        nt = batch.num_targets.numpy()
+        pairs = sum(workload.kept_pairs(int(batch.lengths[i]), int(nt[i])) for i in self.sel)
+        self.H, self.D = batch.q.shape[1], batch.q.shape[2]
+        self.flops = workload.useful_flops(pairs, self.H, self.D, self.D, backward=True)
+        self.kw = dict(max_seq_len=batch.max_seq_len, alpha=batch.alpha, causal=True, num_targets=batch.num_targets)
+        self.what = (f"{len(self.sel)} of {len(batch.lengths)} sequences (every 4th by sorted length) of the N=1 "
+                     f"batch, bf16, fwd+bwd via autograd through the reference operator")
+
+    def step(self):
+        b = self.batch
+        self.ref_op.ref_fwd_bwd_per_sequence(b.dout, b.q, b.k, b.v, b.seq_offsets, select=self.sel, **self.kw)
+
+    def run(self, steps: int, warmup: int):
+        """`warmup` untimed passes (thread pool, allocator, page cache), then `steps` timed ones."""
+        for _ in range(warmup):
+            self.step()
+        per = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            self.step()
+            per.append(time.perf_counter() - t0)
+        total = float(sum(per))
+        return {"value": self.flops * steps / total / 1e12, "seconds": total, "steps": steps,
+                "step_s_min": float(min(per)), "step_s_median": float(np.median(per))}
+
+
 def run_reference(args, rank: int):
     """Reference arm: the reference's own CPU operator on the host cores, same config and metric."""
     if rank != 0:
         return
     from oracle import ref_op
     from recir_b200 import workload
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    batch = build_global_batch(1)
-    kept = workload.total_kept_pairs(batch)
-    # bounded sample per step: every 4th sequence by sorted length (16 of 64), bf16, fwd+bwd
-    order = np.argsort(batch.lengths, kind="stable")
-    sel = [int(i) for i in order[1::4]]
-    nt = batch.num_targets.numpy()
-    pairs = sum(workload.kept_pairs(int(batch.lengths[i]), int(nt[i])) for i in sel)
-    H, D = batch.q.shape[1], batch.q.shape[2]
-    flops = workload.useful_flops(pairs, H, D, D, backward=True)
-    kw = dict(max_seq_len=batch.max_seq_len, alpha=batch.alpha, causal=True, num_targets=batch.num_targets)
-
-    def step():
-        ref_op.ref_fwd_bwd_per_sequence(batch.dout, batch.q, batch.k, batch.v, batch.seq_offsets,
-                                        select=sel, **kw)
-
-    for _ in range(args.warmup):
-        step()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step()
-    dt = time.perf_counter() - t0
-    value = flops * args.steps / dt / 1e12
-    sample = (f"{len(sel)} of {len(batch.lengths)} sequences (every 4th by sorted length) of the N=1 batch, "
-              f"bf16, fwd+bwd via autograd through the reference operator")
+    if not ref_op.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref shared object missing"}), flush=True)
+        return
+    rs = ReferenceSample()
+    warm = max(args.warmup, 2)
+    r = rs.run(args.steps, warm)
+    # same `config` keys and values as the other arm prints at this N (the timed sample is of the N=1 batch)
+    from recir_b200 import sharding
+    n = max(args.gpus, 1)
+    g = rs.batch if n == 1 else build_global_batch(n)
+    parts = sharding.token_balanced_partition(g.lengths, n)
+    cfg = headline_config(n, rs.H, rs.D, g.total_tokens, workload.total_kept_pairs(g),
+                          sharding.shard_summary(g.lengths, parts))
+    sample = rs.what + f"; {r['steps']} timed pass(es) in {r['seconds']:.1f} s after {warm} warm-up(s)"
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "impl": "reference", "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["seconds"] / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "cfg2_stu_layer_fwd_bwd", "B": 64, "H": H, "D": D,
-                   "total_kept_pairs_per_head": kept, "device": "cpu"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "reference", "sample": sample},
-        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": cfg,
+        "cpu_baseline": {"value": r["value"], "unit": UNIT, "cores": rs.cores, "kind": "reference", "sample": sample,
+                         "step_s_min": r["step_s_min"], "step_s_median": r["step_s_median"]},
+        "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
     print(json.dumps(line), flush=True)
 
 
-def cpu_baseline(batch, budget_s: float = 20.0):
-    """Reference operator on the host cores over a bounded sample of the N=1 workload."""
+def cpu_baseline(budget_s: float = 12.0):
+    """Reference operator on the host cores over the same bounded sample, timed the same way as the
+    reference arm (two warm-up passes, then whole passes until the budget is used)."""
     from oracle import ref_op
-    from recir_b200 import workload
     if not ref_op.available():
         return {"value": None, "unit": UNIT, "cores": 0, "kind": "reference",
                 "sample": "oracle/_ref shared object missing"}
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    order = np.argsort(batch.lengths, kind="stable")
-    sel = [int(i) for i in order[1::4]]
-    nt = batch.num_targets.numpy()
-    pairs = sum(workload.kept_pairs(int(batch.lengths[i]), int(nt[i])) for i in sel)
-    H, D = batch.q.shape[1], batch.q.shape[2]
-    flops = workload.useful_flops(pairs, H, D, D, backward=True)
-    kw = dict(max_seq_len=batch.max_seq_len, alpha=batch.alpha, causal=True, num_targets=batch.num_targets)
-    run = lambda: ref_op.ref_fwd_bwd_per_sequence(batch.dout, batch.q, batch.k, batch.v,
-                                                  batch.seq_offsets, select=sel, **kw)
-    run()  # warm-up
-    reps, t0 = 0, time.perf_counter()
-    while True:
-        run()
-        reps += 1
-        dt = time.perf_counter() - t0
-        if dt > budget_s / 2 or reps >= 40:
-            break
-    return {"value": flops * reps / dt / 1e12, "unit": UNIT, "cores": cores, "kind": "reference",
-            "sample": f"{len(sel)} of {len(batch.lengths)} sequences (every 4th by sorted length), bf16, "
-                      f"fwd+bwd, {reps} pass(es) in {dt:.1f} s after one warm-up"}
+    rs = ReferenceSample()
+    rs.step()
+    t0 = time.perf_counter()
+    rs.step()
+    one = time.perf_counter() - t0
+    steps = int(min(40, max(3, budget_s / max(one, 1e-3))))
+    r = rs.run(steps, 0)  # the two passes above were the warm-ups
+    return {"value": r["value"], "unit": UNIT, "cores": rs.cores, "kind": "reference",
+            "sample": rs.what + f"; {steps} timed pass(es) in {r['seconds']:.1f} s after 2 warm-ups",
+            "step_s_min": r["step_s_min"], "step_s_median": r["step_s_median"]}
 
+
+# --------------------------------------------------------------------------------------------------
+# the 8-layer stack over the fixed global Zipf batch (strong scaling) and the gradient check
+# --------------------------------------------------------------------------------------------------
+
+class Stack8:
+    """global B=1024, H=4, D=128 bf16, 8 independent attention layers run
+    forward 0..7 then backward 7..0, sequences token-balanced over the ranks.  Lengths come from the
+    seeded host generator (`workload.config4_lengths`); q/k/v/dO values are N(0, 0.1) / N(0, 0.01) drawn
+    ON THE DEVICE (1.65 M tokens x 8 layers would take minutes on the host), global tensors first, then
+    this rank's rows, so every N sees the same numbers."""
+
+    LAYERS = 8
+
+    def __init__(self, rank: int, world: int, dev):
+        from recir_b200 import sharding, workload
+        self.dev, self.rank, self.world = dev, rank, world
+        hist, tg = workload.config4_lengths(1024)
+        self.lengths = lengths = hist + tg
+        self.targets = tg
+        self.parts = sharding.token_balanced_partition(lengths, world)
+        self.mine = mine = self.parts[rank]
+        self.summary = sharding.shard_summary(lengths, self.parts)
+        self.T_global = int(lengths.sum())
+        self.H, self.D, self.N = 4, 128, 4096 + 128
+        self.alpha = 1.0 / self.D ** 0.5
+        goff = np.concatenate([[0], np.cumsum(lengths)])
+        self.global_off = torch.as_tensor(goff, dtype=torch.int64, device=dev)
+        self.off = sharding.local_offsets(lengths[mine]).to(dev)
+        self.nt = torch.as_tensor(tg[mine], dtype=torch.int64, device=dev)
+        self.T_local = int(lengths[mine].sum())
+        if world == 1:
+            self.rows = None
+        else:  # global token rows of this rank's sequences, in local order
+            starts = torch.as_tensor(goff[:-1][mine], dtype=torch.int64, device=dev)
+            lens = torch.as_tensor(lengths[mine], dtype=torch.int64, device=dev)
+            base = torch.repeat_interleave(starts - self.off[:-1], lens)
+            self.rows = base + torch.arange(self.T_local, device=dev)
+        self.pairs_global = sum(workload.kept_pairs(int(L), int(t)) for L, t in zip(lengths, tg))
+        self.layers = [self._draw(layer) for layer in range(self.LAYERS)]
+        self.args = (self.off, self.N, self.alpha, True, self.nt, 0, 0, None, 0)
+
+    def _draw_global(self, layer: int):
+        g = torch.Generator(device=self.dev).manual_seed(4 + layer)
+        shape = (self.T_global, self.H, self.D)
+        q, k, v = ((torch.randn(shape, generator=g, device=self.dev) * 0.1).to(torch.bfloat16) for _ in range(3))
+        g2 = torch.Generator(device=self.dev).manual_seed(1000 + layer)
+        do = (torch.randn(shape, generator=g2, device=self.dev) * 0.01).to(torch.bfloat16)
+        return q, k, v, do
+
+    def _draw(self, layer: int):
+        t = self._draw_global(layer)
+        if self.rows is None:
+            return t
+        return tuple(x.index_select(0, self.rows) for x in t)
+
+    def step(self):
+        fwd, bwd = torch.ops.recir.b200_hstu_attention_fwd, torch.ops.recir.b200_hstu_attention_bwd
+        outs = None
+        for q, k, v, _do in self.layers:
+            outs = fwd(q, k, v, *self.args)
+        for q, k, v, do in reversed(self.layers):
+            outs = bwd(do, q, k, v, *self.args)
+        return outs
+
+    def flops_global(self) -> float:
+        from recir_b200 import workload
+        return self.LAYERS * workload.useful_flops(self.pairs_global, self.H, self.D, self.D, backward=True)
+
+    # ---- gradient check -----------------------------------------------------------------------
+    @staticmethod
+    def _per_sequence_checksums(grads, off):
+        """float64 [B, 6]: sum and sum of squares of dq, dk, dv over each sequence's rows."""
+        B = off.numel() - 1
+        lens = off[1:] - off[:-1]
+        seg = torch.repeat_interleave(torch.arange(B, device=off.device), lens)
+        out = torch.zeros(B, 6, dtype=torch.float64, device=off.device)
+        for i, g in enumerate(grads):
+            x = g.double().flatten(1)
+            out[:, 2 * i].index_add_(0, seg, x.sum(1))
+            out[:, 2 * i + 1].index_add_(0, seg, (x * x).sum(1))
+        return out
+
+    def grad_check(self, dist):
+        """Every rank: checksums of its shard's gradients (layer 0), placed at the global sequence indices,
+        summed over NCCL; per-rank totals gathered over NCCL; rank 0 also runs the un-sharded global batch
+        and compares.  Sequences are independent and the kernels deterministic, so the match is exact."""
+        q, k, v, do = self.layers[0]
+        grads = torch.ops.recir.b200_hstu_attention_bwd(do, q, k, v, *self.args)
+        local = self._per_sequence_checksums(grads, self.off)
+        B = len(self.lengths)
+        table = torch.zeros(B, 6, dtype=torch.float64, device=self.dev)
+        table[torch.as_tensor(self.mine, device=self.dev)] = local
+        totals = local.sum(0)
+        if self.world > 1:
+            dist.all_reduce(table)  # every sequence belongs to exactly one rank
+            gathered = [torch.zeros_like(totals) for _ in range(self.world)]
+            dist.all_gather(gathered, totals)
+        else:
+            gathered = [totals]
+        if self.rank != 0:
+            return None
+        gq, gk, gv, gdo = self._draw_global(0)
+        gnt = torch.as_tensor(self.targets, dtype=torch.int64, device=self.dev)
+        ref = torch.ops.recir.b200_hstu_attention_bwd(gdo, gq, gk, gv, self.global_off, self.N, self.alpha, True, gnt,
+                                                      0, 0, None, 0)
+        want = self._per_sequence_checksums(ref, self.global_off)
+        diff = (table - want).abs()
+        scale = want.abs().max(0).values.clamp_min(1e-300)
+        sum_ranks = torch.stack(gathered).sum(0)
+        return {"what": "float64 per-sequence sum and sum of squares of dq, dk, dv (stack layer 0), shards vs un-sharded run",
+                "collective": "nccl all_reduce + all_gather" if self.world > 1 else "none (one rank)",
+                "sequences": B, "mismatched_sequences": int((diff > 0).any(1).sum().item()),
+                "max_rel_diff": float((diff / scale).max().item()),
+                "totals_rel_diff": float(((sum_ranks - want.sum(0)).abs() / want.sum(0).abs().clamp_min(1e-300)).max().item()),
+                "ok": bool((diff / scale).max().item() <= 1e-12)}
+
+
+# --------------------------------------------------------------------------------------------------
 
 def main():
     ap = argparse.ArgumentParser()
@@ -207,7 +371,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    args = ap.parse_args()
+    ap.add_argument("--no-extras", action="store_true", help="headline, roofline and e2e only")
+    ap.add_argument("--grad-check", dest="grad_check", action="store_true", default=None)
+    ap.add_argument("--no-grad-check", dest="grad_check", action="store_false")
+    ap.add_argument("--case", default=None, help="run one of the single-purpose runners of bench_cases.py instead")
+    args, rest = ap.parse_known_args()
+    if args.case is not None:
+        import bench_cases
+        bench_cases.main([args.case, *rest])
+        return
+    if rest:
+        ap.error(f"unrecognized arguments: {' '.join(rest)}")
     args.warmup = max(args.warmup, 0)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -220,6 +394,8 @@ def main():
             raise SystemExit("launch with torch.distributed.run --nproc-per-node N for --gpus N > 1")
         args.gpus = world
     warm = max(args.warmup, 3)
+    if args.grad_check is None:
+        args.grad_check = world > 1
 
     import torch.distributed as dist
     import recir_b200
@@ -237,7 +413,6 @@ def main():
     H, D = batch.q.shape[1], batch.q.shape[2]
     pairs_global = workload.total_kept_pairs(batch)
     flops_step = workload.useful_flops(pairs_global, H, D, D, backward=True)
-    flops_fwd = workload.useful_flops(pairs_global, H, D, D, backward=False)
     T_global = batch.total_tokens
 
     host = {k: local[k].pin_memory() for k in ("q", "k", "v", "do")}
@@ -262,21 +437,39 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def all_ranks(x: float) -> list:
+        if world == 1:
+            return [x]
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        out = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        return [float(y.item()) for y in out]
+
+    def timed_region(fn, steps: int):
+        """barrier + synchronize, `steps` calls between two events on the launching stream, barrier +
+        synchronize; returns this rank's milliseconds."""
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        barrier()
+        return e0.elapsed_time(e1)
+
     # ------------------------------------------------------------ resident (value)
     for _ in range(warm):
         step_resident()
-    sampler = ClockSampler(local_rank)
+    # only rank 0 reports clocks, so only rank 0 runs a sampler (of its own GPU)
+    sampler = ClockSampler(local_rank) if rank == 0 else None
     barrier()
-    sampler.start()
+    if sampler is not None:
+        sampler.start()
     launches0 = ops.launch_counter
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(args.steps):
-        step_resident()
-    ev1.record()
-    barrier()
+    my_ms = timed_region(step_resident, args.steps)
     launches = ops.launch_counter - launches0
-    ms_total = max_over_ranks(ev0.elapsed_time(ev1))
+    ms_total = max_over_ranks(my_ms)
+    per_rank_ms = [x / args.steps for x in all_ranks(my_ms)]
     # per-kernel device time (same stream), for the roofline of the dominant kernel: each pass is
     # issued `reps` times back to back between two events so that the host's launch latency does not
     # sit inside the measurement; the backward kernels also run one at a time (C-ABI flag).
@@ -302,6 +495,23 @@ def main():
     dq_ms = time_pass(run_bwd)
     ops.set_backward_passes(True, True)
     value = flops_step * args.steps / (ms_total * 1e-3) / 1e12
+    clocks = sampler.stop() if sampler is not None else None  # over the headline and the per-pass timed regions
+
+    # ------------------------------------------------------------ sustained: the same step for >= 2 s
+    sustained = None
+    if not args.no_extras:
+        n_sus = max(args.steps, int(2200.0 / max(ms_total / args.steps, 1e-3)))
+        s2 = ClockSampler(local_rank, period_ms=50) if rank == 0 else None
+        barrier()
+        if s2 is not None:
+            s2.start()
+        sus_ms = max_over_ranks(timed_region(step_resident, n_sus))
+        c2 = s2.stop() if s2 is not None else None
+        sus_value = flops_step * n_sus / (sus_ms * 1e-3) / 1e12
+        sustained = {"steps": n_sus, "seconds": sus_ms * 1e-3, "ms_per_step": sus_ms / n_sus, "value": sus_value,
+                     "unit": UNIT, "clocks": c2,
+                     "note": "same step as `value`, looped back to back; `value` itself is a burst of "
+                             f"{args.steps} steps, and the per-pass times of `roofline` are bursts of 10 calls"}
 
     # ------------------------------------------------------------ end to end (host buffers)
     # Public host-memory API: chunks of whole sequences stream through copy-in / compute / copy-out
@@ -316,29 +526,96 @@ def main():
 
     for _ in range(3):
         step_e2e()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        step_e2e()
-    e1.record()
-    barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-    clocks = sampler.stop()  # sampled over the resident, per-pass and end-to-end timed regions
+    e2e_ms = max_over_ranks(timed_region(step_e2e, args.steps))
     e2e_value = flops_step * args.steps / (e2e_ms * 1e-3) / 1e12
     bytes_local = sum(host[k].numel() * host[k].element_size() for k in host)
+    # plain-copy floor: the same bytes in and out on two streams, no kernels, all ranks at once
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def copy_only():
+        with torch.cuda.stream(s_in):
+            for kname in host:
+                d[kname].copy_(host[kname], non_blocking=True)
+        with torch.cuda.stream(s_out):
+            for kname in host:
+                out_host[kname].copy_(d[kname], non_blocking=True)
+
+    def copy_step():
+        cur = torch.cuda.current_stream()
+        s_in.wait_stream(cur); s_out.wait_stream(cur)
+        copy_only()
+        cur.wait_stream(s_in); cur.wait_stream(s_out)
+
+    for _ in range(2):
+        copy_step()
+    n_copy = max(3, min(args.steps, 10))
+    copy_ms = max_over_ranks(timed_region(copy_step, n_copy)) / n_copy
     if world > 1:
         tb = torch.tensor([float(bytes_local)], dtype=torch.float64, device=dev)
         dist.all_reduce(tb)
         bytes_global = int(tb.item())
     else:
         bytes_global = bytes_local
+    del pipe
+    out_host.clear()
+
+    # ------------------------------------------------------------ long skewed sequences (N=1 only)
+    long_window = None
+    if not args.no_extras and world == 1:
+        b3 = workload.config3()
+        t3 = {k: getattr(b3, k).to(dev) for k in ("q", "k", "v", "dout")}
+        a3 = (b3.seq_offsets.to(dev), b3.max_seq_len, b3.alpha, True, b3.num_targets.to(dev), b3.contextual_seq_len,
+              b3.max_attn_len, None, 0)
+        f3 = lambda: torch.ops.recir.b200_hstu_attention_fwd(t3["q"], t3["k"], t3["v"], *a3)
+        g3 = lambda: torch.ops.recir.b200_hstu_attention_bwd(t3["dout"], t3["q"], t3["k"], t3["v"], *a3)
+        for _ in range(3):
+            f3(); g3()
+        fm, gm = float(np.median(time_pass(f3))), float(np.median(time_pass(g3)))
+        p3 = workload.total_kept_pairs(b3)
+        H3, D3 = b3.q.shape[1], b3.q.shape[2]
+        long_window = {
+            "workload": "cfg3_long_window_fwd_bwd", "B": len(b3.lengths), "H": H3, "D": D3, "T": b3.total_tokens,
+            "max_len": int(b3.lengths.max()), "max_attn_len": b3.max_attn_len, "contextual_seq_len": b3.contextual_seq_len,
+            "kept_pairs_per_head": p3, "fwd_ms": fm, "bwd_ms": gm,
+            "fwd_tflops": workload.useful_flops(p3, H3, D3, D3, False) / (fm * 1e-3) / 1e12,
+            "bwd_tflops": workload.useful_flops(p3, H3, D3, D3, True, forward=False) / (gm * 1e-3) / 1e12,
+            "fwd_bwd_tflops": workload.useful_flops(p3, H3, D3, D3, True) / ((fm + gm) * 1e-3) / 1e12,
+            "timing": "median of 5 samples of 10 calls issued back to back"}
+        t3.clear()
+
+    # ------------------------------------------------------------ 8-layer stack, fixed global batch
+    stack8, grad_check = None, None
+    if not args.no_extras:
+        d.clear()
+        host.clear()
+        torch.cuda.empty_cache()
+        st = Stack8(rank, world, dev)
+        for _ in range(2):
+            st.step()
+        n8 = 5
+        l0 = ops.launch_counter
+        my8 = timed_region(st.step, n8) / n8
+        launches8 = (ops.launch_counter - l0) // n8
+        ranks8 = all_ranks(my8)
+        t8 = max(ranks8)
+        stack8 = {
+            "workload": "cfg4_stack8_fwd_bwd", "scaling": "strong", "layers": st.LAYERS, "B_global": len(st.lengths),
+            "H": st.H, "D": st.D, "T_global": st.T_global, "kept_pairs_per_head_per_layer": st.pairs_global,
+            "steps": n8, "ms_per_step": t8, "tokens_per_s": st.T_global / (t8 * 1e-3),
+            "token_layers_per_s": st.T_global * st.LAYERS / (t8 * 1e-3),
+            "useful_tflops": st.flops_global() / (t8 * 1e-3) / 1e12,
+            "per_rank_ms": ranks8, "token_imbalance": st.summary["token_imbalance"],
+            "cost_imbalance": st.summary["cost_imbalance"], "tokens_per_rank": st.summary["tokens"],
+            "launches_per_step_per_rank": launches8,
+            "data": "lengths from the seeded host generator; q/k/v/dO drawn on the device per layer (seeds 4+layer, "
+                    "1000+layer), global tensors first, then this rank's rows"}
+        if args.grad_check:
+            grad_check = st.grad_check(dist)
+        del st
 
     # ------------------------------------------------------------ report
     if rank == 0:
         peaks = measured_peaks()
-        uses_tc = {}
-        p = _lib.B200HstuParams()
         fwd_med, bwd_med = float(np.median(fwd_ms)), float(np.median(bwd_ms))
         local_pairs = pairs_global / world  # token-balanced shards of one distribution
         # One launch of each main kernel: useful flops (2*D per kept pair per GEMM: forward 2 GEMMs,
@@ -362,6 +639,7 @@ def main():
             # DRAM bytes of one launch from the ncu capture of the same shapes at T=78262 tokens,
             # scaled by tokens (traffic grows with the token count at a fixed length distribution)
             "traffic": dom_traffic * local_tokens / NCU_CFG1_TOKENS,
+            "traffic_source": NCU_CAPTURE,
             # fwd: q,k,v read + o written; dK/dV pass: q,k,v,dO read + dk,dv written; dQ pass: q,k,v,dO read + dq written
             "algorithmic_bytes": {"hstu_fwd_tc": 4, "hstu_bwd_dkv_tc": 6, "hstu_bwd_dq_tc": 5}[dom]
             * local_tokens * H * D * 2,
@@ -370,27 +648,41 @@ def main():
             "fwd_ms": fwd_med, "bwd_ms": bwd_med,
             "fwd_tflops": workload.useful_flops(local_pairs, H, D, D, backward=False) / (fwd_med * 1e-3) / 1e12,
             "bwd_tflops": workload.useful_flops(local_pairs, H, D, D, backward=True, forward=False) / (bwd_med * 1e-3) / 1e12,
+            "timing": "per-pass and per-kernel times: median of 5 samples of 10 calls issued back to back (a burst, "
+                      "each pass with its two work-list kernels); they need not add up to ms_per_step, which is "
+                      "forward and backward alternating",
         }
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": warm, "ms_per_step": ms_total / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "cfg2_stu_layer_fwd_bwd", "B_global": 64 * world, "H": H, "D": D,
-                       "T_global": T_global, "kept_pairs_per_head": pairs_global,
-                       "sharding": "token-balanced whole sequences, no collective",
-                       "shard": shard_info, "l2": "inputs+outputs per step (~640 MB/GPU) exceed the 126 MB L2"},
+            "config": headline_config(world, H, D, T_global, pairs_global, shard_info),
             "tokens_per_s": T_global * args.steps / (ms_total * 1e-3),
+            "per_rank_ms": {"min": min(per_rank_ms), "median": float(np.median(per_rank_ms)), "max": max(per_rank_ms),
+                            "all": per_rank_ms},
             "pct_of_peak": {"nominal_2250": 100 * value / world / NOMINAL_BF16_TFLOPS,
                             "measured_burst": 100 * value / world / peaks["bf16_tflops"],
                             "measured_sustained": 100 * value / world / peaks["bf16_tflops_sustained"]},
             "clocks": clocks,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": bytes_global,
-                    "d2h_bytes_per_step": bytes_global, "ms_per_step": e2e_ms / args.steps},
+                    "d2h_bytes_per_step": bytes_global, "ms_per_step": e2e_ms / args.steps,
+                    "copy_floor_ms": copy_ms,
+                    "copy_floor_note": "the same bytes host->device and device->host on two streams from pinned "
+                                       "memory, no kernels, every rank at once (max over ranks)"},
             "gpu_launches": launches * world,
             "roofline": roofline,
         }
+        if sustained is not None:
+            sustained["pct_of_measured_sustained"] = 100 * sustained["value"] / world / peaks["bf16_tflops_sustained"]
+            line["sustained"] = sustained
+        if long_window is not None:
+            line["long_window"] = long_window
+        if stack8 is not None:
+            line["stack8"] = stack8
+        if grad_check is not None:
+            line["grad_check"] = grad_check
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(batch)
+            line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -26,8 +26,24 @@
  *  - Return value: 0 on success, a negative B200_HSTU_E* code otherwise.
  *    Argument errors are detected on the host before anything is launched.
  *  - Thread safety: the entry points keep no mutable global state besides
- *    one-time function-attribute set-up; they may be called concurrently from
- *    several host threads on different streams.
+ *    one-time function-attribute set-up and, for b200_hstu_fwd_static_scratch, a
+ *    mutex-guarded per-device cache of its scratch array's address; they may be
+ *    called concurrently from several host threads on different streams (calls of
+ *    b200_hstu_fwd_static_scratch on ONE device share its array and must not
+ *    overlap on the GPU, see there).
+ *  - Device-side diagnostics: kernels cannot return codes, so conditions found
+ *    on the device are reported through params->status (optional, device
+ *    int32[4], zeroed by the caller; the kernels only ever set bits / codes):
+ *      status[0] bit 0  seq_offsets were malformed (negative, decreasing, past T,
+ *                       or describing more 128-row blocks than T/128 + B): the
+ *                       offending values were clamped and the call still ran
+ *                       inside its buffers, but its results are not meaningful;
+ *      status[1]        0, or the code of the first pipeline wait that gave up
+ *                       after its time limit (101 TMA producer, 102 MMA issuer,
+ *                       103 epilogue, 104 work-item scheduler): the kernel drained
+ *                       and returned, outputs are incomplete.
+ *    C callers should pass a status word and read it at a synchronisation point
+ *    they already have.
  */
 #ifndef B200_HSTU_H_
 #define B200_HSTU_H_
@@ -81,7 +97,7 @@ typedef struct B200HstuParams {
   const float* attn_scale; /* NULL => 1/max_seq_len; else 1 or T fp32 values */
   void* workspace;         /* >= b200_hstu_workspace_bytes(), 256-byte aligned */
   uint64_t workspace_bytes;
-  int32_t* status; /* optional int32[4]: device-side diagnostics, see b200_hstu_strerror */
+  int32_t* status; /* optional device int32[4]: device-side diagnostics, see the header comment */
   int64_t T;       /* token rows in q/k/v */
   int64_t q_row_stride, k_row_stride, v_row_stride, o_row_stride;
   int64_t do_row_stride, dq_row_stride, dk_row_stride, dv_row_stride;

@@ -10,7 +10,8 @@
  *   tsb  = clamp(int64(log(dt)) or int64(sqrt(dt)), 0, 2048)
  *   out[i] = x[i] + cast(pos_table[pos] + ts_table[tsb])
  * The kernel writes out, pos and tsb per token; sorting the two index arrays (the reference
- * returns them sorted together with the sort permutations) is left to the caller.
+ * returns them sorted together with the sort permutations) is left to the caller.  Rows at or past
+ * seq_offsets[B] belong to no sequence: their out rows are zeros and their indices 0.
  *
  * Conventions of b200_hstu.h: plain pointers and sizes, caller-owned buffers, nothing allocated
  * or synchronised, launches go to the given stream, negative B200_HSTU_E* codes on error.
@@ -52,6 +53,10 @@ typedef struct B200EmbedParams {
   void* out;               /* [rows, cols] */
   int32_t* pos_index;      /* [rows] */
   int32_t* ts_index;       /* [rows] */
+  int32_t* status;         /* optional device int32[>= 1], zeroed by the caller: bit 0 of status[0] is set when
+                              a position or timestamp index fell outside its table and was clamped into it
+                              (sequence length 0 or beyond ts_cols, more contextual rows than table rows);
+                              the reference refuses such inputs on the host (:363-373) */
 } B200EmbedParams;
 
 int b200_stu_add_ts_pos_emb(const B200EmbedParams* p, void* stream);

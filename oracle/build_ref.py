@@ -11,12 +11,18 @@ into this repository) and only the resulting shared object lands in
 reference tree itself does not.
 
 Usage:  python oracle/build_ref.py [/path/to/reference]
+(default: ``oracle.refroot.reference_root()``, i.e. ``$RECIR_REFERENCE_ROOT`` or the conventional
+checkout location)
 """
 from __future__ import annotations
 
 import os
 import shutil
 import sys
+
+if __package__ in (None, ""):
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from oracle import refroot  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
@@ -29,8 +35,10 @@ def ref_available() -> bool:
     return os.path.exists(LIB_PATH)
 
 
-def build(reference_root: str = "/root/reference", verbose: bool = False) -> str | None:
+def build(reference_root: str | None = None, verbose: bool = False) -> str | None:
     """Compile the reference op; returns the .so path or None if no source tree."""
+    if reference_root is None:
+        reference_root = refroot.reference_root()
     src = os.path.join(reference_root, REL_SOURCE)
     if not os.path.exists(src):
         return LIB_PATH if ref_available() else None
@@ -67,5 +75,5 @@ def load() -> None:
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    root = sys.argv[1] if len(sys.argv) > 1 else None
     print(build(root, verbose=True))

@@ -57,7 +57,8 @@ def ref_fwd_bwd_per_sequence(dout, q, k, v, seq_offsets, max_seq_len, alpha, cau
     by the bounded CPU-baseline sample); rows of other sequences stay zero.
     """
     offs = seq_offsets.tolist()
-    o = torch.zeros(q.shape[0], q.shape[1], v.shape[2], dtype=v.dtype)
+    # the composite is pure ATen: it runs wherever its inputs live (host, or a GPU for full-size checks)
+    o = torch.zeros(q.shape[0], q.shape[1], v.shape[2], dtype=v.dtype, device=v.device)
     dq = torch.zeros_like(q) if backward else None
     dk = torch.zeros_like(k) if backward else None
     dv = torch.zeros_like(v) if backward else None
@@ -67,7 +68,7 @@ def ref_fwd_bwd_per_sequence(dout, q, k, v, seq_offsets, max_seq_len, alpha, cau
         if e == s:
             continue
         local = torch.tensor([0, e - s], dtype=seq_offsets.dtype)
-        nt = None if num_targets is None else num_targets[b:b + 1]
+        nt = None if num_targets is None else num_targets[b:b + 1].cpu()
         sc = attn_scale
         if sc is not None and sc.dim() > 0:
             sc = sc[s:e]

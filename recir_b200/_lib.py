@@ -128,6 +128,7 @@ class B200EmbedParams(ctypes.Structure):
         ("timestamps", ctypes.c_void_p), ("seq_offsets", ctypes.c_void_p), ("seq_lengths", ctypes.c_void_p),
         ("num_targets", ctypes.c_void_p), ("out", ctypes.c_void_p),
         ("pos_index", ctypes.c_void_p), ("ts_index", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
     ]
 
 

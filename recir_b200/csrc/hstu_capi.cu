@@ -227,10 +227,19 @@ constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mutex;
 void* g_scratch_ptr[kMaxDevices] = {};
 
-// Device address of g_static_scratch on the current device (looked up once per device).
-int static_scratch_address(void** out) {
+// Device address of g_static_scratch on the device that owns `device_ptr` (looked up once per device).
+// That device is made current for the lookup: on a host thread that has no context yet, or whose
+// current device is another one, the symbol would otherwise resolve to the wrong GPU's copy.
+int static_scratch_address(const void* device_ptr, void** out) {
   int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return B200_HSTU_ELAUNCH;
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, device_ptr) == cudaSuccess && at.type == cudaMemoryTypeDevice) dev = at.device;
+  else if (cudaGetDevice(&dev) != cudaSuccess) return B200_HSTU_ELAUNCH;
+  if (dev < 0 || dev >= kMaxDevices) return B200_HSTU_ELAUNCH;
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess || cur != dev) {
+    if (cudaSetDevice(dev) != cudaSuccess) return B200_HSTU_ELAUNCH;
+  }
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
   if (g_scratch_ptr[dev] == nullptr) {
     void* ptr = nullptr;
@@ -253,7 +262,7 @@ int b200_hstu_fwd_static_scratch(const B200HstuParams* p, void* stream) {
   if (hstu::tc_supported(*p, a, 0)) {
     if (hstu::tc_workspace_bytes(a, 0) > B200_HSTU_STATIC_SCRATCH_BYTES) return B200_HSTU_ESCRATCH;
     void* scratch = nullptr;
-    const int src = static_scratch_address(&scratch);
+    const int src = static_scratch_address(p->q, &scratch);
     if (src != B200_HSTU_OK) return src;
     e = hstu::tc_forward(a, p->dtype, scratch, st);
   } else {

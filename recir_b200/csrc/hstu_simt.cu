@@ -2,7 +2,7 @@
 //
 // These cover every dtype, head dimension (<= 256) and mask option of the operator and
 // serve (a) the shapes the tensor-core kernels do not take (fp32, Dqk != Dv, head dims
-// other than 128, non-causal masks, per-token attn_scale) and (b) an independent
+// other than 128, non-causal masks) and (b) an independent
 // on-device cross-check of the tensor-core path.  All arithmetic is fp32 with an exact
 // sigmoid; results are rounded once on store.
 //

@@ -5,12 +5,15 @@
 // mask rule).  Anything else is served by the CUDA-core kernels.
 //
 // Work decomposition.  A small device-side pass builds a work list of (sequence, head,
-// 128-row block) items sorted so that the most expensive items come first; persistent CTAs
-// (one per SM) walk the list with a fixed stride.  The forward kernel is warp-specialised:
+// 128-row block) items ordered so that expensive items come first and items that read the same
+// K/V rows sit close together; persistent CTAs (one per SM) claim entries of the list dynamically
+// (an atomic cursor, read by one scheduler warp per CTA).  The forward kernel is warp-specialised:
 //   warp 0      TMA producer: Q tile of the item, then K and V tiles of every kept key block
 //   warp 1      MMA issuer (one elected lane): S = Q K^T into TMEM, O += P V from TMEM
-//   warps 4-7   epilogue group 0   } alternate over key blocks: read S from TMEM, apply
-//   warps 8-11  epilogue group 1   } alpha / SiLU / mask, write P (16-bit) back over S
+//   warp 2      work-item scheduler (claims items, classifies their tiles, feeds the item ring)
+//   warps 4-7   epilogue group 0   } both groups work on EVERY key tile, group g on score columns
+//   warps 8-11  epilogue group 1   } [64 g, 64 g + 64): read S from TMEM, apply alpha / SiLU / mask,
+//                                    write P (16-bit) back over S
 // The output scale (1/N or attn_scale) is a per-query-row factor, so it is applied once
 // when O leaves TMEM, not per score.
 #define SM100_OUTLINE_WAIT_SLOW_PATH  // one shared copy of the wait loop: see sm100_ptx.cuh
@@ -127,7 +130,16 @@ __global__ void __launch_bounds__(1024) build_block_index(KernelArgs a, int* ws,
   for (long long i = tid; i < w.nbins; i += blockDim.x) start[i] *= a.H;
   __syncthreads();
   if (tid == 0) {
-    ws[0] = start[0] + cnt[0] * a.H;
+    // The item array holds max_items = H * (T / 128 + B) entries, which covers every batch whose
+    // sequences do not overlap.  Offsets that go backwards are clamped one sequence at a time
+    // (load_seq), so a malformed array such as [0, T, 0, T, ...] can describe more blocks than that:
+    // the list is cut at the capacity (the extra items are dropped) and the call is flagged.
+    long long total = static_cast<long long>(start[0]) + static_cast<long long>(cnt[0]) * a.H;
+    if (total < 0 || total > w.max_items) {
+      total = w.max_items;
+      if (a.status) atomicOr(a.status, 1);
+    }
+    ws[0] = static_cast<int>(total);
     ws[1] = cnt[0];
   }
   // chunk_base[c] = items owned by the first c * chunk_seqs sequences of the sorted order:
@@ -894,7 +906,9 @@ static cudaError_t launch_prep_t(const KernelArgs& a, int* ws, const WorkspaceLa
     long long c = (budget + n / 2) / n;
     w.chunk_seqs = static_cast<int>(c < 4 ? 4 : (c > 16 ? 16 : c));
   }
+#ifdef B200_HSTU_PROFILING
   if (const char* e = getenv("B200_HSTU_CHUNK")) w.chunk_seqs = atoi(e) > 0 ? atoi(e) : w.chunk_seqs;
+#endif
   // tables in shared memory when they fit under the default 48 KB (next to 4 KB of static shared memory)
   const long long index_ints = 3 * w.nbins;
   const int index_smem = index_ints <= 10240 ? 1 : 0;
@@ -986,9 +1000,16 @@ cudaError_t tc_forward(const KernelArgs& a, int dtype, void* workspace, cudaStre
   if (e != cudaSuccess) return e;
   set_error_stage("forward: main kernel");
   const size_t smem = sizeof(FwdShared) + 1024;
+  // The kernels carry optional cycle accounting and event traces (template parameter PROF).  Those
+  // variants are only instantiated in a build with -DB200_HSTU_PROFILING, which also honours the
+  // tuning environment variables; the shipped library has one instantiation per kernel and dtype.
+#ifdef B200_HSTU_PROFILING
   static const bool profile = getenv("B200_HSTU_PROFILE") != nullptr;  // cycle accounting into workspace ints 2..15
   auto kern = profile ? (bf16 ? hstu_fwd_tc<true, true> : hstu_fwd_tc<false, true>)
                       : (bf16 ? hstu_fwd_tc<true, false> : hstu_fwd_tc<false, false>);
+#else
+  auto kern = bf16 ? hstu_fwd_tc<true, false> : hstu_fwd_tc<false, false>;
+#endif
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   e = launch_dependent(kern, static_cast<unsigned>(main_grid(w)), FWD_THREADS, smem, st, true, maps, a, ws, w.off_items);

@@ -69,11 +69,6 @@ template <bool IS_BF16, bool WANT_P>
 __device__ __forceinline__ void bwd_pair(uint32_t s0, uint32_t s1, uint32_t dp0, uint32_t dp1, float c1, uint32_t& p2,
                                          uint32_t& ds2) {
   const uint32_t u2 = pack2<IS_BF16>(c1 * __uint_as_float(s0), c1 * __uint_as_float(s1));
-#ifdef HSTU_EXPERIMENT_NO_MATH
-  if (WANT_P) p2 = u2;
-  ds2 = pack2<IS_BF16>(__uint_as_float(dp0), __uint_as_float(dp1));
-  return;
-#endif
   const uint32_t t2 = tanh2<IS_BF16>(u2);
   if (WANT_P) p2 = fma2<IS_BF16>(u2, t2, u2);
   const uint32_t w1 = add2<IS_BF16>(t2, one2<IS_BF16>());
@@ -976,9 +971,13 @@ cudaError_t tc_backward(const KernelArgs& a, int dtype, void* workspace, cudaStr
   if (!a.skip_dkv) {
     set_error_stage("backward: dK/dV kernel");
     const size_t smem = sizeof(DkvShared) + 1024;
+#ifdef B200_HSTU_PROFILING
     static const bool profile = getenv("B200_HSTU_PROFILE") != nullptr;
     auto kern = profile ? (bf16 ? hstu_bwd_dkv_tc<true, true> : hstu_bwd_dkv_tc<false, true>)
                         : (bf16 ? hstu_bwd_dkv_tc<true, false> : hstu_bwd_dkv_tc<false, false>);
+#else
+    auto kern = bf16 ? hstu_bwd_dkv_tc<true, false> : hstu_bwd_dkv_tc<false, false>;
+#endif
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     e = launch_dependent(kern, static_cast<unsigned>(grid), BWD_THREADS, smem, st, true, maps, a, ws, w.off_items);
@@ -987,9 +986,13 @@ cudaError_t tc_backward(const KernelArgs& a, int dtype, void* workspace, cudaStr
   if (!a.skip_dq) {
     set_error_stage("backward: dQ kernel");
     const size_t smem = sizeof(DqShared) + 1024;
+#ifdef B200_HSTU_PROFILING
     static const bool profile = getenv("B200_HSTU_PROFILE_DQ") != nullptr;
     auto kern = profile ? (bf16 ? hstu_bwd_dq_tc<true, true> : hstu_bwd_dq_tc<false, true>)
                         : (bf16 ? hstu_bwd_dq_tc<true, false> : hstu_bwd_dq_tc<false, false>);
+#else
+    auto kern = bf16 ? hstu_bwd_dq_tc<true, false> : hstu_bwd_dq_tc<false, false>;
+#endif
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     // a dependent launch only behind the dK/dV kernel, whose output this kernel does not read; alone, it

@@ -211,9 +211,6 @@ __device__ __forceinline__ unsigned long long row_mask_bits64(const RowMask& rm,
 template <bool IS_BF16>
 __device__ __forceinline__ uint32_t silu_pair(uint32_t s0, uint32_t s1, float c1) {
   const uint32_t u2 = pack2<IS_BF16>(c1 * __uint_as_float(s0), c1 * __uint_as_float(s1));
-#ifdef HSTU_EXPERIMENT_NO_MATH
-  return u2;
-#endif
   return sm100::fma2<IS_BF16>(u2, sm100::tanh2<IS_BF16>(u2), u2);
 }
 

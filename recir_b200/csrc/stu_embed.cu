@@ -24,7 +24,7 @@ constexpr int WARPS_PER_BLOCK = 8;
 struct Args {
   const void* x; const void* pos; const void* ts; const long long* stamps;
   const void* off; const void* len; const void* tgt;
-  void* out; int* pos_idx; int* ts_idx;
+  void* out; int* pos_idx; int* ts_idx; int* status;
   long long rows, B, P, S, C, x_rs, out_rs, pos_rs, ts_rs;
   int cols, off64, len64, interleave, use_sqrt;
 };
@@ -106,23 +106,38 @@ __global__ void __launch_bounds__(WARPS_PER_BLOCK * 32) add_ts_pos_emb_kernel(Ar
         long long p = high - (i < high ? i : high) + a.C;  // kjt_split_per_feature.cpp:376-377
         if (p > a.P - 1) p = a.P - 1;
         if (i < a.C) p = i;
+        // The reference rejects these inputs on the host (:363-373) and its index ops throw; a kernel
+        // cannot throw, so out-of-range indices are clamped into the tables and flagged in status[0].
+        bool clamped = false;
+        if (p < 0) { p = 0; clamped = true; }
+        if (p > a.P - 1) { p = a.P - 1; clamped = true; }
         my_pos = static_cast<int>(p);
         const long long* row = a.stamps + b * a.S;
-        float d = static_cast<float>(row[L - 1] - row[i]);  // :385-389
+        long long c_last = L - 1, c_i = i;
+        if (c_last < 0) { c_last = 0; clamped = true; }
+        if (c_last > a.S - 1) { c_last = a.S - 1; clamped = true; }
+        if (c_i > a.S - 1) { c_i = a.S - 1; clamped = true; }
+        if (clamped && a.status) atomicOr(a.status, 1);
+        float d = static_cast<float>(row[c_last] - row[c_i]);  // :385-389
         d = fmaxf(d, 1e-6f) / 60.0f;
         d = a.use_sqrt ? sqrtf(d) : logf(d);
         long long q = static_cast<long long>(d);  // truncation toward zero
         my_tsb = static_cast<int>(q < 0 ? 0 : (q > 2048 ? 2048 : q));
-        a.pos_idx[r] = my_pos;  // coalesced: one index per lane
-        a.ts_idx[r] = my_tsb;
       }
+      a.pos_idx[r] = my_pos;  // coalesced: one index per lane; rows no sequence owns get index 0
+      a.ts_idx[r] = my_tsb;
     }
     const int count = a.rows - r0 < 32 ? static_cast<int>(a.rows - r0) : 32;
     for (int k = 0; k < count; ++k) {
       const int pos = __shfl_sync(0xffffffffu, my_pos, k), tsb = __shfl_sync(0xffffffffu, my_tsb, k);
-      if (!__shfl_sync(0xffffffffu, my_owned, k)) continue;  // rows past the last offset are not touched
       const X* xr = reinterpret_cast<const X*>(a.x) + (r0 + k) * a.x_rs;
       X* orow = reinterpret_cast<X*>(a.out) + (r0 + k) * a.out_rs;
+      if (!__shfl_sync(0xffffffffu, my_owned, k)) {
+        // rows past the last offset belong to no sequence: defined output (zeros), never stale memory
+        const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int v = lane; v < nv; v += 32) store8<X>(orow + 8 * v, z);
+        continue;
+      }
       const TAB* pr = reinterpret_cast<const TAB*>(a.pos) + static_cast<long long>(pos) * a.pos_rs;
       const TAB* tr = reinterpret_cast<const TAB*>(a.ts) + static_cast<long long>(tsb) * a.ts_rs;
       for (int v = lane; v < nv; v += 32) {
@@ -162,7 +177,7 @@ extern "C" int b200_stu_add_ts_pos_emb(const B200EmbedParams* p, void* stream) {
   Args a;
   a.x = p->x; a.pos = p->pos_table; a.ts = p->ts_table; a.stamps = reinterpret_cast<const long long*>(p->timestamps);
   a.off = p->seq_offsets; a.len = p->seq_lengths; a.tgt = p->num_targets;
-  a.out = p->out; a.pos_idx = p->pos_index; a.ts_idx = p->ts_index;
+  a.out = p->out; a.pos_idx = p->pos_index; a.ts_idx = p->ts_index; a.status = p->status;
   a.rows = p->rows; a.B = p->num_seqs; a.P = p->pos_rows; a.S = p->ts_cols; a.C = p->max_contextual_seq_len;
   a.x_rs = p->x_row_stride; a.out_rs = p->out_row_stride; a.pos_rs = p->pos_row_stride; a.ts_rs = p->ts_table_row_stride;
   a.cols = static_cast<int>(p->cols);

@@ -20,6 +20,7 @@ backend: calling the ops with CPU tensors raises, as does a missing shared libra
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
@@ -45,6 +46,13 @@ _LIBDEF.define(
 
 # Set by tests/benchmarks that want the CUDA-core cross-check kernels instead of the tensor-core ones.
 _force_simt = False
+# Checked mode: after every call, wait for it and raise if a kernel reported a problem on the device
+# (costs a device synchronisation per call; off by default, RECIR_B200_CHECK=1 turns it on).
+_checked = os.environ.get("RECIR_B200_CHECK", "0") not in ("", "0")
+# One persistent status word (device int32[4]) per device, handed to every call.
+_status = {}
+_WAIT_NAMES = {101: "WAIT_PRODUCER (TMA producer warp)", 102: "WAIT_MMA (MMA issuer warp)",
+               103: "WAIT_EPILOGUE (epilogue warps)", 104: "WAIT_SCHEDULER (work-item scheduler warp)"}
 # Extra C-ABI flags for the backward (benchmark timing of one pass at a time).
 _bwd_extra_flags = 0
 # Kernel launches issued through this module since import (launch accounting for the benchmark).
@@ -54,6 +62,50 @@ launch_counter = 0
 def set_force_simt(flag: bool) -> None:
     global _force_simt
     _force_simt = bool(flag)
+
+
+def set_checked(flag: bool) -> None:
+    """Checked mode on/off: every operator call then synchronises and raises ``RuntimeError`` if the
+    kernels flagged malformed offsets or a pipeline wait that gave up (see ``check_status``)."""
+    global _checked
+    _checked = bool(flag)
+
+
+def status_tensor(device) -> torch.Tensor:
+    """The device int32[4] status word every call on ``device`` reports into (created on first use)."""
+    device = torch.device(device)
+    if device.type == "cuda" and device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    t = _status.get(device)
+    if t is None:
+        t = torch.zeros(4, dtype=torch.int32, device=device)
+        _status[device] = t
+    return t
+
+
+def check_status(device=None, what: str = "recir_b200") -> None:
+    """Waits for the work queued on ``device`` (default: every device used so far), reads the status
+    word(s), clears them and raises ``RuntimeError`` naming what the kernels reported:
+    malformed ``seq_offsets`` (clamped on the device), or the pipeline wait that gave up
+    (``WAIT_PRODUCER`` / ``WAIT_MMA`` / ``WAIT_EPILOGUE`` / ``WAIT_SCHEDULER``).  Unchecked callers can
+    call this at a synchronisation point of their own, e.g. once per step."""
+    devices = list(_status) if device is None else [status_tensor(device).device]
+    problems = []
+    for dev in devices:
+        t = _status.get(dev)
+        if t is None:
+            continue
+        vals = t.cpu().tolist()  # synchronises with the stream work queued so far
+        if any(vals):
+            t.zero_()
+        if vals[0] & 1:
+            problems.append(f"{dev}: seq_offsets were malformed (negative, decreasing, beyond T, or overlapping) "
+                            "and were clamped on the device; the results are not meaningful")
+        if vals[1]:
+            problems.append(f"{dev}: a pipeline wait gave up after its time limit: "
+                            f"{_WAIT_NAMES.get(vals[1], 'code ' + str(vals[1]))}; outputs are incomplete")
+    if problems:
+        raise RuntimeError(f"{what}: " + "; ".join(problems))
 
 
 def set_backward_passes(dkv: bool = True, dq: bool = True) -> None:
@@ -148,6 +200,7 @@ def _fill(params, q, k, v, seq_offsets, max_seq_len, alpha, causal, num_targets,
     params.contextual_seq_len = int(contextual_seq_len)
     params.full_attn_size = int(full_attn_size)
     params.alpha = float(alpha)
+    params.status = status_tensor(dev).data_ptr()
     return keep
 
 
@@ -189,6 +242,8 @@ def _fwd_cuda(q, k, v, seq_offsets, max_seq_len, alpha, causal, num_targets, con
         rc = lib.b200_hstu_fwd(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         _check(rc, "b200_hstu_fwd")
         launch_counter += lib.b200_hstu_launch_count(ctypes.byref(p), 0)
+        if _checked:
+            check_status(q.device, "b200_hstu_fwd")
     del keep
     return out
 
@@ -217,6 +272,8 @@ def _bwd_cuda(dout, q, k, v, seq_offsets, max_seq_len, alpha, causal, num_target
         rc = lib.b200_hstu_bwd(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         _check(rc, "b200_hstu_bwd")
         launch_counter += lib.b200_hstu_launch_count(ctypes.byref(p), 1)
+        if _checked:
+            check_status(q.device, "b200_hstu_bwd")
     del keep
     return dq, dk, dv
 

@@ -11,20 +11,20 @@ payloads holding small integers, so any element type reproduces them exactly).
 """
 from __future__ import annotations
 
-import importlib.util
 import os
+import sys
 
 import numpy as np
 import torch
 
-REF = "/root/reference/recir/ops/jagged_ops.py"
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+from oracle import refroot  # noqa: E402
+
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "jagged_golden.npz")
 
 
 def main():
-    spec = importlib.util.spec_from_file_location("ref_jagged_ops", REF)
-    mod = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(mod)
+    refroot.load_reference_module("recir/ops/jagged_ops.py", "ref_jagged_ops")
     ops = torch.ops.recir
     g = torch.Generator().manual_seed(5)
     out = {}

@@ -6,22 +6,26 @@ import os
 import numpy as np
 import torch
 
-GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "hstu_golden.npz")
+GOLDEN_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+# "main": outputs of the reference's compiled operator (tests/golden/make_golden.py);
+# "a4": outputs of the reference's second, pure-torch pad-then-compute implementation and of
+# autograd through it (tests/golden/make_golden_a4.py), causal mask with targets only.
+GOLDEN_FILES = {"main": "hstu_golden.npz", "a4": "hstu_golden_a4.npz"}
 _cache = {}
 
 
-def golden():
-    if "z" not in _cache:
-        _cache["z"] = np.load(GOLDEN)
-    return _cache["z"]
+def golden(which: str = "main"):
+    if which not in _cache:
+        _cache[which] = np.load(os.path.join(GOLDEN_DIR, GOLDEN_FILES[which]))
+    return _cache[which]
 
 
-def golden_names():
-    return [str(n) for n in golden()["names"]]
+def golden_names(which: str = "main"):
+    return [str(n) for n in golden(which)["names"]]
 
 
-def golden_case(name: str) -> dict:
-    z = golden()
+def golden_case(name: str, which: str = "main") -> dict:
+    z = golden(which)
     p = name + "/"
     N, causal, w, ctx, f = (int(x) for x in z[p + "params"])
     c = dict(

@@ -181,3 +181,94 @@ def test_batch_dim_rule_and_swap_helper():
         else:
             assert bd is None
     assert seen["fwd"] == 2 and seen["bwd"] == 1 and seen["grad"] >= 1 and seen["aux"] >= 1
+
+
+# ---------------------------------------------------------------------------------------------
+# The swap as a maintainer of the reference would run it: the reference's OWN registry and pass
+# (recir/lowering/op_swap.py:16-97), loaded by file path (the package itself needs jax to import).
+# ---------------------------------------------------------------------------------------------
+
+@torch.library.custom_op("recir_b200_test::source_ragged_attention_bwd", mutates_args=())
+def _source_bwd_op(dout: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, seq_offsets: torch.Tensor,
+                   num_targets: torch.Tensor | None, attn_scale: torch.Tensor | None, N: int, alpha: float,
+                   max_attn_len: int = 0, full_attn_size: int = 0) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    raise RuntimeError("source op is a stand-in and must be swapped out")
+
+
+@_source_bwd_op.register_fake
+def _(dout, q, k, v, seq_offsets, num_targets, attn_scale, N, alpha, max_attn_len=0, full_attn_size=0):
+    return torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+
+def _reference_op_swap():
+    from oracle import refroot
+
+    if not refroot.reference_present():
+        pytest.skip("reference source tree not present")
+    return refroot.load_reference_module("recir/lowering/op_swap.py", "ref_op_swap")
+
+
+def test_swap_through_the_reference_registry_forward_and_backward():
+    ref = _reference_op_swap()
+    mode = FakeTensorMode(allow_non_fake_inputs=True)
+    q, k, v, off, nt = _fake_inputs(mode)
+    src_f = torch.ops.recir_b200_test.source_ragged_attention.default
+    src_b = torch.ops.recir_b200_test.source_ragged_attention_bwd.default
+
+    def step(q, k, v, dout):
+        out, _aux = torch.ops.recir_b200_test.source_ragged_attention(
+            8, 0.5, q, k, v, off, "lower_triangular", nt, None, 0, 0, 0, 0)
+        dq, dk, dv = torch.ops.recir_b200_test.source_ragged_attention_bwd(
+            dout, q, k, v, off, nt, None, 8, 0.5, 0, 0)
+        return out * 2, dq + dk, dv
+
+    with mode:
+        gm = make_fx(step, tracing_mode="fake")(q, k, v, v)
+    registry = ref.OpSwapRegistry()
+    registry.register(src_f, torch.ops.recir.b200_ragged_attention_fwd.default)
+    registry.register(src_b, torch.ops.recir.b200_ragged_attention_bwd.default)
+    assert len(registry) == 2 and registry.has(src_f)
+    out_gm = ref.swap_ops(gm, registry)
+    assert out_gm is gm
+    tg = [n.target for n in gm.graph.nodes if n.op == "call_function"]
+    assert tg.count(torch.ops.recir.b200_ragged_attention_fwd.default) == 1
+    assert tg.count(torch.ops.recir.b200_ragged_attention_bwd.default) == 1
+    assert src_f not in tg and src_b not in tg
+    with mode:  # Meta kernels of the replacements: the swapped graph runs under fake tensors
+        out, dqk, dv = gm(q, k, v, v)
+    assert out.shape == v.shape and dqk.shape == q.shape and dv.shape == v.shape
+    # an empty registry leaves the graph alone, as the reference's pass documents
+    before = [n.target for n in gm.graph.nodes]
+    ref.swap_ops(gm, ref.OpSwapRegistry())
+    assert [n.target for n in gm.graph.nodes] == before
+
+
+def test_swap_table_feeds_the_reference_registry():
+    """recir_b200.graph.swap_table is the mapping to hand to the reference's registry."""
+    from recir_b200 import graph
+
+    ref = _reference_op_swap()
+    src_f = torch.ops.recir_b200_test.source_ragged_attention.default
+    src_b = torch.ops.recir_b200_test.source_ragged_attention_bwd.default
+    registry = ref.OpSwapRegistry()
+    for s, r in graph.swap_table(source_fwd=src_f, source_bwd=src_b).items():
+        registry.register(s, r)
+    assert registry.get(src_f) is torch.ops.recir.b200_ragged_attention_fwd.default
+    assert registry.get(src_b) is torch.ops.recir.b200_ragged_attention_bwd.default
+
+
+def test_status_reader_names_what_the_device_reported():
+    """``check_status`` turns the device status word into an error that names the condition; here the word
+    is a host tensor standing in for the per-device one (no GPU needed for the decoding)."""
+    cpu = torch.device("cpu")
+    try:
+        ops._status[cpu] = torch.tensor([1, 102, 0, 0], dtype=torch.int32)
+        with pytest.raises(RuntimeError, match=r"malformed.*WAIT_MMA"):
+            ops.check_status()
+        assert not ops._status[cpu].any()  # reading clears it
+        ops.check_status()
+        ops._status[cpu] = torch.tensor([0, 777, 0, 0], dtype=torch.int32)
+        with pytest.raises(RuntimeError, match="code 777"):
+            ops.check_status(what="unit")
+    finally:
+        ops._status.pop(cpu, None)

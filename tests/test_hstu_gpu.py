@@ -468,3 +468,58 @@ def test_calls_can_be_captured_in_a_cuda_graph_and_replayed():
         for g, w in zip(got, want):
             assert torch.equal(g, w)
     assert float(got[0].float().abs().max()) > 0
+
+
+def test_status_word_reports_malformed_offsets_and_gave_up_waits():
+    """Kernels cannot raise: conditions found on the device land in the per-device status word that
+    every operator call passes down, and checked mode (or ``check_status`` at a synchronisation point of
+    the caller's choosing) turns them into ``RuntimeError``.  Nothing here faults: decreasing offsets are
+    clamped on the device, and the wait that gives up is the library's own 2 ms self-test."""
+    from recir_b200 import _lib
+
+    q, k, v, do, off, kw = _jagged_case(31, [300, 200], [10, 20])
+    _gpu(q, k, v, do, off, kw)
+    ops.check_status()  # a well-formed call reports nothing
+    bad = off.clone()
+    bad[1], bad[2] = 400, 350  # goes backwards: the second sequence is clamped to length 0 on the device
+    for force_simt in (False, True):
+        out = _gpu(q, k, v, do, bad, kw, force_simt=force_simt)
+        assert all(torch.isfinite(x.float()).all() for x in out)
+        with pytest.raises(RuntimeError, match="seq_offsets were malformed"):
+            ops.check_status(DEV)
+        ops.check_status(DEV)  # reading clears the word
+    ops.set_checked(True)
+    try:
+        with pytest.raises(RuntimeError, match="b200_hstu_fwd.*malformed"):
+            _gpu(q, k, v, do, bad, kw, backward=False)
+        _gpu(q, k, v, do, off, kw)  # and a good call passes in checked mode
+    finally:
+        ops.set_checked(False)
+    # the bounded-wait self-test reports through the same word and the same reader
+    lib = _lib.load()
+    rc = lib.b200_hstu_debug_bounded_wait(ops.status_tensor(DEV).data_ptr(), 103, 2_000_000,
+                                          torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    with pytest.raises(RuntimeError, match="WAIT_EPILOGUE"):
+        ops.check_status(DEV)
+    ops.check_status(DEV)
+    o2 = _gpu(q, k, v, do, off, kw)
+    ro = _oracle(q, k, v, do, off, kw, backward=False)[0]
+    assert rel_l2(o2[0].float(), ro) <= 6e-3
+
+
+def test_overlapping_offsets_cannot_overrun_the_work_list():
+    """Offsets that restart ([0, T, 0, T, ...]) describe more 128-row blocks than the work list can
+    hold; each pair is valid on its own, so only the total gives it away.  The list is cut at its
+    capacity on the device and the call is flagged; every write stays inside the caller's buffers
+    (the guard rows around the outputs keep their canary value)."""
+    T, H, D, B = 1024, 1, 128, 24
+    g = torch.Generator().manual_seed(2)
+    q, k, v = ((torch.randn(T, H, D, generator=g) * 0.5).to(torch.bfloat16).to(DEV) for _ in range(3))
+    off = torch.tensor([0, T] * (B // 2) + [0], dtype=torch.int64, device=DEV)  # B sequences, half of them length T
+    assert off.numel() == B + 1
+    o = torch.ops.recir.b200_hstu_attention_fwd(q, k, v, off, T, 0.1, True, None, 0, 0, None, 0)
+    torch.cuda.synchronize()
+    assert torch.isfinite(o.float()).all()
+    with pytest.raises(RuntimeError, match="malformed"):
+        ops.check_status(DEV)

@@ -57,7 +57,7 @@ def test_gather_rows_matches_offsets():
 def test_length_buckets_of_the_zipf_batch_partition_it():
     """The per-length-bucket runner covers every sequence of the Zipf batch exactly once, keeps each
     batch's lengths inside its bucket and repeats / cuts buckets to the advertised token range."""
-    from recir_b200 import run_case
+    import bench_cases as run_case
 
     hist, tg = workload.config4_lengths(1024)
     lengths = hist + tg

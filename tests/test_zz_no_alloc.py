@@ -70,3 +70,23 @@ def test_static_scratch_rejects_oversized_problems_on_the_host():
     assert lib.b200_hstu_fwd_static_scratch(ctypes.byref(p), None) == -7
     assert "scratch" in _lib.strerror(-7)
     del keep
+
+
+def test_static_scratch_first_use_from_a_fresh_host_thread():
+    """The address of the built-in array is looked up per device, with the device that owns the inputs
+    made current for the lookup: a host thread whose first CUDA work is this entry point gets the same
+    result as the main thread."""
+    import threading
+
+    alpha = 1.0 / 128 ** 0.5
+    q, k, v, off, nt = _problem(3, [257, 400], [10, 0])
+    want = _static_scratch_forward(q, k, v, off, nt, 400, alpha)
+    got = {}
+
+    def work():
+        got["o"] = _static_scratch_forward(q, k, v, off, nt, 400, alpha)
+
+    t = threading.Thread(target=work)
+    t.start()
+    t.join()
+    assert torch.equal(got["o"], want)
