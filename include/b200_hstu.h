@@ -70,6 +70,8 @@ extern "C" {
 #define B200_HSTU_FLAG_FORCE_SIMT 0x10u     /* use the plain CUDA-core kernels (cross-check path) */
 #define B200_HSTU_FLAG_BWD_SKIP_DQ 0x20u    /* backward: run only the dK/dV pass (dq is left untouched) */
 #define B200_HSTU_FLAG_BWD_SKIP_DKV 0x40u   /* backward: run only the dQ pass (dk, dv are left untouched) */
+#define B200_HSTU_FLAG_TRACE 0x80u /* instrumented builds (-DB200_HSTU_PROFILING) only: status is then a buffer of
+                                         16 + 8192 ints and CTA 0 records an event trace behind the four status words */
 
 /* error codes */
 #define B200_HSTU_OK 0

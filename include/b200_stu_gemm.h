@@ -1,0 +1,60 @@
+/* C ABI of the STU-layer projections on the tensor cores: out = bias + A W with A = x or the weighted
+ * layer norm of x computed inside the same kernel.
+ *
+ * Reference semantics (CPU, ATen), recir/ops/kjt_split_per_feature.cpp:
+ *   tritonAddMm        :246-262  at::addmm(bias, x, w); schema generative_recommenders::triton_addmm_fwd
+ *   weightedLayerNorm  :197-244  (the stage in front of the u/v/q/k projection of an STU layer)
+ * The fused form computes addmm(bias, weightedLayerNorm(x, ln_weight, ln_bias, eps, is_swish)[0], w) and also
+ * returns the row statistics the layer norm returns.  As in the reference the normalised rows are rounded to
+ * the element type before the product; sums run in float32; the result is rounded once, after the bias.
+ * The output may be consumed in place as column slices (u | v | q | k with row stride N): the attention entry
+ * points of b200_hstu.h take row-strided inputs.
+ *
+ * Served shapes: bfloat16 / float16, K a multiple of 64 and at most 512 (a CTA keeps its 128 x K operand in
+ * shared memory), N a multiple of 8, 16-byte aligned bases and row strides.  b200_stu_addmm_supported tells.
+ *
+ * Conventions of b200_hstu.h: plain pointers and sizes, caller-owned buffers, nothing allocated or
+ * synchronised, launches go to the given stream, negative B200_HSTU_E* codes on error; status (optional,
+ * device int32[4], zeroed by the caller) receives in status[1] the code of a pipeline wait that gave up
+ * (111 producer, 112 MMA issuer, 113 epilogue).
+ */
+#ifndef B200_STU_GEMM_H
+#define B200_STU_GEMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200_GEMM_FLAG_LAYER_NORM 0x1u /* A = layer norm of x (else A = x) */
+#define B200_GEMM_FLAG_SWISH 0x2u      /* with LAYER_NORM and ln_weight: A = sigmoid(ln(x)) * x   (is_swish) */
+
+typedef struct B200GemmParams {
+  uint32_t struct_size; /* sizeof(B200GemmParams) */
+  uint32_t flags;
+  int32_t dtype;        /* B200_HSTU_BF16 / _F16: element type of x, w, bias, ln_weight, ln_bias, out */
+  float eps;            /* layer norm */
+  int64_t M, K, N;      /* x [M, K], w [K, N], out [M, N] */
+  int64_t x_row_stride, w_row_stride, out_row_stride; /* in elements */
+  int64_t bias_row_stride; /* 0: one bias row [N] for every output row; else bias is [M, N] with this stride */
+  const void* x;
+  const void* w;
+  const void* bias;
+  const void* ln_weight; /* [K] or NULL (then ln_bias must be NULL too) */
+  const void* ln_bias;
+  void* out;
+  float* mean;           /* [M], written with LAYER_NORM */
+  float* rstd;           /* [M] */
+  int32_t* status;       /* optional */
+} B200GemmParams;
+
+/* 1 if b200_stu_addmm serves this dtype and these sizes, else 0. */
+int b200_stu_addmm_supported(const B200GemmParams* p);
+int b200_stu_addmm(const B200GemmParams* p, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -59,6 +59,36 @@ int b200_stu_layer_norm_mul_fwd(const B200RowwiseParams* p, void* stream);
 /* Number of column blocks of the mul output: 1 + concat_u + concat_x. */
 int b200_stu_layer_norm_mul_parts(uint32_t flags);
 
+/* Backward of b200_stu_layer_norm_fwd (statistics computed from x, i.e. without FLAG_STATS_IN).  The
+ * reference has no backward operator for weightedLayerNorm (:197-244): it differentiates the ATen
+ * composite by autograd; this entry point computes the closed form of that derivative,
+ *   dn = dy (is_swish: dy * x * s * (1 - s), s = sigmoid(ln(x) * w + b)),  dweight = sum_rows dn * xh,
+ *   dbias = sum_rows dn,  dx = rstd * (dn * w - mean_cols(dn * w) - xh * mean_cols(dn * w * xh)) (+ dy * s),
+ * in float32 with one rounding per gradient, and deterministically (no atomics: per-CTA partial column sums
+ * go to the caller's workspace and are added in a fixed order).  cols a multiple of 8, at most 1024. */
+typedef struct B200LayerNormBwdParams {
+  uint32_t struct_size; /* sizeof(B200LayerNormBwdParams) */
+  uint32_t flags;       /* B200_ROWWISE_FLAG_SWISH */
+  int32_t dtype;        /* element type of dy, x, weight, bias, dx, dweight, dbias */
+  int32_t reserved;
+  int64_t rows, cols;
+  int64_t dy_row_stride, x_row_stride, dx_row_stride; /* in elements */
+  const void* dy;       /* [rows, cols] gradient of the layer norm's output */
+  const void* x;        /* [rows, cols] the forward input */
+  const void* weight;   /* [cols] or NULL (then bias, dweight, dbias are NULL too) */
+  const void* bias;
+  const float* mean;    /* [rows] as returned by the forward */
+  const float* rstd;
+  void* dx;             /* [rows, cols] */
+  void* dweight;        /* [cols] */
+  void* dbias;          /* [cols] */
+  float* workspace;     /* b200_stu_layer_norm_bwd_workspace_bytes(rows, cols) bytes, 16-byte aligned (with weight) */
+  uint64_t workspace_bytes;
+} B200LayerNormBwdParams;
+
+size_t b200_stu_layer_norm_bwd_workspace_bytes(int64_t rows, int64_t cols);
+int b200_stu_layer_norm_bwd(const B200LayerNormBwdParams* p, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

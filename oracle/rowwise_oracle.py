@@ -152,3 +152,51 @@ def jagged_dense_bmm_add(seq_offsets, jagged, dense, bias, elementwise=False, dt
         parts.append(jag[s:e] @ den[b] + (bia[s:e] if elementwise else bia[b]))
     out = np.concatenate(parts, 0) if parts else np.zeros((0, den.shape[2]))
     return round_to(out.astype(np.float32), dtype)
+
+
+def addmm(x, w, bias, dtype="float32"):
+    """``at::addmm(bias, x, w)`` (``tritonAddMm``, recir/ops/kjt_split_per_feature.cpp:246-262) for operands
+    whose values are representable in ``dtype``: products and sums in float64 (so that only the final
+    rounding matters), bias added before the single rounding to ``dtype``."""
+    acc = np.asarray(x, dtype=np.float64) @ np.asarray(w, dtype=np.float64) + np.asarray(bias, dtype=np.float64)
+    return round_to(acc.astype(np.float32), dtype)
+
+
+def layer_norm_addmm(x, ln_weight, ln_bias, eps, w, bias, dtype="bfloat16", is_swish=False):
+    """The layer norm in front of a projection followed by that projection, as the reference chains them
+    (``weightedLayerNorm`` :197-244 returns rows rounded to ``dtype``; ``tritonAddMm`` :246-262 consumes them).
+    Returns (out, mean, rstd)."""
+    y, mean, rstd = weighted_layer_norm(x, ln_weight, ln_bias, eps, dtype, is_swish=is_swish)
+    return addmm(y, w, bias, dtype), mean, rstd
+
+
+def weighted_layer_norm_bwd(dy, x, weight, bias, eps, dtype="float32", is_swish=False):
+    """Gradients of ``weightedLayerNorm`` (recir/ops/kjt_split_per_feature.cpp:220-243) with respect to x,
+    weight and bias, i.e. what autograd gives through the composite (which is how the reference
+    differentiates it): with xh = (x - mean) * rstd, n = xh * w + b and y = n (or sigmoid(n) * x),
+      dn = dy                      (or dy * x * s * (1 - s) with s = sigmoid(n)),
+      dw = sum_rows dn * xh,   db = sum_rows dn,
+      dxh = dn * w,
+      dx = rstd * (dxh - mean_cols(dxh) - xh * mean_cols(dxh * xh))   (+ dy * s for the gated form).
+    The composite runs in float32 and casts each gradient to its input's element type once; here the
+    arithmetic is float64 and the results are rounded to ``dtype`` once.  Returns (dx, dw, db); dw and db are
+    None without weight."""
+    xf = np.asarray(x, dtype=np.float64)
+    g = np.asarray(dy, dtype=np.float64)
+    mean = xf.mean(axis=1, keepdims=True)
+    c = xf - mean
+    rstd = 1.0 / np.sqrt((c * c).mean(axis=1, keepdims=True) + float(eps))
+    xh = c * rstd
+    w = None if weight is None else np.asarray(weight, dtype=np.float64)
+    n = xh if w is None else xh * w + np.asarray(bias, dtype=np.float64)
+    direct = 0.0
+    dn = g
+    if is_swish:
+        s = 1.0 / (1.0 + np.exp(-n))
+        dn = g * xf * s * (1.0 - s)
+        direct = g * s
+    dxh = dn if w is None else dn * w
+    dx = rstd * (dxh - dxh.mean(axis=1, keepdims=True) - xh * (dxh * xh).mean(axis=1, keepdims=True)) + direct
+    dw = None if w is None else round_to((dn * xh).sum(axis=0).astype(np.float32), dtype)
+    db = None if w is None else round_to(dn.sum(axis=0).astype(np.float32), dtype)
+    return round_to(dx.astype(np.float32), dtype), dw, db

@@ -18,6 +18,7 @@ FLAG_SCALE_PER_TOKEN = 0x8
 FLAG_FORCE_SIMT = 0x10
 FLAG_BWD_SKIP_DQ = 0x20
 FLAG_BWD_SKIP_DKV = 0x40
+FLAG_TRACE = 0x80
 
 EXPORTS = (
     "b200_hstu_fwd", "b200_hstu_bwd", "b200_hstu_workspace_bytes", "b200_hstu_uses_tensor_cores",
@@ -27,6 +28,9 @@ EXPORTS = (
     "b200_hstu_debug_col_mask", "b200_hstu_last_cuda_error", "b200_hstu_debug_bounded_wait",
     # include/b200_stu_rowwise.h
     "b200_stu_layer_norm_fwd", "b200_stu_layer_norm_mul_fwd", "b200_stu_layer_norm_mul_parts",
+    "b200_stu_layer_norm_bwd", "b200_stu_layer_norm_bwd_workspace_bytes",
+    # include/b200_stu_gemm.h
+    "b200_stu_addmm", "b200_stu_addmm_supported",
     # include/b200_stu_jagged.h
     "b200_stu_jagged_copy",
     # include/b200_stu_embed.h
@@ -87,6 +91,40 @@ class B200RowwiseParams(ctypes.Structure):
         ("mean_in", ctypes.c_void_p), ("rstd_in", ctypes.c_void_p),
         ("y", ctypes.c_void_p), ("mean", ctypes.c_void_p), ("rstd", ctypes.c_void_p),
         ("scale", ctypes.c_void_p), ("q8", ctypes.c_void_p),
+    ]
+
+
+class B200LayerNormBwdParams(ctypes.Structure):
+    """Mirror of ``struct B200LayerNormBwdParams`` (include/b200_stu_rowwise.h)."""
+
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32), ("flags", ctypes.c_uint32),
+        ("dtype", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("rows", ctypes.c_int64), ("cols", ctypes.c_int64),
+        ("dy_row_stride", ctypes.c_int64), ("x_row_stride", ctypes.c_int64), ("dx_row_stride", ctypes.c_int64),
+        ("dy", ctypes.c_void_p), ("x", ctypes.c_void_p), ("weight", ctypes.c_void_p), ("bias", ctypes.c_void_p),
+        ("mean", ctypes.c_void_p), ("rstd", ctypes.c_void_p),
+        ("dx", ctypes.c_void_p), ("dweight", ctypes.c_void_p), ("dbias", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
+    ]
+
+
+# flags of include/b200_stu_gemm.h
+GEMM_LAYER_NORM, GEMM_SWISH = 0x1, 0x2
+
+
+class B200GemmParams(ctypes.Structure):
+    """Mirror of ``struct B200GemmParams`` (include/b200_stu_gemm.h)."""
+
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32), ("flags", ctypes.c_uint32),
+        ("dtype", ctypes.c_int32), ("eps", ctypes.c_float),
+        ("M", ctypes.c_int64), ("K", ctypes.c_int64), ("N", ctypes.c_int64),
+        ("x_row_stride", ctypes.c_int64), ("w_row_stride", ctypes.c_int64), ("out_row_stride", ctypes.c_int64),
+        ("bias_row_stride", ctypes.c_int64),
+        ("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("bias", ctypes.c_void_p),
+        ("ln_weight", ctypes.c_void_p), ("ln_bias", ctypes.c_void_p),
+        ("out", ctypes.c_void_p), ("mean", ctypes.c_void_p), ("rstd", ctypes.c_void_p), ("status", ctypes.c_void_p),
     ]
 
 
@@ -186,6 +224,15 @@ def load() -> ctypes.CDLL:
         fn.restype = ctypes.c_int
     lib.b200_stu_layer_norm_mul_parts.argtypes = [ctypes.c_uint32]
     lib.b200_stu_layer_norm_mul_parts.restype = ctypes.c_int
+    lib.b200_stu_layer_norm_bwd.argtypes = [ctypes.POINTER(B200LayerNormBwdParams), ctypes.c_void_p]
+    lib.b200_stu_layer_norm_bwd.restype = ctypes.c_int
+    lib.b200_stu_layer_norm_bwd_workspace_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64]
+    lib.b200_stu_layer_norm_bwd_workspace_bytes.restype = ctypes.c_size_t
+    GP = ctypes.POINTER(B200GemmParams)
+    lib.b200_stu_addmm.argtypes = [GP, ctypes.c_void_p]
+    lib.b200_stu_addmm.restype = ctypes.c_int
+    lib.b200_stu_addmm_supported.argtypes = [GP]
+    lib.b200_stu_addmm_supported.restype = ctypes.c_int
     lib.b200_stu_add_ts_pos_emb.argtypes = [ctypes.POINTER(B200EmbedParams), ctypes.c_void_p]
     lib.b200_stu_add_ts_pos_emb.restype = ctypes.c_int
     lib.b200_stu_jagged_copy.argtypes = [ctypes.POINTER(B200JaggedParams), ctypes.c_void_p]

@@ -14,7 +14,7 @@ import sys
 PKG = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libb200_hstu.so")
-SOURCES = ["hstu_capi.cu", "hstu_simt.cu", "hstu_tc.cu", "hstu_tc_bwd.cu", "stu_rowwise.cu", "stu_jagged.cu", "stu_embed.cu"]
+SOURCES = ["hstu_capi.cu", "hstu_simt.cu", "hstu_tc.cu", "hstu_tc_bwd.cu", "stu_rowwise.cu", "stu_rowwise_bwd.cu", "stu_gemm.cu", "stu_jagged.cu", "stu_embed.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",
     "-Xcompiler", "-fPIC", "-shared", "--use_fast_math=false",

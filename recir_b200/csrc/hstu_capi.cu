@@ -58,6 +58,7 @@ int validate(const B200HstuParams* p, int pass, KernelArgs* a) {
   a->dq = p->dq; a->dk = p->dk; a->dv = p->dv;
   a->seq_offsets = p->seq_offsets; a->num_targets = p->num_targets; a->attn_scale = p->attn_scale;
   a->status = p->status;
+  a->trace_buf = (p->flags & B200_HSTU_FLAG_TRACE) ? p->status : nullptr;
   a->T = p->T;
   a->q_rs = p->q_row_stride; a->k_rs = p->k_row_stride; a->v_rs = p->v_row_stride; a->o_rs = p->o_row_stride;
   a->do_rs = p->do_row_stride; a->dq_rs = p->dq_row_stride; a->dk_rs = p->dk_row_stride; a->dv_rs = p->dv_row_stride;

@@ -81,6 +81,7 @@ struct KernelArgs {
   const void* num_targets;
   const float* attn_scale;
   int* status;
+  int* trace_buf;  // instrumented builds only: event trace of CTA 0 (B200_HSTU_FLAG_TRACE), else null
   long long T;
   long long q_rs, k_rs, v_rs, o_rs, do_rs, dq_rs, dk_rs, dv_rs;
   int B, H, Dqk, Dv;

@@ -493,7 +493,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
           good = wait_all(&sh.v_full[vs], vph);
           sw.stop(pf[PF_MMA_VFULL]);
           if (!good) return false;
-          if (lane == 0) trace_event<PROF>(a.status, 0, pg, 2, 4);
+          if (lane == 0) trace_event<PROF>(a.trace_buf, 0, pg, 2, 4);
           tc_fence_after();
           const uint32_t p_tmem = tmem + (sb ? TMEM_S1 : TMEM_S0);
           const uint32_t v_lo = v_lo0 + vs * (TILE_BYTES >> 4);
@@ -509,7 +509,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
             tc_commit(smem_u32(&sh.v_empty[vs]));
           }
           __syncwarp();
-          if (lane == 0) trace_event<PROF>(a.status, 0, pg, 3, 4);
+          if (lane == 0) trace_event<PROF>(a.trace_buf, 0, pg, 3, 4);
           ++n_pv;
           return true;
         };
@@ -520,7 +520,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
           sw.stop(pf[PF_MMA_KFULL]);
           if (!ok) break;
           last = sh.meta[g & (META_RING - 1)] & 1;
-          if (lane == 0) trace_event<PROF>(a.status, 0, g, 0, 4);
+          if (lane == 0) trace_event<PROF>(a.trace_buf, 0, g, 0, 4);
           tc_fence_after();
           const uint32_t s_tmem = tmem + ((g & 1) ? TMEM_S1 : TMEM_S0);
           const uint32_t k_lo = k_lo0 + ks * (TILE_BYTES >> 4);
@@ -535,7 +535,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
             tc_commit(smem_u32(&sh.s_full[g & 1]));
           }
           __syncwarp();
-          if (lane == 0) trace_event<PROF>(a.status, 0, g, 1, 4);
+          if (lane == 0) trace_event<PROF>(a.trace_buf, 0, g, 1, 4);
           if (have_prev) ok = issue_pv(prev_g, prev_vs, prev_vph);
           prev_g = g; prev_vs = vs_cur; prev_vph = vph_cur;
           have_prev = true;
@@ -701,9 +701,9 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
       bool full = false, full_next = false;
       bool have = have_item && next_tile(n0, full);
       if (have) {
-        if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 0, 6);
+        if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, g, 0, 6);
         ok = wait_scores(g);
-        if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 1, 6);
+        if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, g, 1, 6);
         if (ok) tmem_ld32(s_addr_of(g), sa);
       }
       while ((have || (!have_item && drain_pending)) && ok) {
@@ -715,7 +715,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
           sw.start();
           tmem_wait_ld(sa);
           tmem_ld32(s_addr + 32, sb2);
-          if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 2, 6);
+          if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, g, 2, 6);
           if (full) {
             silu_chunk<IS_BF16, false>(sa, pk, c1, 0u);
             tmem_st16(s_addr, pk);  // P (16 columns per chunk) goes over the group's own score columns
@@ -748,7 +748,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
             }
             tmem_st16(s_addr + 16, pk);
           }
-          if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 3, 6);
+          if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, g, 3, 6);
           if (n0 + BLK > s.len) {
             // Key rows past the end of the sequence belong to someone else (or to nobody) and may
             // hold anything, NaN included; their P columns are exact zeros, but 0 * NaN is NaN,
@@ -765,10 +765,10 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
             tmem_ld32(s_addr_of(g + 1), sa);
           }
           tmem_wait_st();
-          if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 4, 6);
+          if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, g, 4, 6);
           tc_fence_before();
           mbar_arrive(smem_u32(&sh.p_ready[sb]));
-          if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, g, 5, 6);
+          if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, g, 5, 6);
           if (full) { sw.stop(pf_fullt); ++n_fullt; } else { sw.stop(pf_part); ++n_part; }
           ++g;
         }
@@ -853,6 +853,12 @@ bool ensure_current_context(const void* device_ptr) {
 
 // [rows, H*128] 16-bit matrix, box = 64 columns x 128 rows, 128-byte swizzle, zero fill out of range.
 bool make_map(CUtensorMap* m, const void* base, long long rows, long long width, long long row_stride, bool bf16) {
+  return make_map_box(m, base, rows, width, row_stride, BLK, bf16);
+}
+
+// Same with a box of 64 columns x `box_rows` rows (at most 256).
+bool make_map_box(CUtensorMap* m, const void* base, long long rows, long long width, long long row_stride, int box_rows,
+                  bool bf16) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     set_error_stage("tensor map: cuTensorMapEncodeTiled entry point not found");
@@ -860,7 +866,7 @@ bool make_map(CUtensorMap* m, const void* base, long long rows, long long width,
   }
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride) * 2};
-  cuuint32_t box[2] = {64, BLK};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                         const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,

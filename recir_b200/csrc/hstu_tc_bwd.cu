@@ -278,6 +278,16 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
           todo &= todo - 1;
           const int idx = base + bit;
           const int krow = static_cast<int>(s.start) + kr.at(idx) * BLK;
+          // V first: its stage is released when the tile's last dP MMA has run, half a tile before the
+          // K stage (which the dQ MMAs still read), so its copy is already under way when K's can start
+          ok = wait_all(&sh.v_empty[st], ph ^ 1);
+          if (!ok) break;
+          if (elect_one()) {
+            mbar_arrive_expect_tx(smem_u32(&sh.v_full[st]), TILE_BYTES);
+            tma_load_2d(smem_u32(sh.v[st]), &maps.v, smem_u32(&sh.v_full[st]), col0, krow);
+            tma_load_2d(smem_u32(sh.v[st]) + HALF_TILE_BYTES, &maps.v, smem_u32(&sh.v_full[st]), col0 + 64, krow);
+          }
+          __syncwarp();
           ok = wait_all(&sh.k_empty[st], ph ^ 1);
           if (!ok) break;
           if (elect_one()) {
@@ -285,14 +295,6 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
             mbar_arrive_expect_tx(smem_u32(&sh.k_full[st]), TILE_BYTES);
             tma_load_2d(smem_u32(sh.k[st]), &maps.k, smem_u32(&sh.k_full[st]), col0, krow);
             tma_load_2d(smem_u32(sh.k[st]) + HALF_TILE_BYTES, &maps.k, smem_u32(&sh.k_full[st]), col0 + 64, krow);
-          }
-          __syncwarp();
-          ok = wait_all(&sh.v_empty[st], ph ^ 1);
-          if (!ok) break;
-          if (elect_one()) {
-            mbar_arrive_expect_tx(smem_u32(&sh.v_full[st]), TILE_BYTES);
-            tma_load_2d(smem_u32(sh.v[st]), &maps.v, smem_u32(&sh.v_full[st]), col0, krow);
-            tma_load_2d(smem_u32(sh.v[st]) + HALF_TILE_BYTES, &maps.v, smem_u32(&sh.v_full[st]), col0 + 64, krow);
           }
           __syncwarp();
           ++gt;
@@ -325,7 +327,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
       auto issue_acc = [&](uint32_t pgt, uint32_t psub, uint32_t pst) -> bool {
         if (!wait_all(&sh.ds_ready[psub], pgt & 1)) return false;
         if (n_acc == 0 && !wait_all(&sh.acc_empty, (it & 1) ^ 1)) return false;
-        if (lane == 0) trace_event<PROF>(a.status, 0, 2 * pgt + psub, 2, 4);
+        if (lane == 0) trace_event<PROF>(a.trace_buf, 0, 2 * pgt + psub, 2, 4);
         tc_fence_after();
         const uint32_t kn_lo = kn_lo0 + pst * (TILE_BYTES >> 4) + psub * (SUBTILE_BYTES >> 4);
         const uint32_t ds_tmem = tmem + DQ_DP0 + psub * 64;
@@ -338,7 +340,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
           if (psub == 1) tc_commit(smem_u32(&sh.k_empty[pst]));
         }
         __syncwarp();
-        if (lane == 0) trace_event<PROF>(a.status, 0, 2 * pgt + psub, 3, 4);
+        if (lane == 0) trace_event<PROF>(a.trace_buf, 0, 2 * pgt + psub, 3, 4);
         ++n_acc;
         return true;
       };
@@ -348,7 +350,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
         if (ok) ok = wait_all(&sh.v_full[st], ph);
         if (!ok) break;
         last = sh.meta[gt & (META_RING - 1)] & 1;
-        if (lane == 0) trace_event<PROF>(a.status, 0, 2 * gt, 0, 4);
+        if (lane == 0) trace_event<PROF>(a.trace_buf, 0, 2 * gt, 0, 4);
         tc_fence_after();
         for (uint32_t sub = 0; sub < 2 && ok; ++sub) {
           const uint32_t k_lo = k_lo0 + st * (TILE_BYTES >> 4) + sub * (SUBTILE_BYTES >> 4);
@@ -366,7 +368,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
             if (sub == 1) tc_commit(smem_u32(&sh.v_empty[st]));
           }
           __syncwarp();
-          if (lane == 0) trace_event<PROF>(a.status, 0, 2 * gt + sub, 1, 4);
+          if (lane == 0) trace_event<PROF>(a.trace_buf, 0, 2 * gt + sub, 1, 4);
           if (have_prev) ok = issue_acc(prev_gt, prev_sub, prev_st);
           prev_gt = gt; prev_sub = sub; prev_st = st; have_prev = true;
         }
@@ -395,35 +397,41 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
     int2 w;
     SeqInfo s;
     uint32_t todo0 = 0u, full0 = 0u;
-    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, todo0, full0, ok, abort_flag, a.status, WAIT_EPILOGUE); ++n_item) {
+    // A operands of an item: its Q and dO tiles were prefetched into shared memory by TMA; group 0
+    // copies its Q row, group 1 its dO row into TMEM (rows past the sequence end as zeros).  The copy
+    // for item n + 1 is made at the END of item n, right after its last half tile: by then every score
+    // MMA of item n has completed (the epilogue waited for each of them), so nothing reads the operand
+    // columns any more, while the last dQ MMAs and the accumulator drain are still to come.  The MMA
+    // warp can therefore issue the next item's first score MMAs while this item's dQ leaves TMEM.
+    auto copy_a_operands = [&](uint32_t item, int m_row, int len) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.qd_full), item & 1, abort_flag, a.status, WAIT_EPILOGUE)))
+        return false;
+      const unsigned char* tile = wg == 0 ? sh.q : sh.d_o;
+      const uint32_t dst = tmem + lane_addr + (wg == 0 ? DQ_QA : DQ_DOA);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {  // 4 x 16 TMEM columns = 4 x 32 elements; box = c / 2, chunks (c % 2) * 4 ..
+        uint32_t r[16];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int chunk = (c & 1) * 4 + j;  // 16-byte chunk inside the 128-byte box row
+          uint4 x = *reinterpret_cast<const uint4*>(tile + (c >> 1) * HALF_TILE_BYTES + row * 128 +
+                                                    ((chunk ^ (row & 7)) << 4));
+          if (m_row >= len) x = make_uint4(0u, 0u, 0u, 0u);
+          r[4 * j + 0] = x.x; r[4 * j + 1] = x.y; r[4 * j + 2] = x.z; r[4 * j + 3] = x.w;
+        }
+        tmem_st16(dst + c * 16, r);
+      }
+      mbar_arrive(smem_u32(&sh.qd_empty));  // the tile has been read: the item after may land
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&sh.a_ready));
+      return true;
+    };
+    bool have = next_item(sh.ring, 0, w, s, todo0, full0, ok, abort_flag, a.status, WAIT_EPILOGUE);
+    if (have) ok = copy_a_operands(0, w.y * BLK + row, s.len);
+    for (uint32_t n_item = 0; ok && have; ++n_item) {
       const int head = w.x >> 16, qblk = w.y;
       const int m0 = qblk * BLK, m = m0 + row;
-      // ---- A operands: the item's Q and dO tiles were prefetched into shared memory by TMA; group 0
-      // copies its Q row, group 1 its dO row into TMEM (rows past the sequence end as zeros).
-      // The previous item's MMAs are complete: both groups waited for its accumulator.
-      {
-        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.qd_full), it & 1, abort_flag, a.status, WAIT_EPILOGUE));
-        if (!ok) break;
-        const unsigned char* tile = wg == 0 ? sh.q : sh.d_o;
-        const uint32_t dst = tmem + lane_addr + (wg == 0 ? DQ_QA : DQ_DOA);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {  // 4 x 16 TMEM columns = 4 x 32 elements; box = c / 2, chunks (c % 2) * 4 ..
-          uint32_t r[16];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int chunk = (c & 1) * 4 + j;  // 16-byte chunk inside the 128-byte box row
-            uint4 x = *reinterpret_cast<const uint4*>(tile + (c >> 1) * HALF_TILE_BYTES + row * 128 +
-                                                      ((chunk ^ (row & 7)) << 4));
-            if (m >= s.len) x = make_uint4(0u, 0u, 0u, 0u);
-            r[4 * j + 0] = x.x; r[4 * j + 1] = x.y; r[4 * j + 2] = x.z; r[4 * j + 3] = x.w;
-          }
-          tmem_st16(dst + c * 16, r);
-        }
-        mbar_arrive(smem_u32(&sh.qd_empty));  // the tile has been read: the next item's may land
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(smem_u32(&sh.a_ready));
-      }
       const RowMask rm = row_mask(m, s, a.mask);
       const BlockRange kr = key_blocks_for_query_block(m0, s, a.mask);
       const int cnt = kr.count();
@@ -442,9 +450,9 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
           const bool full = (full_bits >> bit) & 1u;
           // both groups work on every 64-column half tile: group wg owns its columns [32 wg, 32 wg + 32)
           for (int sub = 0; sub < 2 && ok; ++sub) {
-            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 0, 6);
+            if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt + sub, 0, 6);
             ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[sub]), gt & 1, abort_flag, a.status, WAIT_EPILOGUE));
-            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 1, 6);
+            if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt + sub, 1, 6);
             if (!ok) break;
             tc_fence_after();
             const uint32_t s_addr = tmem + lane_addr + DQ_S0 + sub * 64 + wg * 32;
@@ -454,7 +462,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
             tmem_ld32(dp_addr, dpv);
             tmem_wait_ld(sv);
             tmem_wait_ld(dpv);
-            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 2, 6);
+            if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt + sub, 2, 6);
             // on partial tiles most 32-column chunks are all-kept or all-dropped for a whole warp
             // (32 consecutive rows): vote, mask per element only where the boundary crosses
             const uint32_t hb = full ? 0xffffffffu
@@ -468,7 +476,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
               bwd_chunk<IS_BF16, false, true>(sv, dpv, unused, pk, c1, hb);
             }
             tmem_st16(dp_addr, pk);  // dS (16 columns) over the group's own dP columns
-            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 3, 6);
+            if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt + sub, 3, 6);
             if (n0 + BLK > s.len && wg == 0) {
               // key rows past the sequence end feed the dQ MMA as B rows: clear them (0 * NaN = NaN)
               const int first_bad = s.len - n0, lo = first_bad > sub * 64 ? first_bad : sub * 64;
@@ -477,12 +485,23 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(smem_u32(&sh.ds_ready[sub]));
-            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 4, 6);
+            if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt + sub, 4, 6);
           }
           ++gt;
         }
       }
       if (!ok) break;
+      // ---- next item: take it from the ring and put its A operands in place (see copy_a_operands)
+      int2 w_next;
+      SeqInfo s_next;
+      uint32_t todo_next = 0u, full_next = 0u;
+      const bool have_next = next_item(sh.ring, n_item + 1, w_next, s_next, todo_next, full_next, ok, abort_flag, a.status,
+                                       WAIT_EPILOGUE);
+      if (!ok) break;
+      if (have_next) {
+        ok = copy_a_operands(it + 1, w_next.y * BLK + row, s_next.len);
+        if (!ok) break;
+      }
       // ---- dQ leaves TMEM: group wg converts columns [64 wg, 64 wg + 64) of its row
       ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.acc_full), it & 1, abort_flag, a.status, WAIT_EPILOGUE));
       if (!ok) break;
@@ -513,8 +532,9 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
         store_staged64(stage, reinterpret_cast<unsigned short*>(a.dq) + (s.start + m0) * a.dq_rs + head * HEAD_DIM + wg * 64,
                        a.dq_rs, s.len - m0, row);
       }
-      if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt, 5, 6);
+      if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt, 5, 6);
       ++it;
+      w = w_next; s = s_next; todo0 = todo_next; full0 = full_next; have = have_next;
     }
     if (row == 0) bulk_wait_all();  // shared memory must outlive the stores that read it
   }
@@ -703,7 +723,7 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
         const bool g2 = n_acc != 0 || wait_all(&sh.acc_empty, (it & 1) ^ 1);
         sw.stop(pf[PB_MMA_WAIT_ACC]);
         if (!g2) return false;
-        if (lane == 0) trace_event<PROF>(a.status, 0, 2 * pgt + psub, 1, 4);
+        if (lane == 0) trace_event<PROF>(a.trace_buf, 0, 2 * pgt + psub, 1, 4);
         tc_fence_after();
         const uint32_t don_lo = don_lo0 + pst * (TILE_BYTES >> 4) + psub * (SUBTILE_BYTES >> 4);
         const uint32_t qn_lo = qn_lo0 + pst * (TILE_BYTES >> 4) + psub * (SUBTILE_BYTES >> 4);
@@ -720,12 +740,12 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
           if (psub == 1) tc_commit(smem_u32(&sh.qd_empty[pst]));
         }
         __syncwarp();
-        if (lane == 0) trace_event<PROF>(a.status, 0, 2 * pgt + psub, 2, 4);
+        if (lane == 0) trace_event<PROF>(a.trace_buf, 0, 2 * pgt + psub, 2, 4);
         ++n_acc;
         return true;
       };
       bool last = false;
-      if (lane == 0) trace_event<PROF>(a.status, 0, 2 * gt, 3, 4);  // item start (kv tiles landed)
+      if (lane == 0) trace_event<PROF>(a.trace_buf, 0, 2 * gt, 3, 4);  // item start (kv tiles landed)
       while (!last && ok) {
         sw.start();
         ok = wait_all(&sh.qd_full[st], ph);
@@ -748,7 +768,7 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
             tc_commit(smem_u32(&sh.s_full[sub]));
           }
           __syncwarp();
-          if (lane == 0) trace_event<PROF>(a.status, 0, 2 * gt + sub, 0, 4);
+          if (lane == 0) trace_event<PROF>(a.trace_buf, 0, 2 * gt + sub, 0, 4);
           if (have_prev) ok = issue_acc(prev_gt, prev_sub, prev_st);
           prev_gt = gt; prev_sub = sub; prev_st = st; have_prev = true;
         }
@@ -808,11 +828,11 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
           const bool full = (full_bits >> bit) & 1u;
           // both groups work on every 64-column half tile: group wg owns its columns [32 wg, 32 wg + 32)
           for (int sub = 0; sub < 2 && ok; ++sub) {
-            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 0, 6);
+            if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt + sub, 0, 6);
             sw.start();
             ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.s_full[sub]), gt & 1, abort_flag, a.status, WAIT_EPILOGUE));
             sw.stop(pe_ws);
-            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 1, 6);
+            if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt + sub, 1, 6);
             if (!ok) break;
             tc_fence_after();
             sw.start();
@@ -826,7 +846,7 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
             tmem_wait_ld(sv);
             tmem_wait_ld(dpv);
             sw2.stop(pe_ld);
-            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 2, 6);
+            if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt + sub, 2, 6);
             const uint32_t hb = full ? 0xffffffffu
                                      : static_cast<uint32_t>(col_mask_bits64(cm, s.len, mbase) >> (32 * wg));
             if (__all_sync(0xffffffffu, hb == 0xffffffffu)) {
@@ -843,7 +863,7 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
             }
             tmem_st16(st_addr, pp);  // P^T and dS^T (16 columns each) over the group's own score columns
             tmem_st16(dp_addr, pd);
-            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 3, 6);
+            if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt + sub, 3, 6);
             if (q0 + BLK > s.len && wg == 0) {
               // query rows past the sequence end are B rows of the dV / dK MMAs: clear them
               const int first_bad = s.len - q0, lo = first_bad > sub * 64 ? first_bad : sub * 64;
@@ -855,7 +875,7 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
             sw2.stop(pe_st);
             tc_fence_before();
             mbar_arrive(smem_u32(&sh.p_ready[sub]));
-            if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt + sub, 4, 6);
+            if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt + sub, 4, 6);
             sw.stop(pe_tile);
           }
           ++gt;
@@ -922,7 +942,7 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
         }
       }
       sw.stop(pe_drain);
-      if (threadIdx.x == 128) trace_event<PROF>(a.status, 4096, 2 * gt, 5, 6);  // drain finished (before half tile 2*gt)
+      if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt, 5, 6);  // drain finished (before half tile 2*gt)
       ++it;
     }
     if (row == 0) bulk_wait_all();  // shared memory must outlive the stores that read it

@@ -4,6 +4,12 @@ Sequences never interact, so a jagged batch can be cut into chunks of whole sequ
 streamed: while chunk ``c`` is computed, chunk ``c+1`` is copied in and the results of
 chunk ``c-1`` are copied out.  PCIe is full duplex, so the two copy directions overlap as
 well.  Three CUDA streams (copy-in, compute, copy-out) and two device buffer slots.
+
+Enqueueing the pipeline from Python costs a few hundred microseconds per chunk, which on a slow or
+busy host can exceed the copy time.  So the first ``run`` on a given set of host buffers records the
+whole multi-stream schedule (copies, kernels, cross-stream dependencies) into one CUDA graph, and
+later calls with the same buffers replay it with a single launch; the device time is then bounded
+by the PCIe copies, not by the host.
 """
 from __future__ import annotations
 
@@ -23,7 +29,7 @@ class HostPipeline:
     def __init__(self, seq_offsets: torch.Tensor, num_targets: torch.Tensor | None, heads: int, dqk: int,
                  dv: int, dtype: torch.dtype, max_seq_len: int, alpha: float, causal: bool = True,
                  contextual_seq_len: int = 0, max_attn_len: int = 0, full_attn_size: int = 0,
-                 n_chunks: int = 6, device: torch.device | str = "cuda"):
+                 n_chunks: int = 6, device: torch.device | str = "cuda", use_graph: bool = True):
         self.device = torch.device(device)
         self.cfg = (int(max_seq_len), float(alpha), bool(causal), int(contextual_seq_len), int(max_attn_len),
                     int(full_attn_size))
@@ -52,10 +58,35 @@ class HostPipeline:
         self.s_in, self.s_comp, self.s_out = (torch.cuda.Stream(self.device) for _ in range(3))
         self.bytes_in = total * heads * (2 * dqk + 2 * dv) * torch.empty((), dtype=dtype).element_size()
         self.bytes_out = self.bytes_in
+        self.use_graph = bool(use_graph)
+        self._graphs = {}  # (data pointers of the eight host tensors) -> captured schedule
 
     def run(self, q, k, v, dout, o, dq, dk, dv) -> None:
         """Enqueues the whole pipeline; returns once everything is queued.  The caller's current
-        stream is ordered before the first copy and after the last one."""
+        stream is ordered before the first copy and after the last one.  With ``use_graph`` the
+        schedule is captured on the first call for a given set of host buffers (which must stay
+        allocated and pinned) and replayed afterwards."""
+        if not self.use_graph:
+            return self._enqueue(q, k, v, dout, o, dq, dk, dv, record_streams=True)
+        key = tuple(t.data_ptr() for t in (q, k, v, dout, o, dq, dk, dv))
+        g = self._graphs.get(key)
+        if g is None:
+            # one eager pass first: everything that initialises lazily (function attributes, the
+            # allocator's pools, the context of the side streams) happens outside the capture
+            self._enqueue(q, k, v, dout, o, dq, dk, dv, record_streams=True)
+            torch.cuda.current_stream(self.device).synchronize()
+            g = torch.cuda.CUDAGraph()
+            cap = torch.cuda.Stream(self.device)
+            cap.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.graph(g, stream=cap):
+                self._enqueue(q, k, v, dout, o, dq, dk, dv, record_streams=False)
+            torch.cuda.current_stream(self.device).wait_stream(cap)
+            if len(self._graphs) >= 4:  # bounded: each graph keeps its own output buffers alive
+                self._graphs.pop(next(iter(self._graphs)))
+            self._graphs[key] = g
+        g.replay()
+
+    def _enqueue(self, q, k, v, dout, o, dq, dk, dv, record_streams: bool) -> None:
         cur = torch.cuda.current_stream(self.device)
         start = torch.cuda.Event()
         start.record(cur)
@@ -85,7 +116,8 @@ class HostPipeline:
                 self.s_out.wait_event(comp_done)
                 for dst, src in ((o, oc), (dq, gq), (dk, gk), (dv, gv)):
                     dst[t0:t1].copy_(src, non_blocking=True)
-                    src.record_stream(self.s_out)
+                    if record_streams:  # (a captured schedule owns its buffers for its whole life)
+                        src.record_stream(self.s_out)
                 done = torch.cuda.Event()
                 done.record(self.s_out)
             # the inputs of this slot may be overwritten once its compute has finished

@@ -14,8 +14,11 @@ Positionally identical to the reference's operators, so the same node-retargetin
   (``:744-747``, semantics ``:558-600``).  Like the reference's CPU operator it applies no dropout
   (``dropout_ratio``, ``training`` and ``seed`` are accepted and ignored).
 
-Forward only (the reference differentiates its composites through ATen; a fused backward is not
-built).  CUDA tensors only; there is no CPU implementation.
+``recir::b200_weighted_layer_norm_fwd`` is differentiable: ``recir::b200_weighted_layer_norm_bwd`` is the
+closed form of what autograd gives through the reference's composite (the reference has no backward
+operator of its own).  The gate stage, the fp8 variants and the projections are forward only.
+``recir::b200_layer_norm_addmm_fwd`` fuses the layer norm into the projection behind it (one tcgen05
+kernel, ``csrc/stu_gemm.cu``).  CUDA tensors only; there is no CPU implementation.
 """
 from __future__ import annotations
 
@@ -24,6 +27,7 @@ import ctypes
 import torch
 
 from . import _lib
+from . import ops as _ops
 from .ops import _check, _DTYPES
 
 _LIBDEF = torch.library.Library("recir", "FRAGMENT")
@@ -35,7 +39,13 @@ _LIBDEF.define(
     "float dropout_ratio, bool training, bool silu_u, bool concat_u, bool concat_x, str mul_u_activation_type, "
     "int seed, bool save_y, int BLOCK_D) -> (Tensor, Tensor, Tensor, Tensor, Tensor)")
 
+_LIBDEF.define(
+    "b200_weighted_layer_norm_bwd(Tensor dy, Tensor x, Tensor? weight, Tensor? bias, Tensor mean, Tensor rstd, "
+    "bool is_swish=False) -> (Tensor, Tensor, Tensor)")
 _LIBDEF.define("b200_addmm_fwd(Tensor x, Tensor w, Tensor y) -> Tensor")
+_LIBDEF.define(
+    "b200_layer_norm_addmm_fwd(Tensor x, Tensor? ln_weight, Tensor? ln_bias, float eps, bool is_swish, Tensor w, "
+    "Tensor bias) -> (Tensor, Tensor, Tensor)")
 _LIBDEF.define(
     "b200_fp8_rowwise_addmm_fwd(Tensor a, Tensor b, Tensor a_scale, Tensor b_scale, Tensor bias, bool has_bias, "
     "bool bias_is_2d, ScalarType dot_out_dtype, bool allow_tf32, bool use_fast_accum) -> Tensor")
@@ -192,23 +202,176 @@ def _layer_norm_quant_fake(x, weight, bias, eps, mean, rstd, BLOCK_D):
 
 _LIBDEF.impl("b200_weighted_layer_norm_quantization_fwd", _layer_norm_quant_cuda, "CUDA")
 torch.library.register_fake("recir::b200_weighted_layer_norm_quantization_fwd", _layer_norm_quant_fake)
+def _layer_norm_bwd_cuda(dy, x, weight, bias, mean, rstd, is_swish=False):
+    """Gradients of ``b200_weighted_layer_norm_fwd`` (statistics computed from ``x``) with respect to x, weight
+    and bias: the closed form of what autograd gives through the reference's composite
+    (``recir/ops/kjt_split_per_feature.cpp:197-244``).  Returns ``(dx, dweight, dbias)``; the last two are empty
+    tensors when there is no weight.  Feature dimension: a multiple of 8, at most 1024."""
+    global launch_counter
+    _validate(x, weight, bias)
+    if dy.shape != x.shape or dy.dtype != x.dtype:
+        raise ValueError("dy must have the shape and dtype of x")
+    if is_swish and weight is None:
+        raise ValueError("is_swish requires learnable layer normalization")
+    if mean.numel() != x.shape[0] or rstd.numel() != x.shape[0]:
+        raise ValueError("mean and rstd must match the row count")
+    if x.shape[1] > 1024:
+        raise ValueError("the layer-norm backward serves feature dimensions up to 1024")
+    x, dy = _rows2d(x), _rows2d(dy)
+    dx = torch.empty_like(x, memory_format=torch.contiguous_format)
+    cols = x.shape[1]
+    dw = torch.empty(cols if weight is not None else 0, dtype=x.dtype, device=x.device)
+    db = torch.empty_like(dw)
+    lib = _lib.load()
+    p = _lib.B200LayerNormBwdParams()
+    p.struct_size = ctypes.sizeof(p)
+    p.flags = _lib.ROWWISE_SWISH if is_swish else 0
+    p.dtype = _DTYPES[x.dtype]
+    p.rows, p.cols = x.shape
+    p.dy, p.x, p.dx = dy.data_ptr(), x.data_ptr(), dx.data_ptr()
+    p.dy_row_stride, p.x_row_stride, p.dx_row_stride = dy.stride(0), x.stride(0), dx.stride(0)
+    keep = [mean.to(torch.float32).contiguous(), rstd.to(torch.float32).contiguous()]
+    p.mean, p.rstd = keep[0].data_ptr(), keep[1].data_ptr()
+    if weight is not None:
+        w, b = weight.to(x.dtype).contiguous(), bias.to(x.dtype).contiguous()
+        keep += [w, b]
+        p.weight, p.bias, p.dweight, p.dbias = w.data_ptr(), b.data_ptr(), dw.data_ptr(), db.data_ptr()
+        need = lib.b200_stu_layer_norm_bwd_workspace_bytes(x.shape[0], cols)
+        if need:
+            ws = torch.empty(need // 4, dtype=torch.float32, device=x.device)
+            keep.append(ws)
+            p.workspace, p.workspace_bytes = ws.data_ptr(), need
+    with torch.cuda.device(x.device):
+        rc = lib.b200_stu_layer_norm_bwd(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    _check(rc, "b200_stu_layer_norm_bwd")
+    launch_counter += 2 if (weight is not None and x.shape[0] > 0) else 1
+    del keep
+    return dx, dw, db
+
+
+def _layer_norm_bwd_fake(dy, x, weight, bias, mean, rstd, is_swish=False):
+    n = x.shape[1] if weight is not None else 0
+    return torch.empty_like(x), x.new_empty((n,)), x.new_empty((n,))
+
+
+def _layer_norm_setup_context(ctx, inputs, output) -> None:
+    x, weight, bias, eps, mean_in, rstd_in, is_swish = inputs
+    _y, mean, rstd = output
+    ctx.save_for_backward(x, weight, bias, mean, rstd)
+    ctx.is_swish = is_swish
+    ctx.stats_given = mean_in is not None and rstd_in is not None
+
+
+def _layer_norm_backward(ctx, dy, _dmean, _drstd):
+    x, weight, bias, mean, rstd = ctx.saved_tensors
+    if ctx.stats_given:
+        raise RuntimeError("b200_weighted_layer_norm_fwd: backward with caller-provided statistics is not built")
+    dx, dw, db = torch.ops.recir.b200_weighted_layer_norm_bwd(dy.contiguous(), x, weight, bias, mean, rstd, ctx.is_swish)
+    has_w = weight is not None
+    return dx, (dw if has_w else None), (db if has_w else None), None, None, None, None
+
+
 _LIBDEF.impl("b200_weighted_layer_norm_fwd", _layer_norm_cuda, "CUDA")
+_LIBDEF.impl("b200_weighted_layer_norm_bwd", _layer_norm_bwd_cuda, "CUDA")
+torch.library.register_fake("recir::b200_weighted_layer_norm_bwd", _layer_norm_bwd_fake)
+torch.library.register_autograd("recir::b200_weighted_layer_norm_fwd", _layer_norm_backward,
+                                setup_context=_layer_norm_setup_context)
 _LIBDEF.impl("b200_layer_norm_mul_dropout_quantization_fwd", _layer_norm_mul_cuda, "CUDA")
 torch.library.register_fake("recir::b200_weighted_layer_norm_fwd", _layer_norm_fake)
 torch.library.register_fake("recir::b200_layer_norm_mul_dropout_quantization_fwd", _layer_norm_mul_fake)
 
 
+def _gemm_params(x, w, bias, out):
+    p = _lib.B200GemmParams()
+    p.struct_size = ctypes.sizeof(p)
+    p.dtype = _DTYPES.get(x.dtype, -1)
+    p.M, p.K, p.N = x.shape[0], x.shape[1], w.shape[1]
+    p.x, p.w, p.bias, p.out = x.data_ptr(), w.data_ptr(), bias.data_ptr(), out.data_ptr()
+    p.x_row_stride, p.w_row_stride, p.out_row_stride = x.stride(0), w.stride(0), out.stride(0)
+    p.bias_row_stride = bias.stride(0) if (bias.dim() == 2 and bias.shape[0] != 1) else 0
+    return p
+
+
+def _tc_gemm_serves(x, w) -> bool:
+    """bfloat16 / float16, K a multiple of 64 up to 512, N a multiple of 8: the sizes of an STU layer's
+    projections (embedding width 512 into u | v | q | k, and back)."""
+    return (x.dtype in (torch.bfloat16, torch.float16) and w.dtype == x.dtype and x.shape[0] > 0
+            and x.shape[1] % 64 == 0 and 0 < x.shape[1] <= 512 and w.shape[1] % 8 == 0 and w.shape[1] > 0)
+
+
 def _addmm_cuda(x, w, y):
-    """The u/v/q/k and output projections of an STU layer: ``y + x @ w``.  A plain GEMM, handed to the
-    vendor library (``generative_recommenders::triton_addmm_fwd``,
-    ``recir/ops/kjt_split_per_feature.cpp:246-262``, does the same with ``at::addmm``)."""
+    """The u/v/q/k and output projections of an STU layer: ``y + x @ w``
+    (``generative_recommenders::triton_addmm_fwd``, ``recir/ops/kjt_split_per_feature.cpp:246-262``:
+    ``at::addmm(bias, x, w)``).  The 16-bit shapes of an STU layer (see ``_tc_gemm_serves``) run on this
+    library's tcgen05 kernel (``csrc/stu_gemm.cu``); any other dtype or size is a plain GEMM handed to
+    the vendor library."""
+    global launch_counter
     if x.dim() != 2 or w.dim() != 2:
         raise ValueError("x and weight must be two-dimensional")
     if x.shape[1] != w.shape[0]:
         raise ValueError("x and weight dimensions are incompatible")
     if not ((y.dim() == 1 and y.shape[0] == w.shape[1]) or (y.dim() == 2 and y.shape[1] == w.shape[1])):
         raise ValueError("bias dimensions are incompatible with the output")
-    return torch.addmm(y, x, w)
+    if not _tc_gemm_serves(x, w) or y.dtype != x.dtype or (y.dim() == 2 and y.shape[0] not in (1, x.shape[0])):
+        return torch.addmm(y, x, w)
+    x, w, y = _rows2d(x), _rows2d(w), (y if y.dim() == 1 else _rows2d(y))
+    if y.data_ptr() % 16 != 0:
+        y = y.clone()
+    out = torch.empty((x.shape[0], w.shape[1]), dtype=x.dtype, device=x.device)
+    p = _gemm_params(x, w, y, out)
+    p.status = _ops.status_tensor(x.device).data_ptr()
+    with torch.cuda.device(x.device):
+        rc = _lib.load().b200_stu_addmm(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    _check(rc, "b200_stu_addmm")
+    launch_counter += 1
+    return out
+
+
+def _layer_norm_addmm_cuda(x, ln_weight, ln_bias, eps, is_swish, w, bias):
+    """``addmm(bias, weighted_layer_norm(x, ln_weight, ln_bias, eps, is_swish)[0], w)`` in one kernel: the
+    layer norm is the prologue of the product's A operand, so the normalised activations never travel
+    through HBM (``recir/ops/kjt_split_per_feature.cpp:197-262``).  Returns ``(out, mean, rstd)``; ``out``
+    is ``[rows, N]`` and can be consumed as column slices (u | v | q | k) without a copy."""
+    global launch_counter
+    _validate(x, ln_weight, ln_bias)
+    if is_swish and ln_weight is None:
+        raise ValueError("is_swish requires learnable layer normalization")
+    if w.dim() != 2 or x.shape[1] != w.shape[0]:
+        raise ValueError("x and weight dimensions are incompatible")
+    if not ((bias.dim() == 1 and bias.shape[0] == w.shape[1]) or (bias.dim() == 2 and bias.shape[1] == w.shape[1])):
+        raise ValueError("bias dimensions are incompatible with the output")
+    if not _tc_gemm_serves(x, w) or bias.dtype != x.dtype:
+        raise ValueError("b200_layer_norm_addmm_fwd serves bfloat16 / float16 with a feature dimension that is a multiple "
+                         "of 64 and at most 512, and an output width that is a multiple of 8")
+    x, w = _rows2d(x), _rows2d(w)
+    bias = bias if bias.dim() == 1 else _rows2d(bias)
+    if bias.data_ptr() % 16 != 0:
+        bias = bias.clone()
+    out = torch.empty((x.shape[0], w.shape[1]), dtype=x.dtype, device=x.device)
+    mean = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+    rstd = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+    p = _gemm_params(x, w, bias, out)
+    p.flags = _lib.GEMM_LAYER_NORM | (_lib.GEMM_SWISH if is_swish else 0)
+    p.eps = float(eps)
+    keep = []
+    if ln_weight is not None:
+        lw, lb = ln_weight.to(x.dtype).contiguous(), ln_bias.to(x.dtype).contiguous()
+        keep += [lw, lb]
+        p.ln_weight, p.ln_bias = lw.data_ptr(), lb.data_ptr()
+    p.mean, p.rstd = mean.data_ptr(), rstd.data_ptr()
+    p.status = _ops.status_tensor(x.device).data_ptr()
+    with torch.cuda.device(x.device):
+        rc = _lib.load().b200_stu_addmm(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    _check(rc, "b200_stu_addmm")
+    launch_counter += 1
+    del keep
+    return out, mean, rstd
+
+
+def _layer_norm_addmm_fake(x, ln_weight, ln_bias, eps, is_swish, w, bias):
+    rows = x.shape[0]
+    return (x.new_empty((rows, w.shape[1])), x.new_empty((rows,), dtype=torch.float32),
+            x.new_empty((rows,), dtype=torch.float32))
 
 
 def _addmm_fake(x, w, y):
@@ -217,6 +380,8 @@ def _addmm_fake(x, w, y):
 
 _LIBDEF.impl("b200_addmm_fwd", _addmm_cuda, "CUDA")
 torch.library.register_fake("recir::b200_addmm_fwd", _addmm_fake)
+_LIBDEF.impl("b200_layer_norm_addmm_fwd", _layer_norm_addmm_cuda, "CUDA")
+torch.library.register_fake("recir::b200_layer_norm_addmm_fwd", _layer_norm_addmm_fake)
 
 
 def _fp8_rowwise_addmm_cuda(a, b, a_scale, b_scale, bias, has_bias, bias_is_2d, dot_out_dtype, allow_tf32,

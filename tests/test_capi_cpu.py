@@ -17,7 +17,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def _header_functions():
     """Every function declared in include/*.h."""
     names = set()
-    for header in ("b200_hstu.h", "b200_stu_rowwise.h", "b200_stu_jagged.h", "b200_stu_embed.h"):
+    for header in sorted(f for f in os.listdir(os.path.join(ROOT, "include")) if f.endswith(".h")):
         text = open(os.path.join(ROOT, "include", header)).read()
         text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
         names |= set(re.findall(r"\b(b200_(?:hstu|stu)_[a-z0-9_]+)\s*\(", text))

@@ -1,0 +1,119 @@
+"""The STU layer's projections on the tensor cores (``csrc/stu_gemm.cu``) against the oracle chain
+``weighted_layer_norm`` -> ``addmm`` (``oracle/rowwise_oracle.py``, pinned against the reference's compiled
+operators by ``tests/test_rowwise_oracle.py``).  Every call goes through the torch operators, i.e. through the
+C ABI of ``include/b200_stu_gemm.h``.
+
+Tolerance: the kernel sums 16-bit products in float32 in tensor-core order and rounds once, the oracle sums
+in float64 and rounds once, so results may differ by one unit in the last place of the element type where
+the exact value sits next to a rounding boundary: at most 1 ulp (relative to the larger of |value| and 1 %
+of the largest output) on every element, and more than half an ulp on at most 2 % of them."""
+import numpy as np
+import pytest
+import torch
+
+import recir_b200  # noqa: F401  (registers the operators)
+from oracle import rowwise_oracle as ro
+
+pytestmark = pytest.mark.gpu
+ULP = {"bfloat16": 2.0 ** -8, "float16": 2.0 ** -11}
+DT = {"bfloat16": torch.bfloat16, "float16": torch.float16}
+
+
+def _close(got, want, dtype, what, floor=1e-2):
+    got = got.float().cpu().numpy().astype(np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    assert got.shape == want.shape, what
+    assert np.isfinite(got).all(), what
+    scale = np.maximum(np.abs(want), float(np.abs(want).max()) * floor)
+    err = np.abs(got - want) / scale
+    assert err.max() <= 1.01 * 2 * ULP[dtype], (what, float(err.max()))
+    assert (err > 0.51 * 2 * ULP[dtype]).mean() <= 0.02, (what, float((err > ULP[dtype]).mean()))
+
+
+def _inputs(seed, M, K, N, dtype, bias_2d=False):
+    g = torch.Generator().manual_seed(seed)
+    t = DT[dtype]
+    x = (torch.randn(M, K, generator=g) * 1.5 + 0.3).to(t)
+    w = (torch.randn(K, N, generator=g) / K ** 0.5).to(t)
+    b = (torch.randn((M, N) if bias_2d else (N,), generator=g) * 0.5).to(t)
+    lw = (torch.randn(K, generator=g) * 0.5 + 1.0).to(t)
+    lb = (torch.randn(K, generator=g) * 0.2).to(t)
+    return x, w, b, lw, lb
+
+
+F = lambda t: t.float().numpy()
+
+SHAPES = [(300, 64, 96), (128, 512, 256), (1, 128, 8), (777, 512, 2048), (129, 320, 520), (4100, 256, 264)]
+
+
+@pytest.mark.parametrize("M,K,N", SHAPES)
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+def test_addmm_on_tensor_cores_matches_oracle(M, K, N, dtype):
+    for bias_2d in (False, True):
+        x, w, b, _, _ = _inputs(M + K + N, M, K, N, dtype, bias_2d)
+        got = torch.ops.recir.b200_addmm_fwd(x.cuda(), w.cuda(), b.cuda())
+        assert got.dtype == DT[dtype]
+        _close(got, ro.addmm(F(x), F(w), F(b), dtype), dtype, f"addmm bias_2d={bias_2d}")
+
+
+@pytest.mark.parametrize("M,K,N", SHAPES)
+@pytest.mark.parametrize("variant", ["plain", "affine", "swish"])
+def test_layer_norm_addmm_fused_matches_oracle_chain(M, K, N, variant):
+    dtype = "bfloat16"
+    x, w, b, lw, lb = _inputs(7 * M + K, M, K, N, dtype)
+    affine, swish = variant != "plain", variant == "swish"
+    out, mean, rstd = torch.ops.recir.b200_layer_norm_addmm_fwd(
+        x.cuda(), lw.cuda() if affine else None, lb.cuda() if affine else None, 1e-5, swish, w.cuda(), b.cuda())
+    want, rmean, rrstd = ro.layer_norm_addmm(F(x), F(lw) if affine else None, F(lb) if affine else None, 1e-5, F(w), F(b),
+                                             dtype, is_swish=swish)
+    assert np.abs(mean.cpu().numpy() - rmean).max() <= 2e-6 * max(1.0, float(np.abs(rmean).max()))
+    assert np.abs(rstd.cpu().numpy() / rrstd - 1).max() <= 1e-5
+    # The A operand is the layer norm ROUNDED to bf16 (as in the reference).  The kernel's float32 statistics
+    # differ from the oracle's in the last bits (summation order), which flips the rounding of a normalised
+    # value here and there; one flip moves every output of that row by about |w| * ulp(a) ~ 2e-4 of the output
+    # range, which is visible on outputs near zero.  So against the oracle chain the error is measured
+    # relative to max(|value|, 5 % of the largest output) ...
+    _close(out, want, dtype, f"layer_norm_addmm {variant}", floor=5e-2)
+    # ... and the product itself is checked strictly on the layer norm this library computes: the fused
+    # kernel against the oracle's addmm of the separate layer-norm kernel's (bit-identical) output
+    y = torch.ops.recir.b200_weighted_layer_norm_fwd(x.cuda(), lw.cuda() if affine else None, lb.cuda() if affine else None,
+                                                     1e-5, None, None, swish)[0]
+    _close(out, ro.addmm(F(y.cpu()), F(w), F(b), dtype), dtype, f"layer_norm_addmm {variant} on this library's rows")
+
+
+def test_projection_output_feeds_attention_as_column_slices():
+    """u | v | q | k come out of one fused call as one [T, 4*H*D] matrix; the attention operator consumes the
+    q, k, v column slices in place (row stride 4*H*D), no copy in between."""
+    import recir_b200
+
+    T, H, D, E = 300, 2, 128, 512
+    g = torch.Generator().manual_seed(3)
+    x = (torch.randn(T, E, generator=g)).to(torch.bfloat16).cuda()
+    w = (torch.randn(E, 4 * H * D, generator=g) / E ** 0.5).to(torch.bfloat16).cuda()
+    b = torch.zeros(4 * H * D, dtype=torch.bfloat16).cuda()
+    lw, lb = torch.ones(E, dtype=torch.bfloat16).cuda(), torch.zeros(E, dtype=torch.bfloat16).cuda()
+    uvqk, _, _ = torch.ops.recir.b200_layer_norm_addmm_fwd(x, lw, lb, 1e-5, False, w, b)
+    hd = H * D
+    v, q, k = (uvqk[:, i * hd:(i + 1) * hd].view(T, H, D) for i in (1, 2, 3))
+    off = torch.tensor([0, 170, 300], device="cuda")
+    a = recir_b200.hstu_attention(q, k, v, off, 200)
+    c = recir_b200.hstu_attention(q.contiguous(), k.contiguous(), v.contiguous(), off, 200)
+    assert torch.equal(a, c) and float(a.float().abs().max()) > 0
+
+
+def test_unsupported_shapes_and_validation():
+    x = torch.zeros(8, 48, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(48, 16, dtype=torch.bfloat16, device="cuda")
+    b = torch.zeros(16, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError, match="multiple of 64"):
+        torch.ops.recir.b200_layer_norm_addmm_fwd(x, None, None, 1e-5, False, w, b)
+    with pytest.raises(ValueError, match="is_swish requires"):
+        torch.ops.recir.b200_layer_norm_addmm_fwd(x, None, None, 1e-5, True, w, b)
+    with pytest.raises(ValueError, match="incompatible"):
+        torch.ops.recir.b200_layer_norm_addmm_fwd(x, None, None, 1e-5, False, w[:32], b)
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    with FakeTensorMode():
+        xf = torch.empty(6, 64, dtype=torch.bfloat16, device="cuda")
+        wf = torch.empty(64, 32, dtype=torch.bfloat16, device="cuda")
+        out = torch.ops.recir.b200_layer_norm_addmm_fwd(xf, None, None, 1e-5, False, wf, wf[0])
+    assert out[0].shape == (6, 32) and out[1].shape == (6,) and out[1].dtype == torch.float32
