@@ -6,6 +6,7 @@ the two library sorts of the embedding operator).
     python bench.py --case attn --config cfg4 --buckets --calls 10
     python bench.py --case rowwise --rows 1650165 --cols 512
     python bench.py --case jagged --batch 1024
+    python bench.py --case gemm --rows 1650165 --k 512 --n 2048
 
 ``attn``: one benchmark configuration of the HSTU attention -- cfg0 (smoke shape, fp32), cfg1 (B=64, H=4,
 D=128 bf16), cfg3 (long skewed sequences, sliding window + contextual flag), cfg4 (one layer of the Zipf
@@ -15,6 +16,7 @@ tokens so that its tensors exceed the L2, and reports useful TFLOP/s and algorit
 sequences sit on the HBM roofline, long ones on the tensor-core roofline.
 ``rowwise``: the row-wise STU kernels (layer norm, gate stage, fp8 copy), HBM throughput.
 ``jagged``: the jagged marshalling kernels and the embedding add, HBM throughput, on the Zipf lengths.
+``gemm``: the fused layer-norm + u/v/q/k projection against the two-kernel chain and the vendor GEMM.
 """
 from __future__ import annotations
 
@@ -274,7 +276,45 @@ def main_jagged(argv):
     print(json.dumps(out))
 
 
-CASES = {"attn": main_attn, "rowwise": main_rowwise, "jagged": main_jagged}
+def main_gemm(argv):
+    """The u | v | q | k projection of an STU layer (embedding width K into N = 4 * H * D columns) on the token
+    count of the Zipf batch: the fused layer-norm + projection kernel against the two-kernel chain (this
+    library's layer norm, then the vendor library's GEMM), and the projection alone against the vendor
+    library.  Useful work: 2 * rows * K * N flops; algorithmic bytes of the fused form: x read, out written,
+    W read once (it stays in L2)."""
+    ap = argparse.ArgumentParser(prog="bench.py --case gemm")
+    ap.add_argument("--rows", type=int, default=1650165)
+    ap.add_argument("--k", type=int, default=512)
+    ap.add_argument("--n", type=int, default=2048)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    args = ap.parse_args(argv)
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(0)
+    M, K, N = args.rows, args.k, args.n
+    x = (torch.randn(M, K, generator=g, device=dev) * 1.5).to(torch.bfloat16)
+    w = (torch.randn(K, N, generator=g, device=dev) / K ** 0.5).to(torch.bfloat16)
+    b = torch.randn(N, generator=g, device=dev).to(torch.bfloat16)
+    lw = torch.ones(K, dtype=torch.bfloat16, device=dev)
+    lb = torch.zeros(K, dtype=torch.bfloat16, device=dev)
+    R = torch.ops.recir
+    y = R.b200_weighted_layer_norm_fwd(x, lw, lb, 1e-5, None, None, False)[0]
+    flops = 2.0 * M * K * N
+    cases = {
+        "fused layer_norm + addmm (this library, one kernel)": lambda: R.b200_layer_norm_addmm_fwd(x, lw, lb, 1e-5, False, w, b),
+        "layer_norm kernel, then vendor GEMM": lambda: torch.addmm(b, R.b200_weighted_layer_norm_fwd(x, lw, lb, 1e-5, None, None, False)[0], w),
+        "addmm (this library)": lambda: R.b200_addmm_fwd(y, w, b),
+        "addmm (vendor GEMM)": lambda: torch.addmm(b, y, w),
+    }
+    out = {"rows": M, "K": K, "N": N, "dtype": "bf16", "useful_flops": flops,
+           "algorithmic_bytes_fused": (M * K + M * N + K * N) * 2}
+    for name, fn in cases.items():
+        ms = _timed(fn, args.iters, args.warmup)
+        out[name] = {"ms": ms, "TFLOP/s": flops / ms / 1e9, "GB/s": out["algorithmic_bytes_fused"] / ms / 1e6}
+    print(json.dumps(out))
+
+
+CASES = {"attn": main_attn, "rowwise": main_rowwise, "jagged": main_jagged, "gemm": main_gemm}
 
 
 def main(argv=None):

