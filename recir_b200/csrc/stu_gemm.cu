@@ -16,14 +16,15 @@
 // a few MB) stays in L2; per 128 rows a CTA ingests it once, which is what bounds the kernel (shared
 // memory ingest per SM), not the tensor pipe.
 //
-// Warp roles (384 threads): warp 0 = TMA producer, warp 1 = MMA issuer (one elected lane), warps 4-11 =
+// Warp roles (320 threads): warp 0 = TMA producer, warp 1 = MMA issuer (one elected lane), warps 2-9 =
 // layer-norm prologue (16 rows per warp, four at a time in registers) and epilogue (TMEM lane quadrant
-// warp % 4, column half (warp - 4) / 4).  Every wait is bounded (see sm100_ptx.cuh).
+// warp % 4, column half (warp - 2) / 4).  Every wait is bounded (see sm100_ptx.cuh).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdio.h>
 #include <stdlib.h>
 
 #include <type_traits>
@@ -48,7 +49,7 @@ constexpr int A_BOX_BYTES = BM * 128;        // 128 rows x 64 k-columns of 16-bi
 constexpr int B_BOX_BYTES = BK * 128;        // 32 k-rows x 64 n-columns
 constexpr int B_STAGE_BYTES = 4 * B_BOX_BYTES;
 constexpr int OUT_BOX_BYTES = BM * 128;      // staging of 128 rows x 64 output columns, one per epilogue group
-constexpr int THREADS = 384;
+constexpr int THREADS = 320;  // 10 warps: 200 registers each without any reallocation
 constexpr int TMEM_COLS = 512;
 enum { WAIT_GEMM_PRODUCER = 111, WAIT_GEMM_MMA = 112, WAIT_GEMM_EPILOGUE = 113 };
 
@@ -112,7 +113,6 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
-  if (warp < 4) setmaxnreg_dec<96>(); else setmaxnreg_inc<200>();
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -224,15 +224,27 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
       if (elect_one()) tc_commit(smem_u32(&sh.a_empty));  // every MMA that reads this block's A has been issued
       __syncwarp();
     }
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------------ prologue + epilogue warps
-    const int ew = warp - 4;                  // 0..7
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------------ prologue + epilogue warps (2..9)
+    const int ew = warp - 2;                  // 0..7
     const int wg = ew >> 2;                   // column half of the output tile
     const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) << 5) << 16;
     const int row_in_blk = ((warp & 3) << 5) | lane;
     const int nv = a.K >> 3;  // 16-byte vectors per row (at most 64: two per lane)
     uint32_t it = 0, g = 0;
     bool ok = true;
+    // layer-norm weight and bias of this lane's columns, packed (16 registers) for the whole kernel: loaded per
+    // use they would come from L2 each time (no L1 to speak of beside 224 KB of shared memory)
+    uint4 lnw[2], lnb[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int v = lane + 32 * j;
+      lnw[j] = lnb[j] = make_uint4(0u, 0u, 0u, 0u);
+      if (a.fuse_ln && a.affine && v < nv) {
+        lnw[j] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.ln_w) + 8 * v));
+        lnb[j] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.ln_b) + 8 * v));
+      }
+    }
     for (long long blk = blockIdx.x; blk < n_blocks && ok; blk += gridDim.x, ++it) {
       if (a.fuse_ln) {
         // ---- layer norm of 16 rows per warp, four rows at a time, into the swizzled A operand
@@ -283,11 +295,9 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
               if (v >= nv) continue;
               uint4 pk = make_uint4(0u, 0u, 0u, 0u);  // rows past M enter the product as zeros
               if (row < a.M) {
-                float n[8], wv[8], bv[8];  // weight and bias of these 8 columns (L1-resident after the first row)
-                if (a.affine) {
-                  load8<T>(reinterpret_cast<const T*>(a.ln_w) + 8 * v, wv);
-                  load8<T>(reinterpret_cast<const T*>(a.ln_b) + 8 * v, bv);
-                }
+                float n[8], wv[8], bv[8];
+                vec::unpack8<T>(lnw[j], wv);
+                vec::unpack8<T>(lnb[j], bv);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                   float y = (xv[r][j][i] - mean) * rstd;
@@ -312,7 +322,7 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
         // the next prologue's loads (four dependent batches of four rows per warp) pay L2 instead of HBM latency
         const long long nblk = blk + gridDim.x;
         if (nblk < n_blocks) {
-          const int tid = threadIdx.x - 128;  // 0..255: two threads per row, alternating 128-byte lines
+          const int tid = threadIdx.x - 64;  // 0..255: two threads per row, alternating 128-byte lines
           const long long prow = nblk * BM + (tid >> 1);
           if (prow < a.M) {
             const char* base = reinterpret_cast<const char*>(a.x) + prow * a.x_rs * static_cast<long long>(sizeof(T));
@@ -338,6 +348,16 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int col0 = nt * BN + wg * 128 + h * 64;
+          // The bias of this box first (eight 16-byte loads in flight together, raw): with nearly all of the
+          // SM's L1 carved out as shared memory they come from L2, and one dependent load per use costs more
+          // than the rest of the box.
+          uint4 braw[8];
+          {
+            const T* brow = reinterpret_cast<const T*>(a.bias) + brow_idx * a.bias_rs + col0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              braw[j] = (col0 + 8 * j < a.N) ? __ldg(reinterpret_cast<const uint4*>(brow + 8 * j)) : make_uint4(0u, 0u, 0u, 0u);
+          }
           uint32_t v0[32], v1[32];
           tmem_ld32(acc + h * 64, v0);
           tmem_ld32(acc + h * 64 + 32, v1);
@@ -351,18 +371,23 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
 #ifdef B200_HSTU_PROFILING
           if (a.dbg & 2) continue;
 #endif
+#ifdef B200_HSTU_PROFILING
+          long long tq0 = 0, tq1 = 0, tq2 = 0, tq3 = 0, tq4 = 0;
+          const bool tr = (a.dbg & 32) && blockIdx.x == 0 && threadIdx.x == 64 && g < 12;
+          if (tr) tq0 = clock64();
+#endif
           if (row_in_blk == 0) bulk_wait_read_all();  // the group's previous box has left the staging buffer
           asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
-          const T* brow = reinterpret_cast<const T*>(a.bias) + brow_idx * a.bias_rs + col0;
+#ifdef B200_HSTU_PROFILING
+          if (tr) tq1 = clock64();
+#endif
           unsigned char* my_row = stage + row_in_blk * 128;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const uint32_t* v = j < 4 ? v0 : v1;
             const int jj = j & 3;
             float bf[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) bf[i] = 0.f;
-            if (col0 + 8 * j < a.N) load8<T>(brow + 8 * j, bf);  // N is a multiple of 8
+            vec::unpack8<T>(braw[j], bf);
             uint4 o;
             o.x = pack2<BF16>(__uint_as_float(v[8 * jj + 0]) + bf[0], __uint_as_float(v[8 * jj + 1]) + bf[1]);
             o.y = pack2<BF16>(__uint_as_float(v[8 * jj + 2]) + bf[2], __uint_as_float(v[8 * jj + 3]) + bf[3]);
@@ -370,12 +395,25 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
             o.w = pack2<BF16>(__uint_as_float(v[8 * jj + 6]) + bf[6], __uint_as_float(v[8 * jj + 7]) + bf[7]);
             *reinterpret_cast<uint4*>(my_row + ((j ^ (row_in_blk & 7)) << 4)) = o;
           }
+#ifdef B200_HSTU_PROFILING
+          if (tr) tq2 = clock64();
+#endif
           fence_proxy_async();
+#ifdef B200_HSTU_PROFILING
+          if (tr) tq3 = clock64();
+#endif
           asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");  // the box is staged
           if (row_in_blk == 0) {
             tma_store_2d(&maps.o, smem_u32(stage), col0, static_cast<int>(blk * BM));
             bulk_commit();
           }
+#ifdef B200_HSTU_PROFILING
+          if (tr) {
+            tq4 = clock64();
+            printf("box g=%u h=%d: wait_read+bar %lld, bias+math+st.shared %lld, fence %lld, bar+tma %lld | t=%lld\n", g, h,
+                   tq1 - tq0, tq2 - tq1, tq3 - tq2, tq4 - tq3, tq4);
+          }
+#endif
         }
       }
     }
