@@ -54,6 +54,23 @@ typedef struct B200GemmParams {
 int b200_stu_addmm_supported(const B200GemmParams* p);
 int b200_stu_addmm(const B200GemmParams* p, void* stream);
 
+/* Per-sequence projection of jagged rows: out[rows of b] = bias_b + x[rows of b] * w[b], where sequence b owns
+ * rows [seq_offsets[b], seq_offsets[b + 1]) of x and w is a stack of num_seqs matrices [K, N].
+ * Reference: jaggedDenseBmmAdd, recir/ops/kjt_split_per_feature.cpp:262-305 (a loop of at::addmm over the
+ * sequences; schema generative_recommenders::triton_jagged_dense_bmm_add_fwd).  p describes x [M, K], out
+ * [M, N] and the sizes as for b200_stu_addmm, with p->flags == 0, p->w = the first matrix and
+ * w_seq_stride = K * w_row_stride (densely stacked matrices); the bias is one row per sequence
+ * (per_row_bias == 0: bias [num_seqs, N], bias_row_stride its row stride) or one row per output row
+ * (per_row_bias != 0: bias [M, N]).  The same tcgen05 kernel as b200_stu_addmm runs over a list of
+ * (sequence, 128-row block) items that a small kernel builds on the device from the offsets (no host read);
+ * workspace: b200_stu_jagged_bmm_workspace_bytes(M, num_seqs) bytes, 16-byte aligned, caller-owned.  Rows at
+ * or past seq_offsets[num_seqs] are written as zeros.  Malformed offsets are clamped into [0, M] and flagged in
+ * status[0] bit 0 like in b200_hstu.h. */
+size_t b200_stu_jagged_bmm_workspace_bytes(int64_t rows, int64_t num_seqs);
+int b200_stu_jagged_dense_bmm_add(const B200GemmParams* p, const void* seq_offsets, int offsets_i64, int64_t num_seqs,
+                                  int64_t w_seq_stride, int per_row_bias, void* workspace, uint64_t workspace_bytes,
+                                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif

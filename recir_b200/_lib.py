@@ -30,7 +30,7 @@ EXPORTS = (
     "b200_stu_layer_norm_fwd", "b200_stu_layer_norm_mul_fwd", "b200_stu_layer_norm_mul_parts",
     "b200_stu_layer_norm_bwd", "b200_stu_layer_norm_bwd_workspace_bytes",
     # include/b200_stu_gemm.h
-    "b200_stu_addmm", "b200_stu_addmm_supported",
+    "b200_stu_addmm", "b200_stu_addmm_supported", "b200_stu_jagged_dense_bmm_add", "b200_stu_jagged_bmm_workspace_bytes",
     # include/b200_stu_jagged.h
     "b200_stu_jagged_copy",
     # include/b200_stu_embed.h
@@ -233,6 +233,11 @@ def load() -> ctypes.CDLL:
     lib.b200_stu_addmm.restype = ctypes.c_int
     lib.b200_stu_addmm_supported.argtypes = [GP]
     lib.b200_stu_addmm_supported.restype = ctypes.c_int
+    lib.b200_stu_jagged_bmm_workspace_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64]
+    lib.b200_stu_jagged_bmm_workspace_bytes.restype = ctypes.c_size_t
+    lib.b200_stu_jagged_dense_bmm_add.argtypes = [GP, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
+                                                  ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p]
+    lib.b200_stu_jagged_dense_bmm_add.restype = ctypes.c_int
     lib.b200_stu_add_ts_pos_emb.argtypes = [ctypes.POINTER(B200EmbedParams), ctypes.c_void_p]
     lib.b200_stu_add_ts_pos_emb.restype = ctypes.c_int
     lib.b200_stu_jagged_copy.argtypes = [ctypes.POINTER(B200JaggedParams), ctypes.c_void_p]

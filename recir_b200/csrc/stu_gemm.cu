@@ -76,6 +76,12 @@ struct Args {
   long long M, x_rs, out_rs, bias_rs;
   int K, N, fuse_ln, swish, affine;
   float eps;
+  // jagged mode (per-sequence weight matrices): the row blocks come from a device-built list
+  const int4* items;     // (sequence, first row, valid rows, 0) per 128-row block; null = plain row blocks of x
+  const int* n_items;    // number of list entries
+  const void* offsets;   // jagged mode: seq_offsets (to find the first row no sequence owns)
+  int off64, num_seqs;
+  int per_seq_bias;      // bias row = sequence index (else: output row index, or the single row when bias_rs == 0)
   int dbg;  // instrumented builds only (B200_GEMM_DBG): 1 no W loads / waits, 2 no output staging, 4 no MMAs, 8 N=128 MMAs
 };
 
@@ -94,7 +100,13 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
   const int kboxes = a.K / 64;   // 64-column boxes of the A operand
   const int kstages = a.K / BK;  // pipeline stages of W per output tile
   const int n_tiles = (a.N + BN - 1) / BN;
-  const long long n_blocks = (a.M + BM - 1) / BM;
+  const long long n_blocks = a.items ? static_cast<long long>(*a.n_items) : (a.M + BM - 1) / BM;
+  // block -> (sequence, first row, valid rows); plain mode: one "sequence" holding every row
+  auto block_of = [&](long long blk) -> int4 {
+    if (a.items) return a.items[blk];
+    const long long row0 = blk * BM, left = a.M - row0;
+    return make_int4(0, static_cast<int>(row0), static_cast<int>(left < BM ? left : BM), 0);
+  };
 
   if (threadIdx.x == 0) {
     sh.abort_flag = 0;
@@ -123,13 +135,15 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
       return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_GEMM_PRODUCER));
     };
     for (long long blk = blockIdx.x; blk < n_blocks && ok; blk += gridDim.x, ++it) {
+      const int4 bi = block_of(blk);
+      const int w_row0 = bi.x * a.K;  // first row of this sequence's matrix in the stacked [B * K, N] weights
       if (!a.fuse_ln) {
         ok = wait_all(&sh.a_empty, (it & 1) ^ 1);
         if (!ok) break;
         if (elect_one()) {
           mbar_arrive_expect_tx(smem_u32(&sh.a_full), static_cast<uint32_t>(kboxes) * A_BOX_BYTES);
           for (int kb = 0; kb < kboxes; ++kb)
-            tma_load_2d(smem_u32(sh.a[kb]), &maps.x, smem_u32(&sh.a_full), kb * 64, static_cast<int>(blk * BM));
+            tma_load_2d(smem_u32(sh.a[kb]), &maps.x, smem_u32(&sh.a_full), kb * 64, bi.y);
         }
         __syncwarp();
       }
@@ -144,7 +158,8 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
             mbar_arrive_expect_tx(smem_u32(&sh.b_full[st]), B_STAGE_BYTES);
 #pragma unroll
             for (int j = 0; j < 4; ++j)  // columns past N are filled with zeros
-              tma_load_2d(smem_u32(sh.b[st]) + j * B_BOX_BYTES, &maps.w, smem_u32(&sh.b_full[st]), nt * BN + j * 64, kb * BK);
+              tma_load_2d(smem_u32(sh.b[st]) + j * B_BOX_BYTES, &maps.w, smem_u32(&sh.b_full[st]), nt * BN + j * 64,
+                          w_row0 + kb * BK);
           }
           __syncwarp();
           if (++st == B_STAGES) { st = 0; ph ^= 1; }
@@ -233,6 +248,17 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
     const int nv = a.K >> 3;  // 16-byte vectors per row (at most 64: two per lane)
     uint32_t it = 0, g = 0;
     bool ok = true;
+    if (a.items) {
+      // rows at or past the last offset belong to no sequence: defined output (zeros), never stale memory
+      long long first = a.off64 ? reinterpret_cast<const long long*>(a.offsets)[a.num_seqs]
+                                : static_cast<long long>(reinterpret_cast<const int*>(a.offsets)[a.num_seqs]);
+      first = first < 0 ? 0 : (first > a.M ? a.M : first);
+      const long long chunks_per_row = a.N >> 3, total = (a.M - first) * chunks_per_row;
+      for (long long c = static_cast<long long>(blockIdx.x) * 256 + (threadIdx.x - 64); c < total; c += static_cast<long long>(gridDim.x) * 256) {
+        const long long r = first + c / chunks_per_row, col = (c % chunks_per_row) * 8;
+        *reinterpret_cast<uint4*>(reinterpret_cast<T*>(a.out) + r * a.out_rs + col) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
     // layer-norm weight and bias of this lane's columns, packed (16 registers) for the whole kernel: loaded per
     // use they would come from L2 each time (no L1 to speak of beside 224 KB of shared memory)
     uint4 lnw[2], lnb[2];
@@ -336,8 +362,9 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
       // 64 columns through its own staging buffer (128-byte-swizzled rows, as the bulk tensor store expects);
       // a thread-per-row store straight to global memory would be 32 separate 16-byte transactions per
       // instruction, which costs more than the MMAs of the tile.
-      const long long row = blk * BM + row_in_blk;
-      const long long brow_idx = row < a.M ? row : a.M - 1;
+      const int4 bi = block_of(blk);
+      const long long row = static_cast<long long>(bi.y) + row_in_blk;
+      const long long brow_idx = a.per_seq_bias ? bi.x : (row < a.M ? row : a.M - 1);
       unsigned char* stage = sh.out[wg];
       for (int nt = 0; nt < n_tiles && ok; ++nt, ++g) {
         const uint32_t buf = g & 1;
@@ -403,10 +430,27 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
           if (tr) tq3 = clock64();
 #endif
           asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");  // the box is staged
-          if (row_in_blk == 0) {
-            tma_store_2d(&maps.o, smem_u32(stage), col0, static_cast<int>(blk * BM));
-            bulk_commit();
-          }
+          if (bi.z >= BM || !a.items) {
+            // whole block (in plain mode the tensor map clips rows past M): one bulk tensor store
+            if (row_in_blk == 0) {
+              tma_store_2d(&maps.o, smem_u32(stage), col0, bi.y);
+              bulk_commit();
+            }
+          } else {
+            // ragged last block of a sequence: the rows behind it belong to the next sequence, so the valid
+            // rows are copied out by the threads (8 lanes per 128-byte row segment)
+            const int chunk = row_in_blk & 7;
+            if (col0 + chunk * 8 < a.N) {
+              T* obase = reinterpret_cast<T*>(a.out) + static_cast<long long>(bi.y) * a.out_rs + col0 + chunk * 8;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const int r = i * 16 + (row_in_blk >> 3);
+                if (r < bi.z)
+                  *reinterpret_cast<uint4*>(obase + static_cast<long long>(r) * a.out_rs) =
+                      *reinterpret_cast<const uint4*>(stage + r * 128 + ((chunk ^ (r & 7)) << 4));
+              }
+            }
+          }  // (the barrier at the top of the next box orders these reads before its writes)
 #ifdef B200_HSTU_PROFILING
           if (tr) {
             tq4 = clock64();
@@ -432,6 +476,54 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
   }
 }
 
+
+// Row blocks of a jagged batch: entry i = (sequence, first row, valid rows) for every 128-row block of
+// every sequence, in sequence order; ws[0] = number of entries.  One CTA; offsets are clamped into [0, T]
+// like everywhere else in this library, and the list is cut at its capacity (T / 128 + B entries cover
+// every batch whose sequences do not overlap).
+__global__ void __launch_bounds__(1024) build_gemm_items(const void* offsets, int off64, int B, long long T, int* ws,
+                                                         long long max_items, int* status) {
+  __shared__ int warp_tot[32];
+  __shared__ int carry;
+  int4* items = reinterpret_cast<int4*>(ws + 4);
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  auto off = [&](int i) -> long long {
+    long long v = off64 ? reinterpret_cast<const long long*>(offsets)[i] : static_cast<long long>(reinterpret_cast<const int*>(offsets)[i]);
+    return v < 0 ? 0 : (v > T ? T : v);
+  };
+  for (int base = 0; base < B; base += 1024) {
+    const int b = base + tid;
+    long long s = 0, e = 0;
+    if (b < B) { s = off(b); e = off(b + 1); if (e < s) e = s; }
+    const int nb = static_cast<int>((e - s + BM - 1) / BM);
+    int incl = nb;  // inclusive scan over the CTA
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) { const int t = __shfl_up_sync(0xffffffffu, incl, o); if (lane >= o) incl += t; }
+    if (lane == 31) warp_tot[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+      int t = warp_tot[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) { const int u = __shfl_up_sync(0xffffffffu, t, o); if (lane >= o) t += u; }
+      warp_tot[lane] = t;
+    }
+    __syncthreads();
+    const int first = carry + (wid > 0 ? warp_tot[wid - 1] : 0) + incl - nb;
+    for (int i = 0; i < nb; ++i) {
+      const long long slot = static_cast<long long>(first) + i;
+      if (slot >= max_items) { if (status) atomicOr(status, 1); break; }
+      const long long row0 = s + static_cast<long long>(i) * BM, left = e - row0;
+      items[slot] = make_int4(b, static_cast<int>(row0), static_cast<int>(left < BM ? left : BM), 0);
+    }
+    __syncthreads();
+    if (tid == 0) carry += warp_tot[31];
+    __syncthreads();
+  }
+  if (tid == 0) ws[0] = static_cast<int>(carry < max_items ? carry : max_items);
+}
+
 }  // namespace
 }  // namespace gemm
 }  // namespace hstu
@@ -445,29 +537,17 @@ extern "C" int b200_stu_addmm_supported(const B200GemmParams* p) {
   return 1;
 }
 
-extern "C" int b200_stu_addmm(const B200GemmParams* p, void* stream) {
+namespace {
+// Shared launch path of the two entry points.
+int launch_gemm(const B200GemmParams* p, const void* w_base, long long w_rows, const int4* items, const int* n_items,
+                long long max_blocks, int per_seq_bias, const void* offsets, int off64, int num_seqs, void* stream) {
   using namespace hstu::gemm;
-  if (p == nullptr) return B200_HSTU_EINVAL;
-  if (p->struct_size != sizeof(B200GemmParams)) return B200_HSTU_EVERSION;
-  if (p->M < 0 || p->K <= 0 || p->N <= 0) return B200_HSTU_EINVAL;
-  if (p->M == 0) return B200_HSTU_OK;
-  if (!b200_stu_addmm_supported(p)) return B200_HSTU_EUNSUPPORTED;
   const bool fuse = (p->flags & B200_GEMM_FLAG_LAYER_NORM) != 0;
-  if (!p->x || !p->w || !p->bias || !p->out) return B200_HSTU_EINVAL;
-  if (fuse && (!p->mean || !p->rstd)) return B200_HSTU_EINVAL;
-  if ((p->ln_weight == nullptr) != (p->ln_bias == nullptr)) return B200_HSTU_EINVAL;
-  if ((p->flags & B200_GEMM_FLAG_SWISH) && (!fuse || !p->ln_weight)) return B200_HSTU_EINVAL;
-  if (p->x_row_stride < p->K || p->w_row_stride < p->N || p->out_row_stride < p->N) return B200_HSTU_EINVAL;
-  if (p->bias_row_stride != 0 && p->bias_row_stride < p->N) return B200_HSTU_EINVAL;
-  auto bad = [](const void* q, long long stride) { return reinterpret_cast<uintptr_t>(q) % 16 != 0 || stride % 8 != 0; };
-  if (bad(p->x, p->x_row_stride) || bad(p->w, p->w_row_stride) || bad(p->out, p->out_row_stride) ||
-      bad(p->bias, p->bias_row_stride) || (p->ln_weight && (bad(p->ln_weight, 0) || bad(p->ln_bias, 0))))
-    return B200_HSTU_EALIGN;
   const bool bf16 = p->dtype == B200_HSTU_BF16;
   hstu::set_error_stage("addmm: tensor maps");
   if (!hstu::tc::ensure_current_context(p->x)) return B200_HSTU_ELAUNCH;
   Maps maps;
-  if (!hstu::tc::make_map_box(&maps.w, p->w, p->K, p->N, p->w_row_stride, BK, bf16)) return B200_HSTU_ELAUNCH;
+  if (!hstu::tc::make_map_box(&maps.w, w_base, w_rows, p->N, p->w_row_stride, BK, bf16)) return B200_HSTU_ELAUNCH;
   if (!hstu::tc::make_map_box(&maps.o, p->out, p->M, p->N, p->out_row_stride, BM, bf16)) return B200_HSTU_ELAUNCH;
   if (fuse) maps.x = maps.w;  // not used by the kernel
   else if (!hstu::tc::make_map_box(&maps.x, p->x, p->M, p->K, p->x_row_stride, 128, bf16)) return B200_HSTU_ELAUNCH;
@@ -478,13 +558,14 @@ extern "C" int b200_stu_addmm(const B200GemmParams* p, void* stream) {
   a.K = static_cast<int>(p->K); a.N = static_cast<int>(p->N);
   a.fuse_ln = fuse ? 1 : 0; a.swish = (p->flags & B200_GEMM_FLAG_SWISH) ? 1 : 0; a.affine = p->ln_weight ? 1 : 0;
   a.eps = p->eps;
+  a.items = items; a.n_items = n_items; a.per_seq_bias = per_seq_bias;
+  a.offsets = offsets; a.off64 = off64; a.num_seqs = num_seqs;
   a.dbg = 0;
 #ifdef B200_HSTU_PROFILING
   if (const char* e = getenv("B200_GEMM_DBG")) a.dbg = atoi(e);
 #endif
-  const long long n_blocks = (p->M + BM - 1) / BM;
   const int sms = hstu::tc::sm_count();
-  const unsigned grid = static_cast<unsigned>(n_blocks < sms ? n_blocks : sms);
+  const unsigned grid = static_cast<unsigned>(max_blocks < sms ? (max_blocks < 1 ? 1 : max_blocks) : sms);
   const size_t smem = sizeof(Shared) + 1024;
   auto kern = bf16 ? stu_addmm_tc<true> : stu_addmm_tc<false>;
   hstu::set_error_stage("addmm: kernel");
@@ -492,4 +573,62 @@ extern "C" int b200_stu_addmm(const B200GemmParams* p, void* stream) {
   if (e != cudaSuccess) return B200_HSTU_ELAUNCH;
   kern<<<grid, THREADS, smem, static_cast<cudaStream_t>(stream)>>>(maps, a);
   return cudaGetLastError() == cudaSuccess ? B200_HSTU_OK : B200_HSTU_ELAUNCH;
+}
+
+int check_common(const B200GemmParams* p) {
+  if (p == nullptr) return B200_HSTU_EINVAL;
+  if (p->struct_size != sizeof(B200GemmParams)) return B200_HSTU_EVERSION;
+  if (p->M < 0 || p->K <= 0 || p->N <= 0) return B200_HSTU_EINVAL;
+  if (p->M == 0) return B200_HSTU_OK;
+  if (!b200_stu_addmm_supported(p)) return B200_HSTU_EUNSUPPORTED;
+  if (!p->x || !p->w || !p->bias || !p->out) return B200_HSTU_EINVAL;
+  if (p->x_row_stride < p->K || p->w_row_stride < p->N || p->out_row_stride < p->N) return B200_HSTU_EINVAL;
+  if (p->bias_row_stride != 0 && p->bias_row_stride < p->N) return B200_HSTU_EINVAL;
+  auto bad = [](const void* q, long long stride) { return reinterpret_cast<uintptr_t>(q) % 16 != 0 || stride % 8 != 0; };
+  if (bad(p->x, p->x_row_stride) || bad(p->w, p->w_row_stride) || bad(p->out, p->out_row_stride) ||
+      bad(p->bias, p->bias_row_stride))
+    return B200_HSTU_EALIGN;
+  return 1;  // go on
+}
+}  // namespace
+
+extern "C" int b200_stu_addmm(const B200GemmParams* p, void* stream) {
+  const int rc = check_common(p);
+  if (rc != 1) return rc;
+  const bool fuse = (p->flags & B200_GEMM_FLAG_LAYER_NORM) != 0;
+  if (fuse && (!p->mean || !p->rstd)) return B200_HSTU_EINVAL;
+  if ((p->ln_weight == nullptr) != (p->ln_bias == nullptr)) return B200_HSTU_EINVAL;
+  if ((p->flags & B200_GEMM_FLAG_SWISH) && (!fuse || !p->ln_weight)) return B200_HSTU_EINVAL;
+  if (p->ln_weight && (reinterpret_cast<uintptr_t>(p->ln_weight) % 16 != 0 || reinterpret_cast<uintptr_t>(p->ln_bias) % 16 != 0))
+    return B200_HSTU_EALIGN;
+  return launch_gemm(p, p->w, p->K, nullptr, nullptr, (p->M + hstu::gemm::BM - 1) / hstu::gemm::BM, 0, nullptr, 0, 0, stream);
+}
+
+extern "C" size_t b200_stu_jagged_bmm_workspace_bytes(int64_t rows, int64_t num_seqs) {
+  if (rows < 0 || num_seqs < 0) return 0;
+  const long long max_items = rows / hstu::gemm::BM + num_seqs;
+  return static_cast<size_t>(16 + 16 * max_items + 255) & ~static_cast<size_t>(255);
+}
+
+extern "C" int b200_stu_jagged_dense_bmm_add(const B200GemmParams* p, const void* seq_offsets, int offsets_i64,
+                                             int64_t num_seqs, int64_t w_seq_stride, int per_row_bias, void* workspace,
+                                             uint64_t workspace_bytes, void* stream) {
+  using namespace hstu::gemm;
+  const int rc = check_common(p);
+  if (rc != 1) return rc;
+  if (p->flags != 0 || seq_offsets == nullptr || num_seqs <= 0) return B200_HSTU_EINVAL;
+  if (w_seq_stride != p->K * p->w_row_stride) return B200_HSTU_EUNSUPPORTED;  // the matrices must be stacked densely
+  if (num_seqs * p->K >= (1LL << 31)) return B200_HSTU_EUNSUPPORTED;
+  if (per_row_bias ? p->bias_row_stride < p->N : (p->bias_row_stride != 0 && p->bias_row_stride < p->N)) return B200_HSTU_EINVAL;
+  const size_t need = b200_stu_jagged_bmm_workspace_bytes(p->M, num_seqs);
+  if (workspace == nullptr || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 16 != 0)
+    return B200_HSTU_EWORKSPACE;
+  const long long max_items = p->M / BM + num_seqs;
+  int* ws = reinterpret_cast<int*>(workspace);
+  hstu::set_error_stage("jagged bmm: row-block list");
+  build_gemm_items<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(seq_offsets, offsets_i64 ? 1 : 0, static_cast<int>(num_seqs),
+                                                                      p->M, ws, max_items, p->status);
+  if (cudaGetLastError() != cudaSuccess) return B200_HSTU_ELAUNCH;
+  return launch_gemm(p, p->w, num_seqs * p->K, reinterpret_cast<const int4*>(ws + 4), ws, max_items, per_row_bias ? 0 : 1,
+                     seq_offsets, offsets_i64 ? 1 : 0, static_cast<int>(num_seqs), stream);
 }

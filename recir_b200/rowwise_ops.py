@@ -431,10 +431,11 @@ def _jagged_dense_bmm_add_cuda(max_seq_len, seq_offsets, jagged, dense, bias, el
     ``out[rows of b] = jagged[rows of b] @ dense[b] + bias[b]``
     (``generative_recommenders::triton_jagged_dense_bmm_add_fwd``,
     ``recir/ops/kjt_split_per_feature.cpp:262-305``, which loops over the sequences with ``at::addmm``).
-    One grouped GEMM of the vendor library over the jagged rows, no padding and no host read of the
-    offsets; bfloat16 only (the library's grouped GEMM: float32 accumulation, bfloat16 product, then the bias
-    is added in float32 and the sum rounded).  ``jagged.shape[0]`` must equal ``seq_offsets[-1]`` (not checked: that would need a
-    host read); rows past it would be left unspecified by the library and are returned as zeros."""
+    bfloat16 / float16 with K a multiple of 64 up to 512 and N a multiple of 8 (the STU sizes) run on this
+    library's tcgen05 projection kernel over a device-built list of (sequence, 128-row block) items; other
+    bfloat16 sizes are one grouped GEMM of the vendor library (which rounds the product to bfloat16 before the
+    bias is added).  No padding and no host read of the offsets either way.  Rows at or past
+    ``seq_offsets[-1]`` are returned as zeros."""
     if jagged.dim() != 2:
         raise ValueError("jagged must be two-dimensional")
     if dense.dim() != 3:
@@ -448,11 +449,16 @@ def _jagged_dense_bmm_add_cuda(max_seq_len, seq_offsets, jagged, dense, bias, el
         raise ValueError("sequence offsets size must match the dense batch size")
     if tuple(bias.shape) != ((jagged.shape[0], N) if elementwise else (B, N)):
         raise ValueError("bias dimensions are incompatible with the output")
-    if jagged.dtype != torch.bfloat16 or dense.dtype != torch.bfloat16:
-        raise ValueError(f"unsupported dtype {jagged.dtype}: the grouped GEMM takes bfloat16")
     T = jagged.shape[0]
     if T == 0 or B == 0:
         return jagged.new_zeros((T, N)), B, K, N
+    if (jagged.dtype in (torch.bfloat16, torch.float16) and dense.dtype == jagged.dtype and bias.dtype == jagged.dtype
+            and K % 64 == 0 and K <= 512 and N % 8 == 0 and seq_offsets.dtype in (torch.int32, torch.int64)
+            and B * K < 2 ** 31):
+        return _jagged_dense_bmm_add_tc(seq_offsets, jagged, dense, bias, elementwise), B, K, N
+    if jagged.dtype != torch.bfloat16 or dense.dtype != torch.bfloat16:
+        raise ValueError(f"unsupported dtype {jagged.dtype}: float16 needs K a multiple of 64 up to 512 and N a multiple "
+                         "of 8 (tensor-core kernel); other bfloat16 sizes go to the vendor library's grouped GEMM")
     ends = seq_offsets[1:].to(torch.int32)
     prod = torch.nn.functional.grouped_mm(jagged.contiguous(), dense.contiguous(), offs=ends).float()
     rows = torch.arange(T, device=jagged.device, dtype=ends.dtype)
@@ -464,6 +470,35 @@ def _jagged_dense_bmm_add_cuda(max_seq_len, seq_offsets, jagged, dense, bias, el
         out = prod + bias.float()[seq.clamp(max=B - 1)]
     return torch.where(owned, out, torch.zeros((), device=out.device)).to(jagged.dtype), B, K, N
 
+
+def _jagged_dense_bmm_add_tc(seq_offsets, jagged, dense, bias, elementwise):
+    """This library's tcgen05 projection kernel over (sequence, 128-row block) items built on the device from
+    the offsets: float32 sums, the bias added before the single rounding, as ``at::addmm`` does per sequence."""
+    global launch_counter
+    lib = _lib.load()
+    x, w = _rows2d(jagged), dense.contiguous()
+    bias = _rows2d(bias)
+    off = seq_offsets.contiguous()
+    T, K = x.shape
+    B, _, N = w.shape
+    out = torch.empty((T, N), dtype=x.dtype, device=x.device)
+    p = _lib.B200GemmParams()
+    p.struct_size = ctypes.sizeof(p)
+    p.dtype = _DTYPES[x.dtype]
+    p.M, p.K, p.N = T, K, N
+    p.x, p.w, p.bias, p.out = x.data_ptr(), w.data_ptr(), bias.data_ptr(), out.data_ptr()
+    p.x_row_stride, p.w_row_stride, p.out_row_stride = x.stride(0), w.stride(1), out.stride(0)
+    p.bias_row_stride = bias.stride(0)
+    p.status = _ops.status_tensor(x.device).data_ptr()
+    need = lib.b200_stu_jagged_bmm_workspace_bytes(T, B)
+    ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        rc = lib.b200_stu_jagged_dense_bmm_add(ctypes.byref(p), off.data_ptr(), int(off.dtype == torch.int64), B, w.stride(0),
+                                               int(bool(elementwise)), ws.data_ptr(), need,
+                                               ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    _check(rc, "b200_stu_jagged_dense_bmm_add")
+    launch_counter += 2
+    return out
 
 
 def _jagged_dense_bmm_add_fake(max_seq_len, seq_offsets, jagged, dense, bias, elementwise=False):

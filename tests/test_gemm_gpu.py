@@ -117,3 +117,46 @@ def test_unsupported_shapes_and_validation():
         wf = torch.empty(64, 32, dtype=torch.bfloat16, device="cuda")
         out = torch.ops.recir.b200_layer_norm_addmm_fwd(xf, None, None, 1e-5, False, wf, wf[0])
     assert out[0].shape == (6, 32) and out[1].shape == (6,) and out[1].dtype == torch.float32
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+@pytest.mark.parametrize("elementwise", [False, True])
+@pytest.mark.parametrize("offsets_dtype", [torch.int64, torch.int32])
+def test_jagged_dense_bmm_add_on_tensor_cores_matches_oracle(dtype, elementwise, offsets_dtype):
+    """Per-sequence weight matrices over jagged rows (kjt_split_per_feature.cpp:262-305): empty sequences,
+    sequences shorter and longer than a 128-row block, exact multiples of it, and rows past the last offset
+    (returned as zeros).  The item list is built on the device; int32 and int64 offsets."""
+    lengths = [7, 0, 333, 128, 1, 256, 129, 0, 64]
+    pad = 5
+    g = torch.Generator().manual_seed(17)
+    B, K, N = len(lengths), 128, 72
+    T = sum(lengths)
+    t = DT[dtype]
+    jag = torch.randn(T + pad, K, generator=g).to(t)
+    den = (torch.randn(B, K, N, generator=g) / K ** 0.5).to(t)
+    bias = torch.randn((T + pad, N) if elementwise else (B, N), generator=g).to(t)
+    offs = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=offsets_dtype)
+    y, b_, k_, n_ = torch.ops.recir.b200_jagged_dense_bmm_add_fwd(max(lengths), offs.cuda(), jag.cuda(), den.cuda(), bias.cuda(),
+                                                                 elementwise)
+    assert (b_, k_, n_) == (B, K, N) and y.shape == (T + pad, N)
+    want = ro.jagged_dense_bmm_add(offs.numpy(), F(jag[:T]), F(den), F(bias[:T]) if elementwise else F(bias), elementwise, dtype)
+    _close(y[:T], want, dtype, "jagged bmm")
+    assert not y[T:].any(), "rows past the last offset must be zeros"
+
+
+def test_jagged_dense_bmm_add_zipf_batch_sequences_do_not_mix():
+    """Every sequence of a Zipf-length batch against its own addmm (the reference's loop), full STU width."""
+    from recir_b200 import workload
+    hist, tg = workload.config4_lengths(96)
+    lengths = hist + tg
+    offs = torch.as_tensor(np.concatenate([[0], np.cumsum(lengths)]))
+    T, B, K, N = int(offs[-1]), len(lengths), 512, 256
+    g = torch.Generator().manual_seed(4)
+    jag = torch.randn(T, K, generator=g).to(torch.bfloat16).cuda()
+    den = (torch.randn(B, K, N, generator=g) / K ** 0.5).to(torch.bfloat16).cuda()
+    bias = torch.randn(B, N, generator=g).to(torch.bfloat16).cuda()
+    y, *_ = torch.ops.recir.b200_jagged_dense_bmm_add_fwd(int(lengths.max()), offs.cuda(), jag, den, bias, False)
+    for b in (0, 1, int(np.argmax(lengths)), int(np.argmin(lengths)), B - 1):
+        s, e = int(offs[b]), int(offs[b + 1])
+        want = ro.addmm(F(jag[s:e].cpu()), F(den[b].cpu()), F(bias[b].cpu()), "bfloat16")
+        _close(y[s:e], want, "bfloat16", f"sequence {b}")

@@ -207,8 +207,9 @@ JBMM = np.load(os.path.join(os.path.dirname(__file__), "golden", "jagged_bmm_gol
 
 @pytest.mark.parametrize("name", [str(n) for n in JBMM["names"] if str(n).startswith("bf16")])
 def test_jagged_dense_bmm_add_matches_reference_golden(name):
-    """Per-sequence projection of jagged rows as one grouped GEMM of the library, against the reference
-    operator's output (bias per sequence and per row, empty sequences in the batch)."""
+    """Per-sequence projection of jagged rows against the reference operator's output (bias per sequence and
+    per row, empty sequences in the batch): K = 64 runs on this library's tensor-core kernel, K = 32 on the
+    vendor library's grouped GEMM."""
     dt, elementwise = JBMM[f"{name}/cfg"]
     offs = torch.as_tensor(JBMM[f"{name}/offsets"]).cuda()
     jag, den, bias = (_t(JBMM[f"{name}/{k}"], dt) for k in ("jagged", "dense", "bias"))
@@ -233,22 +234,27 @@ def test_jagged_dense_bmm_add_on_a_zipf_batch_and_validation():
     den = (torch.randn(B, K, N, generator=g) * 0.2).to(torch.bfloat16).cuda()
     bias = torch.randn(B, N, generator=g).to(torch.bfloat16).cuda()
     y, *_ = torch.ops.recir.b200_jagged_dense_bmm_add_fwd(int(lengths.max()), offs, jag, den, bias, False)
-    # the library's grouped GEMM writes the product in bfloat16 before the bias is added: restate that
-    prod = ro.jagged_dense_bmm_add(offs.cpu().numpy(), jag.float().cpu().numpy(), den.float().cpu().numpy(),
+    # K = 128, N = 64: this library's tensor-core kernel (float32 sums, bias added, ONE rounding, as at::addmm)
+    once = ro.jagged_dense_bmm_add(offs.cpu().numpy(), jag.float().cpu().numpy(), den.float().cpu().numpy(),
+                                   bias.float().cpu().numpy(), False, "bfloat16")
+    got = y.float().cpu().numpy().astype(np.float64)
+    rel = np.abs(got - once) / np.maximum(np.abs(once), float(np.abs(once).max()) * 1e-2)
+    assert rel.max() <= 2.02 * 2.0 ** -8 and (rel > 1.01 * 2.0 ** -8).mean() <= 0.02
+    # K = 32 is not one of its sizes: the vendor library's grouped GEMM, which rounds the product to bfloat16
+    # before the bias is added (restated here)
+    jag2, den2 = jag[:, :32].contiguous(), den[:, :32].contiguous()
+    y2, *_ = torch.ops.recir.b200_jagged_dense_bmm_add_fwd(int(lengths.max()), offs, jag2, den2, bias, False)
+    prod = ro.jagged_dense_bmm_add(offs.cpu().numpy(), jag2.float().cpu().numpy(), den2.float().cpu().numpy(),
                                    np.zeros((B, N), np.float32), False, "bfloat16")
     seq = np.repeat(np.arange(B), lengths)
     want = ro.round_to(prod + bias.float().cpu().numpy()[seq], "bfloat16")
-    got = y.float().cpu().numpy().astype(np.float64)
-    # a last-place flip of the bfloat16 product (summation order) moves the sum by one ulp of the product
+    got2 = y2.float().cpu().numpy().astype(np.float64)
     tol = 2.0 ** -7 * np.maximum(np.abs(prod), np.abs(want)) + 1e-6
-    bad = np.abs(got - want) > tol
-    assert bad.mean() <= 1e-3 and np.abs(got - want).max() <= 4 * tol.max()
-    once = ro.jagged_dense_bmm_add(offs.cpu().numpy(), jag.float().cpu().numpy(), den.float().cpu().numpy(),
-                                   bias.float().cpu().numpy(), False, "float32")
-    assert np.abs(got - once).max() <= 2.0 ** -6 * float(np.abs(prod).max())  # against the single-rounding reference
+    bad = np.abs(got2 - want) > tol
+    assert bad.mean() <= 1e-3 and np.abs(got2 - want).max() <= 4 * tol.max()
     with pytest.raises(ValueError, match="incompatible"):
         torch.ops.recir.b200_jagged_dense_bmm_add_fwd(8, offs, jag, den[:, :64], bias, False)
-    with pytest.raises(ValueError, match="bfloat16"):
+    with pytest.raises(ValueError, match="unsupported dtype"):
         torch.ops.recir.b200_jagged_dense_bmm_add_fwd(8, offs, jag.float(), den.float(), bias.float(), False)
 
 
