@@ -379,13 +379,15 @@ def main():
     ap.add_argument("--grad-check", dest="grad_check", action="store_true", default=None)
     ap.add_argument("--no-grad-check", dest="grad_check", action="store_false")
     ap.add_argument("--case", default=None, help="run one of the single-purpose runners of bench_cases.py instead")
-    args, rest = ap.parse_known_args()
-    if args.case is not None:
+    argv = sys.argv[1:]
+    if "--case" in argv:  # everything else on the line belongs to the runner (its options may share names with ours)
+        i = argv.index("--case")
+        if i + 1 >= len(argv):
+            ap.error("--case needs a name")
         import bench_cases
-        bench_cases.main([args.case, *rest])
+        bench_cases.main([argv[i + 1], *argv[:i], *argv[i + 2:]])
         return
-    if rest:
-        ap.error(f"unrecognized arguments: {' '.join(rest)}")
+    args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 0)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

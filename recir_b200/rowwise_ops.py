@@ -16,7 +16,8 @@ Positionally identical to the reference's operators, so the same node-retargetin
 
 ``recir::b200_weighted_layer_norm_fwd`` is differentiable: ``recir::b200_weighted_layer_norm_bwd`` is the
 closed form of what autograd gives through the reference's composite (the reference has no backward
-operator of its own).  The gate stage, the fp8 variants and the projections are forward only.
+operator of its own).  ``recir::b200_layer_norm_addmm_fwd`` is differentiable too (composed backward).  The gate stage, the fp8
+variants and the plain projections are forward only.
 ``recir::b200_layer_norm_addmm_fwd`` fuses the layer norm into the projection behind it (one tcgen05
 kernel, ``csrc/stu_gemm.cu``).  CUDA tensors only; there is no CPU implementation.
 """
@@ -380,8 +381,33 @@ def _addmm_fake(x, w, y):
 
 _LIBDEF.impl("b200_addmm_fwd", _addmm_cuda, "CUDA")
 torch.library.register_fake("recir::b200_addmm_fwd", _addmm_fake)
+def _layer_norm_addmm_setup_context(ctx, inputs, output) -> None:
+    x, ln_weight, ln_bias, eps, is_swish, w, bias = inputs
+    _out, mean, rstd = output
+    ctx.save_for_backward(x, ln_weight, ln_bias, w, mean, rstd)
+    ctx.eps, ctx.is_swish, ctx.bias_shape = eps, is_swish, tuple(bias.shape)
+
+
+def _layer_norm_addmm_backward(ctx, dout, _dmean, _drstd):
+    """Backward of the fused op, composed: the normalised rows are recomputed by the layer-norm kernel from the
+    saved statistics (they were never stored), the two products of the projection's backward are plain GEMMs
+    (vendor library), and the layer norm's own backward is this library's kernel."""
+    x, ln_weight, ln_bias, w, mean, rstd = ctx.saved_tensors
+    dout = dout.contiguous()
+    a = torch.ops.recir.b200_weighted_layer_norm_fwd(x, ln_weight, ln_bias, ctx.eps, mean, rstd, ctx.is_swish)[0]
+    da = dout @ w.t()
+    dw = a.t() @ dout
+    dbias = dout if len(ctx.bias_shape) == 2 and ctx.bias_shape[0] == x.shape[0] else \
+        dout.float().sum(0).to(dout.dtype).reshape(ctx.bias_shape)
+    dx, dlw, dlb = torch.ops.recir.b200_weighted_layer_norm_bwd(da, x, ln_weight, ln_bias, mean, rstd, ctx.is_swish)
+    has_w = ln_weight is not None
+    return dx, (dlw if has_w else None), (dlb if has_w else None), None, None, dw, dbias
+
+
 _LIBDEF.impl("b200_layer_norm_addmm_fwd", _layer_norm_addmm_cuda, "CUDA")
 torch.library.register_fake("recir::b200_layer_norm_addmm_fwd", _layer_norm_addmm_fake)
+torch.library.register_autograd("recir::b200_layer_norm_addmm_fwd", _layer_norm_addmm_backward,
+                                setup_context=_layer_norm_addmm_setup_context)
 
 
 def _fp8_rowwise_addmm_cuda(a, b, a_scale, b_scale, bias, has_bias, bias_is_2d, dot_out_dtype, allow_tf32,

@@ -160,3 +160,24 @@ def test_jagged_dense_bmm_add_zipf_batch_sequences_do_not_mix():
         s, e = int(offs[b]), int(offs[b + 1])
         want = ro.addmm(F(jag[s:e].cpu()), F(den[b].cpu()), F(bias[b].cpu()), "bfloat16")
         _close(y[s:e], want, "bfloat16", f"sequence {b}")
+
+
+@pytest.mark.parametrize("swish", [False, True])
+def test_fused_projection_is_differentiable(swish):
+    """Gradients of the fused layer norm + projection (x, layer-norm weight and bias, W, bias) against autograd
+    through the same chain written with torch ops in float32 on the same bf16 inputs; relative L2 <= 1e-2 (bf16
+    operands in the two backward GEMMs and one bf16 rounding per gradient)."""
+    M, K, N = 600, 512, 256
+    x, w, b, lw, lb = _inputs(5, M, K, N, "bfloat16")
+    g = torch.Generator().manual_seed(6)
+    dout = torch.randn(M, N, generator=g).to(torch.bfloat16)
+    leaves = [t.cuda().requires_grad_(True) for t in (x, lw, lb, w, b)]
+    out, _, _ = torch.ops.recir.b200_layer_norm_addmm_fwd(leaves[0], leaves[1], leaves[2], 1e-5, swish, leaves[3], leaves[4])
+    out.backward(dout.cuda())
+    ref = [t.float().cuda().requires_grad_(True) for t in (x, lw, lb, w, b)]
+    n = torch.nn.functional.layer_norm(ref[0], (K,), ref[1], ref[2], 1e-5)
+    y = torch.sigmoid(n) * ref[0] if swish else n
+    (y.to(torch.bfloat16).float() @ ref[3] + ref[4]).backward(dout.float().cuda())
+    for name, a, r in zip(("dx", "dln_w", "dln_b", "dW", "dbias"), leaves, ref):
+        err = float((a.grad.float() - r.grad).norm() / r.grad.norm())
+        assert err <= 1e-2, (name, err)
