@@ -17,6 +17,7 @@ sequences sit on the HBM roofline, long ones on the tensor-core roofline.
 ``rowwise``: the row-wise STU kernels (layer norm, gate stage, fp8 copy), HBM throughput.
 ``jagged``: the jagged marshalling kernels and the embedding add, HBM throughput, on the Zipf lengths.
 ``gemm``: the fused layer-norm + u/v/q/k projection against the two-kernel chain and the vendor GEMM.
+``trace``: per-role cycle accounting and event trace inside the attention kernels (instrumented build only).
 """
 from __future__ import annotations
 
@@ -314,7 +315,84 @@ def main_gemm(argv):
     print(json.dumps(out))
 
 
-CASES = {"attn": main_attn, "rowwise": main_rowwise, "jagged": main_jagged, "gemm": main_gemm}
+def main_trace(argv):
+    """In-kernel cycle accounting and event trace of the three tensor-core attention kernels on cfg1.  Needs
+    the instrumented library (`python -m recir_b200.build -DB200_HSTU_PROFILING`, which instantiates the PROF
+    variants of the kernels; rebuild with `--force` afterwards) and goes through the C ABI directly, because
+    the trace wants a status buffer of 16 + 8192 ints (B200_HSTU_FLAG_TRACE).  Prints, per kernel: the time of
+    the traced call, the per-role wait / busy cycles summed over CTAs (workspace ints 2..15), and for CTA 0 the
+    median phases of the epilogue per (half) tile from the event trace."""
+    import ctypes
+    import os
+
+    ap = argparse.ArgumentParser(prog="bench.py --case trace")
+    ap.add_argument("--kernel", default="all", choices=["all", "fwd", "dkv", "dq"])
+    args = ap.parse_args(argv)
+    os.environ["B200_HSTU_PROFILE"] = "1"
+    os.environ["B200_HSTU_PROFILE_DQ"] = "1"
+    from recir_b200 import _lib
+
+    bt = workload.config1()
+    dev = "cuda"
+    q, k, v, do = (x.to(dev) for x in (bt.q, bt.k, bt.v, bt.dout))
+    off, nt = bt.seq_offsets.to(dev), bt.num_targets.to(dev)
+    lib = _lib.load()
+    names_f = ["mma_total", "mma_wait_kfull", "mma_wait_pready", "mma_wait_vfull", "mma_wait_item", "epi_total",
+               "epi_wait_sfull", "epi_wait_ofull", "epi_partial", "epi_full", "-", "epi_drain", "prod_wait", "prod_total"]
+    names_b = ["mma_total", "mma_wait_load", "mma_wait_p", "mma_wait_acc", "mma_wait_item", "epi_total", "epi_wait_s",
+               "epi_wait_acc", "epi_tile", "epi_drain", "epi_ld", "epi_st", "-", "-"]
+    out = {}
+    for which in (("fwd", "dkv", "dq") if args.kernel == "all" else (args.kernel,)):
+        p = _lib.B200HstuParams()
+        keep = ops._fill(p, q, k, v, off, bt.max_seq_len, bt.alpha, True, nt, 0, 0, None, 0)
+        o, dq, dk, dv = (torch.empty_like(x) for x in (v, q, k, v))
+        p.o, p.o_row_stride = o.data_ptr(), o.stride(0)
+        p.d_o, p.do_row_stride = do.data_ptr(), do.stride(0)
+        p.dq, p.dk, p.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
+        p.dq_row_stride = p.dk_row_stride = p.dv_row_stride = dq.stride(0)
+        pass_id = 0 if which == "fwd" else 1
+        p.flags |= _lib.FLAG_TRACE | {"fwd": 0, "dkv": _lib.FLAG_BWD_SKIP_DQ, "dq": _lib.FLAG_BWD_SKIP_DKV}[which]
+        need = lib.b200_hstu_workspace_bytes(ctypes.byref(p), pass_id)
+        ws = torch.zeros(need // 4 + 64, dtype=torch.int32, device=dev)
+        base = ((-ws.data_ptr()) % 256) // 4
+        p.workspace, p.workspace_bytes = ws.data_ptr() + 4 * base, need
+        status = torch.zeros(16 + 8192, dtype=torch.int32, device=dev)
+        p.status = status.data_ptr()
+        fn = lib.b200_hstu_fwd if pass_id == 0 else lib.b200_hstu_bwd
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        for _ in range(2):
+            assert fn(ctypes.byref(p), st) == 0
+        torch.cuda.synchronize()
+        status.zero_(); ws.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(); assert fn(ctypes.byref(p), st) == 0; e1.record()
+        torch.cuda.synchronize()
+        items = int(ws[base]); ncta = min(148, items)
+        vals = ws[base + 2: base + 16].tolist()
+        if which != "dq" and not any(vals):  # (the dQ kernel records the event trace only)
+            raise SystemExit("no counters were written: build the instrumented library first "
+                             "(python -m recir_b200.build -DB200_HSTU_PROFILING)")
+        roles = {n: round(x * 64 / ncta / (2 if n.startswith("epi") else 1) / 1e3, 1)
+                 for n, x in zip(names_f if which == "fwd" else names_b, vals) if n != "-" and x}
+        res = {"ms": e0.elapsed_time(e1), "items": items, "kcycles_per_cta": roles}
+        tr = status[16:].cpu().numpy().astype(np.int64) & 0xffffffff
+        if which != "fwd":  # epilogue thread 128, six events per half tile: wait_begin s_ok ld_done st_issued arrived
+            epi = tr[4096:4096 + 4092].reshape(-1, 6)
+            n = int((epi[:, 1] != 0).sum())
+            d = lambda a, b: (a - b) & 0xffffffff
+            E = epi[:n]
+            ph = {"wait_scores": d(E[:, 1], E[:, 0]), "tmem_ld": d(E[:, 2], E[:, 1]), "math_and_st_issue": d(E[:, 3], E[:, 2]),
+                  "st_wait_and_arrive": d(E[:, 4], E[:, 3]), "period": d(E[1:, 0], E[:-1, 0])}
+            res["cta0_half_tiles"] = n
+            res["cta0_epilogue_cycles_median"] = {k: int(np.median(x[x < 1 << 20])) for k, x in ph.items()}
+            mma = tr[:4096].reshape(-1, 4)[:n]
+            res["cta0_span_cycles_per_half_tile"] = float(d(E[n - 1, 4], E[0, 0])) / max(n, 1)
+        out[which] = res
+        del keep
+    print(json.dumps(out))
+
+
+CASES = {"attn": main_attn, "rowwise": main_rowwise, "jagged": main_jagged, "gemm": main_gemm, "trace": main_trace}
 
 
 def main(argv=None):

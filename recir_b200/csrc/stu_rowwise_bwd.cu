@@ -134,18 +134,39 @@ __global__ void __launch_bounds__(WARPS * 32) layer_norm_bwd_kernel(Args a) {
   }
 }
 
-// dw[c] = sum over CTAs of partial[cta][0][c] (db: [1]) in CTA order; one thread per column.
+// dw[c] = sum over CTAs of partial[cta][0][c] (db: [1]).  A CTA owns 32 columns; its eight warps add up
+// every eighth partial row each (four independent running sums per thread, so that the loads overlap), then
+// the eight per-warp sums are added in warp order: a fixed order, hence bitwise repeatable.
 template <typename T>
-__global__ void layer_norm_bwd_reduce(Args a) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= a.cols) return;
-  float sw = 0.f, sb = 0.f;
-  for (int g = 0; g < a.grid; ++g) {
-    sw += a.partial[(static_cast<long long>(g) * 2 + 0) * a.cols + c];
-    sb += a.partial[(static_cast<long long>(g) * 2 + 1) * a.cols + c];
+__global__ void __launch_bounds__(256) layer_norm_bwd_reduce(Args a) {
+  __shared__ float red[2][8][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
+  float sw[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+  if (c < a.cols) {
+    int g = warp;
+    for (; g + 24 < a.grid; g += 32) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        sw[u] += a.partial[(static_cast<long long>(g + 8 * u) * 2 + 0) * a.cols + c];
+        sb[u] += a.partial[(static_cast<long long>(g + 8 * u) * 2 + 1) * a.cols + c];
+      }
+    }
+    for (; g < a.grid; g += 8) {
+      sw[0] += a.partial[(static_cast<long long>(g) * 2 + 0) * a.cols + c];
+      sb[0] += a.partial[(static_cast<long long>(g) * 2 + 1) * a.cols + c];
+    }
   }
-  reinterpret_cast<T*>(a.dw)[c] = from_float<T>(sw);
-  reinterpret_cast<T*>(a.db)[c] = from_float<T>(sb);
+  red[0][warp][lane] = (sw[0] + sw[1]) + (sw[2] + sw[3]);
+  red[1][warp][lane] = (sb[0] + sb[1]) + (sb[2] + sb[3]);
+  __syncthreads();
+  if (warp == 0 && c < a.cols) {
+    float tw = 0.f, tb = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) { tw += red[0][w][lane]; tb += red[1][w][lane]; }
+    reinterpret_cast<T*>(a.dw)[c] = from_float<T>(tw);
+    reinterpret_cast<T*>(a.db)[c] = from_float<T>(tb);
+  }
 }
 
 int grid_for(long long rows) {
@@ -163,7 +184,7 @@ cudaError_t launch_t(const Args& a, cudaStream_t st) {
   else layer_norm_bwd_kernel<T, 4><<<a.grid, WARPS * 32, 0, st>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || !a.affine) return e;
-  layer_norm_bwd_reduce<T><<<(a.cols + 255) / 256, 256, 0, st>>>(a);
+  layer_norm_bwd_reduce<T><<<(a.cols + 31) / 32, 256, 0, st>>>(a);
   return cudaGetLastError();
 }
 
