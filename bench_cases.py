@@ -376,6 +376,28 @@ def main_trace(argv):
                  for n, x in zip(names_f if which == "fwd" else names_b, vals) if n != "-" and x}
         res = {"ms": e0.elapsed_time(e1), "items": items, "kcycles_per_cta": roles}
         tr = status[16:].cpu().numpy().astype(np.int64) & 0xffffffff
+        if which == "fwd":
+            # epilogue thread 128, six events per key tile: wait_begin, scores ready, first chunk loaded, both
+            # chunks converted and P stored (issue), P visible (+ next tile's scores awaited and its first load
+            # issued), arrived; MMA warp, four per tile: K landed, S issued, P and V ready, PV issued
+            epi = tr[4096:4096 + 4092].reshape(-1, 6)
+            n = int((epi[:, 5] != 0).sum())
+            d = lambda a, b: (a - b) & 0xffffffff
+            E = epi[:n]
+            ok = (E != 0).all(1)
+            E = E[ok]
+            ph = {"wait_scores": d(E[:, 1], E[:, 0]), "first_chunk_ld": d(E[:, 2], E[:, 1]),
+                  "math_both_chunks": d(E[:, 3], E[:, 2]), "next_wait_and_st_wait": d(E[:, 4], E[:, 3]),
+                  "arrive": d(E[:, 5], E[:, 4]), "tile_period": d(E[1:, 5], E[:-1, 5])}
+            res["cta0_tiles"] = int(ok.sum())
+            res["cta0_epilogue_cycles_median"] = {k: int(np.median(x[x < 1 << 20])) for k, x in ph.items()}
+            res["cta0_epilogue_cycles_mean"] = {k: int(np.mean(x[x < 1 << 20])) for k, x in ph.items()}
+            mma = tr[:4096].reshape(-1, 4)[:n]
+            M = mma[(mma != 0).all(1)]
+            mp = {"k_ok_to_S_issued": d(M[:, 1], M[:, 0]), "pv_wait_to_issued": d(M[:, 3], M[:, 2]),
+                  "S_issued_to_pv_ready(prev)": d(M[1:, 2], M[1:, 1]), "tile_period": d(M[1:, 0], M[:-1, 0])}
+            res["cta0_mma_cycles_median"] = {k: int(np.median(x[x < 1 << 20])) for k, x in mp.items()}
+            res["cta0_span_cycles_per_tile"] = float(d(E[-1, 5], E[0, 0])) / max(len(E), 1)
         if which != "fwd":  # epilogue thread 128, six events per half tile: wait_begin s_ok ld_done st_issued arrived
             epi = tr[4096:4096 + 4092].reshape(-1, 6)
             n = int((epi[:, 1] != 0).sum())
