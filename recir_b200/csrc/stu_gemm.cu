@@ -8,17 +8,21 @@
 // rounded once after the bias has been added.  Fusing the two saves one write and one read of the
 // activations (2 * rows * K * 2 bytes) and one launch.
 //
-// Tiling.  A CTA owns a block of 128 rows and keeps its whole A operand (K <= 512: eight 64-column boxes,
-// 128 KB, 128-byte swizzle) in shared memory; W streams through a 4-stage ring of [32 k-rows x 256
-// n-columns] tiles (TMA, four 64-column boxes, used as the N-major B operand).  One tcgen05.mma
-// M128 N256 K16 per k-step accumulates into one of two 256-column TMEM accumulators, so the epilogue of
-// an output tile (bias, rounding, staged bulk tensor stores) overlaps the MMAs of the next one.  W (K x N x 2 bytes, at most
-// a few MB) stays in L2; per 128 rows a CTA ingests it once, which is what bounds the kernel (shared
-// memory ingest per SM), not the tensor pipe.
+// Tiling.  A CTA owns a block of 128 rows and keeps its whole A operand (K <= 512) in tensor memory:
+// 16 k-values of a row are 8 TMEM columns, so K = 512 takes 256 of the 512 columns; the other 256 are two
+// 128-column fp32 accumulators.  The rows reach TMEM 64 at a time through a 64 KB staging buffer in the
+// 128-byte-swizzled box layout: written by TMA (plain and jagged mode) or by the layer-norm prologue, then
+// copied row-per-thread with tcgen05.st by the warps whose TMEM lane quadrant holds those rows.  W streams
+// through an 8-stage ring of [64 k-rows x 128 n-columns] tiles (TMA, two 64-column boxes, N-major B
+// operand); four tcgen05.mma M128 N128 K16 (A from TMEM) per stage.  The epilogue of an output tile (bias,
+// rounding, staged bulk tensor stores) overlaps the MMAs of the next one.  With A out of shared memory the
+// MMAs read only W from it, half of what the SS form reads, and the ring is deep enough (128 KB) to ride
+// out the L2 latency of W, which stays L2-resident (K x N x 2 bytes, a few MB at most).
 //
 // Warp roles (320 threads): warp 0 = TMA producer, warp 1 = MMA issuer (one elected lane), warps 2-9 =
-// layer-norm prologue (16 rows per warp, four at a time in registers) and epilogue (TMEM lane quadrant
-// warp % 4, column half (warp - 2) / 4).  Every wait is bounded (see sm100_ptx.cuh).
+// layer-norm prologue (8 rows per warp and round, four at a time in registers), staging-to-TMEM copy and
+// epilogue (TMEM lane quadrant warp % 4, column half (warp - 2) / 4).  Every wait is bounded (see
+// sm100_ptx.cuh).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -42,31 +46,34 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 256, BK = 32;   // BK: k-rows of W per pipeline stage (two k-steps of 16)
+constexpr int BM = 128, BN = 128, BK = 64;  // BK: k-rows of W per pipeline stage (four k-steps of 16)
 constexpr int MAX_K = 512;
-constexpr int B_STAGES = 4;
-constexpr int A_BOX_BYTES = BM * 128;        // 128 rows x 64 k-columns of 16-bit elements
-constexpr int B_BOX_BYTES = BK * 128;        // 32 k-rows x 64 n-columns
-constexpr int B_STAGE_BYTES = 4 * B_BOX_BYTES;
-constexpr int OUT_BOX_BYTES = BM * 128;      // staging of 128 rows x 64 output columns, one per epilogue group
-constexpr int THREADS = 320;  // 10 warps: 200 registers each without any reallocation
+constexpr int W_STAGES = 8;
+constexpr int W_BOX_BYTES = BK * 128;        // 64 k-rows x 64 n-columns of 16-bit elements
+constexpr int W_STAGE_BYTES = 2 * W_BOX_BYTES;
+constexpr int X_ROWS = 64;                   // rows of x staged at a time on their way into TMEM
+constexpr int X_BOX_BYTES = X_ROWS * 128;    // 64 rows x 64 k-columns
+constexpr int OUT_BOX_BYTES = BM * 128;      // 128 rows x 64 output columns, one box per epilogue group
+constexpr int THREADS = 320;                 // 10 warps: 200 registers each without any reallocation
 constexpr int TMEM_COLS = 512;
+constexpr int TMEM_A = 0, TMEM_ACC0 = 256;   // A operand: K / 2 columns (two 16-bit values each); 2 x 128 accumulator columns
 enum { WAIT_GEMM_PRODUCER = 111, WAIT_GEMM_MMA = 112, WAIT_GEMM_EPILOGUE = 113 };
 
 struct Shared {
-  unsigned char a[MAX_K / 64][A_BOX_BYTES];
-  unsigned char b[B_STAGES][B_STAGE_BYTES];
-  unsigned char out[2][OUT_BOX_BYTES];
-  unsigned long long a_full, a_empty;
-  unsigned long long b_full[B_STAGES], b_empty[B_STAGES];
+  unsigned char w[W_STAGES][W_STAGE_BYTES];       // 128 KB weight ring
+  unsigned char x[MAX_K / 64][X_BOX_BYTES];       // 64 KB: 64 rows of the A operand in the swizzled box layout
+  unsigned char out[2][OUT_BOX_BYTES];            // 32 KB output staging
+  unsigned long long x_full, x_free;              // plain mode: TMA landed a 64-row round / the round was copied to TMEM
+  unsigned long long a_ready, a_free;             // the block's A operand is in TMEM / every MMA reading it has run
+  unsigned long long w_full[W_STAGES], w_empty[W_STAGES];
   unsigned long long acc_full[2], acc_empty[2];
   uint32_t tmem_base;
   int abort_flag;
 };
 
 struct Maps {
-  CUtensorMap x;  // [M, K], box 64 columns x 128 rows (unused with the layer-norm prologue)
-  CUtensorMap w;  // [K, N], box 64 columns x 32 rows
+  CUtensorMap x;  // [M, K], box 64 columns x 64 rows (unused with the layer-norm prologue)
+  CUtensorMap w;  // [K, N] (jagged mode: [B * K, N]), box 64 columns x 64 rows
   CUtensorMap o;  // [M, N], box 64 columns x 128 rows (bulk stores; rows past M and columns past N are clipped)
 };
 
@@ -82,7 +89,7 @@ struct Args {
   const void* offsets;   // jagged mode: seq_offsets (to find the first row no sequence owns)
   int off64, num_seqs;
   int per_seq_bias;      // bias row = sequence index (else: output row index, or the single row when bias_rs == 0)
-  int dbg;  // instrumented builds only (B200_GEMM_DBG): 1 no W loads / waits, 2 no output staging, 4 no MMAs, 8 N=128 MMAs
+  int dbg;  // instrumented builds only (B200_GEMM_DBG): 1 no W loads / waits, 2 no output staging, 4 no MMAs
 };
 
 using vec::load8;
@@ -90,6 +97,7 @@ using vec::warp_sum;
 template <bool BF16> __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return BF16 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
 }
+
 template <bool BF16>
 __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant__ Maps maps, Args a) {
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
@@ -97,8 +105,7 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
   Shared& sh = *reinterpret_cast<Shared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort_flag = &sh.abort_flag;
-  const int kboxes = a.K / 64;   // 64-column boxes of the A operand
-  const int kstages = a.K / BK;  // pipeline stages of W per output tile
+  const int kboxes = a.K / 64;   // 64-column boxes of the A operand = pipeline stages of W per output tile
   const int n_tiles = (a.N + BN - 1) / BN;
   const long long n_blocks = a.items ? static_cast<long long>(*a.n_items) : (a.M + BM - 1) / BM;
   // block -> (sequence, first row, valid rows); plain mode: one "sequence" holding every row
@@ -110,9 +117,11 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
 
   if (threadIdx.x == 0) {
     sh.abort_flag = 0;
-    mbar_init(smem_u32(&sh.a_full), a.fuse_ln ? 256 : 1);
-    mbar_init(smem_u32(&sh.a_empty), 1);
-    for (int i = 0; i < B_STAGES; ++i) { mbar_init(smem_u32(&sh.b_full[i]), 1); mbar_init(smem_u32(&sh.b_empty[i]), 1); }
+    mbar_init(smem_u32(&sh.x_full), 1);
+    mbar_init(smem_u32(&sh.x_free), 128);  // the 128 threads that copy a 64-row round
+    mbar_init(smem_u32(&sh.a_ready), 256);
+    mbar_init(smem_u32(&sh.a_free), 1);
+    for (int i = 0; i < W_STAGES; ++i) { mbar_init(smem_u32(&sh.w_full[i]), 1); mbar_init(smem_u32(&sh.w_empty[i]), 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(smem_u32(&sh.acc_full[i]), 1); mbar_init(smem_u32(&sh.acc_empty[i]), 256); }
     fence_barrier_init();
     fence_proxy_async();
@@ -129,56 +138,65 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) { prefetch_tensormap(&maps.w); if (!a.fuse_ln) prefetch_tensormap(&maps.x); }
-    uint32_t it = 0, st = 0, ph = 0;
+    uint32_t round = 0, st = 0, ph = 0;
     bool ok = true;
     auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_GEMM_PRODUCER));
     };
-    for (long long blk = blockIdx.x; blk < n_blocks && ok; blk += gridDim.x, ++it) {
+    // x of a block arrives in two rounds of 64 rows through the staging buffer (plain and jagged mode)
+    auto load_x_round = [&](const int4& bi, int r) -> bool {
+      if (!wait_all(&sh.x_free, (round & 1) ^ 1)) return false;
+      if (elect_one()) {
+        mbar_arrive_expect_tx(smem_u32(&sh.x_full), static_cast<uint32_t>(kboxes) * X_BOX_BYTES);
+        for (int kb = 0; kb < kboxes; ++kb)
+          tma_load_2d(smem_u32(sh.x[kb]), &maps.x, smem_u32(&sh.x_full), kb * 64, bi.y + r * X_ROWS);
+      }
+      __syncwarp();
+      ++round;
+      return true;
+    };
+    long long blk = blockIdx.x;
+    if (!a.fuse_ln && blk < n_blocks) ok = load_x_round(block_of(blk), 0);
+    for (; blk < n_blocks && ok; blk += gridDim.x) {
       const int4 bi = block_of(blk);
       const int w_row0 = bi.x * a.K;  // first row of this sequence's matrix in the stacked [B * K, N] weights
-      if (!a.fuse_ln) {
-        ok = wait_all(&sh.a_empty, (it & 1) ^ 1);
-        if (!ok) break;
-        if (elect_one()) {
-          mbar_arrive_expect_tx(smem_u32(&sh.a_full), static_cast<uint32_t>(kboxes) * A_BOX_BYTES);
-          for (int kb = 0; kb < kboxes; ++kb)
-            tma_load_2d(smem_u32(sh.a[kb]), &maps.x, smem_u32(&sh.a_full), kb * 64, bi.y);
-        }
-        __syncwarp();
-      }
       for (int nt = 0; nt < n_tiles && ok; ++nt) {
-        for (int kb = 0; kb < kstages; ++kb) {
+        for (int kb = 0; kb < kboxes; ++kb) {
 #ifdef B200_HSTU_PROFILING
           if (a.dbg & 1) continue;
 #endif
-          ok = wait_all(&sh.b_empty[st], ph ^ 1);
+          ok = wait_all(&sh.w_empty[st], ph ^ 1);
           if (!ok) break;
           if (elect_one()) {
-            mbar_arrive_expect_tx(smem_u32(&sh.b_full[st]), B_STAGE_BYTES);
+            mbar_arrive_expect_tx(smem_u32(&sh.w_full[st]), W_STAGE_BYTES);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)  // columns past N are filled with zeros
-              tma_load_2d(smem_u32(sh.b[st]) + j * B_BOX_BYTES, &maps.w, smem_u32(&sh.b_full[st]), nt * BN + j * 64,
+            for (int j = 0; j < 2; ++j)  // columns past N are filled with zeros
+              tma_load_2d(smem_u32(sh.w[st]) + j * W_BOX_BYTES, &maps.w, smem_u32(&sh.w_full[st]), nt * BN + j * 64,
                           w_row0 + kb * BK);
           }
           __syncwarp();
-          if (++st == B_STAGES) { st = 0; ph ^= 1; }
+          if (++st == W_STAGES) { st = 0; ph ^= 1; }
         }
+        if (a.fuse_ln || !ok) continue;
+        // Behind the first output tile's weights (they only wait for the previous block's MMAs): the second
+        // 64 rows of this block, as soon as the first 64 have been copied into TMEM.  Behind the second
+        // tile's weights: the next block's first 64 rows, which then land while this block computes.
+        if (nt == 0) ok = load_x_round(bi, 1);
+        if (ok && nt == (n_tiles > 1 ? 1 : 0) && blk + gridDim.x < n_blocks) ok = load_x_round(block_of(blk + gridDim.x), 0);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    constexpr uint32_t IDESC = idesc_f16(BF16 ? 1 : 0, BM, BN, 0, 1);  // A K-major (shared memory), B N-major
+    constexpr uint32_t IDESC = idesc_f16(BF16 ? 1 : 0, BM, BN, 0, 1);  // A from TMEM, B N-major in shared memory
     constexpr uint32_t HI = desc_hi_sw128(1024);
-    const uint32_t a_lo0 = desc_lo_sw128(smem_u32(sh.a[0]), 16);
-    const uint32_t b_lo0 = desc_lo_sw128(smem_u32(sh.b[0]), B_BOX_BYTES);  // 64-column groups are one box apart
+    const uint32_t w_lo0 = desc_lo_sw128(smem_u32(sh.w[0]), W_BOX_BYTES);  // 64-column groups are one box apart
     uint32_t it = 0, st = 0, ph = 0, g = 0;
     bool ok = true;
     auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_GEMM_MMA));
     };
     for (long long blk = blockIdx.x; blk < n_blocks && ok; blk += gridDim.x, ++it) {
-      ok = wait_all(&sh.a_full, it & 1);
+      ok = wait_all(&sh.a_ready, it & 1);
       if (!ok) break;
       tc_fence_after();
       for (int nt = 0; nt < n_tiles && ok; ++nt, ++g) {
@@ -186,67 +204,52 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
         ok = wait_all(&sh.acc_empty[buf], ((g >> 1) & 1) ^ 1);
         if (!ok) break;
         tc_fence_after();
-        for (int kb = 0; kb < kstages; ++kb) {
+        for (int kb = 0; kb < kboxes; ++kb) {
 #ifdef B200_HSTU_PROFILING
           if (a.dbg & 1) {
             if (elect_one() && !(a.dbg & 4)) {
               for (int kk = 0; kk < BK / 16; ++kk)
-                mma_ss(tmem + buf * BN, desc_join(a_lo0 + (kb >> 1) * (A_BOX_BYTES >> 4) + (((kb & 1) << 1) + kk) * 2, HI),
-                       desc_join(b_lo0 + (kb & 3) * (B_STAGE_BYTES >> 4) + kk * (2048 >> 4), HI), IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+                mma_ts(tmem + TMEM_ACC0 + buf * BN, tmem + TMEM_A + (kb * 4 + kk) * 8,
+                       desc_join(w_lo0 + (kb & 7) * (W_STAGE_BYTES >> 4) + kk * (2048 >> 4), HI), IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
             }
             __syncwarp();
             continue;
           }
 #endif
-          ok = wait_all(&sh.b_full[st], ph);
+          ok = wait_all(&sh.w_full[st], ph);
           if (!ok) break;
           tc_fence_after();
-#ifdef B200_HSTU_PROFILING
-          if (a.dbg & (4 | 8)) {
-            if (elect_one()) {
-              if (a.dbg & 8) {
-                constexpr uint32_t IDESC_H = idesc_f16(BF16 ? 1 : 0, BM, 128, 0, 1);
-                for (int kk = 0; kk < BK / 16; ++kk)
-                  for (int hh = 0; hh < 2; ++hh)
-                    mma_ss(tmem + buf * BN + hh * 128,
-                           desc_join(a_lo0 + (kb >> 1) * (A_BOX_BYTES >> 4) + (((kb & 1) << 1) + kk) * 2, HI),
-                           desc_join(b_lo0 + st * (B_STAGE_BYTES >> 4) + hh * (2 * B_BOX_BYTES >> 4) + kk * (2048 >> 4), HI),
-                           IDESC_H, (kb > 0 || kk > 0) ? 1u : 0u);
-              }
-              tc_commit(smem_u32(&sh.b_empty[st]));
-            }
-            __syncwarp();
-            if (++st == B_STAGES) { st = 0; ph ^= 1; }
-            continue;
-          }
-#endif
           if (elect_one()) {
+#ifdef B200_HSTU_PROFILING
+            if (!(a.dbg & 4))
+#endif
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk)
-              // A: box kb / 2, k-step ((kb % 2) * 2 + kk) of its four (32 bytes each); B: k-step kk of the stage
-              mma_ss(tmem + buf * BN, desc_join(a_lo0 + (kb >> 1) * (A_BOX_BYTES >> 4) + (((kb & 1) << 1) + kk) * 2, HI),
-                     desc_join(b_lo0 + st * (B_STAGE_BYTES >> 4) + kk * (2048 >> 4), HI), IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
-            tc_commit(smem_u32(&sh.b_empty[st]));
+              // A: 16 k-values = 8 TMEM columns; B: k-step kk of the stage (16 rows of 128 bytes per box)
+              mma_ts(tmem + TMEM_ACC0 + buf * BN, tmem + TMEM_A + (kb * 4 + kk) * 8,
+                     desc_join(w_lo0 + st * (W_STAGE_BYTES >> 4) + kk * (2048 >> 4), HI), IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+            tc_commit(smem_u32(&sh.w_empty[st]));
           }
           __syncwarp();
-          if (++st == B_STAGES) { st = 0; ph ^= 1; }
+          if (++st == W_STAGES) { st = 0; ph ^= 1; }
         }
         if (!ok) break;
         if (elect_one()) tc_commit(smem_u32(&sh.acc_full[buf]));
         __syncwarp();
       }
       if (!ok) break;
-      if (elect_one()) tc_commit(smem_u32(&sh.a_empty));  // every MMA that reads this block's A has been issued
+      if (elect_one()) tc_commit(smem_u32(&sh.a_free));  // every MMA that reads this block's A operand has been issued
       __syncwarp();
     }
   } else if (warp >= 2) {
     // ------------------------------------------------------------------ prologue + epilogue warps (2..9)
     const int ew = warp - 2;                  // 0..7
-    const int wg = ew >> 2;                   // column half of the output tile
-    const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) << 5) << 16;
-    const int row_in_blk = ((warp & 3) << 5) | lane;
+    const int wg = ew >> 2;                   // column half of the output tile / k half of the A operand
+    const int quad = warp & 3;                // TMEM lane quadrant this warp may touch
+    const uint32_t lane_addr = static_cast<uint32_t>(quad << 5) << 16;
+    const int row_in_blk = (quad << 5) | lane;
     const int nv = a.K >> 3;  // 16-byte vectors per row (at most 64: two per lane)
-    uint32_t it = 0, g = 0;
+    uint32_t it = 0, g = 0, round = 0;
     bool ok = true;
     if (a.items) {
       // rows at or past the last offset belong to no sequence: defined output (zeros), never stale memory
@@ -271,194 +274,189 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
         lnb[j] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.ln_b) + 8 * v));
       }
     }
+    // Copies this thread's row of the staged 64-row round into the A operand in TMEM: warps of lane quadrants
+    // 2 r and 2 r + 1 own the rows of round r; group wg copies k-columns [K/2 wg, K/2 wg + K/2).
+    auto copy_round_to_tmem = [&](int r) {
+      if ((quad >> 1) != r) return;
+      const int rl = row_in_blk - r * X_ROWS;  // row inside the staging buffer
+      const int boxes_half = kboxes >> 1, b0 = wg * boxes_half, b1 = (wg == 0) ? boxes_half : kboxes;
+      for (int b = b0; b < b1; ++b) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // 2 x 32 elements = 2 x 16 TMEM columns per 64-column box
+          uint32_t rr[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int chunk = h * 4 + j;
+            const uint4 xq = *reinterpret_cast<const uint4*>(sh.x[b] + rl * 128 + ((chunk ^ (rl & 7)) << 4));
+            rr[4 * j + 0] = xq.x; rr[4 * j + 1] = xq.y; rr[4 * j + 2] = xq.z; rr[4 * j + 3] = xq.w;
+          }
+          tmem_st16(tmem + lane_addr + TMEM_A + b * 32 + h * 16, rr);
+        }
+      }
+    };
     for (long long blk = blockIdx.x; blk < n_blocks && ok; blk += gridDim.x, ++it) {
-      if (a.fuse_ln) {
-        // ---- layer norm of 16 rows per warp, four rows at a time, into the swizzled A operand
-        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.a_empty), (it & 1) ^ 1, abort_flag, a.status, WAIT_GEMM_EPILOGUE));
-        if (!ok) break;
-        for (int r0 = 0; r0 < 16; r0 += 4) {
-          float xv[4][2][8];
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const long long row = blk * BM + ew * 16 + r0 + r;
-            const T* xr = reinterpret_cast<const T*>(a.x) + (row < a.M ? row : a.M - 1) * a.x_rs;
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const int v = lane + 32 * j;
-              if (v < nv) {
-                load8<T>(xr + 8 * v, xv[r][j]);
-              } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) xv[r][j][i] = 0.f;
-              }
-            }
-          }
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const int rb = ew * 16 + r0 + r;  // row inside the block
-            const long long row = blk * BM + rb;
-            // mean first, then the mean of squared deviations (kjt_split_per_feature.cpp:223-226)
-            float s = 0.f;
-#pragma unroll
-            for (int j = 0; j < 2; ++j)
-              if (lane + 32 * j < nv) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) s += xv[r][j][i];
-              }
-            const float mean = warp_sum(s) / static_cast<float>(a.K);
-            float q = 0.f;
-#pragma unroll
-            for (int j = 0; j < 2; ++j)
-              if (lane + 32 * j < nv) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) { const float d = xv[r][j][i] - mean; q += d * d; }
-              }
-            const float rstd = rsqrtf(warp_sum(q) / static_cast<float>(a.K) + a.eps);
-            if (lane == 0 && row < a.M) { a.mean[row] = mean; a.rstd[row] = rstd; }
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const int v = lane + 32 * j;
-              if (v >= nv) continue;
-              uint4 pk = make_uint4(0u, 0u, 0u, 0u);  // rows past M enter the product as zeros
-              if (row < a.M) {
-                float n[8], wv[8], bv[8];
-                vec::unpack8<T>(lnw[j], wv);
-                vec::unpack8<T>(lnb[j], bv);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  float y = (xv[r][j][i] - mean) * rstd;
-                  if (a.affine) y = y * wv[i] + bv[i];
-                  if (a.swish) y = __fdividef(1.f, 1.f + __expf(-y)) * xv[r][j][i];
-                  n[i] = y;
-                }
-                pk.x = pack2<BF16>(n[0], n[1]); pk.y = pack2<BF16>(n[2], n[3]);
-                pk.z = pack2<BF16>(n[4], n[5]); pk.w = pack2<BF16>(n[6], n[7]);
-              }
-              // vector v = 8 columns: box v / 8, 16-byte chunk v % 8 of the 128-byte box row, swizzled
-              unsigned char* dst = sh.a[v >> 3] + rb * 128 + (((v & 7) ^ (rb & 7)) << 4);
-              *reinterpret_cast<uint4*>(dst) = pk;
-            }
-          }
-        }
-        fence_proxy_async();
-        mbar_arrive(smem_u32(&sh.a_full));
-      }
-      if (a.fuse_ln) {
-        // pull the rows of this CTA's NEXT block towards L2 while the tensor cores work on this one, so that
-        // the next prologue's loads (four dependent batches of four rows per warp) pay L2 instead of HBM latency
-        const long long nblk = blk + gridDim.x;
-        if (nblk < n_blocks) {
-          const int tid = threadIdx.x - 64;  // 0..255: two threads per row, alternating 128-byte lines
-          const long long prow = nblk * BM + (tid >> 1);
-          if (prow < a.M) {
-            const char* base = reinterpret_cast<const char*>(a.x) + prow * a.x_rs * static_cast<long long>(sizeof(T));
-            for (int off = (tid & 1) * 128; off < a.K * static_cast<int>(sizeof(T)); off += 256)
-              asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
-          }
-        }
-      }
-      // ---- epilogue of every output tile of the block: bias, rounding, staged bulk stores.
-      // Group wg owns output columns [128 wg, 128 wg + 128) of the tile and sends them out as two boxes of
-      // 64 columns through its own staging buffer (128-byte-swizzled rows, as the bulk tensor store expects);
-      // a thread-per-row store straight to global memory would be 32 separate 16-byte transactions per
-      // instruction, which costs more than the MMAs of the tile.
       const int4 bi = block_of(blk);
+      // ---- A operand of the block into TMEM, 64 rows at a time through the staging buffer
+      for (int r = 0; r < 2 && ok; ++r, ++round) {
+        if (a.fuse_ln) {
+          // layer norm of 8 rows per warp (four at a time in registers) into the swizzled staging boxes
+          for (int r0 = 0; r0 < 8; r0 += 4) {
+            float xv[4][2][8];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const long long row = static_cast<long long>(bi.y) + r * X_ROWS + ew * 8 + r0 + q;
+              const T* xr = reinterpret_cast<const T*>(a.x) + (row < a.M ? row : a.M - 1) * a.x_rs;
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                const int v = lane + 32 * j;
+                if (v < nv) {
+                  load8<T>(xr + 8 * v, xv[q][j]);
+                } else {
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) xv[q][j][i] = 0.f;
+                }
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int rl = ew * 8 + r0 + q;  // row inside the staging buffer
+              const long long row = static_cast<long long>(bi.y) + r * X_ROWS + rl;
+              // mean first, then the mean of squared deviations (kjt_split_per_feature.cpp:223-226)
+              float s = 0.f;
+#pragma unroll
+              for (int j = 0; j < 2; ++j)
+                if (lane + 32 * j < nv) {
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) s += xv[q][j][i];
+                }
+              const float mean = warp_sum(s) / static_cast<float>(a.K);
+              float sq = 0.f;
+#pragma unroll
+              for (int j = 0; j < 2; ++j)
+                if (lane + 32 * j < nv) {
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) { const float d = xv[q][j][i] - mean; sq += d * d; }
+                }
+              const float rstd = rsqrtf(warp_sum(sq) / static_cast<float>(a.K) + a.eps);
+              if (lane == 0 && row < a.M) { a.mean[row] = mean; a.rstd[row] = rstd; }
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                const int v = lane + 32 * j;
+                if (v >= nv) continue;
+                uint4 pk = make_uint4(0u, 0u, 0u, 0u);  // rows past M enter the product as zeros
+                if (row < a.M) {
+                  float n[8], wv[8], bv[8];
+                  vec::unpack8<T>(lnw[j], wv);
+                  vec::unpack8<T>(lnb[j], bv);
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) {
+                    float y = (xv[q][j][i] - mean) * rstd;
+                    if (a.affine) y = y * wv[i] + bv[i];
+                    if (a.swish) y = __fdividef(1.f, 1.f + __expf(-y)) * xv[q][j][i];
+                    n[i] = y;
+                  }
+                  pk.x = pack2<BF16>(n[0], n[1]); pk.y = pack2<BF16>(n[2], n[3]);
+                  pk.z = pack2<BF16>(n[4], n[5]); pk.w = pack2<BF16>(n[6], n[7]);
+                }
+                // vector v = 8 columns: box v / 8, 16-byte chunk v % 8 of the 128-byte box row, swizzled
+                *reinterpret_cast<uint4*>(sh.x[v >> 3] + rl * 128 + (((v & 7) ^ (rl & 7)) << 4)) = pk;
+              }
+            }
+          }
+          asm volatile("bar.sync 3, 256;" ::: "memory");  // the 64 rows are staged
+        } else {
+          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.x_full), round & 1, abort_flag, a.status, WAIT_GEMM_EPILOGUE));
+          if (!ok) break;
+        }
+        if (r == 0) {  // the previous block's MMAs must have finished reading the A operand before it is overwritten
+          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.a_free), (it & 1) ^ 1, abort_flag, a.status, WAIT_GEMM_EPILOGUE));
+          if (!ok) break;
+          tc_fence_after();
+        }
+        copy_round_to_tmem(r);
+        if (a.fuse_ln) {
+          asm volatile("bar.sync 3, 256;" ::: "memory");  // the staging buffer may be overwritten
+        } else if ((quad >> 1) == r) {
+          mbar_arrive(smem_u32(&sh.x_free));  // the round has been read: the next one may land
+        }
+      }
+      if (!ok) break;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&sh.a_ready));
+      // ---- epilogue of every output tile of the block: bias, rounding, staged bulk stores.
+      // Group wg owns output columns [64 wg, 64 wg + 64) of the tile and sends them out as one box through
+      // its own staging buffer (128-byte-swizzled rows, as the bulk tensor store expects).
       const long long row = static_cast<long long>(bi.y) + row_in_blk;
       const long long brow_idx = a.per_seq_bias ? bi.x : (row < a.M ? row : a.M - 1);
       unsigned char* stage = sh.out[wg];
       for (int nt = 0; nt < n_tiles && ok; ++nt, ++g) {
         const uint32_t buf = g & 1;
+        const int col0 = nt * BN + wg * 64;
+        // The bias of this box first (eight 16-byte loads in flight together, raw): with nearly all of the
+        // SM's L1 carved out as shared memory they come from L2, and one dependent load per use costs more
+        // than the rest of the box.
+        uint4 braw[8];
+        {
+          const T* brow = reinterpret_cast<const T*>(a.bias) + brow_idx * a.bias_rs + col0;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            braw[j] = (col0 + 8 * j < a.N) ? __ldg(reinterpret_cast<const uint4*>(brow + 8 * j)) : make_uint4(0u, 0u, 0u, 0u);
+        }
         ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.acc_full[buf]), (g >> 1) & 1, abort_flag, a.status, WAIT_GEMM_EPILOGUE));
         if (!ok) break;
         tc_fence_after();
-        const uint32_t acc = tmem + lane_addr + buf * BN + wg * 128;
+        const uint32_t acc = tmem + lane_addr + TMEM_ACC0 + buf * BN + wg * 64;
+        uint32_t v0[32], v1[32];
+        tmem_ld32(acc, v0);
+        tmem_ld32(acc + 32, v1);
+        tmem_wait_ld(v0);
+        tmem_wait_ld(v1);
+        tc_fence_before();
+        mbar_arrive(smem_u32(&sh.acc_empty[buf]));  // the accumulator is in registers: the MMAs may reuse it
+        if (col0 >= a.N) continue;  // uniform for the group
+#ifdef B200_HSTU_PROFILING
+        if (a.dbg & 2) continue;
+#endif
+        if (row_in_blk == 0) bulk_wait_read_all();  // the group's previous box has left the staging buffer
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
+        unsigned char* my_row = stage + row_in_blk * 128;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int col0 = nt * BN + wg * 128 + h * 64;
-          // The bias of this box first (eight 16-byte loads in flight together, raw): with nearly all of the
-          // SM's L1 carved out as shared memory they come from L2, and one dependent load per use costs more
-          // than the rest of the box.
-          uint4 braw[8];
-          {
-            const T* brow = reinterpret_cast<const T*>(a.bias) + brow_idx * a.bias_rs + col0;
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              braw[j] = (col0 + 8 * j < a.N) ? __ldg(reinterpret_cast<const uint4*>(brow + 8 * j)) : make_uint4(0u, 0u, 0u, 0u);
-          }
-          uint32_t v0[32], v1[32];
-          tmem_ld32(acc + h * 64, v0);
-          tmem_ld32(acc + h * 64 + 32, v1);
-          tmem_wait_ld(v0);
-          tmem_wait_ld(v1);
-          if (h == 1) {
-            tc_fence_before();
-            mbar_arrive(smem_u32(&sh.acc_empty[buf]));  // the accumulator is in registers: the MMAs may reuse it
-          }
-          if (col0 >= a.N) continue;  // uniform for the group
-#ifdef B200_HSTU_PROFILING
-          if (a.dbg & 2) continue;
-#endif
-#ifdef B200_HSTU_PROFILING
-          long long tq0 = 0, tq1 = 0, tq2 = 0, tq3 = 0, tq4 = 0;
-          const bool tr = (a.dbg & 32) && blockIdx.x == 0 && threadIdx.x == 64 && g < 12;
-          if (tr) tq0 = clock64();
-#endif
-          if (row_in_blk == 0) bulk_wait_read_all();  // the group's previous box has left the staging buffer
-          asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");
-#ifdef B200_HSTU_PROFILING
-          if (tr) tq1 = clock64();
-#endif
-          unsigned char* my_row = stage + row_in_blk * 128;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint32_t* v = j < 4 ? v0 : v1;
-            const int jj = j & 3;
-            float bf[8];
-            vec::unpack8<T>(braw[j], bf);
-            uint4 o;
-            o.x = pack2<BF16>(__uint_as_float(v[8 * jj + 0]) + bf[0], __uint_as_float(v[8 * jj + 1]) + bf[1]);
-            o.y = pack2<BF16>(__uint_as_float(v[8 * jj + 2]) + bf[2], __uint_as_float(v[8 * jj + 3]) + bf[3]);
-            o.z = pack2<BF16>(__uint_as_float(v[8 * jj + 4]) + bf[4], __uint_as_float(v[8 * jj + 5]) + bf[5]);
-            o.w = pack2<BF16>(__uint_as_float(v[8 * jj + 6]) + bf[6], __uint_as_float(v[8 * jj + 7]) + bf[7]);
-            *reinterpret_cast<uint4*>(my_row + ((j ^ (row_in_blk & 7)) << 4)) = o;
-          }
-#ifdef B200_HSTU_PROFILING
-          if (tr) tq2 = clock64();
-#endif
-          fence_proxy_async();
-#ifdef B200_HSTU_PROFILING
-          if (tr) tq3 = clock64();
-#endif
-          asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");  // the box is staged
-          if (bi.z >= BM || !a.items) {
-            // whole block (in plain mode the tensor map clips rows past M): one bulk tensor store
-            if (row_in_blk == 0) {
-              tma_store_2d(&maps.o, smem_u32(stage), col0, bi.y);
-              bulk_commit();
-            }
-          } else {
-            // ragged last block of a sequence: the rows behind it belong to the next sequence, so the valid
-            // rows are copied out by the threads (8 lanes per 128-byte row segment)
-            const int chunk = row_in_blk & 7;
-            if (col0 + chunk * 8 < a.N) {
-              T* obase = reinterpret_cast<T*>(a.out) + static_cast<long long>(bi.y) * a.out_rs + col0 + chunk * 8;
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const int r = i * 16 + (row_in_blk >> 3);
-                if (r < bi.z)
-                  *reinterpret_cast<uint4*>(obase + static_cast<long long>(r) * a.out_rs) =
-                      *reinterpret_cast<const uint4*>(stage + r * 128 + ((chunk ^ (r & 7)) << 4));
-              }
-            }
-          }  // (the barrier at the top of the next box orders these reads before its writes)
-#ifdef B200_HSTU_PROFILING
-          if (tr) {
-            tq4 = clock64();
-            printf("box g=%u h=%d: wait_read+bar %lld, bias+math+st.shared %lld, fence %lld, bar+tma %lld | t=%lld\n", g, h,
-                   tq1 - tq0, tq2 - tq1, tq3 - tq2, tq4 - tq3, tq4);
-          }
-#endif
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t* v = j < 4 ? v0 : v1;
+          const int jj = j & 3;
+          float bf[8];
+          vec::unpack8<T>(braw[j], bf);
+          uint4 o;
+          o.x = pack2<BF16>(__uint_as_float(v[8 * jj + 0]) + bf[0], __uint_as_float(v[8 * jj + 1]) + bf[1]);
+          o.y = pack2<BF16>(__uint_as_float(v[8 * jj + 2]) + bf[2], __uint_as_float(v[8 * jj + 3]) + bf[3]);
+          o.z = pack2<BF16>(__uint_as_float(v[8 * jj + 4]) + bf[4], __uint_as_float(v[8 * jj + 5]) + bf[5]);
+          o.w = pack2<BF16>(__uint_as_float(v[8 * jj + 6]) + bf[6], __uint_as_float(v[8 * jj + 7]) + bf[7]);
+          *reinterpret_cast<uint4*>(my_row + ((j ^ (row_in_blk & 7)) << 4)) = o;
         }
+        fence_proxy_async();
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + wg) : "memory");  // the box is staged
+        if (bi.z >= BM || !a.items) {
+          // whole block (in plain mode the tensor map clips rows past M): one bulk tensor store
+          if (row_in_blk == 0) {
+            tma_store_2d(&maps.o, smem_u32(stage), col0, bi.y);
+            bulk_commit();
+          }
+        } else {
+          // ragged last block of a sequence: the rows behind it belong to the next sequence, so the valid
+          // rows are copied out by the threads (8 lanes per 128-byte row segment)
+          const int chunk = row_in_blk & 7;
+          if (col0 + chunk * 8 < a.N) {
+            T* obase = reinterpret_cast<T*>(a.out) + static_cast<long long>(bi.y) * a.out_rs + col0 + chunk * 8;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int r = i * 16 + (row_in_blk >> 3);
+              if (r < bi.z)
+                *reinterpret_cast<uint4*>(obase + static_cast<long long>(r) * a.out_rs) =
+                    *reinterpret_cast<const uint4*>(stage + r * 128 + ((chunk ^ (r & 7)) << 4));
+            }
+          }
+        }  // (the barrier at the top of the next box orders these reads before its writes)
       }
     }
     if (row_in_blk == 0) bulk_wait_all();  // shared memory must outlive the stores that read it
@@ -475,7 +473,6 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
     tmem_dealloc(tmem, TMEM_COLS);
   }
 }
-
 
 // Row blocks of a jagged batch: entry i = (sequence, first row, valid rows) for every 128-row block of
 // every sequence, in sequence order; ws[0] = number of entries.  One CTA; offsets are clamped into [0, T]
@@ -550,7 +547,7 @@ int launch_gemm(const B200GemmParams* p, const void* w_base, long long w_rows, c
   if (!hstu::tc::make_map_box(&maps.w, w_base, w_rows, p->N, p->w_row_stride, BK, bf16)) return B200_HSTU_ELAUNCH;
   if (!hstu::tc::make_map_box(&maps.o, p->out, p->M, p->N, p->out_row_stride, BM, bf16)) return B200_HSTU_ELAUNCH;
   if (fuse) maps.x = maps.w;  // not used by the kernel
-  else if (!hstu::tc::make_map_box(&maps.x, p->x, p->M, p->K, p->x_row_stride, 128, bf16)) return B200_HSTU_ELAUNCH;
+  else if (!hstu::tc::make_map_box(&maps.x, p->x, p->M, p->K, p->x_row_stride, X_ROWS, bf16)) return B200_HSTU_ELAUNCH;
   Args a;
   a.x = p->x; a.ln_w = p->ln_weight; a.ln_b = p->ln_bias; a.bias = p->bias; a.out = p->out;
   a.mean = p->mean; a.rstd = p->rstd; a.status = p->status;
