@@ -16,7 +16,7 @@
  * Conventions of b200_hstu.h: plain pointers and sizes, caller-owned buffers, nothing allocated or
  * synchronised, launches go to the given stream, negative B200_HSTU_E* codes on error; status (optional,
  * device int32[4], zeroed by the caller) receives in status[1] the code of a pipeline wait that gave up
- * (111 producer, 112 MMA issuer, 113 epilogue).
+ * (111 producer, 112 MMA issuer, 113 epilogue; 114: shared memory not 1024-byte aligned, nothing ran).
  */
 #ifndef B200_STU_GEMM_H
 #define B200_STU_GEMM_H
