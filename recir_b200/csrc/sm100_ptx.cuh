@@ -42,21 +42,8 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                "r"(bytes)
                : "memory");
 }
-// A translation unit that defines SM100_TRY_WAIT_HINT_NS before including this header lets the hardware
-// keep a waiting thread suspended for up to that many nanoseconds per attempt (it still wakes when the
-// phase completes): warps that poll in a tight loop otherwise take issue slots from the warps of their
-// SM sub-partition that have work to do.
 __device__ __forceinline__ uint32_t mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t done;
-#ifdef SM100_TRY_WAIT_HINT_NS
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(bar), "r"(parity), "r"(static_cast<uint32_t>(SM100_TRY_WAIT_HINT_NS))
-      : "memory");
-#else
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
@@ -64,7 +51,6 @@ __device__ __forceinline__ uint32_t mbar_try_wait(uint32_t bar, uint32_t parity)
       : "=r"(done)
       : "r"(bar), "r"(parity)
       : "memory");
-#endif
   return done;
 }
 __device__ __forceinline__ unsigned long long globaltimer_ns() {

@@ -10,19 +10,26 @@
 //
 // Tiling.  A CTA owns a block of 128 rows and keeps its whole A operand (K <= 512) in tensor memory:
 // 16 k-values of a row are 8 TMEM columns, so K = 512 takes 256 of the 512 columns; the other 256 are two
-// 128-column fp32 accumulators.  The rows reach TMEM 64 at a time through a 64 KB staging buffer in the
-// 128-byte-swizzled box layout: written by TMA (plain and jagged mode) or by the layer-norm prologue, then
-// copied row-per-thread with tcgen05.st by the warps whose TMEM lane quadrant holds those rows.  W streams
-// through an 8-stage ring of [64 k-rows x 128 n-columns] tiles (TMA, two 64-column boxes, N-major B
-// operand); four tcgen05.mma M128 N128 K16 (A from TMEM) per stage.  The epilogue of an output tile (bias,
-// rounding, staged bulk tensor stores) overlaps the MMAs of the next one.  With A out of shared memory the
-// MMAs read only W from it, half of what the SS form reads, and the ring is deep enough (128 KB) to ride
-// out the L2 latency of W, which stays L2-resident (K x N x 2 bytes, a few MB at most).
+// 128-column fp32 accumulators.  The rows of the NEXT block are parked in shared memory while the current
+// one computes (128 x K, 128-byte-swizzled boxes of 64 columns): landed there by TMA, and with the
+// layer-norm prologue normalised there in place by two dedicated warps; when the last accumulator of the
+// current block is complete they are copied row-per-thread into TMEM (tcgen05.st, by the warps whose TMEM
+// lane quadrant holds those rows) BEFORE that accumulator is drained, so the MMAs of the next block start
+// under the drain.  W streams through a ring of [64 k-rows x 128 n-columns] tiles (TMA, N-major B operand)
+// in whatever shared memory is left (64 KB at K = 512); four tcgen05.mma K16 (A from TMEM) per stage.  The
+// epilogue of an output tile (bias, rounding, staged bulk tensor stores) overlaps the MMAs of the next one.
 //
-// Warp roles (320 threads): warp 0 = TMA producer, warp 1 = MMA issuer (one elected lane), warps 2-9 =
-// layer-norm prologue (8 rows per warp and round, four at a time in registers), staging-to-TMEM copy and
-// epilogue (TMEM lane quadrant warp % 4, column half (warp - 2) / 4).  Every wait is bounded (see
-// sm100_ptx.cuh).
+// CTA pairs.  Outside the jagged mode two CTAs (a cluster on the two SMs of a TPC) work on 256 consecutive
+// rows with ONE tcgen05.mma.cta_group::2 M256 N128 K16 per k-step, issued by the CTA of rank 0; each CTA
+// then loads only its half of every W tile (64 of the 128 columns).  W is L2-resident (K x N x 2 bytes, a
+// few MB at most) but every 128-row block reads all of it, and that L2 -> SM stream is what bounds a
+// single-CTA kernel of this shape; the pair halves it.  Nothing is broadcast: each CTA's TMA loads land in
+// its own shared memory and only mbarrier arrivals / byte counts cross to the peer.
+//
+// Warp roles (384 threads): warp 0 = TMA producer, warp 1 = MMA issuer (one elected lane; in a pair only
+// rank 0 issues), warps 2-9 = A-operand install and epilogue (TMEM lane quadrant warp % 4, column half
+// (warp - 2) / 4), warps 10-11 = layer norm (idle without it).  Every wait is bounded (see sm100_ptx.cuh);
+// the waits off the critical path sleep between polls.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -59,7 +66,7 @@ constexpr int THREADS = 384;                 // 12 warps, 168 registers each
 constexpr int TMEM_COLS = 512;
 constexpr int TMEM_A = 0, TMEM_ACC0 = 256;   // A operand: K / 2 columns (two 16-bit values each); 2 x 128 accumulator columns
 constexpr int LN_WARPS = 2;                  // warps 10 and 11 normalise the next block's rows (layer-norm prologue)
-constexpr int LN_BATCH = 2;                  // rows a layer-norm warp has in flight per batch (two batches in registers)
+constexpr int LN_BATCH = 2;                  // rows a layer-norm warp takes through every stage together
 enum { WAIT_GEMM_PRODUCER = 111, WAIT_GEMM_MMA = 112, WAIT_GEMM_EPILOGUE = 113, WAIT_GEMM_LAYOUT = 114 };
 
 // Barriers and the like, in the first KB of the (1024-byte aligned) shared memory; behind it the data:
@@ -524,15 +531,16 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
     uint32_t xr = 0;
     [[maybe_unused]] long long tw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     [[maybe_unused]] const long long t_start_ = clock64();
-    // layer-norm weight and bias of this lane's columns, packed (16 registers) for the whole kernel
-    uint4 lnw[2], lnb[2];
+    // layer-norm weight and bias of this lane's columns, as fp32 in registers for the whole kernel
+    float wv[2][8], bv[2][8];
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const int v = lane + 32 * j;
-      lnw[j] = lnb[j] = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { wv[j][i] = 1.f; bv[j][i] = 0.f; }
       if (a.affine && v < nv) {
-        lnw[j] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.ln_w) + 8 * v));
-        lnb[j] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.ln_b) + 8 * v));
+        vec::unpack8<T>(__ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.ln_w) + 8 * v)), wv[j]);
+        vec::unpack8<T>(__ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(a.ln_b) + 8 * v)), bv[j]);
       }
     }
     // where vector v (8 columns) of row rl lives: box v / 8, 16-byte chunk v % 8 of the 128-byte box row, swizzled
@@ -576,7 +584,7 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
         for (int j = 0; j < 2; ++j)
           if (lane + 32 * j < nv) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) { const float d = xv[q][j][i] - mean[q]; sq += d * d; }
+            for (int i = 0; i < 8; ++i) { const float d = xv[q][j][i] - mean[q]; sq += d * d; if (!a.swish) xv[q][j][i] = d; }
           }
         rstd[q] = sq;
       }
@@ -596,13 +604,12 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
           if (v >= nv) continue;
           uint4 pk = make_uint4(0u, 0u, 0u, 0u);  // rows past M enter the product as zeros
           if (row < a.M) {
-            float n[8], wv[8], bv[8];
-            vec::unpack8<T>(lnw[j], wv);
-            vec::unpack8<T>(lnb[j], bv);
+            float n[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              float y = (xv[q][j][i] - mean[q]) * rstd[q];
-              if (a.affine) y = y * wv[i] + bv[i];
+              // (without the swish gate xv already holds x - mean; with it x itself is needed once more)
+              float y = (a.swish ? xv[q][j][i] - mean[q] : xv[q][j][i]) * rstd[q];
+              y = y * wv[j][i] + bv[j][i];  // (weight 1 and bias 0 without the affine part: exact)
               if (a.swish) y = __fdividef(1.f, 1.f + __expf(-y)) * xv[q][j][i];
               n[i] = y;
             }

@@ -328,6 +328,11 @@ def _addmm_cuda(x, w, y):
     return out
 
 
+# The fused layer norm + projection kernel pays off from about this many multiply-adds per row (K * N): at
+# K = 512 an output width of 1536 (the u | v | q | k projection of an STU layer is 2048 wide).
+FUSED_PROJECTION_MIN_KN = 512 * 1536
+
+
 def _layer_norm_addmm_cuda(x, ln_weight, ln_bias, eps, is_swish, w, bias):
     """``addmm(bias, weighted_layer_norm(x, ln_weight, ln_bias, eps, is_swish)[0], w)`` in one kernel: the
     layer norm is the prologue of the product's A operand, so the normalised activations never travel
@@ -345,6 +350,13 @@ def _layer_norm_addmm_cuda(x, ln_weight, ln_bias, eps, is_swish, w, bias):
         raise ValueError("b200_layer_norm_addmm_fwd serves bfloat16 / float16 with a feature dimension that is a multiple "
                          "of 64 and at most 512, and an output width that is a multiple of 8")
     x, w = _rows2d(x), _rows2d(w)
+    if x.shape[1] * w.shape[1] < FUSED_PROJECTION_MIN_KN:
+        # Too little product per row for the two layer-norm warps of the fused kernel to keep up with its
+        # tensor pipe: the layer-norm kernel (every warp of the GPU on it, at HBM speed) and then the
+        # projection kernel are faster, and give the same bits (both round the normalised rows to the
+        # input dtype before the product).
+        y, mean, rstd = torch.ops.recir.b200_weighted_layer_norm_fwd(x, ln_weight, ln_bias, eps, None, None, is_swish)
+        return _addmm_cuda(y, w, bias), mean, rstd
     bias = bias if bias.dim() == 1 else _rows2d(bias)
     if bias.data_ptr() % 16 != 0:
         bias = bias.clone()

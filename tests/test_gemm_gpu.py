@@ -43,7 +43,11 @@ def _inputs(seed, M, K, N, dtype, bias_2d=False):
 
 F = lambda t: t.float().numpy()
 
-SHAPES = [(300, 64, 96), (128, 512, 256), (1, 128, 8), (777, 512, 2048), (129, 320, 520), (4100, 256, 264)]
+# The last two give every CTA pair of a 148-SM part several 256-row units (the A operand of the next unit is
+# installed under the drain of the last accumulator; barrier parities flip), with three and with one output
+# tile per unit; 777 and 300 rows end in a pair whose second block lies past the end.
+SHAPES = [(300, 64, 96), (128, 512, 256), (1, 128, 8), (777, 512, 2048), (129, 320, 520), (4100, 256, 264),
+          (60001, 512, 384), (45000, 128, 64)]
 
 
 @pytest.mark.parametrize("M,K,N", SHAPES)
@@ -56,9 +60,33 @@ def test_addmm_on_tensor_cores_matches_oracle(M, K, N, dtype):
         _close(got, ro.addmm(F(x), F(w), F(b), dtype), dtype, f"addmm bias_2d={bias_2d}")
 
 
+@pytest.fixture
+def fused_kernel_always(monkeypatch):
+    """The operator hands narrow projections to the layer-norm kernel followed by the projection kernel; the
+    tests of the fused kernel itself switch that off."""
+    from recir_b200 import rowwise_ops
+    monkeypatch.setattr(rowwise_ops, "FUSED_PROJECTION_MIN_KN", 0)
+
+
+def test_narrow_projections_take_the_two_kernel_route_with_the_same_bits(monkeypatch):
+    from recir_b200 import rowwise_ops
+    x, w, b, lw, lb = _inputs(11, 3000, 512, 256, "bfloat16")
+    args = (x.cuda(), lw.cuda(), lb.cuda(), 1e-5, False, w.cuda(), b.cuda())
+    assert 512 * 256 < rowwise_ops.FUSED_PROJECTION_MIN_KN
+    n0 = rowwise_ops.launch_counter
+    two = torch.ops.recir.b200_layer_norm_addmm_fwd(*args)
+    assert rowwise_ops.launch_counter - n0 == 2
+    monkeypatch.setattr(rowwise_ops, "FUSED_PROJECTION_MIN_KN", 0)
+    n0 = rowwise_ops.launch_counter
+    one = torch.ops.recir.b200_layer_norm_addmm_fwd(*args)
+    assert rowwise_ops.launch_counter - n0 == 1
+    for a, c in zip(two, one):
+        assert torch.equal(a, c)
+
+
 @pytest.mark.parametrize("M,K,N", SHAPES)
 @pytest.mark.parametrize("variant", ["plain", "affine", "swish"])
-def test_layer_norm_addmm_fused_matches_oracle_chain(M, K, N, variant):
+def test_layer_norm_addmm_fused_matches_oracle_chain(M, K, N, variant, fused_kernel_always):
     dtype = "bfloat16"
     x, w, b, lw, lb = _inputs(7 * M + K, M, K, N, dtype)
     affine, swish = variant != "plain", variant == "swish"
