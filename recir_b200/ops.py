@@ -52,7 +52,10 @@ _checked = os.environ.get("RECIR_B200_CHECK", "0") not in ("", "0")
 # One persistent status word (device int32[4]) per device, handed to every call.
 _status = {}
 _WAIT_NAMES = {101: "WAIT_PRODUCER (TMA producer warp)", 102: "WAIT_MMA (MMA issuer warp)",
-               103: "WAIT_EPILOGUE (epilogue warps)", 104: "WAIT_SCHEDULER (work-item scheduler warp)"}
+               103: "WAIT_EPILOGUE (epilogue warps)", 104: "WAIT_SCHEDULER (work-item scheduler warp)",
+               111: "projection kernel: TMA producer or layer-norm warps", 112: "projection kernel: MMA issuer warp",
+               113: "projection kernel: epilogue warps",
+               114: "projection kernel: shared memory not 1024-byte aligned (nothing ran)"}
 # Extra C-ABI flags for the backward (benchmark timing of one pass at a time).
 _bwd_extra_flags = 0
 # Kernel launches issued through this module since import (launch accounting for the benchmark).
