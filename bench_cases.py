@@ -225,6 +225,11 @@ def main_rowwise(argv):
                                    3 * el * 2 + 8 * args.rows)
         cases["layer_norm_swish_bwd"] = (lambda: R.b200_weighted_layer_norm_bwd(u, x, w, b, mean, rstd, True),
                                          3 * el * 2 + 8 * args.rows)
+        # gate stage backward: x, u and the incoming gradient read, dx and du written
+        dout = torch.randn_like(x)
+        cases["layer_norm_mul_silu_bwd"] = (
+            lambda: R.b200_layer_norm_mul_dropout_quantization_bwd(dout, x, u, w, b, mean, rstd, False, False, False, "silu"),
+            5 * el * 2 + 8 * args.rows)
     out = {"rows": args.rows, "cols": cols, "dtype": "bf16"}
     for name, (fn, nbytes) in cases.items():
         ms = _timed(fn, args.iters, args.warmup)

@@ -89,6 +89,39 @@ typedef struct B200LayerNormBwdParams {
 size_t b200_stu_layer_norm_bwd_workspace_bytes(int64_t rows, int64_t cols);
 int b200_stu_layer_norm_bwd(const B200LayerNormBwdParams* p, void* stream);
 
+/* Backward of the gate stage (layerNormMulQuantized, recir/ops/kjt_split_per_feature.cpp:558-600), which the
+ * reference differentiates by autograd through the composite: gradients of its saved output
+ * combined = [ (silu(u) or u) | x | layer_norm(x) * act(u) ] (the first two parts as the CONCAT flags say) with
+ * respect to x, u, weight and bias; the fp8 copy and its scale carry no gradient.  With n the layer norm of x,
+ * m = act(u) and d_u | d_x | d_mult the parts of dout:
+ *   dn = d_mult * m,  du = d_mult * n * act'(u) (+ d_u * (silu'(u) or 1)),  dweight / dbias / dx from dn as in
+ *   b200_stu_layer_norm_bwd (+ d_x),
+ * in float32 with one rounding per gradient, deterministically.  flags: B200_ROWWISE_FLAG_SILU_U, _CONCAT_U,
+ * _CONCAT_X, _ACT_SILU, _ACT_SIGMOID as in the forward.  cols a multiple of 8, at most 1024. */
+typedef struct B200LayerNormMulBwdParams {
+  uint32_t struct_size; /* sizeof(B200LayerNormMulBwdParams) */
+  uint32_t flags;
+  int32_t dtype;        /* element type of dout, x, u, weight, bias and of every gradient */
+  int32_t reserved;
+  int64_t rows, cols;   /* of x and u; dout has parts * cols columns */
+  int64_t dout_row_stride, x_row_stride, u_row_stride, dx_row_stride, du_row_stride; /* in elements */
+  const void* dout;     /* [rows, parts * cols] gradient of the forward's saved output */
+  const void* x;        /* [rows, cols] */
+  const void* u;        /* [rows, cols] */
+  const void* weight;   /* [cols] */
+  const void* bias;     /* [cols] */
+  const float* mean;    /* [rows] as returned by the forward */
+  const float* rstd;
+  void* dx;             /* [rows, cols] */
+  void* du;             /* [rows, cols] */
+  void* dweight;        /* [cols] */
+  void* dbias;          /* [cols] */
+  float* workspace;     /* b200_stu_layer_norm_bwd_workspace_bytes(rows, cols) bytes, 16-byte aligned */
+  uint64_t workspace_bytes;
+} B200LayerNormMulBwdParams;
+
+int b200_stu_layer_norm_mul_bwd(const B200LayerNormMulBwdParams* p, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

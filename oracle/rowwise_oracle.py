@@ -113,6 +113,55 @@ def layer_norm_mul_quantized(x, u, weight, bias, eps, dtype="float32", silu_u=Fa
     return combined, mean, rstd, scale, q8
 
 
+def layer_norm_mul_bwd(dout, x, u, weight, bias, eps, dtype="float32", silu_u=False, concat_u=False,
+                       concat_x=False, mul_u_activation="none"):
+    """Gradients of ``layerNormMulQuantized``'s saved output (recir/ops/kjt_split_per_feature.cpp:558-600; the
+    fp8 copy and its scale carry no gradient) with respect to x, u, weight and bias, i.e. what autograd gives
+    through the composite: with n = weighted layer norm of x, m = act(u) and
+    combined = [ (silu(u) or u) | x | n * m ] (the first two parts optional),
+      dn = d_mult * m,   du = d_mult * n * act'(u)  (+ d_u * (silu'(u) or 1) with concat_u),
+      dx = layer-norm backward of dn                (+ d_x with concat_x),   dw, db as for the layer norm.
+    float64 arithmetic, every gradient rounded to ``dtype`` once.  Returns (dx, du, dw, db)."""
+    xf = np.asarray(x, dtype=np.float64)
+    uf = np.asarray(u, dtype=np.float64)
+    g = np.asarray(dout, dtype=np.float64)
+    cols = xf.shape[1]
+    parts = 1 + int(bool(concat_u)) + int(bool(concat_x))
+    assert g.shape == (xf.shape[0], parts * cols)
+    at = 0
+    d_u = d_x = None
+    if concat_u:
+        d_u, at = g[:, at:at + cols], at + cols
+    if concat_x:
+        d_x, at = g[:, at:at + cols], at + cols
+    d_mult = g[:, at:at + cols]
+    mean = xf.mean(axis=1, keepdims=True)
+    c = xf - mean
+    rstd = 1.0 / np.sqrt((c * c).mean(axis=1, keepdims=True) + float(eps))
+    xh = c * rstd
+    w = np.asarray(weight, dtype=np.float64)
+    n = xh * w + np.asarray(bias, dtype=np.float64)
+    s = 1.0 / (1.0 + np.exp(-uf))
+    silu_grad = s * (1.0 + uf * (1.0 - s))
+    if mul_u_activation == "silu":
+        m, dm = uf * s, silu_grad
+    elif mul_u_activation == "sigmoid":
+        m, dm = s, s * (1.0 - s)
+    else:
+        m, dm = uf, np.ones_like(uf)
+    dn = d_mult * m
+    du = d_mult * n * dm
+    if d_u is not None:
+        du = du + d_u * (silu_grad if silu_u else 1.0)
+    dxh = dn * w
+    dx = rstd * (dxh - dxh.mean(axis=1, keepdims=True) - xh * (dxh * xh).mean(axis=1, keepdims=True))
+    if d_x is not None:
+        dx = dx + d_x
+    dw = round_to((dn * xh).sum(axis=0).astype(np.float32), dtype)
+    db = round_to(dn.sum(axis=0).astype(np.float32), dtype)
+    return round_to(dx.astype(np.float32), dtype), round_to(du.astype(np.float32), dtype), dw, db
+
+
 def e4m3_decode(code):
     """float8 e4m3fn bytes -> float32 (exact)."""
     c = np.asarray(code, dtype=np.uint8).astype(np.int64)

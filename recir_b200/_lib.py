@@ -28,7 +28,7 @@ EXPORTS = (
     "b200_hstu_debug_col_mask", "b200_hstu_last_cuda_error", "b200_hstu_debug_bounded_wait",
     # include/b200_stu_rowwise.h
     "b200_stu_layer_norm_fwd", "b200_stu_layer_norm_mul_fwd", "b200_stu_layer_norm_mul_parts",
-    "b200_stu_layer_norm_bwd", "b200_stu_layer_norm_bwd_workspace_bytes",
+    "b200_stu_layer_norm_bwd", "b200_stu_layer_norm_bwd_workspace_bytes", "b200_stu_layer_norm_mul_bwd",
     # include/b200_stu_gemm.h
     "b200_stu_addmm", "b200_stu_addmm_supported", "b200_stu_jagged_dense_bmm_add", "b200_stu_jagged_bmm_workspace_bytes",
     # include/b200_stu_jagged.h
@@ -105,6 +105,23 @@ class B200LayerNormBwdParams(ctypes.Structure):
         ("dy", ctypes.c_void_p), ("x", ctypes.c_void_p), ("weight", ctypes.c_void_p), ("bias", ctypes.c_void_p),
         ("mean", ctypes.c_void_p), ("rstd", ctypes.c_void_p),
         ("dx", ctypes.c_void_p), ("dweight", ctypes.c_void_p), ("dbias", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
+    ]
+
+
+class B200LayerNormMulBwdParams(ctypes.Structure):
+    """Mirror of ``struct B200LayerNormMulBwdParams`` (include/b200_stu_rowwise.h)."""
+
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32), ("flags", ctypes.c_uint32),
+        ("dtype", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("rows", ctypes.c_int64), ("cols", ctypes.c_int64),
+        ("dout_row_stride", ctypes.c_int64), ("x_row_stride", ctypes.c_int64), ("u_row_stride", ctypes.c_int64),
+        ("dx_row_stride", ctypes.c_int64), ("du_row_stride", ctypes.c_int64),
+        ("dout", ctypes.c_void_p), ("x", ctypes.c_void_p), ("u", ctypes.c_void_p),
+        ("weight", ctypes.c_void_p), ("bias", ctypes.c_void_p),
+        ("mean", ctypes.c_void_p), ("rstd", ctypes.c_void_p),
+        ("dx", ctypes.c_void_p), ("du", ctypes.c_void_p), ("dweight", ctypes.c_void_p), ("dbias", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
     ]
 
@@ -226,6 +243,8 @@ def load() -> ctypes.CDLL:
     lib.b200_stu_layer_norm_mul_parts.restype = ctypes.c_int
     lib.b200_stu_layer_norm_bwd.argtypes = [ctypes.POINTER(B200LayerNormBwdParams), ctypes.c_void_p]
     lib.b200_stu_layer_norm_bwd.restype = ctypes.c_int
+    lib.b200_stu_layer_norm_mul_bwd.argtypes = [ctypes.POINTER(B200LayerNormMulBwdParams), ctypes.c_void_p]
+    lib.b200_stu_layer_norm_mul_bwd.restype = ctypes.c_int
     lib.b200_stu_layer_norm_bwd_workspace_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64]
     lib.b200_stu_layer_norm_bwd_workspace_bytes.restype = ctypes.c_size_t
     GP = ctypes.POINTER(B200GemmParams)

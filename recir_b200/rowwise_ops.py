@@ -16,8 +16,9 @@ Positionally identical to the reference's operators, so the same node-retargetin
 
 ``recir::b200_weighted_layer_norm_fwd`` is differentiable: ``recir::b200_weighted_layer_norm_bwd`` is the
 closed form of what autograd gives through the reference's composite (the reference has no backward
-operator of its own).  ``recir::b200_layer_norm_addmm_fwd`` is differentiable too (composed backward).  The gate stage, the fp8
-variants and the plain projections are forward only.
+operator of its own).  The gate stage is differentiable through its saved output in the same way
+(``recir::b200_layer_norm_mul_dropout_quantization_bwd``), and ``recir::b200_layer_norm_addmm_fwd`` through a
+composed backward.  The fp8 variants and the plain projections are forward only.
 ``recir::b200_layer_norm_addmm_fwd`` fuses the layer norm into the projection behind it (one tcgen05
 kernel, ``csrc/stu_gemm.cu``).  CUDA tensors only; there is no CPU implementation.
 """
@@ -43,6 +44,10 @@ _LIBDEF.define(
 _LIBDEF.define(
     "b200_weighted_layer_norm_bwd(Tensor dy, Tensor x, Tensor? weight, Tensor? bias, Tensor mean, Tensor rstd, "
     "bool is_swish=False) -> (Tensor, Tensor, Tensor)")
+_LIBDEF.define(
+    "b200_layer_norm_mul_dropout_quantization_bwd(Tensor dout, Tensor x, Tensor u, Tensor weight, Tensor bias, "
+    "Tensor mean, Tensor rstd, bool silu_u, bool concat_u, bool concat_x, str mul_u_activation_type) "
+    "-> (Tensor, Tensor, Tensor, Tensor)")
 _LIBDEF.define("b200_addmm_fwd(Tensor x, Tensor w, Tensor y) -> Tensor")
 _LIBDEF.define(
     "b200_layer_norm_addmm_fwd(Tensor x, Tensor? ln_weight, Tensor? ln_bias, float eps, bool is_swish, Tensor w, "
@@ -272,12 +277,89 @@ def _layer_norm_backward(ctx, dy, _dmean, _drstd):
     return dx, (dw if has_w else None), (db if has_w else None), None, None, None, None
 
 
+def _layer_norm_mul_bwd_cuda(dout, x, u, weight, bias, mean, rstd, silu_u, concat_u, concat_x, mul_u_activation_type):
+    """Gradients of the saved output of ``b200_layer_norm_mul_dropout_quantization_fwd`` with respect to x, u,
+    weight and bias: the closed form of what autograd gives through the reference's composite
+    (``recir/ops/kjt_split_per_feature.cpp:558-600``; the fp8 copy and its scale carry no gradient, and like the
+    forward no dropout is applied).  ``dout`` is ``[rows, parts * cols]`` in the forward's part order.  Returns
+    ``(dx, du, dweight, dbias)``.  Feature dimension: a multiple of 8, at most 1024."""
+    global launch_counter
+    _validate(x, weight, bias)
+    if u.shape != x.shape or u.dtype != x.dtype:
+        raise ValueError("u must have the shape and dtype of x")
+    flags = _mul_flags(silu_u, concat_u, concat_x, mul_u_activation_type)
+    parts = 1 + int(bool(concat_u)) + int(bool(concat_x))
+    x, u, dout = _rows2d(x), _rows2d(u), _rows2d(dout)
+    rows, cols = x.shape
+    if dout.shape != (rows, parts * cols) or dout.dtype != x.dtype:
+        raise ValueError("dout must be [rows, parts * cols] in the dtype of x")
+    if mean.numel() != rows or rstd.numel() != rows:
+        raise ValueError("mean and rstd must match the row count")
+    if cols > 1024:
+        raise ValueError("the gate-stage backward serves feature dimensions up to 1024")
+    dx = torch.empty_like(x, memory_format=torch.contiguous_format)
+    du = torch.empty_like(x, memory_format=torch.contiguous_format)
+    dw = torch.empty(cols, dtype=x.dtype, device=x.device)
+    db = torch.empty_like(dw)
+    lib = _lib.load()
+    p = _lib.B200LayerNormMulBwdParams()
+    p.struct_size = ctypes.sizeof(p)
+    p.flags = flags
+    p.dtype = _DTYPES[x.dtype]
+    p.rows, p.cols = rows, cols
+    p.dout, p.x, p.u, p.dx, p.du = dout.data_ptr(), x.data_ptr(), u.data_ptr(), dx.data_ptr(), du.data_ptr()
+    p.dout_row_stride, p.x_row_stride, p.u_row_stride = dout.stride(0), x.stride(0), u.stride(0)
+    p.dx_row_stride, p.du_row_stride = dx.stride(0), du.stride(0)
+    keep = [mean.to(torch.float32).contiguous(), rstd.to(torch.float32).contiguous(),
+            weight.to(x.dtype).contiguous(), bias.to(x.dtype).contiguous()]
+    p.mean, p.rstd, p.weight, p.bias = (t.data_ptr() for t in keep)
+    p.dweight, p.dbias = dw.data_ptr(), db.data_ptr()
+    need = lib.b200_stu_layer_norm_bwd_workspace_bytes(rows, cols)
+    if need:
+        ws = torch.empty(need // 4, dtype=torch.float32, device=x.device)
+        keep.append(ws)
+        p.workspace, p.workspace_bytes = ws.data_ptr(), need
+    with torch.cuda.device(x.device):
+        rc = lib.b200_stu_layer_norm_mul_bwd(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    _check(rc, "b200_stu_layer_norm_mul_bwd")
+    launch_counter += 2 if rows > 0 else 0
+    del keep
+    return dx, du, dw, db
+
+
+def _layer_norm_mul_bwd_fake(dout, x, u, weight, bias, mean, rstd, silu_u, concat_u, concat_x, mul_u_activation_type):
+    return torch.empty_like(x), torch.empty_like(x), x.new_empty((x.shape[1],)), x.new_empty((x.shape[1],))
+
+
+def _layer_norm_mul_setup_context(ctx, inputs, output) -> None:
+    (x, u, weight, bias, _eps, _dropout_ratio, _training, silu_u, concat_u, concat_x, act, _seed, save_y, _block) = inputs
+    _y, mean, rstd, _scale, _q8 = output
+    ctx.save_for_backward(x, u, weight, bias, mean, rstd)
+    ctx.cfg = (silu_u, concat_u, concat_x, act)
+    ctx.save_y = save_y
+
+
+def _layer_norm_mul_backward(ctx, dy, _dmean, _drstd, _dscale, _dq8):
+    x, u, weight, bias, mean, rstd = ctx.saved_tensors
+    if not ctx.save_y:
+        raise RuntimeError("b200_layer_norm_mul_dropout_quantization_fwd: only the saved output (save_y=True) is "
+                           "differentiable; the fp8 copy carries no gradient")
+    silu_u, concat_u, concat_x, act = ctx.cfg
+    dx, du, dw, db = torch.ops.recir.b200_layer_norm_mul_dropout_quantization_bwd(
+        dy.contiguous(), x, u, weight, bias, mean, rstd, silu_u, concat_u, concat_x, act)
+    return (dx, du, dw, db) + (None,) * 10
+
+
 _LIBDEF.impl("b200_weighted_layer_norm_fwd", _layer_norm_cuda, "CUDA")
 _LIBDEF.impl("b200_weighted_layer_norm_bwd", _layer_norm_bwd_cuda, "CUDA")
+_LIBDEF.impl("b200_layer_norm_mul_dropout_quantization_bwd", _layer_norm_mul_bwd_cuda, "CUDA")
+torch.library.register_fake("recir::b200_layer_norm_mul_dropout_quantization_bwd", _layer_norm_mul_bwd_fake)
 torch.library.register_fake("recir::b200_weighted_layer_norm_bwd", _layer_norm_bwd_fake)
 torch.library.register_autograd("recir::b200_weighted_layer_norm_fwd", _layer_norm_backward,
                                 setup_context=_layer_norm_setup_context)
 _LIBDEF.impl("b200_layer_norm_mul_dropout_quantization_fwd", _layer_norm_mul_cuda, "CUDA")
+torch.library.register_autograd("recir::b200_layer_norm_mul_dropout_quantization_fwd", _layer_norm_mul_backward,
+                                setup_context=_layer_norm_mul_setup_context)
 torch.library.register_fake("recir::b200_weighted_layer_norm_fwd", _layer_norm_fake)
 torch.library.register_fake("recir::b200_layer_norm_mul_dropout_quantization_fwd", _layer_norm_mul_fake)
 

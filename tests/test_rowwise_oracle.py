@@ -148,3 +148,31 @@ def test_layer_norm_backward_matches_reference_autograd(name):
         else:
             assert rel.max() <= 2.02 * ULP[dt], (what, float(rel.max()))
             assert (rel > 1.01 * ULP[dt]).mean() <= 5e-3, what
+
+
+MULBWD = np.load(os.path.join(os.path.dirname(__file__), "golden", "layer_norm_mul_bwd_golden.npz"))
+MULBWD_NAMES = sorted({k.split("/")[0] for k in MULBWD.files})
+# relative L2 / largest error over largest value: the composite differentiates through 16-bit intermediates
+# (normalised rows, gate, product each rounded), the restatement is float64 rounded once
+MULBWD_TOL = {"float32": (1e-6, 1e-6), "bfloat16": (6e-3, 8e-3), "float16": (8e-4, 1.5e-3)}
+
+
+def mul_bwd_case(name):
+    dt, silu_u, concat_u, concat_x, act = MULBWD[f"{name}/cfg"]
+    return dt, dict(silu_u=silu_u == "1", concat_u=concat_u == "1", concat_x=concat_x == "1", mul_u_activation=str(act))
+
+
+@pytest.mark.parametrize("name", MULBWD_NAMES)
+def test_gate_stage_backward_matches_reference_autograd(name):
+    """Closed-form gradients of the gate stage (layer norm times act(u), optional pass-through parts) against
+    autograd through the reference's compiled composite (tests/golden/make_layer_norm_mul_bwd_golden.py)."""
+    dt, kw = mul_bwd_case(name)
+    got = ro.layer_norm_mul_bwd(MULBWD[f"{name}/dout"], MULBWD[f"{name}/x"], MULBWD[f"{name}/u"], MULBWD[f"{name}/w"],
+                                MULBWD[f"{name}/b"], 1e-5, dt, **kw)
+    for what, g in zip(("dx", "du", "dw", "db"), got):
+        want = MULBWD[f"{name}/{what}"].astype(np.float64)
+        g = np.asarray(g, np.float64)
+        assert g.shape == want.shape
+        l2, mx = MULBWD_TOL[dt]
+        assert np.linalg.norm(g - want) / np.linalg.norm(want) <= l2, what
+        assert np.abs(g - want).max() / np.abs(want).max() <= mx, what
