@@ -317,6 +317,25 @@ def main_gemm(argv):
     for name, fn in cases.items():
         ms = _timed(fn, args.iters, args.warmup)
         out[name] = {"ms": ms, "TFLOP/s": flops / ms / 1e9, "GB/s": out["algorithmic_bytes_fused"] / ms / 1e6}
+    # the row-wise scaled fp8 projection on the same sizes (a [M, K] and W [N, K] in e4m3, bf16 out):
+    # this library's kernel against the vendor library's fp8 GEMM followed by the scaling pass
+    if K % 128 == 0 and K <= 1024:
+        a8 = (torch.randn(M, K, generator=g, device=dev) * 60.0).clamp(-448, 448).to(torch.float8_e4m3fn)
+        w8 = (torch.randn(N, K, generator=g, device=dev) * 40.0).clamp(-448, 448).to(torch.float8_e4m3fn)
+        sa = torch.rand(M, generator=g, device=dev) * 0.02 + 0.001
+        sb = torch.rand(N, generator=g, device=dev) * 0.01 + 0.001
+        one = torch.ones((), dtype=torch.float32, device=dev)
+
+        def vendor_fp8():
+            o = torch._scaled_mm(a8, w8.t(), scale_a=one, scale_b=one, out_dtype=torch.float32) * sa[:, None] * sb[None, :]
+            return (o + b.float()).to(torch.bfloat16)
+
+        fp8_bytes = M * K + N * K + M * N * 2
+        for name, fn in (("fp8 rowwise addmm (this library)",
+                          lambda: R.b200_fp8_rowwise_addmm_fwd(a8, w8, sa, sb, b, True, False, torch.bfloat16, False, False)),
+                         ("fp8 rowwise addmm (vendor fp8 GEMM, then scales and bias)", vendor_fp8)):
+            ms = _timed(fn, args.iters, args.warmup)
+            out[name] = {"ms": ms, "TFLOP/s": flops / ms / 1e9, "GB/s": fp8_bytes / ms / 1e6}
     print(json.dumps(out))
 
 

@@ -71,6 +71,33 @@ int b200_stu_jagged_dense_bmm_add(const B200GemmParams* p, const void* seq_offse
                                   int64_t w_seq_stride, int per_row_bias, void* workspace, uint64_t workspace_bytes,
                                   void* stream);
 
+/* Row-wise scaled fp8 projection: out = (a * a_scale[:, None]) (b * b_scale[:, None])^T (+ bias), with a [M, K] and
+ * b [N, K] in float8 e4m3 (b is the weight, K-major as the reference takes it) and float32 scales per row of each.
+ * Reference: fp8RowwiseAddMm, recir/ops/kjt_split_per_feature.cpp:533-556 (dequantise, at::mm in float32, add the
+ * bias, cast; schema generative_recommenders::_triton_fp8_rowwise_addmm_fwd_impl).  Here the 8-bit products are
+ * summed in float32 on the tensor cores (tcgen05.mma kind::f8f6f4, the same CTA-pair kernel as b200_stu_addmm)
+ * and each sum is multiplied by its row's and its column's scale before the bias is added and the result
+ * rounded once to bfloat16.  Served: K a multiple of 128 up to 1024, N a multiple of 8, bfloat16 bias [N] (or
+ * NULL) and output, 16-byte aligned bases and row strides (strides in elements). */
+typedef struct B200Fp8GemmParams {
+  uint32_t struct_size; /* sizeof(B200Fp8GemmParams) */
+  uint32_t flags;       /* 0 */
+  int32_t out_dtype;    /* B200_HSTU_BF16 */
+  int32_t reserved;
+  int64_t M, K, N;
+  int64_t a_row_stride, b_row_stride, out_row_stride;
+  const void* a;        /* [M, K] float8 e4m3 */
+  const void* b;        /* [N, K] float8 e4m3 */
+  const float* a_scale; /* [M] */
+  const float* b_scale; /* [N] */
+  const void* bias;     /* [N] bfloat16 or NULL */
+  void* out;            /* [M, N] bfloat16 */
+  int32_t* status;      /* optional, as above */
+} B200Fp8GemmParams;
+
+int b200_stu_fp8_rowwise_addmm_supported(const B200Fp8GemmParams* p);
+int b200_stu_fp8_rowwise_addmm(const B200Fp8GemmParams* p, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -31,6 +31,7 @@ EXPORTS = (
     "b200_stu_layer_norm_bwd", "b200_stu_layer_norm_bwd_workspace_bytes", "b200_stu_layer_norm_mul_bwd",
     # include/b200_stu_gemm.h
     "b200_stu_addmm", "b200_stu_addmm_supported", "b200_stu_jagged_dense_bmm_add", "b200_stu_jagged_bmm_workspace_bytes",
+    "b200_stu_fp8_rowwise_addmm", "b200_stu_fp8_rowwise_addmm_supported",
     # include/b200_stu_jagged.h
     "b200_stu_jagged_copy",
     # include/b200_stu_embed.h
@@ -123,6 +124,19 @@ class B200LayerNormMulBwdParams(ctypes.Structure):
         ("mean", ctypes.c_void_p), ("rstd", ctypes.c_void_p),
         ("dx", ctypes.c_void_p), ("du", ctypes.c_void_p), ("dweight", ctypes.c_void_p), ("dbias", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_uint64),
+    ]
+
+
+class B200Fp8GemmParams(ctypes.Structure):
+    """Mirror of ``struct B200Fp8GemmParams`` (include/b200_stu_gemm.h)."""
+
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32), ("flags", ctypes.c_uint32),
+        ("out_dtype", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("M", ctypes.c_int64), ("K", ctypes.c_int64), ("N", ctypes.c_int64),
+        ("a_row_stride", ctypes.c_int64), ("b_row_stride", ctypes.c_int64), ("out_row_stride", ctypes.c_int64),
+        ("a", ctypes.c_void_p), ("b", ctypes.c_void_p), ("a_scale", ctypes.c_void_p), ("b_scale", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p), ("out", ctypes.c_void_p), ("status", ctypes.c_void_p),
     ]
 
 
@@ -250,6 +264,11 @@ def load() -> ctypes.CDLL:
     GP = ctypes.POINTER(B200GemmParams)
     lib.b200_stu_addmm.argtypes = [GP, ctypes.c_void_p]
     lib.b200_stu_addmm.restype = ctypes.c_int
+    FP = ctypes.POINTER(B200Fp8GemmParams)
+    lib.b200_stu_fp8_rowwise_addmm.argtypes = [FP, ctypes.c_void_p]
+    lib.b200_stu_fp8_rowwise_addmm.restype = ctypes.c_int
+    lib.b200_stu_fp8_rowwise_addmm_supported.argtypes = [FP]
+    lib.b200_stu_fp8_rowwise_addmm_supported.restype = ctypes.c_int
     lib.b200_stu_addmm_supported.argtypes = [GP]
     lib.b200_stu_addmm_supported.restype = ctypes.c_int
     lib.b200_stu_jagged_bmm_workspace_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64]

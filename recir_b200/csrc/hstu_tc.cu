@@ -881,6 +881,24 @@ bool make_map_box(CUtensorMap* m, const void* base, long long rows, long long wi
   return r == CUDA_SUCCESS;
 }
 
+// [rows, width] matrix of bytes (8-bit elements), box = 128 columns x `box_rows` rows, 128-byte swizzle, zero fill.
+bool make_map_bytes(CUtensorMap* m, const void* base, long long rows, long long width, long long row_stride, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) {
+    set_error_stage("tensor map: cuTensorMapEncodeTiled entry point not found");
+    return false;
+  }
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride)};
+  cuuint32_t box[2] = {128, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) set_error_stage("tensor map: encoding a byte matrix failed");
+  return r == CUDA_SUCCESS;
+}
+
 // Grid of the persistent kernels: one CTA per SM, fewer if there cannot be that many items.
 int main_grid(const WorkspaceLayout& w) {
   long long grid = w.max_items < sm_count() ? w.max_items : sm_count();

@@ -15,6 +15,8 @@ bool ensure_current_context(const void* device_ptr);
 bool make_map(CUtensorMap* m, const void* base, long long rows, long long width, long long row_stride, bool bf16);
 bool make_map_box(CUtensorMap* m, const void* base, long long rows, long long width, long long row_stride, int box_rows,
                   bool bf16);
+// The same over a [rows, width] matrix of bytes: box = 128 columns x box_rows rows.
+bool make_map_bytes(CUtensorMap* m, const void* base, long long rows, long long width, long long row_stride, int box_rows);
 int sm_count();
 // Grid of the persistent kernels (also the stride with which CTAs walk the work list).
 int main_grid(const WorkspaceLayout& w);

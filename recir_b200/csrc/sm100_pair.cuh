@@ -68,6 +68,21 @@ __device__ __forceinline__ void mma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, ui
       ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z)
       : "memory");
 }
+// The same for 8-bit floating-point operands (K = 32 per instruction).
+__device__ __forceinline__ void mma_ts_pair_f8(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], [%1], %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z)
+      : "memory");
+}
+// Instruction descriptor for kind::f8f6f4 with e4m3 A and B (format code 0), both K-major, fp32 accumulation.
+__host__ __device__ constexpr uint32_t idesc_f8_e4m3(int M, int N) {
+  return (1u << 4) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
+
 // Arrive on an mbarrier (cluster-window address) once every paired tcgen05 operation issued so far by this
 // thread has completed.
 __device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster_addr) {

@@ -101,6 +101,8 @@ struct Args {
   const void* offsets;   // jagged mode: seq_offsets (to find the first row no sequence owns)
   int off64, num_seqs;
   int per_seq_bias;      // bias row = sequence index (else: output row index, or the single row when bias_rs == 0)
+  const float* a_scale;  // fp8: [M] scale of every row of A
+  const float* b_scale;  // fp8: [N] scale of every row of W, i.e. of every output column
   int dbg;  // instrumented builds only (B200_GEMM_DBG): 1 no W loads / waits, 2 no output staging, 4 no MMAs
 };
 
@@ -151,9 +153,14 @@ template <bool BF16> __device__ __forceinline__ uint32_t pack2(float lo, float h
 // its half of the B operand (64 of the tile's 128 columns), so each SM pulls half as much of W out of L2 -
 // and L2 bandwidth for W is what bounds the single-CTA form.  The jagged mode (a weight matrix per
 // sequence, so two neighbouring row blocks may need different B operands) runs unpaired.
-template <bool BF16, bool PAIR, bool FUSE>
+// ET: 0 float16, 1 bfloat16, 2 float8 e4m3 operands with bfloat16 bias and output (row-wise scaled product:
+// A is [M, K] with a scale per row, W is given K-major as [N, K] with a scale per row, i.e. per output column;
+// pairs only, no layer norm).  In bytes everything is the same: 128-byte box rows, 32 bytes of K per MMA.
+template <int ET, bool PAIR, bool FUSE>
 __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant__ Maps maps, Args a) {
-  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  constexpr bool FP8 = ET == 2, BF16 = ET != 0;
+  static_assert(!FP8 || (PAIR && !FUSE), "the fp8 form runs on pairs, without the layer-norm prologue");
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;  // element type of bias and out
   extern __shared__ __align__(1024) unsigned char smem[];  // the swizzled boxes need 1024-byte alignment (checked below)
   Control& c = *reinterpret_cast<Control*>(smem);
   if ((smem_u32(smem) & 1023u) != 0u) {  // (the same in every CTA: nobody is left waiting)
@@ -162,7 +169,7 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort_flag = &c.abort_flag;
-  const int kboxes = a.K / 64;   // 64-column boxes of the A operand = pipeline stages of W per output tile
+  const int kboxes = FP8 ? a.K / 128 : a.K / 64;  // 128-byte boxes of a row of the A operand = stages of W per tile
   unsigned char* const out_stage = smem + CONTROL_BYTES;
   unsigned char* const park = out_stage + 2 * OUT_BOX_BYTES;
   unsigned char* const wring = park + kboxes * PARK_BOX_BYTES;
@@ -238,7 +245,7 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
         const int4 bi = block_of(blk);
         mbar_arrive_expect_tx(x_landed, static_cast<uint32_t>(kboxes) * PARK_BOX_BYTES);
         for (int kb = 0; kb < kboxes; ++kb)
-          tma_load_2d(smem_u32(park + kb * PARK_BOX_BYTES), &maps.x, x_landed, kb * 64, bi.y);
+          tma_load_2d(smem_u32(park + kb * PARK_BOX_BYTES), &maps.x, x_landed, kb * (FP8 ? 128 : 64), bi.y);
       }
       __syncwarp();
       ++xr;
@@ -262,7 +269,10 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
             if constexpr (PAIR) {
               // both halves of the stage are credited to the issuing CTA's barrier; columns past N arrive as zeros
               if (rank == 0) mbar_arrive_expect_tx(smem_u32(&c.w_full[st]), 2 * W_BOX_BYTES);
-              tma_load_2d_pair(dst, &maps.w, w_full_issuer + st * 8, tile_of(nt) * BN + static_cast<int>(rank) * 64, w_row0 + kb * BK);
+              if constexpr (FP8)  // W is [N, K]: this CTA's 64 output columns are 64 rows of it, 128 bytes of K each
+                tma_load_2d_pair(dst, &maps.w, w_full_issuer + st * 8, kb * 128, tile_of(nt) * BN + static_cast<int>(rank) * 64);
+              else
+                tma_load_2d_pair(dst, &maps.w, w_full_issuer + st * 8, tile_of(nt) * BN + static_cast<int>(rank) * 64, w_row0 + kb * BK);
             } else {
               mbar_arrive_expect_tx(smem_u32(&c.w_full[st]), STAGE_BYTES);
 #pragma unroll
@@ -280,7 +290,9 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
     GEMM_REPORT("producer (w_empty, x_free)");
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (in a pair: rank 0 only)
-    constexpr uint32_t IDESC = idesc_f16(BF16 ? 1 : 0, PAIR ? 2 * BM : BM, BN, 0, 1);  // A from TMEM, B N-major in shared memory
+    // A from TMEM; B from shared memory, N-major (16-bit: W is [K, N]) or K-major (fp8: W is [N, K])
+    constexpr uint32_t IDESC = FP8 ? idesc_f8_e4m3(PAIR ? 2 * BM : BM, BN) : idesc_f16(BF16 ? 1 : 0, PAIR ? 2 * BM : BM, BN, 0, 1);
+    constexpr uint32_t KSTEP = FP8 ? (32 >> 4) : (2048 >> 4);  // descriptor units per k-step: 32 bytes along a row / 16 rows
     constexpr uint32_t HI = desc_hi_sw128(1024);
     const uint32_t w_lo0 = desc_lo_sw128(smem_u32(wring), W_BOX_BYTES);  // 64-column groups are one box apart
     const uint32_t w_empty_peer = PAIR ? map_to_cta(smem_u32(&c.w_empty[0]), 1) : 0u;
@@ -309,8 +321,9 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
           if (a.dbg & 1) {
             if (elect_one() && !(a.dbg & 4)) {
               for (int kk = 0; kk < BK / 16; ++kk) {
-                const uint64_t bd = desc_join(w_lo0 + (kb % w_stages) * (STAGE_BYTES >> 4) + kk * (2048 >> 4), HI);
-                if constexpr (PAIR) mma_ts_pair(d_tmem, tmem + TMEM_A + (kb * 4 + kk) * 8, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+                const uint64_t bd = desc_join(w_lo0 + (kb % w_stages) * (STAGE_BYTES >> 4) + kk * KSTEP, HI);
+                if constexpr (FP8) mma_ts_pair_f8(d_tmem, tmem + TMEM_A + (kb * 4 + kk) * 8, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+                else if constexpr (PAIR) mma_ts_pair(d_tmem, tmem + TMEM_A + (kb * 4 + kk) * 8, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
                 else mma_ts(d_tmem, tmem + TMEM_A + (kb * 4 + kk) * 8, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
               }
             }
@@ -328,8 +341,9 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk) {
               // A: 16 k-values = 8 TMEM columns; B: k-step kk of the stage (16 rows of 128 bytes per box)
-              const uint64_t bd = desc_join(w_lo0 + st * (STAGE_BYTES >> 4) + kk * (2048 >> 4), HI);
-              if constexpr (PAIR) mma_ts_pair(d_tmem, tmem + TMEM_A + (kb * 4 + kk) * 8, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+              const uint64_t bd = desc_join(w_lo0 + st * (STAGE_BYTES >> 4) + kk * KSTEP, HI);
+              if constexpr (FP8) mma_ts_pair_f8(d_tmem, tmem + TMEM_A + (kb * 4 + kk) * 8, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+              else if constexpr (PAIR) mma_ts_pair(d_tmem, tmem + TMEM_A + (kb * 4 + kk) * 8, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
               else mma_ts(d_tmem, tmem + TMEM_A + (kb * 4 + kk) * 8, bd, IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
             }
             if constexpr (PAIR) { tc_commit_pair(w_empty_own + st * 8); tc_commit_pair(w_empty_peer + st * 8); }
@@ -358,6 +372,7 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
     bool ok = true;
     const bool bias_shared = a.bias_rs == 0 || a.per_seq_bias;
     uint4 bnext = make_uint4(0u, 0u, 0u, 0u);
+    [[maybe_unused]] float4 snext = make_float4(0.f, 0.f, 0.f, 0.f);
     [[maybe_unused]] long long tw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     [[maybe_unused]] const long long t_start_ = clock64();
     [[maybe_unused]] long long mark_ = 0;
@@ -422,15 +437,28 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
       const T* bias_row = reinterpret_cast<const T*>(a.bias) + (row < a.M ? row : a.M - 1) * a.bias_rs;
       auto bias_piece = [&](int tile) -> uint4 {
         const int col = tile * BN + wg * 64 + 8 * (lane & 7);
-        return col < a.N ? __ldg(reinterpret_cast<const uint4*>(bias_blk + col)) : make_uint4(0u, 0u, 0u, 0u);
+        return (a.bias != nullptr && col < a.N) ? __ldg(reinterpret_cast<const uint4*>(bias_blk + col)) : make_uint4(0u, 0u, 0u, 0u);
       };
       if (bias_shared && (a.per_seq_bias || u == u0)) bnext = bias_piece(tile_of(0));
+      // fp8: the scale of this thread's row of A, and the scales of the box's 64 columns of W the way the bias
+      // travels (lane l keeps the four of piece l % 16, a tile ahead)
+      float row_scale = 1.f;
+      auto scale_piece = [&](int tile) -> float4 {
+        const int col = tile * BN + wg * 64 + 4 * (lane & 15);
+        return col < a.N ? __ldg(reinterpret_cast<const float4*>(a.b_scale + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      };
+      if constexpr (FP8) {
+        row_scale = a.a_scale[row < a.M ? row : a.M - 1];
+        if (u == u0) snext = scale_piece(tile_of(0));
+      }
       unsigned char* stage = out_stage + wg * OUT_BOX_BYTES;
       for (int nt = 0; nt < n_tiles && ok; ++nt, ++g) {
         const uint32_t buf = g & 1;
         const int col0 = tile_of(nt) * BN + wg * 64;
         const uint4 bcur = bnext;
         if (bias_shared) bnext = bias_piece(tile_of(nt + 1 < n_tiles ? nt + 1 : 0));
+        [[maybe_unused]] const float4 scur = snext;
+        if constexpr (FP8) snext = scale_piece(tile_of(nt + 1 < n_tiles ? nt + 1 : 0));
         { GEMM_T0(); ok = __all_sync(0xffffffffu, mbar_wait_idle(smem_u32(&c.acc_full[buf]), (g >> 1) & 1, abort_flag, a.status, WAIT_GEMM_EPILOGUE)); GEMM_T1(tw[0]); }
         if (!ok) break;
         tc_fence_after();
@@ -478,11 +506,24 @@ __global__ void __launch_bounds__(THREADS, 1) stu_addmm_tc(const __grid_constant
             }
             float bf[8];
             vec::unpack8<T>(bj, bf);
+            float acc8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc8[e] = __uint_as_float(v[8 * jj + e]);
+            if constexpr (FP8) {  // out = (sum of products) * scale of the row of A * scale of the column of W + bias
+              float sc[8];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                sc[4 * h + 0] = __shfl_sync(0xffffffffu, scur.x, 2 * j + h); sc[4 * h + 1] = __shfl_sync(0xffffffffu, scur.y, 2 * j + h);
+                sc[4 * h + 2] = __shfl_sync(0xffffffffu, scur.z, 2 * j + h); sc[4 * h + 3] = __shfl_sync(0xffffffffu, scur.w, 2 * j + h);
+              }
+#pragma unroll
+              for (int e = 0; e < 8; ++e) acc8[e] *= row_scale * sc[e];
+            }
             uint4 o;
-            o.x = pack2<BF16>(__uint_as_float(v[8 * jj + 0]) + bf[0], __uint_as_float(v[8 * jj + 1]) + bf[1]);
-            o.y = pack2<BF16>(__uint_as_float(v[8 * jj + 2]) + bf[2], __uint_as_float(v[8 * jj + 3]) + bf[3]);
-            o.z = pack2<BF16>(__uint_as_float(v[8 * jj + 4]) + bf[4], __uint_as_float(v[8 * jj + 5]) + bf[5]);
-            o.w = pack2<BF16>(__uint_as_float(v[8 * jj + 6]) + bf[6], __uint_as_float(v[8 * jj + 7]) + bf[7]);
+            o.x = pack2<BF16>(acc8[0] + bf[0], acc8[1] + bf[1]);
+            o.y = pack2<BF16>(acc8[2] + bf[2], acc8[3] + bf[3]);
+            o.z = pack2<BF16>(acc8[4] + bf[4], acc8[5] + bf[5]);
+            o.w = pack2<BF16>(acc8[6] + bf[6], acc8[7] + bf[7]);
             *reinterpret_cast<uint4*>(my_row + ((j ^ (row_in_blk & 7)) << 4)) = o;
           }
         }
@@ -707,6 +748,31 @@ extern "C" int b200_stu_addmm_supported(const B200GemmParams* p) {
 }
 
 namespace {
+// One persistent CTA (or CTA pair) per SM (pair of SMs), fewer if there are not that many row blocks.
+template <typename Kern>
+int launch_kernel(Kern kern, bool pair, long long max_blocks, const hstu::gemm::Maps& maps, const hstu::gemm::Args& a, void* stream) {
+  using namespace hstu::gemm;
+  const int sms = hstu::tc::sm_count();
+  const long long units = pair ? (max_blocks + 1) / 2 : max_blocks;
+  const long long ctas = pair ? sms / 2 : sms;
+  const unsigned grid = static_cast<unsigned>((units < ctas ? (units < 1 ? 1 : units) : ctas) * (pair ? 2 : 1));
+  const size_t smem = CONTROL_BYTES + DATA_BYTES;  // 227 KB: all a CTA can have
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return B200_HSTU_ELAUNCH;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pair ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, kern, maps, a);
+  return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? B200_HSTU_OK : B200_HSTU_ELAUNCH;
+}
+
 // Shared launch path of the two entry points.
 int launch_gemm(const B200GemmParams* p, const void* w_base, long long w_rows, const int4* items, const int* n_items,
                 long long max_blocks, int per_seq_bias, const void* offsets, int off64, int num_seqs, void* stream) {
@@ -728,35 +794,19 @@ int launch_gemm(const B200GemmParams* p, const void* w_base, long long w_rows, c
   a.eps = p->eps;
   a.items = items; a.n_items = n_items; a.per_seq_bias = per_seq_bias;
   a.offsets = offsets; a.off64 = off64; a.num_seqs = num_seqs;
+  a.a_scale = a.b_scale = nullptr;
   a.dbg = 0;
 #ifdef B200_HSTU_PROFILING
   if (const char* e = getenv("B200_GEMM_DBG")) a.dbg = atoi(e);
 #endif
   const int sms = hstu::tc::sm_count();
   const bool pair = items == nullptr && sms >= 2;  // per-sequence weights cannot share a B operand across two row blocks
-  const long long units = pair ? (max_blocks + 1) / 2 : max_blocks;
-  const long long ctas = pair ? sms / 2 : sms;
-  const unsigned grid = static_cast<unsigned>((units < ctas ? (units < 1 ? 1 : units) : ctas) * (pair ? 2 : 1));
-  const size_t smem = CONTROL_BYTES + DATA_BYTES;  // 227 KB: all a CTA can have
   if (fuse && !pair) return B200_HSTU_EUNSUPPORTED;  // (the jagged mode has no layer-norm prologue)
-  auto kern = fuse   ? (bf16 ? stu_addmm_tc<true, true, true> : stu_addmm_tc<false, true, true>)
-              : pair ? (bf16 ? stu_addmm_tc<true, true, false> : stu_addmm_tc<false, true, false>)
-                     : (bf16 ? stu_addmm_tc<true, false, false> : stu_addmm_tc<false, false, false>);
+  auto kern = fuse   ? (bf16 ? stu_addmm_tc<1, true, true> : stu_addmm_tc<0, true, true>)
+              : pair ? (bf16 ? stu_addmm_tc<1, true, false> : stu_addmm_tc<0, true, false>)
+                     : (bf16 ? stu_addmm_tc<1, false, false> : stu_addmm_tc<0, false, false>);
   hstu::set_error_stage("addmm: kernel");
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) return B200_HSTU_ELAUNCH;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(THREADS, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pair ? 1 : 0;
-  e = cudaLaunchKernelEx(&cfg, kern, maps, a);
-  return e == cudaSuccess && cudaGetLastError() == cudaSuccess ? B200_HSTU_OK : B200_HSTU_ELAUNCH;
+  return launch_kernel(kern, pair, max_blocks, maps, a, stream);
 }
 
 int check_common(const B200GemmParams* p) {
@@ -815,4 +865,46 @@ extern "C" int b200_stu_jagged_dense_bmm_add(const B200GemmParams* p, const void
   if (cudaGetLastError() != cudaSuccess) return B200_HSTU_ELAUNCH;
   return launch_gemm(p, p->w, num_seqs * p->K, reinterpret_cast<const int4*>(ws + 4), ws, max_items, per_row_bias ? 0 : 1,
                      seq_offsets, offsets_i64 ? 1 : 0, static_cast<int>(num_seqs), stream);
+}
+
+extern "C" int b200_stu_fp8_rowwise_addmm_supported(const B200Fp8GemmParams* p) {
+  if (p == nullptr || p->struct_size != sizeof(B200Fp8GemmParams)) return 0;
+  if (p->out_dtype != B200_HSTU_BF16) return 0;
+  if (p->M <= 0 || p->K <= 0 || p->N <= 0) return 0;
+  if (p->K % 128 != 0 || p->K > 2 * hstu::gemm::MAX_K || p->N % 8 != 0) return 0;
+  if (p->M >= (1LL << 31) - 256 || p->N >= (1LL << 30)) return 0;
+  return hstu::tc::sm_count() >= 2 ? 1 : 0;
+}
+
+extern "C" int b200_stu_fp8_rowwise_addmm(const B200Fp8GemmParams* p, void* stream) {
+  using namespace hstu::gemm;
+  if (p == nullptr) return B200_HSTU_EINVAL;
+  if (p->struct_size != sizeof(B200Fp8GemmParams)) return B200_HSTU_EVERSION;
+  if (p->M < 0 || p->K <= 0 || p->N <= 0) return B200_HSTU_EINVAL;
+  if (p->M == 0) return B200_HSTU_OK;
+  if (!b200_stu_fp8_rowwise_addmm_supported(p)) return B200_HSTU_EUNSUPPORTED;
+  if (!p->a || !p->b || !p->a_scale || !p->b_scale || !p->out) return B200_HSTU_EINVAL;
+  if (p->a_row_stride < p->K || p->b_row_stride < p->K || p->out_row_stride < p->N) return B200_HSTU_EINVAL;
+  auto bad = [](const void* q, long long stride, int unit) { return reinterpret_cast<uintptr_t>(q) % 16 != 0 || stride % unit != 0; };
+  if (bad(p->a, p->a_row_stride, 16) || bad(p->b, p->b_row_stride, 16) || bad(p->out, p->out_row_stride, 8) ||
+      bad(p->b_scale, 0, 1) || (p->bias && bad(p->bias, 0, 1)))
+    return B200_HSTU_EALIGN;
+  hstu::set_error_stage("fp8 addmm: tensor maps");
+  if (!hstu::tc::ensure_current_context(p->a)) return B200_HSTU_ELAUNCH;
+  Maps maps;
+  if (!hstu::tc::make_map_bytes(&maps.x, p->a, p->M, p->K, p->a_row_stride, BM)) return B200_HSTU_ELAUNCH;
+  if (!hstu::tc::make_map_bytes(&maps.w, p->b, p->N, p->K, p->b_row_stride, 64)) return B200_HSTU_ELAUNCH;
+  if (!hstu::tc::make_map_box(&maps.o, p->out, p->M, p->N, p->out_row_stride, BM, true)) return B200_HSTU_ELAUNCH;
+  Args a;
+  a.x = p->a; a.ln_w = nullptr; a.ln_b = nullptr; a.bias = p->bias; a.out = p->out;
+  a.mean = nullptr; a.rstd = nullptr; a.status = p->status;
+  a.M = p->M; a.x_rs = p->a_row_stride; a.out_rs = p->out_row_stride; a.bias_rs = 0;
+  a.K = static_cast<int>(p->K); a.N = static_cast<int>(p->N);
+  a.fuse_ln = 0; a.swish = 0; a.affine = 0; a.eps = 0.f;
+  a.items = nullptr; a.n_items = nullptr; a.per_seq_bias = 0;
+  a.offsets = nullptr; a.off64 = 0; a.num_seqs = 0;
+  a.a_scale = p->a_scale; a.b_scale = p->b_scale;
+  a.dbg = 0;
+  hstu::set_error_stage("fp8 addmm: kernel");
+  return launch_kernel(stu_addmm_tc<2, true, false>, true, (p->M + BM - 1) / BM, maps, a, stream);
 }

@@ -504,15 +504,52 @@ torch.library.register_autograd("recir::b200_layer_norm_addmm_fwd", _layer_norm_
                                 setup_context=_layer_norm_addmm_setup_context)
 
 
+def _fp8_rowwise_addmm_tc(a, b, a_scale, b_scale, bias, out_dtype):
+    """The tcgen05 route of ``_fp8_rowwise_addmm_cuda``; None when the sizes or types are not the kernel's."""
+    global launch_counter
+    if out_dtype != torch.bfloat16 or a.shape[0] == 0:
+        return None
+    if bias is not None and (bias.dim() != 1 or bias.shape[0] != b.shape[0]):
+        return None
+    a, b = _rows2d(a), _rows2d(b)
+    lib = _lib.load()
+    p = _lib.B200Fp8GemmParams()
+    p.struct_size = ctypes.sizeof(p)
+    p.out_dtype = _DTYPES[torch.bfloat16]
+    p.M, p.K, p.N = a.shape[0], a.shape[1], b.shape[0]
+    p.a_row_stride, p.b_row_stride = a.stride(0), b.stride(0)
+    if not lib.b200_stu_fp8_rowwise_addmm_supported(ctypes.byref(p)):
+        return None
+    if a.data_ptr() % 16 or b.data_ptr() % 16 or a.stride(0) % 16 or b.stride(0) % 16:
+        return None
+    out = torch.empty((a.shape[0], b.shape[0]), dtype=torch.bfloat16, device=a.device)
+    keep = [a_scale.reshape(-1).to(torch.float32).contiguous(), b_scale.reshape(-1).to(torch.float32).contiguous()]
+    if bias is not None:
+        keep.append(bias.to(torch.bfloat16).contiguous())
+        p.bias = keep[-1].data_ptr()
+    p.a, p.b, p.out = a.data_ptr(), b.data_ptr(), out.data_ptr()
+    p.out_row_stride = out.stride(0)
+    p.a_scale, p.b_scale = keep[0].data_ptr(), keep[1].data_ptr()
+    p.status = _ops.status_tensor(a.device).data_ptr()
+    with torch.cuda.device(a.device):
+        rc = lib.b200_stu_fp8_rowwise_addmm(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    _check(rc, "b200_stu_fp8_rowwise_addmm")
+    launch_counter += 1
+    del keep
+    return out
+
+
 def _fp8_rowwise_addmm_cuda(a, b, a_scale, b_scale, bias, has_bias, bias_is_2d, dot_out_dtype, allow_tf32,
                             use_fast_accum):
     """The projection behind the quantised layer-norm stage: ``(a * a_scale[:, None]) @ (b * b_scale[:, None]).T
     + bias`` with ``a`` [M, K] and ``b`` [N, K] in float8 e4m3 and one float32 scale per row of each
     (``generative_recommenders::_triton_fp8_rowwise_addmm_fwd_impl``,
     ``recir/ops/kjt_split_per_feature.cpp:533-556``, which dequantises and calls ``at::mm``; it ignores
-    ``bias_is_2d``, ``allow_tf32`` and ``use_fast_accum``, and so does this).  A plain GEMM, handed to the
-    vendor library's fp8 path: the float8 products are exact and accumulate in float32, so only the
-    summation order differs from the reference."""
+    ``bias_is_2d``, ``allow_tf32`` and ``use_fast_accum``, and so does this).  The float8 products are exact and
+    accumulate in float32, so only the summation order differs from the reference.  The STU sizes (K a
+    multiple of 128 up to 1024, N a multiple of 8, bfloat16 output, a bias vector or none) run on this
+    library's tcgen05 kernel (``csrc/stu_gemm.cu``, ``kind::f8f6f4`` on CTA pairs); any other size or output
+    type is a plain GEMM handed to the vendor library's fp8 path."""
     if a.dim() != 2 or b.dim() != 2:
         raise ValueError("a and b must be two-dimensional")
     if a.shape[1] != b.shape[1]:
@@ -521,8 +558,12 @@ def _fp8_rowwise_addmm_cuda(a, b, a_scale, b_scale, bias, has_bias, bias_is_2d, 
         raise ValueError("a and b must be float8_e4m3fn")
     if a_scale.numel() != a.shape[0] or b_scale.numel() != b.shape[0]:
         raise ValueError("one scale per row of a and of b is required")
+    out = _fp8_rowwise_addmm_tc(a, b, a_scale, b_scale, bias if has_bias else None, dot_out_dtype)
+    if out is not None:
+        return out
     if a.shape[1] % 16 != 0 or b.shape[0] % 16 != 0:
-        raise ValueError("the reduction and output dimensions must be multiples of 16")
+        raise ValueError("the reduction and output dimensions must be multiples of 16 (this library's kernel: K a "
+                         "multiple of 128 up to 1024, N a multiple of 8, bfloat16 output)")
     sa = a_scale.reshape(-1, 1).to(torch.float32).contiguous()
     sb = b_scale.reshape(1, -1).to(torch.float32).contiguous()
     # the library wants a row-major [M, K] and a column-major [K, N]: b.T of a contiguous [N, K] is that

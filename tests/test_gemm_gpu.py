@@ -209,3 +209,43 @@ def test_fused_projection_is_differentiable(swish):
     for name, a, r in zip(("dx", "dln_w", "dln_b", "dW", "dbias"), leaves, ref):
         err = float((a.grad.float() - r.grad).norm() / r.grad.norm())
         assert err <= 1e-2, (name, err)
+
+
+FP8_SHAPES = [(300, 128, 96), (1, 256, 8), (777, 512, 520), (129, 1024, 264), (60001, 1024, 384), (45000, 128, 64)]
+
+
+@pytest.mark.parametrize("M,K,N", FP8_SHAPES)
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_fp8_rowwise_addmm_on_tensor_cores_matches_oracle(M, K, N, with_bias):
+    """Row-wise scaled float8 projection (kjt_split_per_feature.cpp:533-556) on the tcgen05 kernel: e4m3 products
+    are exact, sums run in float32 in tensor-core order, scales and bias are applied to the sum and the result is
+    rounded once to bfloat16; the oracle dequantises, sums in float64 and rounds once."""
+    from recir_b200 import rowwise_ops
+    g = torch.Generator().manual_seed(M + K + N)
+    a = (torch.randn(M, K, generator=g) * 60.0).clamp(-448, 448).to(torch.float8_e4m3fn).cuda()
+    b = (torch.randn(N, K, generator=g) * 40.0).clamp(-448, 448).to(torch.float8_e4m3fn).cuda()
+    sa = (torch.rand(M, generator=g) * 0.02 + 0.001).cuda()
+    sb = (torch.rand(N, generator=g) * 0.01 + 0.001).cuda()
+    bias = (torch.randn(N, generator=g) * 0.5).to(torch.bfloat16).cuda() if with_bias else torch.empty(0, device="cuda")
+    n0 = rowwise_ops.launch_counter
+    out = torch.ops.recir.b200_fp8_rowwise_addmm_fwd(a, b, sa, sb, bias, with_bias, False, torch.bfloat16, False, False)
+    assert rowwise_ops.launch_counter - n0 == 1  # this library's kernel, not the vendor route
+    recir_b200.check_status(what="fp8 projection")
+    want = ro.fp8_rowwise_addmm(a.view(torch.uint8).cpu().numpy(), b.view(torch.uint8).cpu().numpy(), sa.cpu().numpy(),
+                                sb.cpu().numpy(), bias.float().cpu().numpy() if with_bias else None, "bfloat16")
+    _close(out, want, "bfloat16", f"fp8 addmm bias={with_bias}")
+
+
+def test_fp8_rowwise_addmm_other_sizes_take_the_vendor_route():
+    from recir_b200 import rowwise_ops
+    g = torch.Generator().manual_seed(2)
+    a = (torch.randn(64, 48, generator=g) * 60.0).to(torch.float8_e4m3fn).cuda()   # K = 48: not the kernel's
+    b = (torch.randn(32, 48, generator=g) * 40.0).to(torch.float8_e4m3fn).cuda()
+    sa, sb = torch.rand(64, generator=g).cuda() * 0.01, torch.rand(32, generator=g).cuda() * 0.01
+    n0 = rowwise_ops.launch_counter
+    out = torch.ops.recir.b200_fp8_rowwise_addmm_fwd(a, b, sa, sb, torch.empty(0, device="cuda"), False, False,
+                                                     torch.bfloat16, False, False)
+    assert rowwise_ops.launch_counter == n0
+    want = ro.fp8_rowwise_addmm(a.view(torch.uint8).cpu().numpy(), b.view(torch.uint8).cpu().numpy(), sa.cpu().numpy(),
+                                sb.cpu().numpy(), None, "bfloat16")
+    _close(out, want, "bfloat16", "fp8 addmm, vendor route")
