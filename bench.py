@@ -18,6 +18,7 @@ The same JSON line also carries, measured in the same process:
                 through all layers then backward through all layers, token-balanced over the N ranks
                 (strong scaling: ``tokens_per_s`` at every N, per-rank times, imbalance);
 * ``long_window`` the long skewed sequences with a 1024-token window (N=1 only);
+* ``stu_layer`` the projections and row-wise kernels around the attention on the cfg4 token count (N=1 only);
 * ``sustained`` the headline step looped for >= 2 s with the SM clock sampled meanwhile;
 * ``per_rank_ms`` every rank's own time for the headline region;
 * ``grad_check`` (N>1) per-sequence float64 checksums of dq, dk, dv of every rank's shard, exchanged
@@ -619,6 +620,22 @@ def main():
             grad_check = st.grad_check(dist)
         del st
 
+    # ------------------------------------------------------------ the STU layer around the attention (N=1 only)
+    stu_layer = None
+    if not args.no_extras and world == 1:
+        import argparse as _ap
+        import bench_cases
+        torch.cuda.empty_cache()
+        rows = 1650165  # tokens of the cfg4 batch (one layer)
+        stu_layer = {
+            "note": "the layer's other operators on the cfg4 token count, bf16, embedding width 512: projections "
+                    "(u|v|q|k: K = 512 -> N = 2048; fp8 output projection sizes) against the vendor GEMM, row-wise "
+                    "kernels as algorithmic GB/s; same code as `bench.py --case gemm` / `--case rowwise`",
+            "projection": bench_cases.gemm_numbers(_ap.Namespace(rows=rows, k=512, n=2048, iters=5, warmup=2)),
+            "rowwise": bench_cases.rowwise_numbers(_ap.Namespace(rows=rows, cols=512, iters=5, warmup=2)),
+        }
+        torch.cuda.empty_cache()
+
     # ------------------------------------------------------------ report
     if rank == 0:
         peaks = measured_peaks()
@@ -687,6 +704,8 @@ def main():
             line["stack8"] = stack8
         if grad_check is not None:
             line["grad_check"] = grad_check
+        if stu_layer is not None:
+            line["stu_layer"] = stu_layer
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)

@@ -196,6 +196,11 @@ def main_rowwise(argv):
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     args = ap.parse_args(argv)
+    print(json.dumps(rowwise_numbers(args)))
+
+
+def rowwise_numbers(args):
+    """The measurements of ``main_rowwise`` as a dict; ``args`` has rows, cols, iters, warmup."""
     dev = "cuda"
     g = torch.Generator().manual_seed(0)
     cols = args.cols
@@ -234,7 +239,7 @@ def main_rowwise(argv):
     for name, (fn, nbytes) in cases.items():
         ms = _timed(fn, args.iters, args.warmup)
         out[name] = {"ms": ms, "algorithmic_bytes": nbytes, "GB/s": nbytes / ms / 1e6}
-    print(json.dumps(out))
+    return out
 
 
 def main_jagged(argv):
@@ -279,7 +284,7 @@ def main_jagged(argv):
     for name, (fn, nbytes) in cases.items():
         ms = _timed(fn, args.iters, args.warmup)
         out[name] = {"ms": ms, "algorithmic_bytes": nbytes, "GB/s": nbytes / ms / 1e6}
-    print(json.dumps(out))
+    return out
 
 
 def main_gemm(argv):
@@ -295,6 +300,11 @@ def main_gemm(argv):
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     args = ap.parse_args(argv)
+    print(json.dumps(gemm_numbers(args)))
+
+
+def gemm_numbers(args):
+    """The measurements of ``main_gemm`` as a dict; ``args`` has rows, k, n, iters, warmup."""
     dev = "cuda"
     g = torch.Generator(device=dev).manual_seed(0)
     M, K, N = args.rows, args.k, args.n
@@ -336,7 +346,7 @@ def main_gemm(argv):
                          ("fp8 rowwise addmm (vendor fp8 GEMM, then scales and bias)", vendor_fp8)):
             ms = _timed(fn, args.iters, args.warmup)
             out[name] = {"ms": ms, "TFLOP/s": flops / ms / 1e9, "GB/s": fp8_bytes / ms / 1e6}
-    print(json.dumps(out))
+    return out
 
 
 def main_trace(argv):

@@ -856,9 +856,44 @@ bool make_map(CUtensorMap* m, const void* base, long long rows, long long width,
   return make_map_box(m, base, rows, width, row_stride, BLK, bf16);
 }
 
+// Encoded tensor maps are kept per (base, shape, stride, box, element type): a training step calls the same
+// operators on the same buffers again and again, and each encoding is a driver call on the launch path.  The
+// map holds nothing but those values, so a hit is exact; 64 entries, replaced round robin.
+namespace {
+struct MapKey {
+  const void* base; long long rows, width, row_stride; int box_rows, kind;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && rows == o.rows && width == o.width && row_stride == o.row_stride && box_rows == o.box_rows &&
+           kind == o.kind;
+  }
+};
+struct MapCache {
+  static constexpr int N = 64;
+  std::mutex mu;
+  MapKey key[N];
+  CUtensorMap map[N];
+  bool used[N] = {};
+  int next = 0;
+  bool find(const MapKey& k, CUtensorMap* out) {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < N; ++i)
+      if (used[i] && key[i] == k) { *out = map[i]; return true; }
+    return false;
+  }
+  void put(const MapKey& k, const CUtensorMap& m) {
+    std::lock_guard<std::mutex> lock(mu);
+    key[next] = k; map[next] = m; used[next] = true;
+    next = (next + 1) % N;
+  }
+};
+MapCache& map_cache() { static MapCache c; return c; }
+}  // namespace
+
 // Same with a box of 64 columns x `box_rows` rows (at most 256).
 bool make_map_box(CUtensorMap* m, const void* base, long long rows, long long width, long long row_stride, int box_rows,
                   bool bf16) {
+  const MapKey k{base, rows, width, row_stride, box_rows, bf16 ? 1 : 0};
+  if (map_cache().find(k, m)) return true;
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     set_error_stage("tensor map: cuTensorMapEncodeTiled entry point not found");
@@ -877,6 +912,8 @@ bool make_map_box(CUtensorMap* m, const void* base, long long rows, long long wi
     snprintf(why, sizeof(why), "tensor map: CUresult %d for base %p rows %lld width %lld row stride %lld", (int)r, base, rows,
              width, row_stride);
     set_error_stage(why);
+  } else {
+    map_cache().put(k, *m);
   }
   return r == CUDA_SUCCESS;
 }
@@ -888,6 +925,8 @@ bool make_map_bytes(CUtensorMap* m, const void* base, long long rows, long long 
     set_error_stage("tensor map: cuTensorMapEncodeTiled entry point not found");
     return false;
   }
+  const MapKey k{base, rows, width, row_stride, box_rows, 2};
+  if (map_cache().find(k, m)) return true;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride)};
   cuuint32_t box[2] = {128, static_cast<cuuint32_t>(box_rows)};
@@ -896,6 +935,7 @@ bool make_map_bytes(CUtensorMap* m, const void* base, long long rows, long long 
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) set_error_stage("tensor map: encoding a byte matrix failed");
+  else map_cache().put(k, *m);
   return r == CUDA_SUCCESS;
 }
 
