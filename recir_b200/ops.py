@@ -226,12 +226,35 @@ def _check(rc: int, what: str) -> None:
         raise RuntimeError(f"{what}: {msg}")
 
 
+TC_HEAD_DIM = 128  # the head dimension of the tensor-core kernels
+
+
+def _pads_to_tensor_core_width(q, k, v, causal) -> bool:
+    """16-bit causal attention with one head dimension below 128 (a multiple of 8) for q, k and v: zero columns
+    change neither q kT nor the leading columns of p v, so the tensor-core kernels serve it on inputs padded to
+    128 columns (twice the tensor work at D = 64, still far ahead of the CUDA-core kernels, which are what a
+    head dimension the tensor-core kernels do not take falls back to)."""
+    d = q.shape[2]
+    return (not _force_simt and causal and q.dtype in (torch.bfloat16, torch.float16) and k.shape[2] == d
+            and v.shape[2] == d and d < TC_HEAD_DIM and d % 8 == 0 and q.shape[0] > 0)
+
+
+def _pad_head_dim(t: torch.Tensor) -> torch.Tensor:
+    out = t.new_zeros((t.shape[0], t.shape[1], TC_HEAD_DIM))
+    out[:, :, :t.shape[2]] = t
+    return out
+
+
 def _fwd_cuda(q, k, v, seq_offsets, max_seq_len, alpha, causal, num_targets, contextual_seq_len,
               max_attn_len, attn_scale, full_attn_size=0):
     global launch_counter
     validate_inputs(q, k, v, seq_offsets, num_targets, max_seq_len, attn_scale)
     lib = _lib.load()
     q, k, v = _rows(q), _rows(k), _rows(v)
+    if _pads_to_tensor_core_width(q, k, v, causal):
+        out = _fwd_cuda(_pad_head_dim(q), _pad_head_dim(k), _pad_head_dim(v), seq_offsets, max_seq_len, alpha, causal,
+                        num_targets, contextual_seq_len, max_attn_len, attn_scale, full_attn_size)
+        return out[:, :, :v.shape[2]].contiguous()
     out = torch.empty((q.shape[0], q.shape[1], v.shape[2]), dtype=v.dtype, device=v.device)
     if q.shape[0] == 0:
         return out
@@ -257,6 +280,11 @@ def _bwd_cuda(dout, q, k, v, seq_offsets, max_seq_len, alpha, causal, num_target
     validate_inputs(q, k, v, seq_offsets, num_targets, max_seq_len, attn_scale, dout)
     lib = _lib.load()
     q, k, v, dout = _rows(q), _rows(k), _rows(v), _rows(dout)
+    if _pads_to_tensor_core_width(q, k, v, causal):
+        d = q.shape[2]
+        grads = _bwd_cuda(_pad_head_dim(dout), _pad_head_dim(q), _pad_head_dim(k), _pad_head_dim(v), seq_offsets, max_seq_len,
+                          alpha, causal, num_targets, contextual_seq_len, max_attn_len, attn_scale, full_attn_size)
+        return tuple(g[:, :, :d].contiguous() for g in grads)
     dq = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
     dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
