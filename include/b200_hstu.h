@@ -70,6 +70,8 @@ extern "C" {
 #define B200_HSTU_FLAG_FORCE_SIMT 0x10u     /* use the plain CUDA-core kernels (cross-check path) */
 #define B200_HSTU_FLAG_BWD_SKIP_DQ 0x20u    /* backward: run only the dK/dV pass (dq is left untouched) */
 #define B200_HSTU_FLAG_BWD_SKIP_DKV 0x40u   /* backward: run only the dQ pass (dk, dv are left untouched) */
+#define B200_HSTU_FLAG_BWD_RECOMPUTE_DQ 0x100u /* backward: the dQ pass recomputes S and dP (small workspace) instead of
+                                                 reading the dS tiles the dK/dV pass stored (see b200_hstu_workspace_bytes) */
 #define B200_HSTU_FLAG_TRACE 0x80u /* instrumented builds (-DB200_HSTU_PROFILING) only: status is then a buffer of
                                          16 + 8192 ints and CTA 0 records an event trace behind the four status words */
 
@@ -122,7 +124,14 @@ int b200_hstu_fwd(const B200HstuParams* params, void* cuda_stream);
 int b200_hstu_bwd(const B200HstuParams* params, void* cuda_stream);
 
 /* Scratch bytes the call needs in params->workspace.  pass: 0 = forward, 1 = backward.
- * Depends only on B, H, T, Dqk, Dv, dtype and flags. */
+ * Depends only on B, H, T, Dqk, Dv, dtype, max_seq_len, contextual_seq_len and flags.
+ * The forward needs a few hundred KB (the device-built work list).  The tensor-core backward by default also
+ * keeps every 128 x 128 dS tile the dK/dV pass computes (32 KB each) for the dQ pass, which then has one
+ * GEMM per tile left instead of three and no transcendental: room for H * (T / 128 + B) * (ceil(max_seq_len /
+ * 128) + 1) / 2 tiles (twice that with a contextual prefix), of which only the tiles the mask keeps are
+ * touched.  Above B200_HSTU_DS_WORKSPACE_LIMIT bytes, or with B200_HSTU_FLAG_BWD_RECOMPUTE_DQ, the dQ pass
+ * recomputes S and dP instead and the workspace is as small as the forward's. */
+#define B200_HSTU_DS_WORKSPACE_LIMIT (48ull << 30)
 size_t b200_hstu_workspace_bytes(const B200HstuParams* params, int pass);
 
 /* 1 if the tensor-core (tcgen05/TMA) kernels will serve this problem, 0 if the CUDA-core

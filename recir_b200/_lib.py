@@ -19,6 +19,7 @@ FLAG_FORCE_SIMT = 0x10
 FLAG_BWD_SKIP_DQ = 0x20
 FLAG_BWD_SKIP_DKV = 0x40
 FLAG_TRACE = 0x80
+FLAG_BWD_RECOMPUTE_DQ = 0x100
 
 EXPORTS = (
     "b200_hstu_fwd", "b200_hstu_bwd", "b200_hstu_workspace_bytes", "b200_hstu_uses_tensor_cores",

@@ -69,6 +69,8 @@ int validate(const B200HstuParams* p, int pass, KernelArgs* a) {
   a->skip_dq = (p->flags & B200_HSTU_FLAG_BWD_SKIP_DQ) ? 1 : 0;
   a->skip_dkv = (p->flags & B200_HSTU_FLAG_BWD_SKIP_DKV) ? 1 : 0;
   a->max_seq_len = static_cast<int>(p->max_seq_len > 0x3fffffff ? 0x3fffffff : p->max_seq_len);
+  a->recompute_dq = (p->flags & B200_HSTU_FLAG_BWD_RECOMPUTE_DQ) ? 1 : 0;
+  a->ds_tiles = nullptr; a->ds_tile_base = nullptr; a->ds_tile_cap = 0; a->ds_square = 0;
   a->alpha = p->alpha;
   a->inv_n = 1.0f / static_cast<float>(p->max_seq_len);
   a->mask.causal = (p->flags & B200_HSTU_FLAG_CAUSAL) ? 1 : 0;

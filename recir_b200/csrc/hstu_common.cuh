@@ -32,6 +32,7 @@ struct SeqInfo {
   int hist;         // L - num_targets when targets are given (may be <= 0), else L
   int has_targets;
   int boundary;     // L - num_targets - full_attn_size
+  long long tile_base;  // backward with stored dS tiles: index of the sequence's first tile (else unused)
 };
 
 // keep(m, n) for 0 <= m, n < len.  Same rule as the reference builds with tensors in
@@ -88,6 +89,14 @@ struct KernelArgs {
   int offsets_i64, targets_i64, scale_mode;  // scale_mode: 0 = 1/N, 1 = scalar, 2 = per token
   int skip_dq, skip_dkv;                     // backward: leave one of the two passes out (timing aid)
   int max_seq_len;                           // the caller's bound on sequence lengths (sizes locality chunks)
+  int recompute_dq;                          // backward: the dQ pass recomputes S and dP instead of reading stored dS tiles
+  // Backward with stored dS tiles (set by the tensor-core launch code from the workspace, null otherwise):
+  // the dK/dV pass writes every 128 x 128 dS^T tile it computes (keys x queries, 16-bit, 32 KB), the dQ
+  // pass reads them back as the A operand of dQ += dS K.
+  unsigned char* ds_tiles;                   // first tile
+  const long long* ds_tile_base;             // [B] first tile index of every sequence (per head)
+  long long ds_tile_cap;                     // tiles the region holds (indices are clamped to it)
+  int ds_square;                             // tiles of a sequence indexed as a square (else as a triangle)
   float alpha;
   float inv_n;
   MaskOpts mask;
@@ -122,6 +131,7 @@ __device__ __forceinline__ SeqInfo load_seq(const KernelArgs& a, int b) {
   }
   r.hist = r.has_targets ? static_cast<int>(r.len - t) : r.len;
   r.boundary = static_cast<int>(r.len - t) - a.mask.full;
+  r.tile_base = 0;
   return r;
 }
 
@@ -144,6 +154,7 @@ __device__ __forceinline__ SeqInfo load_seq_quiet(const KernelArgs& a, int b) {
   }
   r.hist = r.has_targets ? static_cast<int>(r.len - t) : r.len;
   r.boundary = static_cast<int>(r.len - t) - a.mask.full;
+  r.tile_base = 0;
   return r;
 }
 
@@ -171,6 +182,7 @@ __device__ __forceinline__ SeqInfo finish_seq(const KernelArgs& a, const SeqRaw&
   r.has_targets = a.num_targets != nullptr;
   r.hist = r.has_targets ? static_cast<int>(r.len - t) : r.len;
   r.boundary = static_cast<int>(r.len - t) - a.mask.full;
+  r.tile_base = 0;
   return r;
 }
 

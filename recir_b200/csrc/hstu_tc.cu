@@ -165,6 +165,44 @@ __global__ void __launch_bounds__(1024) build_block_index(KernelArgs a, int* ws,
       g_start[i] = start[i];
     }
   }
+  if (a.ds_tile_base != nullptr) {
+    // Backward with stored dS tiles: first tile of every sequence = exclusive prefix sum of the sequences'
+    // tile counts (per head).  Every thread sums a contiguous run of sequences; the per-thread totals are
+    // scanned with warp shuffles.
+    long long* tile_base = const_cast<long long*>(a.ds_tile_base);
+    const int nt = blockDim.x, lane = tid & 31, wid = tid >> 5;
+    const long long chunk = (a.B + nt - 1) / nt;
+    long long b0 = static_cast<long long>(tid) * chunk, b1 = b0 + chunk;
+    if (b0 > a.B) b0 = a.B;
+    if (b1 > a.B) b1 = a.B;
+    long long local = 0;
+    for (long long b = b0; b < b1; ++b) local += ds_tiles_of(blocks_of(a, static_cast<int>(b)), a.ds_square);
+    long long incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    long long* wtot = reinterpret_cast<long long*>(sh);  // one entry per warp
+    __syncthreads();
+    if (lane == 31) wtot[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+      long long v = lane < (nt >> 5) ? wtot[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const long long t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+      }
+      wtot[lane] = v;
+    }
+    __syncthreads();
+    long long base = (wid > 0 ? wtot[wid - 1] : 0) + incl - local;
+    for (long long b = b0; b < b1; ++b) {
+      tile_base[b] = base;
+      base += ds_tiles_of(blocks_of(a, static_cast<int>(b)), a.ds_square);
+    }
+  }
 }
 
 // One thread per work-list entry: decode its rank into (sequence, head, block index).
@@ -990,6 +1028,14 @@ static cudaError_t launch_prep_t(const KernelArgs& a, int* ws, const WorkspaceLa
                           a.H * a.Dqk, reinterpret_cast<T*>(a.dv), a.dv_rs, a.H * a.Dv);
 }
 
+// Workspace of a backward call: the work list, and (unless the caller asked for the recomputing dQ pass, or
+// one of the two passes is left out, or the region would exceed B200_HSTU_DS_WORKSPACE_LIMIT) the dS tiles.
+WorkspaceLayout backward_layout(const KernelArgs& a) {
+  WorkspaceLayout w = workspace_layout(a.T, a.B, a.H);
+  if (!a.recompute_dq) add_ds_region(w, a.T, a.B, a.H, a.max_seq_len, a.mask.ctx ? 1 : 0, B200_HSTU_DS_WORKSPACE_LIMIT);
+  return w;
+}
+
 cudaError_t launch_prep(const KernelArgs& a, bool bf16, int* ws, const WorkspaceLayout& w, bool backward,
                         cudaStream_t st) {
   return bf16 ? launch_prep_t<__nv_bfloat16>(a, ws, w, backward, st) : launch_prep_t<__half>(a, ws, w, backward, st);
@@ -1037,9 +1083,8 @@ bool tc_supported(const B200HstuParams& p, const KernelArgs& a, int pass) {
 }
 
 size_t tc_workspace_bytes(const KernelArgs& a, int pass) {
-  (void)pass;
-  const tc::WorkspaceLayout w = tc::workspace_layout(a.T, a.B, a.H);
-  return (static_cast<size_t>(w.total_ints) * sizeof(int) + 255) & ~static_cast<size_t>(255);
+  const tc::WorkspaceLayout w = pass == 1 ? tc::backward_layout(a) : tc::workspace_layout(a.T, a.B, a.H);
+  return static_cast<size_t>(w.total_bytes);
 }
 
 int tc_launch_count(const KernelArgs& a, int pass) {

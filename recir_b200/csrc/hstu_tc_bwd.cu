@@ -57,6 +57,7 @@ struct Stopwatch {
 struct MapsBwd {
   CUtensorMap q, k, v, d_o;
   CUtensorMap dq, dk, dv;  // outputs (bulk stores of whole 128-row blocks)
+  CUtensorMap ds;          // stored dS^T tiles as one [tiles * 128, 128] matrix (dQ pass from stored tiles only)
 };
 
 // low-word offset (16-byte units) of k-step kk inside a K-major tile: 32 bytes inside a
@@ -863,6 +864,36 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
             }
             tmem_st16(st_addr, pp);  // P^T and dS^T (16 columns each) over the group's own score columns
             tmem_st16(dp_addr, pd);
+            if (a.ds_tiles != nullptr) {
+              // The dQ pass reads this dS^T tile back (keys x queries) instead of recomputing it.  The group
+              // stages its 2 x 32 query columns of the tile as ONE 64-column box (row = this thread's key row,
+              // 128-byte-swizzled as the bulk store expects) and sends the box out once per tile: the stored
+              // tile therefore holds the query columns in the order [group][half][32], i.e. with bits 5 and 6
+              // of the column index swapped, which the dQ pass undoes when it drains its accumulator.
+              if (sub == 0) {
+                if (row == 0) bulk_wait_read_all();  // the group's previous box (or drain) has left the buffer
+                group_barrier(wg);
+              }
+              unsigned char* my = stage + row * 128;
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                *reinterpret_cast<uint4*>(my + (((sub * 4 + i) ^ (row & 7)) << 4)) =
+                    make_uint4(pd[4 * i], pd[4 * i + 1], pd[4 * i + 2], pd[4 * i + 3]);
+              if (sub == 1) {
+                fence_proxy_async();
+                group_barrier(wg);
+                if (row == 0) {
+                  long long t = s.tile_base + ds_tile_index(q0 / BLK, kvblk, (s.len + BLK - 1) / BLK, a.ds_square);
+                  t = t * a.H + head;
+                  if (t >= a.ds_tile_cap) {  // a sequence longer than the caller's bound: stay inside the region
+                    t = a.ds_tile_cap - 1;
+                    if (a.status) atomicOr(a.status, 1);
+                  }
+                  tma_store_2d(&maps.ds, smem_u32(stage), wg * 64, static_cast<int>(t * BLK));
+                  bulk_commit();
+                }
+              }
+            }
             if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt + sub, 3, 6);
             if (q0 + BLK > s.len && wg == 0) {
               // query rows past the sequence end are B rows of the dV / dK MMAs: clear them
@@ -967,14 +998,251 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
   }
 }
 
+// ------------------------------------------------------------------------------------
+// dQ pass from stored dS tiles
+// ------------------------------------------------------------------------------------
+// The dK/dV pass has written every dS^T tile it computed (keys x queries, 16-bit, masked entries zero, the
+// per-token scale folded in).  What is left of the dQ pass is dQ[query block] = sum over its key blocks of
+// dS K: per tile ONE GEMM (M128 N128 K128, both operands from shared memory: dS^T as the M-major A operand, K
+// as the N-major B operand) instead of three, no transcendental, no mask, no operand copies into TMEM.  The
+// pass is bound by bringing in 64 KB per tile (the dS tile from HBM, the K tile mostly from L2).
+// Two accumulators: the MMAs of the next query block run while the previous one leaves TMEM.
+constexpr int DQS_STAGES = 3;
+constexpr int DQS_ACC0 = 0;  // accumulator b at columns 128 b
+
+struct DqsShared {
+  unsigned char ds[DQS_STAGES][TILE_BYTES];
+  unsigned char k[DQS_STAGES][TILE_BYTES];
+  unsigned char stage[TILE_BYTES];
+  unsigned long long full[DQS_STAGES], empty[DQS_STAGES];
+  unsigned long long acc_full[2], acc_empty[2];
+  int meta[META_RING];  // per tile: bit 0 = last tile of its item, bits 8.. = key rows of the tile inside the sequence
+  ItemRing ring;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <bool IS_BF16>
+__global__ void __launch_bounds__(BWD_THREADS, 1)
+hstu_bwd_dq_stored_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restrict__ ws, long long off_items) {
+  extern __shared__ unsigned char smem_raw[];
+  DqsShared& sh = *reinterpret_cast<DqsShared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Every tile this kernel reads was written by the dK/dV kernel before it in the stream: nothing starts
+  // until that kernel has completed and its writes are visible (a no-op for an ordinary launch).
+  grid_dependency_wait();
+  const int total_items = ws[0];
+  if (static_cast<int>(blockIdx.x) >= total_items) return;
+  const int2* items = reinterpret_cast<const int2*>(ws + off_items);
+  volatile int* abort_flag = &sh.abort_flag;
+
+  if (threadIdx.x == 0) {
+    sh.abort_flag = 0;
+    item_ring_init(sh.ring);
+    for (int i = 0; i < DQS_STAGES; ++i) { mbar_init(smem_u32(&sh.full[i]), 1); mbar_init(smem_u32(&sh.empty[i]), 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(smem_u32(&sh.acc_full[i]), 1); mbar_init(smem_u32(&sh.acc_empty[i]), 256); }
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(&sh.tmem_base), 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer / tile scheduler
+    if (lane == 0) { prefetch_tensormap(&maps.k); prefetch_tensormap(&maps.ds); }
+    uint32_t gt = 0, st = 0, ph = 0;
+    bool ok = true;
+    auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_PRODUCER));
+    };
+    int2 w;
+    SeqInfo s;
+    uint32_t todo0 = 0u, full0 = 0u;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, todo0, full0, ok, abort_flag, a.status, WAIT_PRODUCER); ++n_item) {
+      const int head = w.x >> 16, qblk = w.y;
+      const int m0 = qblk * BLK, col0 = head * HEAD_DIM;
+      const long long nb = (s.len + BLK - 1) / BLK;
+      const BlockRange kr = key_blocks_for_query_block(m0, s, a.mask);
+      const int cnt = kr.count();
+      // The tiles of this query block are the ones the dK/dV pass did not skip (the same classification;
+      // whether a tile is skipped does not depend on which pass asks).
+      int n_tiles = __popc(todo0);  // the scheduler warp classified the first 32 candidates
+      for (int base = 32; base < cnt; base += 32) {
+        int my_cls = TILE_SKIP;
+        if (base + lane < cnt) my_cls = classify_tile(m0, kr.at(base + lane) * BLK, s, a.mask);
+        n_tiles += __popc(__ballot_sync(0xffffffffu, my_cls != TILE_SKIP));
+      }
+      int emitted = 0;
+      for (int base = 0; base < cnt && ok; base += 32) {
+        uint32_t todo = todo0;
+        if (base > 0) {
+          int my_cls = TILE_SKIP;
+          if (base + lane < cnt) my_cls = classify_tile(m0, kr.at(base + lane) * BLK, s, a.mask);
+          todo = __ballot_sync(0xffffffffu, my_cls != TILE_SKIP);
+        }
+        while (todo != 0u && ok) {
+          const int bit = __ffs(todo) - 1;
+          todo &= todo - 1;
+          const int kblk = kr.at(base + bit);
+          ok = wait_all(&sh.empty[st], ph ^ 1);
+          if (!ok) break;
+          ++emitted;
+          if (elect_one()) {
+            long long t = (s.tile_base + ds_tile_index(qblk, kblk, nb, a.ds_square)) * a.H + head;
+            if (t >= a.ds_tile_cap) t = a.ds_tile_cap - 1;  // (flagged by the pass that wrote the tiles)
+            const int trow = static_cast<int>(t * BLK), krow = static_cast<int>(s.start) + kblk * BLK;
+            const int rows_in = s.len - kblk * BLK;  // key rows of the tile that belong to the sequence
+            sh.meta[gt & (META_RING - 1)] = ((emitted == n_tiles) ? 1 : 0) | ((rows_in < BLK ? rows_in : BLK) << 8);
+            mbar_arrive_expect_tx(smem_u32(&sh.full[st]), 2 * TILE_BYTES);
+            tma_load_2d(smem_u32(sh.ds[st]), &maps.ds, smem_u32(&sh.full[st]), 0, trow);
+            tma_load_2d(smem_u32(sh.ds[st]) + HALF_TILE_BYTES, &maps.ds, smem_u32(&sh.full[st]), 64, trow);
+            tma_load_2d(smem_u32(sh.k[st]), &maps.k, smem_u32(&sh.full[st]), col0, krow);
+            tma_load_2d(smem_u32(sh.k[st]) + HALF_TILE_BYTES, &maps.k, smem_u32(&sh.full[st]), col0 + 64, krow);
+          }
+          __syncwarp();
+          ++gt;
+          if (++st == DQS_STAGES) { st = 0; ph ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    constexpr uint32_t IDESC = idesc_f16(IS_BF16 ? 1 : 0, BLK, HEAD_DIM, 1, 1);  // dS^T (M-major A) x K (N-major B)
+    constexpr uint32_t HI = desc_hi_sw128(1024);
+    const uint32_t ds_lo0 = desc_lo_sw128(smem_u32(sh.ds[0]), HALF_TILE_BYTES);  // 64-query groups one box apart
+    const uint32_t k_lo0 = desc_lo_sw128(smem_u32(sh.k[0]), HALF_TILE_BYTES);    // 64-column groups one box apart
+    uint32_t gt = 0, it = 0, st = 0, ph = 0;
+    bool ok = true;
+    auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(smem_u32(bar), parity, abort_flag, a.status, WAIT_MMA));
+    };
+    int2 w_unused;
+    SeqInfo s_unused;
+    uint32_t t_unused = 0u, f_unused = 0u;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w_unused, s_unused, t_unused, f_unused, ok, abort_flag, a.status, WAIT_MMA); ++n_item, ++it) {
+      const uint32_t ab = it & 1;
+      ok = wait_all(&sh.acc_empty[ab], ((it >> 1) & 1) ^ 1);
+      if (!ok) break;
+      tc_fence_after();
+      bool last = false;
+      uint32_t n_acc = 0;
+      while (!last && ok) {
+        ok = wait_all(&sh.full[st], ph);
+        if (!ok) break;
+        const int meta = sh.meta[gt & (META_RING - 1)];
+        last = meta & 1;
+        const int rows_in = meta >> 8;
+        if (rows_in < BLK) {
+          // Key rows past the sequence end belong to the next sequence (or are zero fill): their dS entries
+          // are zero, but 0 * NaN would not be, so the rows are cleared before they feed the MMA.
+          zero_box_rows(sh.k[st], rows_in, BLK, lane, 32);
+          zero_box_rows(sh.k[st] + HALF_TILE_BYTES, rows_in, BLK, lane, 32);
+          __syncwarp();
+        }
+        tc_fence_after();
+        if (elect_one()) {
+          const uint32_t a_lo = ds_lo0 + st * (TILE_BYTES >> 4), b_lo = k_lo0 + st * (TILE_BYTES >> 4);
+#pragma unroll
+          for (int kk = 0; kk < BLK / 16; ++kk)  // 16 keys per step: 16 rows of 128 bytes in each box
+            mma_ss(tmem + DQS_ACC0 + ab * HEAD_DIM, desc_join(a_lo + kk * (2048 >> 4), HI), desc_join(b_lo + kk * (2048 >> 4), HI),
+                   IDESC, (n_acc > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(smem_u32(&sh.empty[st]));
+          if (last) tc_commit(smem_u32(&sh.acc_full[ab]));
+        }
+        __syncwarp();
+        ++n_acc;
+        ++gt;
+        if (++st == DQS_STAGES) { st = 0; ph ^= 1; }
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ work-item scheduler
+    run_item_scheduler<false>(sh.ring, a, items, total_items, ws + WS_CURSOR1, abort_flag);
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ accumulator drain (two groups, 64 columns each)
+    const int wg = (warp - 4) >> 2;
+    const int row = ((warp & 3) << 5) | lane;  // query row inside the block = thread index in the group
+    const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) << 5) << 16;
+    unsigned char* stage = sh.stage + wg * HALF_TILE_BYTES;
+    const bool per_token = a.scale_mode == 2;
+    uint32_t it = 0;
+    bool ok = true;
+    int2 w;
+    SeqInfo s;
+    uint32_t todo0 = 0u, full0 = 0u;
+    for (uint32_t n_item = 0; ok && next_item(sh.ring, n_item, w, s, todo0, full0, ok, abort_flag, a.status, WAIT_EPILOGUE); ++n_item, ++it) {
+      // accumulator row r holds the query whose index inside the block is r with bits 5 and 6 swapped (the
+      // column order of the stored tiles)
+      const int qrow = (row & 31) | (((row >> 6) & 1) << 5) | (((row >> 5) & 1) << 6);
+      const int head = w.x >> 16, m0 = w.y * BLK, m = m0 + qrow;
+      const uint32_t ab = it & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sh.acc_full[ab]), (it >> 1) & 1, abort_flag, a.status, WAIT_EPILOGUE));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t ov0[32], ov1[32];
+      const uint32_t acc = tmem + lane_addr + DQS_ACC0 + ab * HEAD_DIM + wg * 64;
+      tmem_ld32(acc, ov0);
+      tmem_ld32(acc + 32, ov1);
+      tmem_wait_ld(ov0);
+      tmem_wait_ld(ov1);
+      tc_fence_before();
+      mbar_arrive(smem_u32(&sh.acc_empty[ab]));
+      // 1/2 and alpha once per output row; the stored tiles carry a per-token scale already, a scalar one not
+      const float sc = m < s.len ? 0.5f * a.alpha * (per_token ? 1.f : row_scale(a, 0)) : 0.f;
+      if (row == 0) bulk_wait_read_all();  // the previous item's store has read the staging buffer
+      group_barrier(wg);
+      stage_row64<IS_BF16>(stage, qrow, ov0, ov1, sc);
+      if (m0 + BLK <= s.len) {
+        fence_proxy_async();
+        group_barrier(wg);
+        if (row == 0) {
+          tma_store_2d(&maps.dq, smem_u32(stage), head * HEAD_DIM + wg * 64, static_cast<int>(s.start) + m0);
+          bulk_commit();
+        }
+      } else {
+        group_barrier(wg);
+        store_staged64(stage, reinterpret_cast<unsigned short*>(a.dq) + (s.start + m0) * a.dq_rs + head * HEAD_DIM + wg * 64,
+                       a.dq_rs, s.len - m0, row);
+      }
+    }
+    if (row == 0) bulk_wait_all();  // shared memory must outlive the stores that read it
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    if (*abort_flag) {
+      const unsigned long long t0 = globaltimer_ns();
+      while (globaltimer_ns() - t0 < 200000ull) __nanosleep(1000);
+    }
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
 }  // namespace
 }  // namespace tc
 
-cudaError_t tc_backward(const KernelArgs& a, int dtype, void* workspace, cudaStream_t st) {
+cudaError_t tc_backward(const KernelArgs& a_in, int dtype, void* workspace, cudaStream_t st) {
   using namespace tc;
   const bool bf16 = dtype == B200_HSTU_BF16;
-  const WorkspaceLayout w = workspace_layout(a.T, a.B, a.H);
+  const WorkspaceLayout w = backward_layout(a_in);
   int* ws = reinterpret_cast<int*>(workspace);
+  KernelArgs a = a_in;
+  const bool stored_ds = w.ds_tile_cap > 0;
+  if (stored_ds) {
+    unsigned char* base = reinterpret_cast<unsigned char*>(workspace);
+    a.ds_tiles = base + w.off_ds_tiles;
+    a.ds_tile_base = reinterpret_cast<const long long*>(base + w.off_tile_base);
+    a.ds_tile_cap = w.ds_tile_cap;
+    a.ds_square = w.ds_square;
+  }
   MapsBwd maps;
   const long long width = (long long)a.H * HEAD_DIM;
   set_error_stage("backward: tensor maps");
@@ -984,6 +1252,11 @@ cudaError_t tc_backward(const KernelArgs& a, int dtype, void* workspace, cudaStr
       !make_map(&maps.dq, a.dq, a.T, width, a.dq_rs, bf16) || !make_map(&maps.dk, a.dk, a.T, width, a.dk_rs, bf16) ||
       !make_map(&maps.dv, a.dv, a.T, width, a.dv_rs, bf16))
     return cudaErrorInvalidValue;
+  if (stored_ds) {
+    if (!make_map(&maps.ds, a.ds_tiles, w.ds_tile_cap * BLK, BLK, BLK, bf16)) return cudaErrorInvalidValue;
+  } else {
+    maps.ds = maps.q;  // not used
+  }
   set_error_stage("backward: work-list kernels");
   cudaError_t e = launch_prep(a, bf16, ws, w, true, st);
   if (e != cudaSuccess) return e;
@@ -1003,7 +1276,17 @@ cudaError_t tc_backward(const KernelArgs& a, int dtype, void* workspace, cudaStr
     e = launch_dependent(kern, static_cast<unsigned>(grid), BWD_THREADS, smem, st, true, maps, a, ws, w.off_items);
     if (e != cudaSuccess) return e;
   }
-  if (!a.skip_dq) {
+  if (!a.skip_dq && stored_ds) {
+    set_error_stage("backward: dQ kernel (stored dS tiles)");
+    const size_t smem = sizeof(DqsShared) + 1024;
+    auto kern = bf16 ? hstu_bwd_dq_stored_tc<true> : hstu_bwd_dq_stored_tc<false>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    // behind the dK/dV kernel as a dependent launch: its CTAs become resident early, and wait at their top
+    // until that kernel has completed
+    e = launch_dependent(kern, static_cast<unsigned>(grid), BWD_THREADS, smem, st, !a.skip_dkv, maps, a, ws, w.off_items);
+    if (e != cudaSuccess) return e;
+  } else if (!a.skip_dq) {
     set_error_stage("backward: dQ kernel");
     const size_t smem = sizeof(DqShared) + 1024;
 #ifdef B200_HSTU_PROFILING

@@ -25,6 +25,12 @@ struct WorkspaceLayout {
   long long nbins, max_items;
   long long off_sorted, off_hist, off_cnt, off_start, off_chunk, off_items, total_ints;
   int chunk_seqs;  // sequences per locality chunk of the work list
+  // backward with stored dS tiles (ds_tile_cap == 0: not used), behind the ints above:
+  long long off_tile_base;   // byte offset of the per-sequence first-tile indices ([B] long long)
+  long long off_ds_tiles;    // byte offset of the tile region (1024-byte aligned)
+  long long ds_tile_cap;     // tiles it holds
+  long long total_bytes;     // whole workspace
+  int ds_square;             // tiles of a sequence indexed as a square (contextual prefix) or a triangle
 };
 
 HSTU_HD WorkspaceLayout workspace_layout(long long T, int B, int H) {
@@ -39,7 +45,37 @@ HSTU_HD WorkspaceLayout workspace_layout(long long T, int B, int H) {
   w.off_items = (w.off_chunk + B + 2 + 1) & ~1LL;  // int2 alignment
   w.chunk_seqs = 8;
   w.total_ints = w.off_items + 2 * w.max_items;
+  w.off_tile_base = w.off_ds_tiles = w.ds_tile_cap = 0;
+  w.ds_square = 0;
+  w.total_bytes = (w.total_ints * 4 + 255) & ~255LL;
   return w;
+}
+
+constexpr int DS_TILE_BYTES = BLK * BLK * 2;  // one 128 x 128 16-bit dS^T tile
+
+// Tiles of one (sequence, head) with nb 128-row blocks, and the index of tile (query block i, key block j)
+// among them.  Causal masks keep j <= i (a triangle); with a contextual prefix a sequence whose tokens are all
+// targets keeps the whole square.
+HSTU_HD long long ds_tiles_of(long long nb, int square) { return square ? nb * nb : nb * (nb + 1) / 2; }
+HSTU_HD long long ds_tile_index(int i, int j, long long nb, int square) {
+  return square ? i * nb + j : static_cast<long long>(i) * (i + 1) / 2 + j;
+}
+
+// Adds the stored-dS region to a backward workspace: room for every tile any batch of T tokens in B
+// sequences of at most max_seq_len tokens can have.  limit_bytes: leave the region out above this size.
+HSTU_HD void add_ds_region(WorkspaceLayout& w, long long T, int B, int H, long long max_seq_len, int square,
+                           unsigned long long limit_bytes) {
+  if (max_seq_len <= 0) return;
+  const long long nbmax = (max_seq_len + BLK - 1) / BLK, blocks = T / BLK + B;
+  // sum over sequences of tiles(nb_b) <= (sum of nb_b) * max over nb <= nbmax of tiles(nb) / nb
+  const long long per_block_2 = square ? 2 * nbmax : nbmax + 1;  // twice the bound per block
+  const long long cap = (blocks * per_block_2 + 1) / 2 * H;
+  if (cap <= 0 || static_cast<unsigned long long>(cap) > limit_bytes / DS_TILE_BYTES) return;
+  w.off_tile_base = (w.total_ints * 4 + 255) & ~255LL;
+  w.off_ds_tiles = (w.off_tile_base + 8LL * (B + 1) + 1023) & ~1023LL;
+  w.ds_tile_cap = cap;
+  w.ds_square = square;
+  w.total_bytes = w.off_ds_tiles + cap * DS_TILE_BYTES;
 }
 
 // Workspace header slots: next unclaimed work-list entry, one cursor per main kernel of a call.
@@ -288,12 +324,13 @@ __device__ __forceinline__ void run_item_scheduler(ItemRing& r, const KernelArgs
     const bool have = idx < total;
     ItemSlot it;
     it.w = make_int2(-1, 0);
-    it.s.start = 0; it.s.len = 0; it.s.hist = 0; it.s.has_targets = 0; it.s.boundary = 0;
+    it.s.start = 0; it.s.len = 0; it.s.hist = 0; it.s.has_targets = 0; it.s.boundary = 0; it.s.tile_base = 0;
     it.todo = 0u; it.full = 0u;
     if (have) {
       if (lane == 0) {
         it.w = items[idx];
         it.s = load_seq(a, it.w.x & 0xffff);
+        if (a.ds_tile_base != nullptr) it.s.tile_base = a.ds_tile_base[it.w.x & 0xffff];
       }
       it.w.x = __shfl_sync(0xffffffffu, it.w.x, 0);
       it.w.y = __shfl_sync(0xffffffffu, it.w.y, 0);
@@ -302,6 +339,7 @@ __device__ __forceinline__ void run_item_scheduler(ItemRing& r, const KernelArgs
       it.s.hist = __shfl_sync(0xffffffffu, it.s.hist, 0);
       it.s.has_targets = __shfl_sync(0xffffffffu, it.s.has_targets, 0);
       it.s.boundary = __shfl_sync(0xffffffffu, it.s.boundary, 0);
+      it.s.tile_base = __shfl_sync(0xffffffffu, it.s.tile_base, 0);
       int count = 0;
       const int cls = item_tile_class<KEY_MAJOR>(it.w, it.s, a.mask, lane, &count);
       it.todo = __ballot_sync(0xffffffffu, cls != TILE_SKIP);

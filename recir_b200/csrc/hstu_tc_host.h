@@ -20,6 +20,8 @@ bool make_map_bytes(CUtensorMap* m, const void* base, long long rows, long long 
 int sm_count();
 // Grid of the persistent kernels (also the stride with which CTAs walk the work list).
 int main_grid(const WorkspaceLayout& w);
+// Workspace layout of a backward call (work list, and the stored dS tiles when they are used).
+WorkspaceLayout backward_layout(const KernelArgs& a);
 // Builds the work list in the workspace and zeroes the output rows no sequence owns.
 cudaError_t launch_prep(const KernelArgs& a, bool bf16, int* ws, const WorkspaceLayout& w, bool backward,
                         cudaStream_t st);

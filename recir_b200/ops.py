@@ -111,10 +111,25 @@ def check_status(device=None, what: str = "recir_b200") -> None:
         raise RuntimeError(f"{what}: " + "; ".join(problems))
 
 
-def set_backward_passes(dkv: bool = True, dq: bool = True) -> None:
-    """Timing aid: leave one of the two backward passes out (its outputs stay unwritten)."""
+_recompute_dq = False
+
+
+def set_backward_passes(dkv: bool = True, dq: bool = True, timing_only: bool = False) -> None:
+    """Leave one of the two backward passes out (its outputs stay unwritten).  By default the dQ pass reads the dS
+    tiles the dK/dV pass of the SAME call stored in the workspace, so a pass run alone uses the recomputing dQ
+    kernel and the gradients are valid.  ``timing_only``: keep the stored-tile kernels (a dQ pass run alone then
+    reads whatever the workspace holds: its time is meaningful, its output is not)."""
     global _bwd_extra_flags
     _bwd_extra_flags = (0 if dkv else _lib.FLAG_BWD_SKIP_DKV) | (0 if dq else _lib.FLAG_BWD_SKIP_DQ)
+    if not (dkv and dq) and not timing_only:
+        _bwd_extra_flags |= _lib.FLAG_BWD_RECOMPUTE_DQ
+
+
+def set_recompute_dq(flag: bool) -> None:
+    """Backward: make the dQ pass recompute S and dP (a workspace of a few hundred KB) instead of reading the dS
+    tiles the dK/dV pass stores (32 KB per 128 x 128 tile the mask keeps; see ``b200_hstu_workspace_bytes``)."""
+    global _recompute_dq
+    _recompute_dq = bool(flag)
 
 
 # ---------------------------------------------------------------------------
@@ -294,7 +309,7 @@ def _bwd_cuda(dout, q, k, v, seq_offsets, max_seq_len, alpha, causal, num_target
     with torch.cuda.device(q.device):
         keep = _fill(p, q, k, v, seq_offsets, max_seq_len, alpha, causal, num_targets,
                      contextual_seq_len, max_attn_len, attn_scale, full_attn_size)
-        p.flags |= _bwd_extra_flags
+        p.flags |= _bwd_extra_flags | (_lib.FLAG_BWD_RECOMPUTE_DQ if _recompute_dq else 0)
         p.d_o = dout.data_ptr()
         p.do_row_stride = dout.stride(0)
         p.dq, p.dk, p.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
