@@ -53,7 +53,7 @@ NOMINAL_BF16_TFLOPS = 2250.0
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from the committed ncu capture of the same
 # B/H/D and length distribution (profiles/tc_kernels_cfg1_ncu_full.md names the build it was taken
 # from), and that capture's token count.
-NCU_CFG1_DRAM_BYTES = {"hstu_fwd_tc": 315.5e6, "hstu_bwd_dkv_tc": 471.2e6, "hstu_bwd_dq_tc": 410.8e6}
+NCU_CFG1_DRAM_BYTES = {"hstu_fwd_tc": 314.4e6, "hstu_bwd_dkv_tc": 1060.8e6, "hstu_bwd_dq_tc": 715.8e6}
 NCU_CFG1_TOKENS = 78262
 NCU_CAPTURE = "profiles/tc_kernels_cfg1_ncu_full.md"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -663,9 +663,13 @@ def main():
             # scaled by tokens (traffic grows with the token count at a fixed length distribution)
             "traffic": dom_traffic * local_tokens / NCU_CFG1_TOKENS,
             "traffic_source": NCU_CAPTURE,
-            # fwd: q,k,v read + o written; dK/dV pass: q,k,v,dO read + dk,dv written; dQ pass: q,k,v,dO read + dq written
-            "algorithmic_bytes": {"hstu_fwd_tc": 4, "hstu_bwd_dkv_tc": 6, "hstu_bwd_dq_tc": 5}[dom]
+            # tensors of T*H*D 16-bit elements: fwd q,k,v read + o written; dK/dV pass q,k,v,dO read + dk,dv
+            # written; dQ pass k read + dq written.  The dS tiles that the dK/dV pass writes and the dQ pass
+            # reads (32 KB per kept 128x128 tile) are this design's own traffic on top: see `traffic`.
+            "algorithmic_bytes": {"hstu_fwd_tc": 4, "hstu_bwd_dkv_tc": 6, "hstu_bwd_dq_tc": 2}[dom]
             * local_tokens * H * D * 2,
+            "kernels": {"hstu_bwd_dq_tc": "hstu_bwd_dq_stored_tc: dQ from the dS tiles the dK/dV pass stored "
+                                          "(C-ABI default; B200_HSTU_FLAG_BWD_RECOMPUTE_DQ selects the recomputing kernel)"},
             "per_kernel_ms": {k: v[1] for k, v in kernels.items()},
             "per_kernel_tflops": {k: v[0] / (v[1] * 1e-3) / 1e12 for k, v in kernels.items()},
             "fwd_ms": fwd_med, "bwd_ms": bwd_med,

@@ -102,7 +102,7 @@ def check_status(device=None, what: str = "recir_b200") -> None:
         if any(vals):
             t.zero_()
         if vals[0] & 1:
-            problems.append(f"{dev}: seq_offsets were malformed (negative, decreasing, beyond T, or overlapping) "
+            problems.append(f"{dev}: seq_offsets were malformed (negative, decreasing, beyond T, overlapping, or a sequence longer than max_seq_len) "
                             "and were clamped on the device; the results are not meaningful")
         if vals[1]:
             problems.append(f"{dev}: a pipeline wait gave up after its time limit: "

@@ -376,6 +376,77 @@ def test_backward_passes_can_run_one_at_a_time():
     assert torch.equal(dk, dk1) and torch.equal(dv, dv1) and torch.equal(dq, dq2)
 
 
+@pytest.mark.parametrize("name", ["ragged_targets", "window_ctx", "all_targets_ctx", "full_tail", "scalar_scale"])
+def test_dq_from_stored_ds_tiles_equals_the_recomputing_pass(name):
+    """The default backward keeps the dS tiles of the dK/dV pass for the dQ pass; with the C-ABI flag
+    B200_HSTU_FLAG_BWD_RECOMPUTE_DQ the dQ pass recomputes S and dP instead.  Both round dS to 16 bits the same
+    way and add the same products in the same order: the gradients are bit-identical (contextual prefixes use
+    the square tile index, everything else the triangular one)."""
+    spec = dict(TC_CASES[name])
+    lengths, targets = spec.pop("lengths"), spec.pop("targets")
+    q, k, v, do, off, kw = _jagged_case(17, lengths, targets, H=3, **spec)
+    try:
+        ops.set_recompute_dq(False)
+        a = _gpu(q, k, v, do, off, kw)
+        ops.set_recompute_dq(True)
+        b = _gpu(q, k, v, do, off, kw)
+    finally:
+        ops.set_recompute_dq(False)
+    for x, y, nm in zip(a, b, ("o", "dq", "dk", "dv")):
+        assert torch.equal(x, y), nm
+    ops.check_status(what="stored dS tiles")
+
+
+def test_per_token_scale_with_stored_ds_tiles_matches_oracle():
+    g = torch.Generator().manual_seed(3)
+    lengths = [300, 129, 517]
+    q, k, v, do, off, kw = _jagged_case(19, lengths, [20, 0, 64], H=2, max_attn_len=200,
+                                        attn_scale=torch.rand(sum(lengths), generator=g) * 0.01 + 0.001)
+    ro, rdq, rdk, rdv = _oracle(q, k, v, do, off, kw)
+    o, dq, dk, dv = _gpu(q, k, v, do, off, kw)
+    for got, ref, nm in ((o, ro, "o"), (dq, rdq, "dq"), (dk, rdk, "dk"), (dv, rdv, "dv")):
+        assert rel_l2(got.float(), ref) <= 6e-3, nm
+
+
+def test_backward_workspace_sizes_and_length_bound():
+    """Workspace of the backward: with stored dS tiles it holds room for every tile a batch within the caller's
+    length bound can have; with the recompute flag, or when that would exceed the limit of the header, it is
+    the small work-list workspace.  A sequence LONGER than max_seq_len (outside the reference's contract: it
+    pads to that length) cannot overrun the region: tile indices are clamped and the call is flagged."""
+    import ctypes
+    from recir_b200 import _lib
+    lib = _lib.load()
+    q, k, v, do, off, kw = _jagged_case(23, [700, 300], [10, 0], H=2)
+    d = lambda x: x.to(DEV)
+    p = _lib.B200HstuParams()
+    qd = d(q)
+    keep = ops._fill(p, qd, d(k), d(v), d(off), kw["max_seq_len"], kw["alpha"], True, d(kw["num_targets"]), 0, 0, None, 0)
+    scratch = torch.empty_like(qd)  # stands in for every output and for dout: only sizes and alignment matter here
+    p.o = p.d_o = p.dq = p.dk = p.dv = scratch.data_ptr()
+    p.o_row_stride = p.do_row_stride = p.dq_row_stride = p.dk_row_stride = p.dv_row_stride = scratch.stride(0)
+    fwd = lib.b200_hstu_workspace_bytes(ctypes.byref(p), 0)
+    stored = lib.b200_hstu_workspace_bytes(ctypes.byref(p), 1)
+    p.flags |= _lib.FLAG_BWD_RECOMPUTE_DQ
+    recompute = lib.b200_hstu_workspace_bytes(ctypes.byref(p), 1)
+    p.flags &= ~_lib.FLAG_BWD_RECOMPUTE_DQ
+    blocks, nbmax = 1000 // 128 + 2, (700 + 127) // 128
+    tiles = (blocks * (nbmax + 1) + 1) // 2 * 2
+    assert recompute == fwd and stored >= recompute + tiles * 32768 and stored < recompute + tiles * 32768 + 8192
+    p.T, p.max_seq_len = 1 << 30, 1 << 20  # would need far more than the limit: the small workspace again
+    assert lib.b200_hstu_workspace_bytes(ctypes.byref(p), 1) < (1 << 33)
+    del keep
+    # a length bound that is too small: clamped tile indices, flagged, the context stays usable
+    kw_small = dict(kw, max_seq_len=128)
+    ops.check_status(what="before")
+    _gpu(q, k, v, do, off, kw_small)
+    with pytest.raises(RuntimeError, match="offsets"):
+        ops.check_status(what="length bound")
+    o, dq, dk, dv = _gpu(q, k, v, do, off, kw)
+    ops.check_status(what="after")
+    ro, rdq, _, _ = _oracle(q, k, v, do, off, kw)
+    assert rel_l2(dq.float(), rdq) <= 6e-3
+
+
 def test_first_call_on_a_fresh_thread_and_in_a_fresh_process():
     """Tensor-map encoding needs a current CUDA context on the calling thread; a worker thread whose
     first CUDA work is this library (an autograd thread in a new process) has none until the library
