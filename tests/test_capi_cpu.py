@@ -56,6 +56,37 @@ def test_argument_errors_detected_on_host():
     assert lib.b200_hstu_workspace_bytes(ctypes.byref(p), 0) == 0
 
 
+def test_backward_workspace_size_is_host_arithmetic():
+    """b200_hstu_workspace_bytes needs no GPU: the backward's size follows from T, B, H, max_seq_len, the
+    contextual prefix and the recompute flag alone (pointers are only checked for null and alignment)."""
+    lib = _lib.load()
+    p = _lib.B200HstuParams()
+    p.struct_size = ctypes.sizeof(p)
+    p.dtype = _lib.BF16
+    p.H, p.Dqk, p.Dv, p.T, p.B, p.max_seq_len = 4, 128, 128, 100_000, 64, 2048
+    p.flags = _lib.FLAG_CAUSAL | _lib.FLAG_OFFSETS_I64
+    fake = 0x7f0000000000  # never dereferenced on the host
+    for name in ("q", "k", "v", "o", "d_o", "dq", "dk", "dv", "seq_offsets"):
+        setattr(p, name, fake)
+    for name in ("q", "k", "v", "o", "do", "dq", "dk", "dv"):
+        setattr(p, name + "_row_stride", 4 * 128)
+    p.alpha = 0.1
+    fwd = lib.b200_hstu_workspace_bytes(ctypes.byref(p), 0)
+    bwd = lib.b200_hstu_workspace_bytes(ctypes.byref(p), 1)
+    assert 0 < fwd < (1 << 22)
+    blocks, nbmax = 100_000 // 128 + 64, 2048 // 128
+    tiles = (blocks * (nbmax + 1) + 1) // 2 * 4
+    assert fwd + tiles * 32768 <= bwd < fwd + tiles * 32768 + 4096
+    p.contextual_seq_len = 2  # all-target sequences keep the whole square: twice the triangle's bound
+    assert lib.b200_hstu_workspace_bytes(ctypes.byref(p), 1) >= fwd + blocks * nbmax * 4 * 32768
+    p.contextual_seq_len = 0
+    p.flags |= _lib.FLAG_BWD_RECOMPUTE_DQ
+    assert lib.b200_hstu_workspace_bytes(ctypes.byref(p), 1) == fwd
+    p.flags &= ~_lib.FLAG_BWD_RECOMPUTE_DQ
+    p.max_seq_len = 1 << 20  # the region would pass the limit of the header: the small workspace again
+    assert lib.b200_hstu_workspace_bytes(ctypes.byref(p), 1) == fwd
+
+
 def _mq(L, t, causal, w, ctx, f):
     q = _lib.B200HstuMaskQuery()
     q.len, q.has_targets, q.num_targets = L, int(t is not None), 0 if t is None else t
