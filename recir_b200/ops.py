@@ -226,7 +226,16 @@ def _workspace(lib, params, pass_id, device):
     need = lib.b200_hstu_workspace_bytes(ctypes.byref(params), pass_id)
     if need == 0:
         return None
-    ws = torch.empty(need + 256, dtype=torch.uint8, device=device)
+    try:
+        ws = torch.empty(need + 256, dtype=torch.uint8, device=device)
+    except torch.cuda.OutOfMemoryError:
+        # The backward's dS tiles do not fit beside what the caller holds: the recomputing dQ pass needs
+        # only the work list (same gradients, bit for bit).
+        if pass_id != 1 or (params.flags & _lib.FLAG_BWD_RECOMPUTE_DQ):
+            raise
+        params.flags |= _lib.FLAG_BWD_RECOMPUTE_DQ
+        need = lib.b200_hstu_workspace_bytes(ctypes.byref(params), pass_id)
+        ws = torch.empty(need + 256, dtype=torch.uint8, device=device)
     off = (-ws.data_ptr()) % 256
     params.workspace = ws.data_ptr() + off
     params.workspace_bytes = need
