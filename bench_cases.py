@@ -385,7 +385,10 @@ def main_trace(argv):
         p.dq, p.dk, p.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
         p.dq_row_stride = p.dk_row_stride = p.dv_row_stride = dq.stride(0)
         pass_id = 0 if which == "fwd" else 1
-        p.flags |= _lib.FLAG_TRACE | {"fwd": 0, "dkv": _lib.FLAG_BWD_SKIP_DQ, "dq": _lib.FLAG_BWD_SKIP_DKV}[which]
+        # "dq" traces the recomputing dQ kernel (the one from stored dS tiles has no instrumented variant:
+        # it has no epilogue phases to speak of); "dkv" runs as in a default call, storing its tiles
+        p.flags |= _lib.FLAG_TRACE | {"fwd": 0, "dkv": _lib.FLAG_BWD_SKIP_DQ,
+                                      "dq": _lib.FLAG_BWD_SKIP_DKV | _lib.FLAG_BWD_RECOMPUTE_DQ}[which]
         need = lib.b200_hstu_workspace_bytes(ctypes.byref(p), pass_id)
         ws = torch.zeros(need // 4 + 64, dtype=torch.int32, device=dev)
         base = ((-ws.data_ptr()) % 256) // 4

@@ -864,6 +864,20 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
             }
             tmem_st16(st_addr, pp);  // P^T and dS^T (16 columns each) over the group's own score columns
             tmem_st16(dp_addr, pd);
+            if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt + sub, 3, 6);
+            if (q0 + BLK > s.len && wg == 0) {
+              // query rows past the sequence end are B rows of the dV / dK MMAs: clear them
+              const int first_bad = s.len - q0, lo = first_bad > sub * 64 ? first_bad : sub * 64;
+              zero_box_rows(sh.q[gt % KV_STAGES] + (row >> 6) * HALF_TILE_BYTES, lo, sub * 64 + 64, row & 63, 64);
+              zero_box_rows(sh.d_o[gt % KV_STAGES] + (row >> 6) * HALF_TILE_BYTES, lo, sub * 64 + 64, row & 63, 64);
+            }
+            sw2.start();
+            tmem_wait_st();
+            sw2.stop(pe_st);
+            tc_fence_before();
+            mbar_arrive(smem_u32(&sh.p_ready[sub]));
+            if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt + sub, 4, 6);
+            // (behind the hand-over, so that the dV / dK MMAs of this half tile run meanwhile)
             if (a.ds_tiles != nullptr) {
               // The dQ pass reads this dS^T tile back (keys x queries) instead of recomputing it.  The group
               // stages its 2 x 32 query columns of the tile as ONE 64-column box (row = this thread's key row,
@@ -894,19 +908,6 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
                 }
               }
             }
-            if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt + sub, 3, 6);
-            if (q0 + BLK > s.len && wg == 0) {
-              // query rows past the sequence end are B rows of the dV / dK MMAs: clear them
-              const int first_bad = s.len - q0, lo = first_bad > sub * 64 ? first_bad : sub * 64;
-              zero_box_rows(sh.q[gt % KV_STAGES] + (row >> 6) * HALF_TILE_BYTES, lo, sub * 64 + 64, row & 63, 64);
-              zero_box_rows(sh.d_o[gt % KV_STAGES] + (row >> 6) * HALF_TILE_BYTES, lo, sub * 64 + 64, row & 63, 64);
-            }
-            sw2.start();
-            tmem_wait_st();
-            sw2.stop(pe_st);
-            tc_fence_before();
-            mbar_arrive(smem_u32(&sh.p_ready[sub]));
-            if (threadIdx.x == 128) trace_event<PROF>(a.trace_buf, 4096, 2 * gt + sub, 4, 6);
             sw.stop(pe_tile);
           }
           ++gt;
