@@ -1,9 +1,15 @@
 """Forward+backward for callers whose tensors live in (pinned) host memory.
 
-Sequences never interact, so a jagged batch can be cut into chunks of whole sequences and
-streamed: while chunk ``c`` is computed, chunk ``c+1`` is copied in and the results of
-chunk ``c-1`` are copied out.  PCIe is full duplex, so the two copy directions overlap as
-well.  Three CUDA streams (copy-in, compute, copy-out) and two device buffer slots.
+Sequences never interact, so a jagged batch can be streamed: the token rows are copied in as
+chunks of equal size, every sequence is computed as soon as its last row has arrived, and results
+leave in chunks of the same size as soon as their last sequence has been computed.  PCIe is full
+duplex, so the two copy directions overlap with each other and with the kernels.  Three CUDA
+streams (copy-in, compute, copy-out) over device buffers that hold the whole batch.
+
+The copy chunks are cut by token count, not at sequence ends: with chunks of whole sequences the
+sizes differ by the length of a sequence, and copies of unequal sizes running in both directions
+at once move about a tenth less per second on PCIe than equal ones (measured: 7.97 against 7.14 ms
+for 2 x 320 MB in 16 chunks).
 
 Enqueueing the pipeline from Python costs a few hundred microseconds per chunk, which on a slow or
 busy host can exceed the copy time.  So the first ``run`` on a given set of host buffers records the
@@ -36,25 +42,20 @@ class HostPipeline:
         offs = seq_offsets.to(torch.int64).cpu().numpy()
         B = len(offs) - 1
         total = int(offs[-1])
-        n_chunks = max(1, min(n_chunks, B))
-        # contiguous groups of whole sequences with about equal token counts
-        bounds = [0]
-        for c in range(1, n_chunks):
-            target = total * c / n_chunks
-            b = int(np.searchsorted(offs, target, side="left"))
-            bounds.append(min(max(b, bounds[-1] + 1), B - (n_chunks - c)))
-        bounds.append(B)
-        self.chunks = []
-        max_tokens = 0
-        for c in range(n_chunks):
-            b0, b1 = bounds[c], bounds[c + 1]
-            t0, t1 = int(offs[b0]), int(offs[b1])
-            local = torch.from_numpy(offs[b0:b1 + 1] - offs[b0]).to(self.device)
-            nt = None if num_targets is None else num_targets[b0:b1].to(self.device)
-            self.chunks.append((t0, t1, local, nt))
-            max_tokens = max(max_tokens, t1 - t0)
-        mk = lambda d: torch.empty(max_tokens, heads, d, dtype=dtype, device=self.device)
-        self.slots = [dict(q=mk(dqk), k=mk(dqk), v=mk(dv), do=mk(dv)) for _ in range(2)]
+        n_chunks = max(1, min(n_chunks, total))
+        self.steps = plan_steps(offs, n_chunks)
+        # per step: the group of whole sequences whose last row arrives with the step's rows
+        self.groups = []
+        for st in self.steps:
+            b0, b1 = st["seqs"]
+            if b1 > b0:
+                local = torch.from_numpy(offs[b0:b1 + 1] - offs[b0]).to(self.device)
+                nt = None if num_targets is None else num_targets[b0:b1].to(self.device)
+                self.groups.append((int(offs[b0]), int(offs[b1]), local, nt))
+            else:
+                self.groups.append(None)
+        mk = lambda d: torch.empty(total, heads, d, dtype=dtype, device=self.device)
+        self.dev = dict(q=mk(dqk), k=mk(dqk), v=mk(dv), do=mk(dv), o=mk(dv), dq=mk(dqk), dk=mk(dqk), dv=mk(dv))
         self.s_in, self.s_comp, self.s_out = (torch.cuda.Stream(self.device) for _ in range(3))
         self.bytes_in = total * heads * (2 * dqk + 2 * dv) * torch.empty((), dtype=dtype).element_size()
         self.bytes_out = self.bytes_in
@@ -67,60 +68,83 @@ class HostPipeline:
         schedule is captured on the first call for a given set of host buffers (which must stay
         allocated and pinned) and replayed afterwards."""
         if not self.use_graph:
-            return self._enqueue(q, k, v, dout, o, dq, dk, dv, record_streams=True)
+            return self._enqueue(q, k, v, dout, o, dq, dk, dv)
         key = tuple(t.data_ptr() for t in (q, k, v, dout, o, dq, dk, dv))
         g = self._graphs.get(key)
         if g is None:
             # one eager pass first: everything that initialises lazily (function attributes, the
             # allocator's pools, the context of the side streams) happens outside the capture
-            self._enqueue(q, k, v, dout, o, dq, dk, dv, record_streams=True)
+            self._enqueue(q, k, v, dout, o, dq, dk, dv)
             torch.cuda.current_stream(self.device).synchronize()
             g = torch.cuda.CUDAGraph()
             cap = torch.cuda.Stream(self.device)
             cap.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.graph(g, stream=cap):
-                self._enqueue(q, k, v, dout, o, dq, dk, dv, record_streams=False)
+                self._enqueue(q, k, v, dout, o, dq, dk, dv)
             torch.cuda.current_stream(self.device).wait_stream(cap)
-            if len(self._graphs) >= 4:  # bounded: each graph keeps its own output buffers alive
+            if len(self._graphs) >= 4:  # bounded: each graph keeps its workspaces alive
                 self._graphs.pop(next(iter(self._graphs)))
             self._graphs[key] = g
         g.replay()
 
-    def _enqueue(self, q, k, v, dout, o, dq, dk, dv, record_streams: bool) -> None:
+    def _enqueue(self, q, k, v, dout, o, dq, dk, dv) -> None:
         cur = torch.cuda.current_stream(self.device)
         start = torch.cuda.Event()
         start.record(cur)
         for st in (self.s_in, self.s_comp, self.s_out):
             st.wait_event(start)
         max_seq_len, alpha, causal, ctx, win, full = self.cfg
-        slot_free = [None, None]
-        for c, (t0, t1, local, nt) in enumerate(self.chunks):
-            slot = self.slots[c % 2]
-            n = t1 - t0
+        d = self.dev
+        for st, grp in zip(self.steps, self.groups):
+            t0, t1 = st["rows_in"]
             with torch.cuda.stream(self.s_in):
-                if slot_free[c % 2] is not None:
-                    self.s_in.wait_event(slot_free[c % 2])
-                for name, src in (("q", q), ("k", k), ("v", v), ("do", dout)):
-                    slot[name][:n].copy_(src[t0:t1], non_blocking=True)
+                if t1 > t0:
+                    for name, src in (("q", q), ("k", k), ("v", v), ("do", dout)):
+                        d[name][t0:t1].copy_(src[t0:t1], non_blocking=True)
                 in_done = torch.cuda.Event()
                 in_done.record(self.s_in)
             with torch.cuda.stream(self.s_comp):
                 self.s_comp.wait_event(in_done)
-                a = (local, max_seq_len, alpha, causal, nt, ctx, win, None, full)
-                oc = torch.ops.recir.b200_hstu_attention_fwd(slot["q"][:n], slot["k"][:n], slot["v"][:n], *a)
-                gq, gk, gv = torch.ops.recir.b200_hstu_attention_bwd(slot["do"][:n], slot["q"][:n], slot["k"][:n],
-                                                                     slot["v"][:n], *a)
+                if grp is not None:
+                    g0, g1, local, nt = grp
+                    a = (local, max_seq_len, alpha, causal, nt, ctx, win, None, full)
+                    ops._fwd_cuda(d["q"][g0:g1], d["k"][g0:g1], d["v"][g0:g1], *a, out=d["o"][g0:g1])
+                    ops._bwd_cuda(d["do"][g0:g1], d["q"][g0:g1], d["k"][g0:g1], d["v"][g0:g1], *a,
+                                  grads=(d["dq"][g0:g1], d["dk"][g0:g1], d["dv"][g0:g1]))
                 comp_done = torch.cuda.Event()
                 comp_done.record(self.s_comp)
+            r0, r1 = st["rows_out"]
             with torch.cuda.stream(self.s_out):
                 self.s_out.wait_event(comp_done)
-                for dst, src in ((o, oc), (dq, gq), (dk, gk), (dv, gv)):
-                    dst[t0:t1].copy_(src, non_blocking=True)
-                    if record_streams:  # (a captured schedule owns its buffers for its whole life)
-                        src.record_stream(self.s_out)
-                done = torch.cuda.Event()
-                done.record(self.s_out)
-            # the inputs of this slot may be overwritten once its compute has finished
-            slot_free[c % 2] = comp_done
-        cur.wait_event(done)
+                if r1 > r0:
+                    for dst, name in ((o, "o"), (dq, "dq"), (dk, "dk"), (dv, "dv")):
+                        dst[r0:r1].copy_(d[name][r0:r1], non_blocking=True)
+        cur.wait_stream(self.s_out)
         cur.wait_stream(self.s_comp)
+        cur.wait_stream(self.s_in)
+
+
+def plan_steps(offs: np.ndarray, n_chunks: int) -> list[dict]:
+    """The pipeline's schedule for sequence offsets ``offs`` (``[B + 1]``, starting at 0): a list of steps,
+    each ``{"rows_in": (t0, t1), "seqs": (b0, b1), "rows_out": (r0, r1)}``.  Step ``c`` copies in rows
+    ``[t0, t1)`` (``n_chunks`` pieces of equal size), computes the sequences ``[b0, b1)`` that are complete
+    with those rows, and copies out rows ``[r0, r1)``: as many whole pieces as are computed by then.  The
+    last step copies out the rest."""
+    total = int(offs[-1])
+    B = len(offs) - 1
+    cuts = [total * c // n_chunks for c in range(n_chunks + 1)]
+    steps, b_prev, r_prev = [], 0, 0
+    for c in range(n_chunks):
+        t0, t1 = cuts[c], cuts[c + 1]
+        # sequences whose end is at or before t1 (empty sequences at the very end are swept up by the last step)
+        b1 = int(np.searchsorted(offs, t1, side="right")) - 1
+        b1 = B if c == n_chunks - 1 else max(b_prev, min(b1, B))
+        ready = int(offs[b1])  # every row below this is computed after this step
+        if c == n_chunks - 1:
+            r1 = total
+        else:
+            j = int(np.searchsorted(np.asarray(cuts), ready, side="right")) - 1  # largest cut <= ready
+            r1 = max(r_prev, cuts[j])
+        steps.append({"rows_in": (t0, t1), "seqs": (b_prev, b1), "rows_out": (r_prev, r1)})
+        b_prev, r_prev = b1, r1
+    return steps

@@ -270,16 +270,24 @@ def _pad_head_dim(t: torch.Tensor) -> torch.Tensor:
 
 
 def _fwd_cuda(q, k, v, seq_offsets, max_seq_len, alpha, causal, num_targets, contextual_seq_len,
-              max_attn_len, attn_scale, full_attn_size=0):
+              max_attn_len, attn_scale, full_attn_size=0, out=None):
+    """``out``: optional result tensor of the caller ([T, H, Dv], rows contiguous); allocated when absent."""
     global launch_counter
     validate_inputs(q, k, v, seq_offsets, num_targets, max_seq_len, attn_scale)
     lib = _lib.load()
     q, k, v = _rows(q), _rows(k), _rows(v)
     if _pads_to_tensor_core_width(q, k, v, causal):
-        out = _fwd_cuda(_pad_head_dim(q), _pad_head_dim(k), _pad_head_dim(v), seq_offsets, max_seq_len, alpha, causal,
-                        num_targets, contextual_seq_len, max_attn_len, attn_scale, full_attn_size)
-        return out[:, :, :v.shape[2]].contiguous()
-    out = torch.empty((q.shape[0], q.shape[1], v.shape[2]), dtype=v.dtype, device=v.device)
+        padded = _fwd_cuda(_pad_head_dim(q), _pad_head_dim(k), _pad_head_dim(v), seq_offsets, max_seq_len, alpha, causal,
+                           num_targets, contextual_seq_len, max_attn_len, attn_scale, full_attn_size)
+        if out is None:
+            return padded[:, :, :v.shape[2]].contiguous()
+        out.copy_(padded[:, :, :v.shape[2]])
+        return out
+    if out is None:
+        out = torch.empty((q.shape[0], q.shape[1], v.shape[2]), dtype=v.dtype, device=v.device)
+    elif out.shape != (q.shape[0], q.shape[1], v.shape[2]) or out.dtype != v.dtype or out.device != v.device \
+            or out.stride(2) != 1 or out.stride(1) != out.shape[2]:
+        raise ValueError("out must be a [T, H, Dv] tensor of v's dtype and device with contiguous rows")
     if q.shape[0] == 0:
         return out
     p = _lib.B200HstuParams()
@@ -299,19 +307,31 @@ def _fwd_cuda(q, k, v, seq_offsets, max_seq_len, alpha, causal, num_targets, con
 
 
 def _bwd_cuda(dout, q, k, v, seq_offsets, max_seq_len, alpha, causal, num_targets, contextual_seq_len,
-              max_attn_len, attn_scale, full_attn_size=0):
+              max_attn_len, attn_scale, full_attn_size=0, grads=None):
+    """``grads``: optional (dq, dk, dv) tensors of the caller, shaped like q, k, v with contiguous rows."""
     global launch_counter
     validate_inputs(q, k, v, seq_offsets, num_targets, max_seq_len, attn_scale, dout)
     lib = _lib.load()
     q, k, v, dout = _rows(q), _rows(k), _rows(v), _rows(dout)
     if _pads_to_tensor_core_width(q, k, v, causal):
         d = q.shape[2]
-        grads = _bwd_cuda(_pad_head_dim(dout), _pad_head_dim(q), _pad_head_dim(k), _pad_head_dim(v), seq_offsets, max_seq_len,
-                          alpha, causal, num_targets, contextual_seq_len, max_attn_len, attn_scale, full_attn_size)
-        return tuple(g[:, :, :d].contiguous() for g in grads)
-    dq = torch.empty(q.shape, dtype=q.dtype, device=q.device)
-    dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
-    dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
+        padded = _bwd_cuda(_pad_head_dim(dout), _pad_head_dim(q), _pad_head_dim(k), _pad_head_dim(v), seq_offsets, max_seq_len,
+                           alpha, causal, num_targets, contextual_seq_len, max_attn_len, attn_scale, full_attn_size)
+        if grads is None:
+            return tuple(g[:, :, :d].contiguous() for g in padded)
+        for dst, g in zip(grads, padded):
+            dst.copy_(g[:, :, :d])
+        return tuple(grads)
+    if grads is None:
+        dq = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+        dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
+        dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
+    else:
+        dq, dk, dv = grads
+        for g, like in ((dq, q), (dk, k), (dv, v)):
+            if g.shape != like.shape or g.dtype != like.dtype or g.device != like.device or g.stride(2) != 1 \
+                    or g.stride(1) != g.shape[2]:
+                raise ValueError("grads must be (dq, dk, dv) shaped like q, k, v with contiguous rows")
     if q.shape[0] == 0:
         return dq, dk, dv
     p = _lib.B200HstuParams()

@@ -301,15 +301,16 @@ def test_strided_rows_and_empty_batch():
     assert recir_b200.hstu_attention(e, e, e, torch.tensor([0, 0], device=DEV), 4).shape == (0, H, D)
 
 
-def test_host_pipeline_matches_direct_call():
+@pytest.mark.parametrize("n_chunks", [4, 25])  # 25: pieces shorter than most sequences, steps that compute nothing
+def test_host_pipeline_matches_direct_call(n_chunks):
     bt = workload.config1(batch=12)
     H, D = bt.q.shape[1], bt.q.shape[2]
     pipe = recir_b200.HostPipeline(bt.seq_offsets, bt.num_targets, H, D, D, bt.q.dtype, bt.max_seq_len, bt.alpha,
-                                   n_chunks=4)
+                                   n_chunks=n_chunks)
     hq, hk, hv, hdo = (x.pin_memory() for x in (bt.q, bt.k, bt.v, bt.dout))
     outs = [torch.empty_like(hq).pin_memory() for _ in range(4)]
     pipe.run(hq, hk, hv, hdo, *outs)
-    pipe.run(hq, hk, hv, hdo, *outs)  # slots are reused across calls
+    pipe.run(hq, hk, hv, hdo, *outs)  # the second call replays the captured schedule
     torch.cuda.synchronize()
     d = lambda x: x.to(DEV)
     a = (d(bt.seq_offsets), bt.max_seq_len, bt.alpha, True, d(bt.num_targets), 0, 0, None, 0)
