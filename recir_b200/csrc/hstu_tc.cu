@@ -357,7 +357,7 @@ static __device__ __noinline__ int classify_tile_cold(int m0, int n0, SeqInfo s,
 
 // One 32-column chunk of scores -> 16 packed 16-bit pairs of P; `bits` = kept columns of the chunk.
 template <bool IS_BF16, bool MASKED>
-__device__ __forceinline__ void silu_chunk(const uint32_t (&sv)[32], uint32_t (&pk)[16], float c1, uint32_t bits) {
+__device__ __forceinline__ void silu_chunk(const uint32_t (&sv)[32], uint32_t (&pk)[16], uint64_t c1, uint32_t bits) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     uint32_t p2 = silu_pair<IS_BF16>(sv[2 * i], sv[2 * i + 1], c1);
@@ -602,7 +602,7 @@ hstu_fwd_tc(const __grid_constant__ TensorMaps maps, KernelArgs a, int* __restri
     const int wg = (warp - 4) >> 2;                 // 0 or 1
     const int row = ((warp & 3) << 5) | lane;       // TMEM lane = query row inside the block
     const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) << 5) << 16;
-    const float c1 = 0.5f * a.alpha;
+    const uint64_t c1 = dup_f32x2(0.5f * a.alpha);
     const bool prof_thread = PROF && (threadIdx.x == 128 || threadIdx.x == 256);
     long long pf_total = 0, pf_sfull = 0, pf_ofull = 0, pf_part = 0, pf_fullt = 0, pf_fence = 0, pf_drain = 0;
     int n_part = 0, n_fullt = 0;

@@ -67,9 +67,11 @@ __device__ __forceinline__ constexpr uint32_t kstep_lo(int kk) { return (kk >> 2
 // P and dS for two scores with packed 16-bit math (one MUFU operation for the pair).
 //   u = (alpha/2) s, t = tanh(u);  p = u t + u;  2 silu'(x) = (1 + t)(1 + u (1 - t));  ds = dp * 2 silu'
 template <bool IS_BF16, bool WANT_P>
-__device__ __forceinline__ void bwd_pair(uint32_t s0, uint32_t s1, uint32_t dp0, uint32_t dp1, float c1, uint32_t& p2,
+__device__ __forceinline__ void bwd_pair(uint32_t s0, uint32_t s1, uint32_t dp0, uint32_t dp1, uint64_t c1, uint32_t& p2,
                                          uint32_t& ds2) {
-  const uint32_t u2 = pack2<IS_BF16>(c1 * __uint_as_float(s0), c1 * __uint_as_float(s1));
+  float u0, u1;
+  mul_f32x2(s0, s1, c1, u0, u1);
+  const uint32_t u2 = pack2<IS_BF16>(u0, u1);
   const uint32_t t2 = tanh2<IS_BF16>(u2);
   if (WANT_P) p2 = fma2<IS_BF16>(u2, t2, u2);
   const uint32_t w1 = add2<IS_BF16>(t2, one2<IS_BF16>());
@@ -82,7 +84,7 @@ __device__ __forceinline__ void bwd_pair(uint32_t s0, uint32_t s1, uint32_t dp0,
 // per-token scale are compile-time variants, so the 16 pairs interleave freely.
 template <bool IS_BF16, bool WANT_P, bool MASKED>
 __device__ __forceinline__ void bwd_chunk(const uint32_t (&sv)[32], const uint32_t (&dpv)[32], uint32_t (&pp)[16],
-                                          uint32_t (&pd)[16], float c1, uint32_t bits) {
+                                          uint32_t (&pd)[16], uint64_t c1, uint32_t bits) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     uint32_t p2 = 0u, d2;
@@ -391,7 +393,7 @@ hstu_bwd_dq_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restri
     const int wg = (warp - 4) >> 2;
     const int row = ((warp & 3) << 5) | lane;  // query row inside the block = thread index in the group
     const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) << 5) << 16;
-    const float c1 = 0.5f * a.alpha;
+    const uint64_t c1 = dup_f32x2(0.5f * a.alpha);
     unsigned char* stage = sh.stage + wg * HALF_TILE_BYTES;
     uint32_t gt = 0, it = 0;
     bool ok = true;
@@ -796,7 +798,7 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
     const int wg = (warp - 4) >> 2;
     const int row = ((warp & 3) << 5) | lane;  // key row inside the block = thread index in the group
     const uint32_t lane_addr = static_cast<uint32_t>((warp & 3) << 5) << 16;
-    const float c1 = 0.5f * a.alpha;
+    const uint64_t c1 = dup_f32x2(0.5f * a.alpha);
     const bool per_token = a.scale_mode == 2;
     unsigned char* stage = sh.stage + wg * HALF_TILE_BYTES;
     uint32_t gt = 0, it = 0;

@@ -245,8 +245,10 @@ __device__ __forceinline__ unsigned long long row_mask_bits64(const RowMask& rm,
 // x sigma(x) for two scores with packed 16-bit math: u = (alpha/2) s in fp32, then
 // t = tanh(u) (one MUFU operation for the pair) and p = u t + u in 16-bit FMA.
 template <bool IS_BF16>
-__device__ __forceinline__ uint32_t silu_pair(uint32_t s0, uint32_t s1, float c1) {
-  const uint32_t u2 = pack2<IS_BF16>(c1 * __uint_as_float(s0), c1 * __uint_as_float(s1));
+__device__ __forceinline__ uint32_t silu_pair(uint32_t s0, uint32_t s1, uint64_t c1x2) {
+  float u0, u1;
+  sm100::mul_f32x2(s0, s1, c1x2, u0, u1);
+  const uint32_t u2 = pack2<IS_BF16>(u0, u1);
   return sm100::fma2<IS_BF16>(u2, sm100::tanh2<IS_BF16>(u2), u2);
 }
 

@@ -301,6 +301,17 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   return r;
 }
 
+// Two fp32 products in one instruction: (a0, a1) * (c, c), c given twice in one 64-bit register.
+__device__ __forceinline__ uint64_t dup_f32x2(float c) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(c));
+  return r;
+}
+__device__ __forceinline__ void mul_f32x2(uint32_t a0, uint32_t a1, uint64_t c2, float& r0, float& r1) {
+  asm("{ .reg .b64 a, r; mov.b64 a, {%2, %3}; mul.rn.f32x2 r, a, %4; mov.b64 {%0, %1}, r; }"
+      : "=f"(r0), "=f"(r1) : "r"(a0), "r"(a1), "l"(c2));
+}
+
 // Packed 16-bit math: two elements per instruction (and per MUFU operation for tanh).
 template <bool BF16> __device__ __forceinline__ uint32_t tanh2(uint32_t x) {
   uint32_t y;
