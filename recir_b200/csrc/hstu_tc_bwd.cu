@@ -588,9 +588,11 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
   const int total_items = ws[0];
   // Launched as a dependent of build_work_items: the work list is complete from here on.
   grid_dependency_wait();
-  // The dQ kernel that follows in the stream reads nothing this kernel writes: let its CTAs start on
-  // the SMs that this kernel's CTAs leave, instead of after the last of them has finished.  (After the
-  // wait above, so that the dQ kernel cannot start before the work list is complete either.)
+  // Let the CTAs of the dQ kernel that follows in the stream become resident on the SMs that this kernel's
+  // CTAs leave, instead of after the last of them has finished.  The recomputing dQ kernel reads nothing this
+  // kernel writes and starts working at once; the one that reads the stored dS tiles waits at its top until
+  // this whole grid has completed and its writes are visible.  (After the wait above, so that neither can
+  // start before the work list is complete.)
   grid_launch_dependents();
   if (static_cast<int>(blockIdx.x) >= total_items) return;
   const int2* items = reinterpret_cast<const int2*>(ws + off_items);
@@ -1031,11 +1033,17 @@ hstu_bwd_dq_stored_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* _
   extern __shared__ unsigned char smem_raw[];
   DqsShared& sh = *reinterpret_cast<DqsShared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Every tile this kernel reads was written by the dK/dV kernel before it in the stream: nothing starts
-  // until that kernel has completed and its writes are visible (a no-op for an ordinary launch).
-  grid_dependency_wait();
+  // Every dS tile this kernel reads was written by the dK/dV kernel before it in the stream, which may still be
+  // running when this CTA becomes resident (programmatic dependent launch).  The producer warp therefore waits
+  // for that kernel to have completed, with its writes visible, before its first load (a no-op for an ordinary
+  // launch); barrier set-up, the TMEM allocation and the first claims from the work list, which was complete
+  // before the dK/dV kernel started, do not wait.  A CTA without work waits too, so that this kernel never
+  // completes before the one ahead of it.
   const int total_items = ws[0];
-  if (static_cast<int>(blockIdx.x) >= total_items) return;
+  if (static_cast<int>(blockIdx.x) >= total_items) {
+    grid_dependency_wait();
+    return;
+  }
   const int2* items = reinterpret_cast<const int2*>(ws + off_items);
   volatile int* abort_flag = &sh.abort_flag;
 
@@ -1059,6 +1067,7 @@ hstu_bwd_dq_stored_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* _
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer / tile scheduler
     if (lane == 0) { prefetch_tensormap(&maps.k); prefetch_tensormap(&maps.ds); }
+    grid_dependency_wait();  // the dS tiles are complete and visible from here on
     uint32_t gt = 0, st = 0, ph = 0;
     bool ok = true;
     auto wait_all = [&](unsigned long long* bar, uint32_t parity) -> bool {
