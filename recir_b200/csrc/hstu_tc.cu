@@ -28,6 +28,7 @@
 #include "hstu_launch.h"
 #include "hstu_tc_common.cuh"
 #include "hstu_tc_host.h"
+#include "sm100_pair.cuh"
 
 namespace hstu {
 namespace tc {
@@ -87,10 +88,8 @@ __device__ void suffix_sum_exclusive(const int* in, int* out, long long n, int* 
 // fit (tables_in_smem; 3 * nbins ints of dynamic shared memory), so that the dozen dependent phases of
 // this single-CTA kernel pay shared-memory instead of global-memory latency; the suffix counts are
 // copied to the workspace at the end for build_work_items.
-__global__ void __launch_bounds__(1024) build_block_index(KernelArgs a, int* ws, WorkspaceLayout w, int tables_in_smem) {
-  __shared__ int sh[1024];
-  extern __shared__ int tab[];
-  grid_launch_dependents();  // build_work_items may be made resident now; it waits for this kernel to finish
+__device__ __forceinline__ void block_index_body(const KernelArgs& a, int* ws, const WorkspaceLayout& w, int tables_in_smem,
+                                                 int* sh /* 1024 ints */, int* tab) {
   int* sorted = ws + w.off_sorted;
   int* hist = tables_in_smem ? tab : ws + w.off_hist;
   int* cnt = tables_in_smem ? tab + w.nbins : ws + w.off_cnt;
@@ -205,18 +204,23 @@ __global__ void __launch_bounds__(1024) build_block_index(KernelArgs a, int* ws,
   }
 }
 
+__global__ void __launch_bounds__(1024) build_block_index(KernelArgs a, int* ws, WorkspaceLayout w, int tables_in_smem) {
+  __shared__ int sh[1024];
+  extern __shared__ int tab[];
+  grid_launch_dependents();  // build_work_items may be made resident now; it waits for this kernel to finish
+  block_index_body(a, ws, w, tables_in_smem, sh, tab);
+}
+
 // One thread per work-list entry: decode its rank into (sequence, head, block index).
 // `stride` is the grid of the main kernels: CTA c starts with entry c and claims further entries
 // from a cursor, so the list only has to be in a good ORDER (expensive items early, items that
 // share K/V or Q/dO rows close together); no static deal is needed.
 // Also zeroes the output rows no sequence owns (rows at or past the last offset).
 template <typename T>
-__global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, WorkspaceLayout w, int stride,
-                                                        int tables_in_smem, T* z0,
-                                                        long long rs0, int w0, T* z1, long long rs1, int w1,
-                                                        T* z2, long long rs2, int w2) {
-  grid_dependency_wait();    // build_block_index has finished and its tables are visible
-  grid_launch_dependents();  // the main kernel may be made resident; it waits for this kernel to finish
+__device__ __forceinline__ void work_items_body(const KernelArgs& a, int* ws, const WorkspaceLayout& w, int stride,
+                                                int tables_in_smem, int* tab, long long gtid, long long gsz, T* z0,
+                                                long long rs0, int w0, T* z1, long long rs1, int w1, T* z2,
+                                                long long rs2, int w2) {
   const int* sorted = ws + w.off_sorted;
   const int* cnt = ws + w.off_cnt;
   const int* chunk_base = ws + w.off_chunk;
@@ -224,8 +228,7 @@ __global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, W
   const int total = ws[0];
   // the two tables every thread searches are copied to shared memory first when they fit
   // (tables_in_smem: nbins + n_chunks + 1 ints of dynamic shared memory)
-  extern __shared__ int tab[];
-  if (tables_in_smem) {
+    if (tables_in_smem) {
     const int n_chunks1 = (ws[1] + w.chunk_seqs - 1) / w.chunk_seqs + 1;
     int* s_cnt = tab;
     int* s_chunk = tab + w.nbins;
@@ -235,8 +238,6 @@ __global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, W
     cnt = s_cnt;
     chunk_base = s_chunk;
   }
-  const long long gtid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-  const long long gsz = (long long)gridDim.x * blockDim.x;
   for (long long slot = gtid; slot < total; slot += gsz) {
     const long long p = slot;  // rank in the list order
     // Rank p -> item.  The sorted sequences are cut into chunks of chunk_seqs; the list is
@@ -291,6 +292,38 @@ __global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, W
     if (z1 && c < w1) z1[r * rs1 + c] = from_f32<T>(0.f);
     if (z2 && c < w2) z2[r * rs2 + c] = from_f32<T>(0.f);
   }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) build_work_items(KernelArgs a, int* ws, WorkspaceLayout w, int stride,
+                                                        int tables_in_smem, T* z0,
+                                                        long long rs0, int w0, T* z1, long long rs1, int w1,
+                                                        T* z2, long long rs2, int w2) {
+  extern __shared__ int tab[];
+  grid_dependency_wait();    // build_block_index has finished and its tables are visible
+  grid_launch_dependents();  // the main kernel may be made resident; it waits for this kernel to finish
+  work_items_body<T>(a, ws, w, stride, tables_in_smem, tab, blockIdx.x * (long long)blockDim.x + threadIdx.x,
+                     (long long)gridDim.x * blockDim.x, z0, rs0, w0, z1, rs1, w1, z2, rs2, w2);
+}
+
+// Both steps in one launch: a cluster of WORK_LIST_CLUSTER CTAs.  The CTA of rank 0 builds the tables (one
+// CTA's work: a dozen dependent phases over the sequences), the cluster barrier publishes them, and all CTAs
+// decode the entries.  One launch and no dependency between two grids: about a third less time in front of
+// every main kernel than the two kernels above, which remain for tables too large for shared memory.
+constexpr int WORK_LIST_CLUSTER = 8;
+template <typename T>
+__global__ void __launch_bounds__(1024) build_work_list(KernelArgs a, int* ws, WorkspaceLayout w, int stride, T* z0,
+                                                       long long rs0, int w0, T* z1, long long rs1, int w1, T* z2,
+                                                       long long rs2, int w2) {
+  __shared__ int sh[1024];
+  extern __shared__ int tab[];
+  grid_launch_dependents();  // the main kernel may be made resident; it waits for this kernel to finish
+  const uint32_t rank = cluster_cta_rank();
+  if (rank == 0) block_index_body(a, ws, w, 1, sh, tab);
+  __threadfence();
+  cluster_sync_all();  // the tables in the workspace are complete and visible to the whole cluster
+  work_items_body<T>(a, ws, w, stride, 1, tab, rank * (long long)blockDim.x + threadIdx.x,
+                     (long long)WORK_LIST_CLUSTER * blockDim.x, z0, rs0, w0, z1, rs1, w1, z2, rs2, w2);
 }
 
 // ------------------------------------------------------------------------------------
@@ -995,37 +1028,67 @@ int sm_count() {
   return n;
 }
 
+// Sequences per locality chunk of the work list: the K/V (or Q/dO) rows of one chunk should stay in
+// L2 while its items run, about 16 k tokens of 4 heads x 128 columns; chunks start with the longest
+// sequences, so the caller's length bound sizes them.  Measured: 4 is best for sequences up to 4224
+// tokens (1 % over 8), 6-12 are level for 2112-token sequences, 4 and 8 are level for 8 heads x 8 k.
+static int chunk_seqs_for(const KernelArgs& a) {
+  const long long budget = 16384LL * 4 / (a.H > 0 ? a.H : 1);
+  const long long n = a.max_seq_len > 0 ? a.max_seq_len : 1;
+  const long long c = (budget + n / 2) / n;
+  int chunk = static_cast<int>(c < 4 ? 4 : (c > 16 ? 16 : c));
+#ifdef B200_HSTU_PROFILING
+  if (const char* e = getenv("B200_HSTU_CHUNK")) chunk = atoi(e) > 0 ? atoi(e) : chunk;
+#endif
+  return chunk;
+}
+
+// Ints of dynamic shared memory of the table step and of the entry step of the work-list construction; the
+// tables live in shared memory when they fit under the default 48 KB (next to 4 KB of static shared memory).
+constexpr long long WORK_LIST_SMEM_INTS = 10240;
+static long long index_table_ints(const WorkspaceLayout& w) { return 3 * w.nbins; }
+static long long item_table_ints(const KernelArgs& a, const WorkspaceLayout& w) {
+  return w.nbins + (a.B + w.chunk_seqs - 1) / w.chunk_seqs + 1;
+}
+
 template <typename T>
 static cudaError_t launch_prep_t(const KernelArgs& a, int* ws, const WorkspaceLayout& w_in, bool backward, cudaStream_t st) {
   WorkspaceLayout w = w_in;
-  // Sequences per locality chunk of the work list: the K/V (or Q/dO) rows of one chunk should stay in
-  // L2 while its items run, about 16 k tokens of 4 heads x 128 columns; chunks start with the longest
-  // sequences, so the caller's length bound sizes them.  Measured: 4 is best for sequences up to 4224
-  // tokens (1 % over 8), 6-12 are level for 2112-token sequences, 4 and 8 are level for 8 heads x 8 k.
-  {
-    const long long budget = 16384LL * 4 / (a.H > 0 ? a.H : 1);
-    const long long n = a.max_seq_len > 0 ? a.max_seq_len : 1;
-    long long c = (budget + n / 2) / n;
-    w.chunk_seqs = static_cast<int>(c < 4 ? 4 : (c > 16 ? 16 : c));
+  w.chunk_seqs = chunk_seqs_for(a);
+  const long long index_ints = index_table_ints(w);
+  const int index_smem = index_ints <= WORK_LIST_SMEM_INTS ? 1 : 0;
+  const int stride = main_grid(w);
+  const long long item_ints = item_table_ints(a, w);
+  const int item_smem = item_ints <= WORK_LIST_SMEM_INTS ? 1 : 0;
+  const size_t item_bytes = item_smem ? item_ints * sizeof(int) : 0;
+  T *z0 = reinterpret_cast<T*>(a.o), *z1 = nullptr, *z2 = nullptr;
+  long long rs0 = a.o_rs, rs1 = 0, rs2 = 0;
+  int w0 = a.H * a.Dv, w1 = 0, w2 = 0;
+  if (backward) {
+    z0 = reinterpret_cast<T*>(a.dq); rs0 = a.dq_rs; w0 = a.H * a.Dqk;
+    z1 = reinterpret_cast<T*>(a.dk); rs1 = a.dk_rs; w1 = a.H * a.Dqk;
+    z2 = reinterpret_cast<T*>(a.dv); rs2 = a.dv_rs; w2 = a.H * a.Dv;
   }
-#ifdef B200_HSTU_PROFILING
-  if (const char* e = getenv("B200_HSTU_CHUNK")) w.chunk_seqs = atoi(e) > 0 ? atoi(e) : w.chunk_seqs;
-#endif
-  // tables in shared memory when they fit under the default 48 KB (next to 4 KB of static shared memory)
-  const long long index_ints = 3 * w.nbins;
-  const int index_smem = index_ints <= 10240 ? 1 : 0;
+  if (index_smem && item_smem) {
+    // one launch: a cluster whose first CTA builds the tables and whose CTAs all decode the entries
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(WORK_LIST_CLUSTER);
+    cfg.blockDim = dim3(1024);
+    cfg.dynamicSmemBytes = static_cast<size_t>(index_ints > item_ints ? index_ints : item_ints) * sizeof(int);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = WORK_LIST_CLUSTER;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, build_work_list<T>, a, ws, w, stride, z0, rs0, w0, z1, rs1, w1, z2, rs2, w2);
+  }
   build_block_index<<<1, 1024, index_smem ? index_ints * sizeof(int) : 0, st>>>(a, ws, w, index_smem);
   const int blocks = sm_count() * 2;
-  const int stride = main_grid(w);
-  const long long item_ints = w.nbins + (a.B + w.chunk_seqs - 1) / w.chunk_seqs + 1;
-  const int item_smem = item_ints <= 10240 ? 1 : 0;
-  const size_t item_bytes = item_smem ? item_ints * sizeof(int) : 0;
-  if (!backward)
-    return launch_dependent(build_work_items<T>, blocks, 256, item_bytes, st, true, a, ws, w, stride, item_smem,
-                            reinterpret_cast<T*>(a.o), a.o_rs, a.H * a.Dv, (T*)nullptr, 0, 0, (T*)nullptr, 0, 0);
-  return launch_dependent(build_work_items<T>, blocks, 256, item_bytes, st, true, a, ws, w, stride, item_smem,
-                          reinterpret_cast<T*>(a.dq), a.dq_rs, a.H * a.Dqk, reinterpret_cast<T*>(a.dk), a.dk_rs,
-                          a.H * a.Dqk, reinterpret_cast<T*>(a.dv), a.dv_rs, a.H * a.Dv);
+  return launch_dependent(build_work_items<T>, blocks, 256, item_bytes, st, true, a, ws, w, stride, item_smem, z0, rs0,
+                          w0, z1, rs1, w1, z2, rs2, w2);
 }
 
 // Workspace of a backward call: the work list, and (unless the caller asked for the recomputing dQ pass, or
@@ -1088,8 +1151,11 @@ size_t tc_workspace_bytes(const KernelArgs& a, int pass) {
 }
 
 int tc_launch_count(const KernelArgs& a, int pass) {
-  (void)a;
-  return pass == 0 ? 3 : 4;
+  // the work list (one launch when its tables fit shared memory, else two), then the main kernel(s)
+  tc::WorkspaceLayout w = tc::workspace_layout(a.T, a.B, a.H);
+  w.chunk_seqs = tc::chunk_seqs_for(a);
+  const bool one = tc::index_table_ints(w) <= tc::WORK_LIST_SMEM_INTS && tc::item_table_ints(a, w) <= tc::WORK_LIST_SMEM_INTS;
+  return (one ? 1 : 2) + (pass == 0 ? 1 : 2);
 }
 
 cudaError_t tc_forward(const KernelArgs& a, int dtype, void* workspace, cudaStream_t st) {

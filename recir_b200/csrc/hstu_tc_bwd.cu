@@ -585,9 +585,10 @@ hstu_bwd_dkv_tc(const __grid_constant__ MapsBwd maps, KernelArgs a, int* __restr
   extern __shared__ unsigned char smem_raw[];
   DkvShared& sh = *reinterpret_cast<DkvShared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total_items = ws[0];
-  // Launched as a dependent of build_work_items: the work list is complete from here on.
+  // Launched as a dependent of the work-list kernel, which lets its dependents become resident as soon as it
+  // starts: nothing of the workspace is read before this wait, after which the work list is complete.
   grid_dependency_wait();
+  const int total_items = ws[0];
   // Let the CTAs of the dQ kernel that follows in the stream become resident on the SMs that this kernel's
   // CTAs leave, instead of after the last of them has finished.  The recomputing dQ kernel reads nothing this
   // kernel writes and starts working at once; the one that reads the stored dS tiles waits at its top until

@@ -60,6 +60,8 @@ _WAIT_NAMES = {101: "WAIT_PRODUCER (TMA producer warp)", 102: "WAIT_MMA (MMA iss
 _bwd_extra_flags = 0
 # Kernel launches issued through this module since import (launch accounting for the benchmark).
 launch_counter = 0
+# Forward / backward calls served by the tensor-core kernels since import (the rest ran on the CUDA-core kernels).
+tensor_core_calls = 0
 
 
 def set_force_simt(flag: bool) -> None:
@@ -272,7 +274,7 @@ def _pad_head_dim(t: torch.Tensor) -> torch.Tensor:
 def _fwd_cuda(q, k, v, seq_offsets, max_seq_len, alpha, causal, num_targets, contextual_seq_len,
               max_attn_len, attn_scale, full_attn_size=0, out=None):
     """``out``: optional result tensor of the caller ([T, H, Dv], rows contiguous); allocated when absent."""
-    global launch_counter
+    global launch_counter, tensor_core_calls
     validate_inputs(q, k, v, seq_offsets, num_targets, max_seq_len, attn_scale)
     lib = _lib.load()
     q, k, v = _rows(q), _rows(k), _rows(v)
@@ -300,6 +302,7 @@ def _fwd_cuda(q, k, v, seq_offsets, max_seq_len, alpha, causal, num_targets, con
         rc = lib.b200_hstu_fwd(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         _check(rc, "b200_hstu_fwd")
         launch_counter += lib.b200_hstu_launch_count(ctypes.byref(p), 0)
+        tensor_core_calls += lib.b200_hstu_uses_tensor_cores(ctypes.byref(p), 0) == 1
         if _checked:
             check_status(q.device, "b200_hstu_fwd")
     del keep
@@ -309,7 +312,7 @@ def _fwd_cuda(q, k, v, seq_offsets, max_seq_len, alpha, causal, num_targets, con
 def _bwd_cuda(dout, q, k, v, seq_offsets, max_seq_len, alpha, causal, num_targets, contextual_seq_len,
               max_attn_len, attn_scale, full_attn_size=0, grads=None):
     """``grads``: optional (dq, dk, dv) tensors of the caller, shaped like q, k, v with contiguous rows."""
-    global launch_counter
+    global launch_counter, tensor_core_calls
     validate_inputs(q, k, v, seq_offsets, num_targets, max_seq_len, attn_scale, dout)
     lib = _lib.load()
     q, k, v, dout = _rows(q), _rows(k), _rows(v), _rows(dout)
@@ -347,6 +350,7 @@ def _bwd_cuda(dout, q, k, v, seq_offsets, max_seq_len, alpha, causal, num_target
         rc = lib.b200_hstu_bwd(ctypes.byref(p), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         _check(rc, "b200_hstu_bwd")
         launch_counter += lib.b200_hstu_launch_count(ctypes.byref(p), 1)
+        tensor_core_calls += lib.b200_hstu_uses_tensor_cores(ctypes.byref(p), 1) == 1
         if _checked:
             check_status(q.device, "b200_hstu_bwd")
     del keep
