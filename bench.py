@@ -493,6 +493,21 @@ def main():
                 out.append(e[0].elapsed_time(e[1]) / reps)
         return out
 
+    # One call at a time with the L2 written over in between (a 256 MB fill): the cold-cache variant.
+    def time_cold(fn, rounds=7):
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        out = []
+        for _ in range(rounds):
+            flush.fill_(1)
+            e[0].record()
+            fn()
+            e[1].record()
+            torch.cuda.synchronize()
+            out.append(e[0].elapsed_time(e[1]))
+        del flush
+        return float(np.median(out[1:]))
+
     run_fwd = lambda: torch.ops.recir.b200_hstu_attention_fwd(d["q"], d["k"], d["v"], *args_op)
     run_bwd = lambda: torch.ops.recir.b200_hstu_attention_bwd(d["do"], d["q"], d["k"], d["v"], *args_op)
     fwd_ms, bwd_ms = time_pass(run_fwd), time_pass(run_bwd)
@@ -501,6 +516,8 @@ def main():
     ops.set_backward_passes(dkv=False, dq=True, timing_only=True)
     dq_ms = time_pass(run_bwd)
     ops.set_backward_passes(True, True)
+    cold = None if args.no_extras else {"fwd_ms": time_cold(run_fwd), "bwd_ms": time_cold(run_bwd),
+                                        "note": "one call at a time, a 256 MB fill before each (L2 holds 126 MB)"}
     value = flops_step * args.steps / (ms_total * 1e-3) / 1e12
     clocks = sampler.stop() if sampler is not None else None  # over the headline and the per-pass timed regions
 
@@ -676,8 +693,9 @@ def main():
             "fwd_tflops": workload.useful_flops(local_pairs, H, D, D, backward=False) / (fwd_med * 1e-3) / 1e12,
             "bwd_tflops": workload.useful_flops(local_pairs, H, D, D, backward=True, forward=False) / (bwd_med * 1e-3) / 1e12,
             "timing": "per-pass and per-kernel times: median of 5 samples of 10 calls issued back to back (a burst, "
-                      "each pass with its two work-list kernels); they need not add up to ms_per_step, which is "
+                      "each pass with its work-list kernel); they need not add up to ms_per_step, which is "
                       "forward and backward alternating",
+            "cold_l2": cold,
         }
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
