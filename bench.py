@@ -53,7 +53,7 @@ NOMINAL_BF16_TFLOPS = 2250.0
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from the committed ncu capture of the same
 # B/H/D and length distribution (profiles/tc_kernels_cfg1_ncu_full.md names the build it was taken
 # from), and that capture's token count.
-NCU_CFG1_DRAM_BYTES = {"hstu_fwd_tc": 314.4e6, "hstu_bwd_dkv_tc": 1060.8e6, "hstu_bwd_dq_tc": 715.8e6}
+NCU_CFG1_DRAM_BYTES = {"hstu_fwd_tc": 313.8e6, "hstu_bwd_dkv_tc": 1071.1e6, "hstu_bwd_dq_tc": 717.8e6}
 NCU_CFG1_TOKENS = 78262
 NCU_CAPTURE = "profiles/tc_kernels_cfg1_ncu_full.md"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
