@@ -515,7 +515,15 @@ def main():
     dkv_ms = time_pass(run_bwd)
     ops.set_backward_passes(dkv=False, dq=True, timing_only=True)
     dq_ms = time_pass(run_bwd)
+    # the same two kernels in the recomputing form of the backward (no dS tiles written or read)
+    ops.set_backward_passes(dkv=True, dq=False)
+    dkv_plain_ms = float(np.median(time_pass(run_bwd)))
+    ops.set_backward_passes(dkv=False, dq=True)
+    dq_plain_ms = float(np.median(time_pass(run_bwd)))
     ops.set_backward_passes(True, True)
+    ops.set_recompute_dq(True)
+    bwd_plain_ms = float(np.median(time_pass(run_bwd)))
+    ops.set_recompute_dq(False)
     cold = None if args.no_extras else {"fwd_ms": time_cold(run_fwd), "bwd_ms": time_cold(run_bwd),
                                         "note": "one call at a time, a 256 MB fill before each (L2 holds 126 MB)"}
     value = flops_step * args.steps / (ms_total * 1e-3) / 1e12
@@ -696,6 +704,13 @@ def main():
                       "each pass with its work-list kernel); they need not add up to ms_per_step, which is "
                       "forward and backward alternating",
             "cold_l2": cold,
+            # The dominant kernel also writes the dS tiles (32 KB per kept tile) that spare the dQ pass two of its
+            # three GEMMs and its transcendental pass: the same pair of kernels without the tiles, for comparison.
+            "recomputing_backward": {
+                "hstu_bwd_dkv_tc_ms": dkv_plain_ms, "hstu_bwd_dq_tc_ms": dq_plain_ms, "bwd_ms": bwd_plain_ms,
+                "hstu_bwd_dkv_tc_frac": kernels["hstu_bwd_dkv_tc"][0] / (dkv_plain_ms * 1e-3) / 1e12 / peak,
+                "note": "B200_HSTU_FLAG_BWD_RECOMPUTE_DQ: dK/dV kernel without the tile stores, dQ kernel "
+                        "recomputing S and dP; the default backward is `bwd_ms` above"},
         }
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
