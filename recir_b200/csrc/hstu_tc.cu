@@ -1083,7 +1083,10 @@ static cudaError_t launch_prep_t(const KernelArgs& a, int* ws, const WorkspaceLa
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, build_work_list<T>, a, ws, w, stride, z0, rs0, w0, z1, rs1, w1, z2, rs2, w2);
+    if (cudaLaunchKernelEx(&cfg, build_work_list<T>, a, ws, w, stride, z0, rs0, w0, z1, rs1, w1, z2, rs2, w2) ==
+        cudaSuccess)
+      return cudaSuccess;
+    (void)cudaGetLastError();  // a device that cannot place the cluster: the two kernels below do the same work
   }
   build_block_index<<<1, 1024, index_smem ? index_ints * sizeof(int) : 0, st>>>(a, ws, w, index_smem);
   const int blocks = sm_count() * 2;
