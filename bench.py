@@ -550,7 +550,7 @@ def main():
     # streams (recir_b200.HostPipeline), so both PCIe directions overlap with the kernels.
     out_host = {k: torch.empty_like(host[k]).pin_memory() for k in ("q", "k", "v", "do")}
     pipe = recir_b200.HostPipeline(local["off"], local["nt"], H, D, D, torch.bfloat16, batch.max_seq_len,
-                                   batch.alpha, n_chunks=14, device=dev)
+                                   batch.alpha, n_chunks=12, device=dev)
 
     def step_e2e():
         pipe.run(host["q"], host["k"], host["v"], host["do"], out_host["do"], out_host["q"], out_host["k"],

@@ -2,7 +2,7 @@
 
 Sequences never interact, so a jagged batch can be streamed: the token rows are copied in as
 chunks of equal size, every sequence is computed as soon as its last row has arrived, and results
-leave in chunks of the same size as soon as their last sequence has been computed.  PCIe is full
+leave in chunks of the same size, trailing the inputs by at most one sequence.  PCIe is full
 duplex, so the two copy directions overlap with each other and with the kernels.  Three CUDA
 streams (copy-in, compute, copy-out) over device buffers that hold the whole batch.
 
@@ -128,23 +128,24 @@ def plan_steps(offs: np.ndarray, n_chunks: int) -> list[dict]:
     """The pipeline's schedule for sequence offsets ``offs`` (``[B + 1]``, starting at 0): a list of steps,
     each ``{"rows_in": (t0, t1), "seqs": (b0, b1), "rows_out": (r0, r1)}``.  Step ``c`` copies in rows
     ``[t0, t1)`` (``n_chunks`` pieces of equal size), computes the sequences ``[b0, b1)`` that are complete
-    with those rows, and copies out rows ``[r0, r1)``: as many whole pieces as are computed by then.  The
-    last step copies out the rest."""
+    with those rows, and copies out rows ``[r0, r1)``.  The copy-out pieces are the copy-in pieces shifted back
+    by ``lag`` rows, the largest number of rows any step leaves uncomputed behind its cut (at most the longest
+    sequence): equal sizes again, except a shorter first and a longer last one, and the results trail the
+    inputs by ``lag`` rows instead of a whole piece."""
     total = int(offs[-1])
     B = len(offs) - 1
     cuts = [total * c // n_chunks for c in range(n_chunks + 1)]
+    ends, b_prev = [], 0
+    for c in range(n_chunks):
+        # sequences whose end is at or before the cut (empty sequences at the very end are swept up by the last step)
+        b1 = int(np.searchsorted(offs, cuts[c + 1], side="right")) - 1
+        b1 = B if c == n_chunks - 1 else max(b_prev, min(b1, B))
+        ends.append(b1)
+        b_prev = b1
+    lag = max((cuts[c + 1] - int(offs[ends[c]]) for c in range(n_chunks - 1)), default=0)
     steps, b_prev, r_prev = [], 0, 0
     for c in range(n_chunks):
-        t0, t1 = cuts[c], cuts[c + 1]
-        # sequences whose end is at or before t1 (empty sequences at the very end are swept up by the last step)
-        b1 = int(np.searchsorted(offs, t1, side="right")) - 1
-        b1 = B if c == n_chunks - 1 else max(b_prev, min(b1, B))
-        ready = int(offs[b1])  # every row below this is computed after this step
-        if c == n_chunks - 1:
-            r1 = total
-        else:
-            j = int(np.searchsorted(np.asarray(cuts), ready, side="right")) - 1  # largest cut <= ready
-            r1 = max(r_prev, cuts[j])
-        steps.append({"rows_in": (t0, t1), "seqs": (b_prev, b1), "rows_out": (r_prev, r1)})
-        b_prev, r_prev = b1, r1
+        r1 = total if c == n_chunks - 1 else max(r_prev, cuts[c + 1] - lag)
+        steps.append({"rows_in": (cuts[c], cuts[c + 1]), "seqs": (b_prev, ends[c]), "rows_out": (r_prev, r1)})
+        b_prev, r_prev = ends[c], r1
     return steps
